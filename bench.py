@@ -1,0 +1,402 @@
+#!/usr/bin/env python3
+"""Benchmark of the b-posit W8A8 hot path on B200.
+
+Headline (one JSON line on rank 0): bit-exact bp8 quire-GEMM throughput in
+TOPS (2*M*N*K / time) on the large bp8 GEMM M=4096, N=4096, K=65536 with
+operands N(0,1) * 2^U{-8..8} per row (seeded, synthetic), the output dimension
+N sharded over the ranks and the bposit32 result all-gathered over NCCL.
+The same line carries the encode/decode sweep (2^28 fp32 per rank) in GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+--impl reference times the CPU oracle port (oracle/, all host threads) on a
+bounded row sample of the same GEMM: rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "open-bposit_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+M_, N_, K_ = 4096, 4096, 65536
+METRIC = "bit-exact bp8 W8A8 quire-GEMM TOPS (bp8 4096x4096x65536, N-sharded)"
+WORKLOAD = ("bp8 exact quire GEMM M=4096 N=4096 K=65536, operands N(0,1)*2^U{-8..8} per row, "
+            "RTN-quantized; one bposit32 round per output; N sharded over ranks + NCCL all-gather")
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"bposit_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_operand(ops, torch, rows, K, gen, device):
+    """bp8 RTN codes of N(0,1) * 2^U{-8..8} per row (generated in chunks)."""
+    out = torch.empty((rows, K), dtype=torch.uint8, device=device)
+    step = 512
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        x = torch.randn((r1 - r0, K), device=device, generator=gen)
+        e = torch.randint(-8, 9, (r1 - r0, 1), device=device, generator=gen).float()
+        ops.quantize_bp8(x * torch.exp2(e), nearest=True, out=out[r0:r1])
+    return out
+
+
+def cpu_reference(A_rows, B, target_s: float, threads: int):
+    """Time the oracle port's quire GEMM (one row per host thread) on a row
+    sample sized to about target_s seconds; returns (TOPS, rows, seconds)."""
+    from oracle import oracle
+    n = min(threads, A_rows.shape[0])
+    t0 = time.perf_counter()
+    oracle.quire_gemm(A_rows[:n], B, 8, nthreads=threads)
+    t1 = time.perf_counter() - t0
+    rows, dt = n, t1
+    reps = int(round(target_s / max(t1, 1e-6)))
+    if reps > 1:
+        rows = min(A_rows.shape[0], n * reps)
+        t0 = time.perf_counter()
+        oracle.quire_gemm(A_rows[:rows], B, 8, nthreads=threads)
+        dt = time.perf_counter() - t0
+    tops = 2.0 * rows * B.shape[0] * B.shape[1] / dt / 1e12
+    return tops, rows, dt
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    from oracle import oracle  # noqa: F401  (built by __graft_entry__.build)
+    threads = max(1, len(os.sched_getaffinity(0)))
+    # same operand distribution as the GPU arm, generated on the host
+    rng = np.random.default_rng(0)
+    rows_needed = max(64, 4 * threads)
+    from oracle import oracle as orc
+    A = orc.quantize_bp8((rng.standard_normal((rows_needed, K_)) *
+                          np.exp2(rng.integers(-8, 9, (rows_needed, 1)))).astype(np.float32))[0]
+    B = orc.quantize_bp8((rng.standard_normal((N_, K_)) *
+                          np.exp2(rng.integers(-8, 9, (N_, 1)))).astype(np.float32))[0]
+    per_step = max(2.0, 60.0 / max(1, args.steps + args.warmup))
+    for _ in range(args.warmup):
+        orc.quire_gemm(A[:1], B[:256], 8, nthreads=threads)
+    vals, rows_used, secs = [], 0, 0.0
+    for _ in range(args.steps):
+        v, rows_used, dt = cpu_reference(A, B, per_step, threads)
+        vals.append(v)
+        secs += dt
+    value = statistics.median(vals)
+    sample = f"{rows_used} of {M_} rows x N={N_} x K={K_} per step (oracle port, {threads} threads)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / max(1, args.steps),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "M": M_, "N": N_, "K": K_, "fmt": "bp8",
+                                        "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def codec_sweep(ops, torch, device, world, steps, peaks):
+    """2^28 fp32 per rank: bp8 RTN encode, bp8 decode, bp16 RTNE encode, bp16 decode."""
+    import torch.distributed as dist
+    n = 1 << 28
+    gen = torch.Generator(device=device).manual_seed(1234 + (dist.get_rank() if world > 1 else 0))
+    x = torch.empty(n, dtype=torch.float32, device=device)
+    half = n // 2
+    x[:half].normal_(generator=gen)
+    e = torch.empty(n - half, dtype=torch.float32, device=device).uniform_(-26, 26, generator=gen)
+    x[half:] = torch.exp2(e) * torch.where(torch.rand(n - half, device=device, generator=gen) < 0.5, -1.0, 1.0)
+    del e
+    c8 = torch.empty(n, dtype=torch.uint8, device=device)
+    c16 = torch.empty(n, dtype=torch.uint16, device=device)
+    y = torch.empty(n, dtype=torch.float32, device=device)
+    kernels = {
+        "bp8_encode_rtn": (lambda: ops.quantize_bp8(x, nearest=True, out=c8), 5),
+        "bp8_decode": (lambda: _decode_into(ops, c8, y), 5),
+        "bp16_encode_rtne": (lambda: ops.encode_bp16(x, rtne=True, out=c16), 6),
+        "bp16_decode": (lambda: _decode_into(ops, c16, y), 6),
+    }
+    res = {}
+    for name, (fn, bpe) in kernels.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(steps):
+            fn()
+        t.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(t) / steps
+        if world > 1:
+            tt = torch.tensor([ms], device=device)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms = float(tt.item())
+        gbs = bpe * n * world / (ms * 1e-3) / 1e9
+        res[name] = {"GB/s": round(gbs, 1), "ms": round(ms, 4), "bytes_per_elem": bpe,
+                     "frac_of_measured_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+    del x, c8, c16, y
+    torch.cuda.empty_cache()
+    return {"elements_per_gpu": n, "scaling": "weak", "l2": "1 GiB input > L2", "kernels": res}
+
+
+def _decode_into(ops, codes, y):
+    """decode through the C ABI straight into a preallocated output."""
+    import ctypes
+
+    import torch
+    from bposit_b200 import _lib
+    f = 8 if codes.dtype == torch.uint8 else 16
+    _lib.check(_lib.lib().bp_decode(f, ctypes.c_void_p(codes.data_ptr()), codes.numel(),
+                                    ctypes.c_void_p(y.data_ptr()),
+                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from bposit_b200 import _lib, ops
+    from bposit_b200.dist import ShardedQuireGemm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    peaks, peak_src = load_peaks()
+
+    gen = torch.Generator(device=device).manual_seed(0)
+    A = make_operand(ops, torch, M_, K_, gen, device)
+    B = make_operand(ops, torch, N_, K_, gen, device)
+    g = ShardedQuireGemm(M_, N_, device, algo=args.algo)
+    n0, n1 = g.plan.bounds
+    Bs = B[n0:n1].contiguous()
+    del B
+    torch.cuda.empty_cache()
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+
+    stream = torch.cuda.current_stream()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+
+    def gemm_only(i=None):
+        if i is not None:
+            kev[i][0].record(stream)
+        out_view = g.local[:, :n1 - n0] if world > 1 else g.result
+        g.gemm_fn(A, Bs, out_view, None, None)
+        if i is not None:
+            kev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(g.gathered.view(-1).view(torch.int32),
+                                        g.local.view(-1).view(torch.int32))
+            from bposit_b200.dist import assemble
+            assemble(g.gathered, g.plan, g.result)
+        return g.result
+
+    for _ in range(args.warmup):
+        gemm_only()
+    sync_all()
+    clocks = Clocks(local) if local == 0 else None
+    if clocks:
+        clocks.start()
+    launches0 = _lib.lib().bp_launch_count()
+    s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sync_all()
+    s.record(stream)
+    for i in range(args.steps):
+        gemm_only(i)
+    t.record(stream)
+    sync_all()
+    launches = _lib.lib().bp_launch_count() - launches0
+    clk = clocks.stop() if clocks else None
+    ms = s.elapsed_time(t) / args.steps
+    kms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    if world > 1:
+        tt = torch.tensor([ms, kms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms, kms = float(tt[0]), float(tt[1])
+    tops = 2.0 * M_ * N_ * K_ / (ms * 1e-3) / 1e12
+    per_rank_ops = 2.0 * M_ * (n1 - n0) * K_
+    k_tops = per_rank_ops / (kms * 1e-3) / 1e12
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+
+    # end to end through the public API with host buffers (pinned)
+    hA = A.cpu().pin_memory()
+    hB = Bs.cpu().pin_memory()
+    hOut = torch.empty((M_, N_), dtype=torch.uint32).pin_memory()
+    dA = torch.empty_like(A)
+    dB = torch.empty_like(Bs)
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        out_view = g.local[:, :n1 - n0] if world > 1 else g.result
+        g.gemm_fn(dA, dB, out_view, None, None)
+        if world > 1:
+            dist.all_gather_into_tensor(g.gathered.view(-1).view(torch.int32), g.local.view(-1).view(torch.int32))
+            from bposit_b200.dist import assemble
+            assemble(g.gathered, g.plan, g.result)
+        hOut.copy_(g.result, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_step()
+    sync_all()
+    es, et = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    et.record(stream)
+    sync_all()
+    ems = es.elapsed_time(et) / e2e_steps
+    if world > 1:
+        tt = torch.tensor([ems], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ems = float(tt.item())
+    e2e_tops = 2.0 * M_ * N_ * K_ / (ems * 1e-3) / 1e12
+    del hA, hB, dA, dB
+
+    codec = codec_sweep(ops, torch, device, world, 10, peaks)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = max(1, len(os.sched_getaffinity(0)))
+        An = A[:max(64, 4 * threads)].cpu().numpy()
+        Bn = Bs.cpu().numpy()
+        v, rows, dt = cpu_reference(An, Bn, 15.0, threads)
+        cpu = {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
+               "sample": f"{rows} rows x N={N_} x K={K_} of the same operands ({dt:.1f} s)"}
+
+    traffic = None
+    tp = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tj = json.load(f)
+        ent = tj.get("quire_gemm_" + ("tc" if args.algo != 1 else "simt"))
+        if ent and "bytes_per_mac" in ent:
+            traffic = ent["bytes_per_mac"] * M_ * (n1 - n0) * K_
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tops, 3), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "M": M_, "N": N_, "K": K_, "fmt": "bp8",
+                       "parallelism": f"N-shard x{world} + NCCL all-gather",
+                       "l2": "inputs 512 MiB > L2 (no flush needed)", "algo": args.algo},
+            "roofline": {"bound": "tensor", "achieved": round(k_tops, 3), "peak": round(int8_peak, 1),
+                         "unit": "TOPS", "frac": round(k_tops / int8_peak, 5), "traffic": traffic,
+                         "peak_source": f"int8 dense = 2 x {peak_src} bf16 {peaks['bf16_tflops']} TF/s",
+                         "kernel": "quire GEMM (row stats + GEMM launches)", "kernel_ms": round(kms, 3)},
+            "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS", "ms_per_step": round(ems, 3),
+                    "h2d_bytes_per_step": int(M_ * K_ + (n1 - n0) * K_),
+                    "d2h_bytes_per_step": int(M_ * N_ * 4)},
+            "cpu_baseline": cpu,
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "encode_decode": codec,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,128 @@
+/*
+ * bposit_b200.h -- C ABI of the B200 (sm_100a) b-posit W8A8 hot path.
+ *
+ * Plain pointers, sizes and an opaque CUDA stream (cudaStream_t passed as
+ * void*; NULL = the legacy default stream).  Every device pointer must point
+ * to memory of the current CUDA device.  Every call is asynchronous on
+ * `stream` and returns a status: BP_OK (0) or a negative BP_E* code, with a
+ * message in bp_last_error() (thread-local).  No C++ exception crosses the ABI.
+ * Library-owned state is limited to immutable tables each kernel builds in
+ * shared memory; calls on different streams are independent.
+ *
+ * Formats: fmt = 8 (bp8: 8-bit posit, eS=2, codes uint8) or 16 (bp16: 16-bit
+ * posit, eS=3, codes uint16).  bp32 results are uint32 codes (eS=3).  Quires
+ * are two's complement integers with 96 fraction bits stored as
+ * little-endian 32-bit limbs.
+ *
+ * Reference interfaces each entry point replaces (paths relative to the
+ * open-bposit project root) are cited per function.
+ */
+#ifndef BPOSIT_B200_H
+#define BPOSIT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BP_OK 0
+#define BP_EINVAL (-1)     /* null pointer, negative size, bad group / limb count */
+#define BP_EFMT (-2)       /* unsupported format */
+#define BP_EALIGN (-3)     /* pointer alignment the call requires is not met */
+#define BP_ECUDA (-4)      /* CUDA error (launch or runtime) */
+#define BP_ERANGE (-5)     /* size beyond what the call supports */
+#define BP_ENODEV (-6)     /* no sm_100 device is current */
+#define BP_EWORKSPACE (-7) /* workspace missing or too small */
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+int bp_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char *bp_last_error(void);
+
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads).  Diagnostic; no reference counterpart. */
+unsigned long long bp_launch_count(void);
+
+/* Decode n codes to their exact fp32 values; zero and NaR give +0.0.
+ * Replaces bposit_ref.code_value (reference/bposit_ref.py:1022-1025) and the
+ * (mantissa, exponent) LUT of bposit_fast._lut (reference/bposit_fast.py:27-43).
+ * Both bp8 and bp16 values are exactly representable in fp32. */
+int bp_decode(int fmt, const void *codes, size_t n, float *out, void *stream);
+
+/* fp32 -> bp8 codes (and, when `values` is non-NULL, their exact fp32 values).
+ * nearest = 1: bposit_fast.quantize_bp8(x, nearest=True) -- round to the
+ * nearest grid magnitude, ties toward the smaller magnitude; nearest = 0: the
+ * truncating mode (largest magnitude <= |x|).  Nonzero |x| < 2^-24 -> +-minpos;
+ * |x| >= 2^24 and +-inf -> +-maxpos; NaN -> NaR (0x80, value NaN).
+ * Replaces reference/bposit_fast.py:69-99 plus the value->code map of
+ * examples/w8a8_rounding_demo.py:30-31,47-49. */
+int bp_quantize_bp8(const float *x, size_t n, int nearest, uint8_t *codes, float *values,
+                    void *stream);
+
+/* float64 input variant of bp_quantize_bp8 (the reference's own input dtype,
+ * reference/bposit_fast.py:90): identical rounding decisions on the exact
+ * float64 value; `values` (optional) receives the float64 quantized values,
+ * with +-0 keeping the sign of x as np.sign(x) * 0 does. */
+int bp_quantize_bp8_f64(const double *x, size_t n, int nearest, uint8_t *codes, double *values,
+                        void *stream);
+
+/* Row-wise grouped bp8 quantization of x[rows, K] (row-major): every run of
+ * `group` elements along K of a row shares a power-of-two exponent s, and the
+ * code is quantize_bp8(x / 2^s).  compute_scales = 1 computes
+ * s = ceil(log2(absmax / 2^maxpos_log2)) (0 for an all-zero group) and writes it
+ * to exps[rows, ceil(K / group)]; compute_scales = 0 reads exps.  maxpos_log2 is
+ * 24 for bp8's maxpos 2^24 (reference/bposit_ref.py:226-227).  No reference
+ * counterpart: composes quantize_bp8 with an exact power-of-two scale. */
+int bp_quantize_bp8_grouped(const float *x, int rows, int K, int group, int nearest,
+                            int compute_scales, int maxpos_log2, int32_t *exps, uint8_t *codes,
+                            void *stream);
+
+/* fp32 -> bp16 codes.  rtne = 1: encode_bposit16(Fraction(x), "rtne"),
+ * rtne = 0: encode_bposit16(Fraction(x), "truncate")
+ * (reference/bposit_ref.py:382-507).  NaN -> NaR (0x8000), +-inf -> +-maxpos. */
+int bp_encode_bp16(const float *x, size_t n, int rtne, uint16_t *codes, void *stream);
+
+/* Round n quires (nlimbs = 8, 12 or 16 limbs each) once to bposit32.
+ * Replaces bposit_ref.quire256_to_bposit32 (reference/bposit_ref.py:703-722). */
+int bp_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out, void *stream);
+
+/* Exact quire GEMM: for m < M, n < N
+ *   q[m,n] = sum_k trunc0( v(A[m,k]) * v(B[n,k]) * 2^(sa[m,k/group] + sb[n,k/group]) * 2^96 )
+ *   out_bp32[m * ldo + n] = bposit32 of q[m,n] (one truncating round)
+ * A[M,K] and B[N,K] are codes of format fmt, row-major with K contiguous; sa,
+ * sb (optional, may be NULL) are int32 per-(row, group) exponents
+ * [rows, ceil(K/group)].  If out_quire is non-NULL, the raw quires are also
+ * written as [M, N, quire_limbs] (quire_limbs 8, 12 or 16; truncated two's
+ * complement).  algo: 0 = auto, 1 = CUDA cores, 2 = tensor cores (tcgen05).
+ * workspace: device memory of at least bp_quire_gemm_workspace_size() bytes,
+ * 256-byte aligned; NULL lets the library take it stream-ordered from the
+ * device's default memory pool for the duration of the call.
+ * Replaces bposit_fast.dot_quire / dot / matmul_quire
+ * (reference/bposit_fast.py:102-176) with the final quire256_to_bposit32 of
+ * bposit_ref (reference/bposit_ref.py:703-722) and dot_at_precision
+ * (reference/bposit_ref.py:1028-1035). */
+int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
+                  const int32_t *sa, const int32_t *sb, int group,
+                  uint32_t *out_bp32, int64_t ldo, uint32_t *out_quire, int quire_limbs,
+                  int algo, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Workspace bytes bp_quire_gemm needs for this shape and algo. */
+size_t bp_quire_gemm_workspace_size(int fmt, int M, int N, int K, int algo);
+
+/* bposit32 codes -> float64 values times 2^(row_exp[m] + col_exp[n]) for an
+ * [M, N] matrix (row/col exponents may be NULL = 0); NaR -> 0.0 as in
+ * _bp32_to_float.  Exact (unless the scaled value leaves the float64 range): bp32
+ * values carry at most 28 significant bits.  Replaces the rescale step
+ * _bp32_to_float(c) * 2^(ex+ew) of bposit_quantize.quantize_w8a8
+ * (reference/bposit_quantize.py:66-68, 88). */
+int bp_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *row_exp,
+                   const int32_t *col_exp, double *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BPOSIT_B200_H */

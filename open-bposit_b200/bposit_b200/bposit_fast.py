@@ -1,0 +1,145 @@
+"""Drop-in for the reference's numpy fast path (reference/bposit_fast.py) on a
+B200: the same function names, argument meaning, return types and errors,
+computed by the library's sm_100a kernels.
+
+    import bposit_fast as bf                      # reference
+    from bposit_b200 import bposit_fast as bf     # this library
+
+Inputs may be numpy arrays / lists (copied to the current CUDA device, results
+returned as numpy / Python ints like the reference) or CUDA tensors (kept on
+the device, except where the reference returns Python ints).  Formats: "bp8"
+and "bp16" (the reference's fast path has bp4 / aip5 / bp8; the low rungs are
+not part of the B200 path and raise KeyError, as an unknown format does).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import ops
+
+QUIRE_FRAC_BITS = 96
+_NBITS = {"bp8": 8, "bp16": 16}
+
+
+def _nbits(fmt: str) -> int:
+    try:
+        return _NBITS[fmt]
+    except KeyError:
+        raise KeyError(fmt) from None
+
+
+def _device():
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _codes_to_dev(c, nb: int) -> torch.Tensor:
+    dt = torch.uint8 if nb == 8 else torch.uint16
+    if isinstance(c, torch.Tensor) and c.is_cuda:
+        if c.dtype == dt:
+            return c.contiguous()
+        return (c.to(torch.int64) & ((1 << nb) - 1)).to(dt)
+    a = np.asarray(c, dtype=np.int64) & ((1 << nb) - 1)      # the reference's `& mask`
+    a = a.astype(np.uint8 if nb == 8 else np.uint16)
+    return torch.from_numpy(np.ascontiguousarray(a)).to(_device())
+
+
+def _limbs_to_ints(q: np.ndarray) -> np.ndarray:
+    """[..., nl] uint32 two's complement limbs -> object array of Python ints."""
+    shape = q.shape[:-1]
+    flat = np.ascontiguousarray(q).reshape(-1, q.shape[-1])
+    out = np.empty(flat.shape[0], dtype=object)
+    for i in range(flat.shape[0]):
+        out[i] = int.from_bytes(flat[i].tobytes(), "little", signed=True)
+    return out.reshape(shape)
+
+
+def _broadcast(a: torch.Tensor, b: torch.Tensor):
+    """numpy broadcasting of the reference's elementwise `mant[a] * mant[b]`."""
+    ka, kb = a.shape[1], b.shape[1]
+    if ka == kb:
+        return a, b
+    if ka == 1:
+        return a.expand(1, kb).contiguous(), b
+    if kb == 1:
+        return a, b.expand(1, ka).contiguous()
+    raise ValueError(f"operands could not be broadcast together with shapes ({ka},) ({kb},)")
+
+
+def quantize_bp8(x, *, nearest: bool = False):
+    """bposit8 quantize -> dequantize of every element of x (reference/bposit_fast.py:69-99):
+    nearest=False keeps the largest grid magnitude <= |x| (bit-identical to the
+    reference's truncating encode for |x| >= minpos), nearest=True rounds to the
+    nearest grid value with ties to the smaller magnitude; nonzero values below
+    minpos go to +-minpos.  Returns float64 values (numpy for array input, a
+    CUDA tensor for CUDA tensor input)."""
+    if isinstance(x, torch.Tensor) and x.is_cuda:
+        xx = x if x.dtype in (torch.float32, torch.float64) else x.to(torch.float64)
+        _, v = ops.quantize_bp8(xx, nearest=nearest, return_values=True)
+        return v.to(torch.float64)
+    xa = np.asarray(x, dtype=np.float64)
+    xt = torch.from_numpy(np.ascontiguousarray(xa)).to(_device())
+    _, v = ops.quantize_bp8(xt, nearest=nearest, return_values=True)
+    return v.cpu().numpy().reshape(xa.shape)
+
+
+def quantize_bp8_codes(x, *, nearest: bool = True):
+    """The bp8 codes of quantize_bp8(x, nearest=...) (the value->code map of
+    examples/w8a8_rounding_demo.py:30-31, 47-49): uint8, same shape."""
+    if isinstance(x, torch.Tensor) and x.is_cuda:
+        return ops.quantize_bp8(x if x.dtype in (torch.float32, torch.float64) else x.to(torch.float64),
+                                nearest=nearest)
+    xa = np.asarray(x, dtype=np.float64)
+    xt = torch.from_numpy(np.ascontiguousarray(xa)).to(_device())
+    return ops.quantize_bp8(xt, nearest=nearest).cpu().numpy().reshape(xa.shape)
+
+
+def dot_quire(a_codes, b_codes, fmt: str) -> int:
+    """Exact quire (integer, 96 fraction bits) of the dot of two code vectors
+    (reference/bposit_fast.py:102-128)."""
+    nb = _nbits(fmt)
+    a = _codes_to_dev(a_codes, nb).reshape(1, -1)
+    b = _codes_to_dev(b_codes, nb).reshape(1, -1)
+    a, b = _broadcast(a, b)
+    _, q = ops.quire_gemm(a, b, nb, quire_limbs=16)
+    return int(_limbs_to_ints(q.cpu().numpy())[0, 0])
+
+
+def dot(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
+    """Exact dot rounded once to out_fmt (reference/bposit_fast.py:131-133)."""
+    if out_fmt != "bp32":
+        raise KeyError(out_fmt)
+    nb = _nbits(fmt)
+    a = _codes_to_dev(a_codes, nb).reshape(1, -1)
+    b = _codes_to_dev(b_codes, nb).reshape(1, -1)
+    a, b = _broadcast(a, b)
+    out, _ = ops.quire_gemm(a, b, nb)
+    return int(out.cpu().numpy()[0, 0])
+
+
+def matmul_quire(A_codes, B_codes, fmt: str):
+    """Exact quire of every output of A[T,K] @ B[N,K]^T as a [T,N] object
+    array of Python ints (reference/bposit_fast.py:136-176)."""
+    nb = _nbits(fmt)
+    if np.ndim(A_codes) != 2 or np.ndim(B_codes) != 2:
+        raise ValueError("matmul_quire expects A[T,K] and B[N,K]")
+    A = _codes_to_dev(A_codes, nb)
+    B = _codes_to_dev(B_codes, nb)
+    _, q = ops.quire_gemm(A, B, nb, quire_limbs=16)
+    return _limbs_to_ints(q.cpu().numpy())
+
+
+def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,
+                algo: int = 0):
+    """A[T,K] @ B[N,K]^T with every output rounded once to bposit32 (the
+    reference's matmul_quire followed by quire256_to_bposit32 per element), with
+    optional per-(row, group) power-of-two exponents.  Returns uint32 codes
+    (numpy for host input, a CUDA tensor for CUDA input)."""
+    nb = _nbits(fmt)
+    on_dev = isinstance(A_codes, torch.Tensor) and A_codes.is_cuda
+    A = _codes_to_dev(A_codes, nb)
+    B = _codes_to_dev(B_codes, nb)
+    sa = None if a_exps is None else torch.as_tensor(a_exps, dtype=torch.int32).to(A.device).contiguous()
+    sb = None if b_exps is None else torch.as_tensor(b_exps, dtype=torch.int32).to(A.device).contiguous()
+    out, _ = ops.quire_gemm(A, B, nb, sa=sa, sb=sb, group=group, algo=algo)
+    return out if on_dev else out.cpu().numpy()

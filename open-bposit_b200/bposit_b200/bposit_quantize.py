@@ -1,0 +1,67 @@
+"""Drop-in for the reference's W8A8 recipe (reference/bposit_quantize.py) on a
+B200: per-row power-of-two exponents, truncating bp8 encode, exact quire
+matmul and a single bposit32 round per output, rescaled by 2^(e_x + e_w) in
+float64.
+
+The exponent heuristic is float64 numpy preprocessing (RMS with a p95
+outlier guard, reference/bposit_quantize.py:46-63); it fixes the codes once and
+is evaluated on the host with the same numpy primitives so that the codes it
+produces match the reference's.  Everything after it -- encode, quire GEMM,
+bposit32 round and rescale -- runs in the library's sm_100a kernels.
+"""
+from __future__ import annotations
+
+from fractions import Fraction
+
+import numpy as np
+import torch
+
+from . import ops
+
+
+def recommended_exponents(M: np.ndarray) -> np.ndarray:
+    """Per-row integer exponent: round(log2(ref)) with ref = the row's RMS, or its
+    95th percentile of |x| when that exceeds twice the RMS; 0 for an all-zero
+    row (reference/bposit_quantize.py:46-63)."""
+    M = np.asarray(M, dtype=np.float64)
+    out = np.zeros(M.shape[0], dtype=np.int64)
+    for r in range(M.shape[0]):
+        v = M[r]
+        rms = float(np.sqrt(np.mean(v ** 2)))
+        if not rms > 0:
+            continue
+        p95 = float(np.percentile(np.abs(v), 95))
+        ref = p95 if (p95 > 0 and p95 > 2 * rms) else rms
+        out[r] = int(np.round(np.log2(ref)))
+    return out
+
+
+# Fraction(x).limit_denominator(10**8) is 0 exactly when |x| < 1 / (2 * 10**8);
+# the largest double below that bound, used by the truncating encode of
+# encode_bposit8 (reference/bposit_ref.py:258-270).
+_LIMIT_ZERO = 5e-9 if Fraction(5e-9) < Fraction(1, 2 * 10 ** 8) else float(np.nextafter(5e-9, 0.0))
+
+
+def _encode_rows(M: np.ndarray, exps: np.ndarray, dev) -> torch.Tensor:
+    scaled = M / np.exp2(exps.astype(np.float64))[:, None]
+    xt = torch.from_numpy(np.ascontiguousarray(scaled)).to(dev)
+    codes = ops.quantize_bp8(xt, nearest=False)
+    # encode_bposit8 sends floats closer to 0 than to 1e-8 to the zero code
+    tiny = xt.abs() <= _LIMIT_ZERO
+    return torch.where(tiny, torch.zeros_like(codes), codes)
+
+
+def quantize_w8a8(W: np.ndarray, X: np.ndarray) -> np.ndarray:
+    """X @ W^T in bp8 W8A8 with exact quire accumulation; returns Y[tok, out]
+    float64 (reference/bposit_quantize.py:71-89)."""
+    W = np.asarray(W, dtype=np.float64)
+    X = np.asarray(X, dtype=np.float64)
+    w_exp = recommended_exponents(W)
+    x_exp = recommended_exponents(X)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    wc = _encode_rows(W, w_exp, dev)
+    xc = _encode_rows(X, x_exp, dev)
+    bp32, _ = ops.quire_gemm(xc, wc, 8)
+    y = ops.bp32_to_f64(bp32, torch.from_numpy(x_exp.astype(np.int32)).to(dev),
+                        torch.from_numpy(w_exp.astype(np.int32)).to(dev))
+    return y.cpu().numpy()

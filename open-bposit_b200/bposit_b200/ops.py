@@ -1,0 +1,150 @@
+"""Device-level API: torch CUDA tensors in, torch CUDA tensors out, zero copy.
+
+Each op launches the library's sm_100a kernels through the C ABI on the
+current torch stream.  Codes are uint8 (bp8), uint16 (bp16) and uint32
+(bposit32) tensors; quires are [..., nlimbs] uint32 two's-complement limbs with
+96 fraction bits.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_FMT = {"bp8": 8, "bp16": 16, 8: 8, 16: 16}
+_CODE_DTYPE = {8: torch.uint8, 16: torch.uint16}
+
+
+def fmt_bits(fmt) -> int:
+    try:
+        return _FMT[fmt]
+    except KeyError:
+        raise KeyError(fmt) from None
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _dev(t: torch.Tensor, name: str, dtype=None) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    return t.contiguous()
+
+
+def decode(codes: torch.Tensor, fmt=None) -> torch.Tensor:
+    """code -> exact fp32 value (zero and NaR -> 0)."""
+    f = fmt_bits(fmt) if fmt is not None else (8 if codes.dtype == torch.uint8 else 16)
+    c = _dev(codes, "codes", _CODE_DTYPE[f])
+    out = torch.empty(c.shape, dtype=torch.float32, device=c.device)
+    _lib.check(_lib.lib().bp_decode(f, _p(c), c.numel(), _p(out), _stream()))
+    return out
+
+
+def quantize_bp8(x: torch.Tensor, nearest: bool = True, return_values: bool = False, out=None):
+    """fp32 (or float64) -> bp8 codes; with return_values also the exact values
+    (fp32 for fp32 input, float64 for float64 input)."""
+    if x.dtype == torch.float64:
+        xx = _dev(x, "x")
+        codes = out if out is not None else torch.empty(xx.shape, dtype=torch.uint8, device=xx.device)
+        vals = torch.empty(xx.shape, dtype=torch.float64, device=xx.device) if return_values else None
+        _lib.check(_lib.lib().bp_quantize_bp8_f64(_p(xx), xx.numel(), int(nearest), _p(codes), _p(vals),
+                                                  _stream()))
+        return (codes, vals) if return_values else codes
+    xx = _dev(x, "x", torch.float32)
+    codes = out if out is not None else torch.empty(xx.shape, dtype=torch.uint8, device=xx.device)
+    vals = torch.empty(xx.shape, dtype=torch.float32, device=xx.device) if return_values else None
+    _lib.check(_lib.lib().bp_quantize_bp8(_p(xx), xx.numel(), int(nearest), _p(codes), _p(vals), _stream()))
+    return (codes, vals) if return_values else codes
+
+
+def quantize_bp8_grouped(x: torch.Tensor, group: int = 128, nearest: bool = True, exps=None,
+                         maxpos_log2: int = 24, out=None):
+    """Row-wise grouped quantization of x[rows, K]: returns (codes[rows, K],
+    exps[rows, ceil(K/group)] int32).  When exps is None the power-of-two
+    exponents ceil(log2(absmax / 2^maxpos_log2)) are computed."""
+    xx = _dev(x, "x", torch.float32)
+    if xx.dim() != 2:
+        raise ValueError("x must be 2-D [rows, K]")
+    rows, K = xx.shape
+    G = (K + group - 1) // group
+    compute = exps is None
+    e = torch.empty((rows, G), dtype=torch.int32, device=xx.device) if compute else _dev(exps, "exps", torch.int32)
+    codes = out if out is not None else torch.empty((rows, K), dtype=torch.uint8, device=xx.device)
+    _lib.check(_lib.lib().bp_quantize_bp8_grouped(_p(xx), rows, K, group, int(nearest), int(compute),
+                                                  maxpos_log2, _p(e), _p(codes), _stream()))
+    return codes, e
+
+
+def encode_bp16(x: torch.Tensor, rtne: bool = True, out=None) -> torch.Tensor:
+    xx = _dev(x, "x", torch.float32)
+    codes = out if out is not None else torch.empty(xx.shape, dtype=torch.uint16, device=xx.device)
+    _lib.check(_lib.lib().bp_encode_bp16(_p(xx), xx.numel(), int(rtne), _p(codes), _stream()))
+    return codes
+
+
+def quire_to_bp32(limbs: torch.Tensor) -> torch.Tensor:
+    """[..., nlimbs] uint32 quires (nlimbs 8, 12 or 16) -> [...] bp32 codes."""
+    q = _dev(limbs, "limbs", torch.uint32)
+    nl = q.shape[-1]
+    out = torch.empty(q.shape[:-1], dtype=torch.uint32, device=q.device)
+    _lib.check(_lib.lib().bp_quire_to_bp32(_p(q), nl, out.numel(), _p(out), _stream()))
+    return out
+
+
+def gemm_workspace_size(fmt, M: int, N: int, K: int, algo: int = 0) -> int:
+    return int(_lib.lib().bp_quire_gemm_workspace_size(fmt_bits(fmt), M, N, K, algo))
+
+
+def quire_gemm(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, group: int = 128,
+               out=None, quire_limbs: int = 0, algo: int = 0, workspace=None):
+    """Exact quire GEMM A[M,K] @ B[N,K]^T -> (bp32 codes [M,N], raw quires
+    [M,N,quire_limbs] or None).  `out` may be a [M, ldo >= N] uint32 view (a
+    column block of a wider matrix is allowed: its row stride is used)."""
+    f = fmt_bits(fmt) if fmt is not None else (8 if A.dtype == torch.uint8 else 16)
+    a = _dev(A, "A", _CODE_DTYPE[f])
+    b = _dev(B, "B", _CODE_DTYPE[f])
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("quire_gemm expects A[M,K] and B[N,K]")
+    M, K = a.shape
+    N, K2 = b.shape
+    if K2 != K:
+        raise ValueError(f"inner dimensions differ: {K} vs {K2}")
+    sa_ = None if sa is None else _dev(sa, "sa", torch.int32)
+    sb_ = None if sb is None else _dev(sb, "sb", torch.int32)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.uint32, device=a.device)
+        ldo = N
+    else:
+        if out.dtype != torch.uint32 or out.shape != (M, N) or out.stride(1) != 1:
+            raise ValueError("out must be a [M, N] uint32 view with unit column stride")
+        ldo = out.stride(0)
+    q = torch.empty((M, N, quire_limbs), dtype=torch.uint32, device=a.device) if quire_limbs else None
+    need = gemm_workspace_size(f, M, N, K, algo)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.device)
+    _lib.check(_lib.lib().bp_quire_gemm(f, _p(a), _p(b), M, N, K, _p(sa_), _p(sb_), group, _p(out), ldo,
+                                        _p(q), quire_limbs, algo, _p(workspace), workspace.numel(),
+                                        _stream()))
+    return out, q
+
+
+def bp32_to_f64(codes: torch.Tensor, row_exp=None, col_exp=None) -> torch.Tensor:
+    """[M, N] bp32 codes -> float64 values * 2^(row_exp[m] + col_exp[n])."""
+    c = _dev(codes, "codes", torch.uint32)
+    if c.dim() == 1:
+        c = c.view(1, -1)
+    M, N = c.shape
+    re = None if row_exp is None else _dev(row_exp, "row_exp", torch.int32)
+    ce = None if col_exp is None else _dev(col_exp, "col_exp", torch.int32)
+    out = torch.empty((M, N), dtype=torch.float64, device=c.device)
+    _lib.check(_lib.lib().bp_bp32_to_f64(_p(c), M, N, _p(re), _p(ce), _p(out), _stream()))
+    return out

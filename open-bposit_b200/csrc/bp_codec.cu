@@ -1,0 +1,430 @@
+// bp_codec.cu -- elementwise b-posit codec kernels (HBM-bound).
+//
+//  * decode: code -> exact fp32 value (bp8 via a 256-entry shared-memory LUT,
+//    bp16 arithmetically), replacing code_value / bposit_fast._lut
+//    (reference/bposit_ref.py:1022-1025, reference/bposit_fast.py:27-43).
+//  * quantize_bp8: fp32 -> bp8 code (+ optional exact fp32 value),
+//    bposit_fast.quantize_bp8(x, nearest=True|False) (reference/bposit_fast.py:69-99)
+//    through the per-binade table of bp_format.cuh.
+//  * encode_bp16: fp32 -> bp16, encode_bposit16(Fraction(x), "rtne"|"truncate")
+//    (reference/bposit_ref.py:382-507).
+//  * group_quantize_bp8: per-(row, group) power-of-two scale
+//    2^ceil(log2(absmax / 2^24)) folded into the exponent, then quantize_bp8.
+//  * quire_to_bp32: quire256_to_bposit32 (reference/bposit_ref.py:703-722).
+//
+// Layout: flat arrays; the fast paths move 16 elements per thread per step with
+// 128-bit loads and stores and fall back to scalar code for unaligned heads,
+// tails and pointers.  Grids are grid-stride loops sized to a multiple of the
+// SM count.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bp_gemm_common.cuh"
+#include "bp_internal.cuh"
+
+namespace bp {
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(size_t work_items, int per_sm = 8) {
+  size_t want = (work_items + kThreads - 1) / kThreads;
+  size_t cap = (size_t)sm_count() * per_sm;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return (int)want;
+}
+
+// ---------------------------------------------------------------- decode ---
+__global__ void __launch_bounds__(kThreads) k_decode_bp8(const uint8_t *__restrict__ codes, size_t n,
+                                                         float *__restrict__ out, bool vec) {
+  __shared__ uint32_t lut[256];
+  lut[threadIdx.x] = posit_to_f32_bits<8, 2>(threadIdx.x);
+  __syncthreads();
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t nv = vec ? n / 16 : 0;
+  const uint4 *c4 = reinterpret_cast<const uint4 *>(codes);
+  uint4 *o4 = reinterpret_cast<uint4 *>(out);
+  for (size_t i = tid; i < nv; i += stride) {
+    uint4 c = __ldcs(c4 + i);
+    uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 r;
+      r.x = lut[w[q] & 0xFFu];
+      r.y = lut[(w[q] >> 8) & 0xFFu];
+      r.z = lut[(w[q] >> 16) & 0xFFu];
+      r.w = lut[w[q] >> 24];
+      __stcs(o4 + 4 * i + q, r);
+    }
+  }
+  for (size_t i = nv * 16 + tid; i < n; i += stride) out[i] = __uint_as_float(lut[codes[i]]);
+}
+
+__global__ void __launch_bounds__(kThreads) k_decode_bp16(const uint16_t *__restrict__ codes, size_t n,
+                                                          float *__restrict__ out, bool vec) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t nv = vec ? n / 8 : 0;
+  const uint4 *c4 = reinterpret_cast<const uint4 *>(codes);
+  uint4 *o4 = reinterpret_cast<uint4 *>(out);
+  for (size_t i = tid; i < nv; i += stride) {
+    uint4 c = __ldcs(c4 + i);
+    uint32_t w[4] = {c.x, c.y, c.z, c.w};
+    uint32_t r[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      r[2 * q] = posit_to_f32_bits<16, 3>(w[q] & 0xFFFFu);
+      r[2 * q + 1] = posit_to_f32_bits<16, 3>(w[q] >> 16);
+    }
+    __stcs(o4 + 2 * i, make_uint4(r[0], r[1], r[2], r[3]));
+    __stcs(o4 + 2 * i + 1, make_uint4(r[4], r[5], r[6], r[7]));
+  }
+  for (size_t i = nv * 8 + tid; i < n; i += stride) out[i] = __uint_as_float(posit_to_f32_bits<16, 3>(codes[i]));
+}
+
+// ------------------------------------------------------------ quantize bp8 ---
+__device__ __forceinline__ uint32_t q8_one(const uint2 *tbl, uint32_t u) {
+  uint32_t a = u & 0x7FFFFFFFu;
+  uint2 t = tbl[a >> 23];
+  QEntry q{t.x, t.y};
+  uint32_t mag = bp8_apply(q, a & 0x7FFFFFu);
+  uint32_t code = (u >> 31) ? ((0u - mag) & 0xFFu) : mag;
+  return a > 0x7F800000u ? 0x80u : code;   // NaN -> NaR
+}
+
+template <bool NEAREST, bool VALUES>
+__global__ void __launch_bounds__(kThreads) k_quantize_bp8(const float *__restrict__ x, size_t n,
+                                                           uint8_t *__restrict__ codes,
+                                                           float *__restrict__ vals, bool vec) {
+  __shared__ uint2 tbl[256];
+  __shared__ uint32_t lut[256];
+  {
+    QEntry q = bp8_qentry(threadIdx.x, NEAREST);
+    tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
+    if (VALUES) lut[threadIdx.x] = posit_to_f32_bits<8, 2>(threadIdx.x);
+  }
+  __syncthreads();
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t nv = vec ? n / 16 : 0;
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+  uint4 *c4 = reinterpret_cast<uint4 *>(codes);
+  uint4 *v4 = reinterpret_cast<uint4 *>(vals);
+  for (size_t i = tid; i < nv; i += stride) {
+    uint4 in[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) in[q] = __ldcs(x4 + 4 * i + q);
+    uint32_t cw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t c0 = q8_one(tbl, in[q].x), c1 = q8_one(tbl, in[q].y);
+      uint32_t c2 = q8_one(tbl, in[q].z), c3 = q8_one(tbl, in[q].w);
+      cw[q] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
+      if (VALUES) {
+        uint4 v;
+        v.x = (c0 == 0x80u) ? 0x7FC00000u : lut[c0];
+        v.y = (c1 == 0x80u) ? 0x7FC00000u : lut[c1];
+        v.z = (c2 == 0x80u) ? 0x7FC00000u : lut[c2];
+        v.w = (c3 == 0x80u) ? 0x7FC00000u : lut[c3];
+        __stcs(v4 + 4 * i + q, v);
+      }
+    }
+    __stcs(c4 + i, make_uint4(cw[0], cw[1], cw[2], cw[3]));
+  }
+  for (size_t i = nv * 16 + tid; i < n; i += stride) {
+    uint32_t c = q8_one(tbl, __float_as_uint(x[i]));
+    codes[i] = (uint8_t)c;
+    if (VALUES) vals[i] = __uint_as_float(c == 0x80u ? 0x7FC00000u : lut[c]);
+  }
+}
+
+// ------------------------------------------------------------ encode bp16 ---
+template <bool RTNE>
+__global__ void __launch_bounds__(kThreads) k_encode_bp16(const float *__restrict__ x, size_t n,
+                                                          uint16_t *__restrict__ codes, bool vec) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  size_t nv = vec ? n / 8 : 0;
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+  uint4 *c4 = reinterpret_cast<uint4 *>(codes);
+  for (size_t i = tid; i < nv; i += stride) {
+    uint4 a = __ldcs(x4 + 2 * i), b = __ldcs(x4 + 2 * i + 1);
+    uint4 r;
+    r.x = bp16_encode_bits(a.x, RTNE) | (bp16_encode_bits(a.y, RTNE) << 16);
+    r.y = bp16_encode_bits(a.z, RTNE) | (bp16_encode_bits(a.w, RTNE) << 16);
+    r.z = bp16_encode_bits(b.x, RTNE) | (bp16_encode_bits(b.y, RTNE) << 16);
+    r.w = bp16_encode_bits(b.z, RTNE) | (bp16_encode_bits(b.w, RTNE) << 16);
+    __stcs(c4 + i, r);
+  }
+  for (size_t i = nv * 8 + tid; i < n; i += stride) codes[i] = (uint16_t)bp16_encode_bits(__float_as_uint(x[i]), RTNE);
+}
+
+// ------------------------------------------------- grouped quantize (bp8) ---
+// One warp per (row, group).  The exponent of the scaled value x / 2^s is
+// formed as an integer (no rounding, no underflow), then the quantize table
+// is applied to it.
+__device__ __forceinline__ int ceil_log2_f32(uint32_t a) {   // a = |x| bits, a != 0
+  int b = (int)(a >> 23);
+  uint32_t M = a & 0x7FFFFFu;
+  if (b == 0) {                         // subnormal: a = M * 2^-149
+    int msb = 31 - __clz((int)M);
+    return -149 + msb + ((M & (M - 1u)) ? 1 : 0);
+  }
+  return (b - 127) + (M ? 1 : 0);
+}
+
+__device__ __forceinline__ uint32_t q8_scaled(const uint2 *tbl, uint32_t u, int s) {
+  uint32_t a = u & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return 0x80u;
+  if (a == 0u) return 0u;
+  int b = (int)(a >> 23);
+  uint32_t M = a & 0x7FFFFFu;
+  int E;
+  if (b == 0) {                         // normalise a subnormal input
+    int msb = 31 - __clz((int)M);
+    E = -149 + msb;
+    M = (M << (23 - msb)) & 0x7FFFFFu;
+  } else if (b == 255) {
+    E = 1000;                           // inf: saturates
+  } else {
+    E = b - 127;
+  }
+  int be = E - s + 127;
+  be = be < 1 ? 1 : (be > 255 ? 255 : be);
+  uint2 t = tbl[be];
+  QEntry q{t.x, t.y};
+  uint32_t mag = bp8_apply(q, M);
+  return (u >> 31) ? ((0u - mag) & 0xFFu) : mag;
+}
+
+template <bool NEAREST>
+__global__ void __launch_bounds__(kThreads) k_group_quantize_bp8(const float *__restrict__ x, int rows,
+                                                                 int K, int group, int G,
+                                                                 bool compute, int maxpos_log2,
+                                                                 int32_t *__restrict__ exps,
+                                                                 uint8_t *__restrict__ codes) {
+  __shared__ uint2 tbl[256];
+  {
+    QEntry q = bp8_qentry(threadIdx.x, NEAREST);
+    tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
+  }
+  __syncthreads();
+  int lane = threadIdx.x & 31;
+  long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+  long long total = (long long)rows * G;
+  for (long long w = warp; w < total; w += nwarps) {
+    int r = (int)(w / G), g = (int)(w % G);
+    int k0 = g * group, k1 = min(K, k0 + group);
+    const float *row = x + (size_t)r * K;
+    int s;
+    if (compute) {
+      uint32_t amax = 0u;
+      for (int k = k0 + lane; k < k1; k += 32) {
+        uint32_t a = __float_as_uint(row[k]) & 0x7FFFFFFFu;
+        if (a > 0x7F800000u) a = 0u;          // NaN does not take part in absmax
+        amax = max(amax, a);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+      s = amax ? (amax >= 0x7F800000u ? 128 - maxpos_log2 : ceil_log2_f32(amax) - maxpos_log2) : 0;
+      if (lane == 0) exps[w] = s;
+    } else {
+      s = exps[w];
+    }
+    for (int k = k0 + lane; k < k1; k += 32)
+      codes[(size_t)r * K + k] = (uint8_t)q8_scaled(tbl, __float_as_uint(row[k]), s);
+  }
+}
+
+// ------------------------------------------------------------- quire->bp32 ---
+template <int NL>
+__global__ void __launch_bounds__(kThreads) k_quire_to_bp32(const uint32_t *__restrict__ limbs, size_t n,
+                                                            uint32_t *__restrict__ out) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) {
+    uint32_t q[NL];
+#pragma unroll
+    for (int j = 0; j < NL; ++j) q[j] = limbs[i * NL + j];
+    out[i] = bp32_from_limbs<NL>(q);
+  }
+}
+
+}  // namespace
+
+// --------------------------------------------------------------- launchers ---
+int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t s) {
+  if (n == 0) return kOk;
+  if (fmt == 8) {
+    bool vec = aligned16(codes) && aligned16(out);
+    k_decode_bp8<<<grid_for(vec ? n / 16 + 1 : n), kThreads, 0, s>>>((const uint8_t *)codes, n, out, vec);
+  } else {
+    bool vec = aligned16(codes) && aligned16(out);
+    k_decode_bp16<<<grid_for(vec ? n / 8 + 1 : n), kThreads, 0, s>>>((const uint16_t *)codes, n, out, vec);
+  }
+  return check_launch("decode");
+}
+
+int launch_quantize_bp8(const float *x, size_t n, bool nearest, uint8_t *codes, float *values,
+                        cudaStream_t s) {
+  if (n == 0) return kOk;
+  bool vec = aligned16(x) && aligned16(codes) && (values == nullptr || aligned16(values));
+  int g = grid_for(vec ? n / 16 + 1 : n);
+  if (nearest) {
+    if (values) k_quantize_bp8<true, true><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    else k_quantize_bp8<true, false><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+  } else {
+    if (values) k_quantize_bp8<false, true><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    else k_quantize_bp8<false, false><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+  }
+  return check_launch("quantize_bp8");
+}
+
+int launch_encode_bp16(const float *x, size_t n, bool rtne, uint16_t *codes, cudaStream_t s) {
+  if (n == 0) return kOk;
+  bool vec = aligned16(x) && aligned16(codes);
+  int g = grid_for(vec ? n / 8 + 1 : n);
+  if (rtne) k_encode_bp16<true><<<g, kThreads, 0, s>>>(x, n, codes, vec);
+  else k_encode_bp16<false><<<g, kThreads, 0, s>>>(x, n, codes, vec);
+  return check_launch("encode_bp16");
+}
+
+int launch_group_quantize_bp8(const float *x, int rows, int K, int group, bool nearest,
+                              bool compute_scales, int maxpos_log2, int32_t *exps, uint8_t *codes,
+                              cudaStream_t s) {
+  if (rows == 0 || K == 0) return kOk;
+  int G = (K + group - 1) / group;
+  size_t warps = (size_t)rows * G;
+  int g = grid_for(warps * 32);
+  if (nearest)
+    k_group_quantize_bp8<true><<<g, kThreads, 0, s>>>(x, rows, K, group, G, compute_scales, maxpos_log2, exps, codes);
+  else
+    k_group_quantize_bp8<false><<<g, kThreads, 0, s>>>(x, rows, K, group, G, compute_scales, maxpos_log2, exps, codes);
+  return check_launch("group_quantize_bp8");
+}
+
+int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out, cudaStream_t s) {
+  if (n == 0) return kOk;
+  int g = grid_for(n);
+  switch (nlimbs) {
+    case 8: k_quire_to_bp32<8><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    case 12: k_quire_to_bp32<12><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    case 16: k_quire_to_bp32<16><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    default: return set_error(kEInval, "quire_to_bp32: nlimbs must be 8, 12 or 16 (got %d)", nlimbs);
+  }
+  return check_launch("quire_to_bp32");
+}
+
+}  // namespace bp
+
+// ------------------------------------------------------------ bp32 -> f64 ---
+namespace bp {
+namespace {
+
+// value(bp32 code) * 2^(re[m] + ce[n]); NaR -> 0.0 like _bp32_to_float
+// (reference/bposit_quantize.py:66-68).
+__global__ void __launch_bounds__(256) k_bp32_to_f64(const uint32_t *__restrict__ codes, int M, int N,
+                                                     const int32_t *__restrict__ re,
+                                                     const int32_t *__restrict__ ce,
+                                                     double *__restrict__ out) {
+  size_t n = (size_t)M * N;
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) {
+    Dec d = decode_posit<32, 3>(codes[i]);
+    double v = 0.0;
+    if (d.kind == 0) {
+      int ex = d.scale - d.fw + (re ? re[i / N] : 0) + (ce ? ce[i % N] : 0);
+      v = scalbn((double)((1u << d.fw) + d.fbits), ex);
+      if (d.sign) v = -v;
+    }
+    out[i] = v;
+  }
+}
+
+}  // namespace
+
+int launch_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
+                       double *out, cudaStream_t s) {
+  size_t n = (size_t)M * N;
+  if (n == 0) return kOk;
+  size_t blocks = (n + 255) / 256, cap = (size_t)sm_count() * 8;
+  k_bp32_to_f64<<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(codes, M, N, re, ce, out);
+  return check_launch("bp32_to_f64");
+}
+
+}  // namespace bp
+
+// ----------------------------------------------------- quantize bp8 (f64) ---
+// The reference quantizes float64 (reference/bposit_fast.py:90); rounding
+// such input to fp32 first could cross a midpoint, so this variant applies the
+// same per-binade table to the 52-bit mantissa (shift + 29, threshold << 29).
+namespace bp {
+namespace {
+
+template <bool NEAREST, bool VALUES>
+__global__ void __launch_bounds__(256) k_quantize_bp8_f64(const unsigned long long *__restrict__ x, size_t n,
+                                                          uint8_t *__restrict__ codes,
+                                                          unsigned long long *__restrict__ vals) {
+  __shared__ uint2 tbl[256];
+  __shared__ uint32_t lut[256];
+  {
+    QEntry q = bp8_qentry(threadIdx.x, NEAREST);
+    tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
+    lut[threadIdx.x] = posit_to_f32_bits<8, 2>(threadIdx.x);
+  }
+  __syncthreads();
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) {
+    unsigned long long u = x[i];
+    unsigned long long a = u & 0x7FFFFFFFFFFFFFFFull;
+    uint32_t code;
+    if (a > 0x7FF0000000000000ull) {
+      code = 0x80u;
+    } else {
+      int b64 = (int)(a >> 52);
+      unsigned long long M = a & 0xFFFFFFFFFFFFFull;
+      int b32 = b64 == 0 ? 0 : (b64 - 1023 + 127);
+      if (b64 != 0) b32 = b32 < 1 ? 1 : (b32 > 255 ? 255 : b32);
+      uint2 t = tbl[b32];
+      uint32_t sh = (t.x >> 8) + 29u;
+      unsigned long long thr = t.y == 0x7FFFFFu ? 0xFFFFFFFFFFFFFull : ((unsigned long long)t.y << 29);
+      unsigned long long mask = (1ull << sh) - 1ull;
+      uint32_t mag = (t.x & 0xFFu) + (uint32_t)(M >> sh) + ((M & mask) > thr ? 1u : 0u);
+      code = (u >> 63) ? ((0u - mag) & 0xFFu) : mag;
+    }
+    codes[i] = (uint8_t)code;
+    if (VALUES) {
+      unsigned long long v;
+      if (code == 0x80u) v = 0x7FF8000000000000ull;
+      else if (code == 0u) v = u & 0x8000000000000000ull;          // +-0 keeps its sign
+      else v = __double_as_longlong((double)__uint_as_float(lut[code]));
+      vals[i] = v;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_quantize_bp8_f64(const double *x, size_t n, bool nearest, uint8_t *codes, double *values,
+                            cudaStream_t s) {
+  if (n == 0) return kOk;
+  size_t blocks = (n + 255) / 256, cap = (size_t)sm_count() * 8;
+  int g = (int)(blocks < cap ? blocks : cap);
+  auto xu = (const unsigned long long *)x;
+  auto vu = (unsigned long long *)values;
+  if (nearest) {
+    if (values) k_quantize_bp8_f64<true, true><<<g, 256, 0, s>>>(xu, n, codes, vu);
+    else k_quantize_bp8_f64<true, false><<<g, 256, 0, s>>>(xu, n, codes, vu);
+  } else {
+    if (values) k_quantize_bp8_f64<false, true><<<g, 256, 0, s>>>(xu, n, codes, vu);
+    else k_quantize_bp8_f64<false, false><<<g, 256, 0, s>>>(xu, n, codes, vu);
+  }
+  return check_launch("quantize_bp8_f64");
+}
+
+}  // namespace bp

@@ -1,0 +1,267 @@
+// bp_format.cuh -- b-posit bit-level format helpers shared by host and device.
+//
+// Formats (reference/bposit_ref.py): bp8 = 8-bit posit, eS=2 (useed 16, values
+// 2^-24..2^24); bp16 = 16-bit, eS=3 (useed 256, 2^-112..2^112); bp32 = 32-bit,
+// eS=3.  Decoding follows the regime run-length rule of decode_bposit8/16/32
+// (reference/bposit_ref.py:162-193, 306-355, 43-74): two's complement of the
+// trailing bits for negatives, exponent left-padded when the regime leaves
+// fewer than eS bits.  Every helper here is integer-only.
+#pragma once
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define BP_HD __host__ __device__ __forceinline__
+#else
+#define BP_HD inline
+#endif
+
+namespace bp {
+
+BP_HD int clz32(uint32_t x) {
+#ifdef __CUDA_ARCH__
+  return __clz((int)x);
+#else
+  return x ? __builtin_clz(x) : 32;
+#endif
+}
+BP_HD int clz64(uint64_t x) {
+#ifdef __CUDA_ARCH__
+  return __clzll((long long)x);
+#else
+  return x ? __builtin_clzll(x) : 64;
+#endif
+}
+
+// Decoded posit: kind 0 = finite nonzero, 1 = zero, 2 = NaR.  For finite values
+// |value| = (2^fw + fbits) * 2^(scale - fw), scale = k*2^eS + e is the binade.
+struct Dec {
+  int kind;
+  int sign;
+  int scale;
+  int fw;
+  uint32_t fbits;
+};
+
+template <int NB, int ES>
+BP_HD Dec decode_posit(uint32_t p) {
+  const uint32_t sbit = 1u << (NB - 1);
+  const uint32_t fmask = sbit - 1u;
+  const uint32_t mask = (NB == 32) ? 0xFFFFFFFFu : ((sbit << 1) - 1u);
+  p &= mask;
+  Dec d{0, 0, 0, 0, 0u};
+  if (p == 0u) { d.kind = 1; return d; }
+  if (p == sbit) { d.kind = 2; return d; }
+  d.sign = (int)(p >> (NB - 1));
+  uint32_t rest = p & fmask;
+  if (d.sign) rest = (0u - rest) & fmask;
+  uint32_t al = rest << (33 - NB);          // field MSB at bit 31, zero padding below
+  int lead = (int)(al >> 31);
+  uint32_t inv = lead ? ~al : al;           // count the run of `lead` bits
+  int rs = clz32(inv);
+  if (rs > NB - 1) rs = NB - 1;
+  int k = lead ? rs - 1 : -rs;
+  int rem = NB - 2 - rs;                    // bits after regime + terminator
+  int e = 0, fw = 0;
+  uint32_t fb = 0;
+  if (rem > 0) {
+    uint32_t rest2 = rest & ((1u << rem) - 1u);
+    int ew = rem < ES ? rem : ES;
+    e = (int)((rest2 >> (rem - ew)) << (ES - ew));
+    fw = rem - ew;
+    fb = rest2 & ((1u << fw) - 1u);
+  }
+  d.scale = k * (1 << ES) + e;
+  d.fw = fw;
+  d.fbits = fb;
+  return d;
+}
+
+// fp32 bit pattern of a bp8 / bp16 code (exact: |scale| <= 112 keeps it a
+// normal float).  Zero and NaR give +0.0 (code_value semantics,
+// reference/bposit_ref.py:1022-1025).
+template <int NB, int ES>
+BP_HD uint32_t posit_to_f32_bits(uint32_t code) {
+  Dec d = decode_posit<NB, ES>(code);
+  if (d.kind != 0) return 0u;
+  return ((uint32_t)d.sign << 31) | ((uint32_t)(d.scale + 127) << 23) | (d.fbits << (23 - d.fw));
+}
+
+// Exact integer form: value = mant * 2^exp, |mant| = 2^fw + fbits (unreduced,
+// the form of the bp8 decode ROM in reference/gen_rtl_vectors.py:289-298).
+template <int NB, int ES>
+BP_HD void posit_to_me(uint32_t code, int &mant, int &exp) {
+  Dec d = decode_posit<NB, ES>(code);
+  if (d.kind != 0) { mant = 0; exp = 0; return; }
+  int m = (1 << d.fw) + (int)d.fbits;
+  mant = d.sign ? -m : m;
+  exp = d.scale - d.fw;
+}
+
+// ---------------------------------------------------------------------------
+// bp8 code of the largest grid value <= 2^E, for E in [-24, 24] (the
+// truncating encode of reference/bposit_ref.py:216-255 applied to 2^E).
+// ---------------------------------------------------------------------------
+BP_HD uint32_t bp8_trunc_pow2(int E) {
+  int k = E >> 2;                 // arithmetic shift = floor division
+  int e = E & 3;
+  int rl = k >= 0 ? k + 2 : 1 - k;
+  if (rl >= 7) {
+    if (k >= 0) return k >= 5 ? (k >= 6 ? 0x7Fu : 0x7Eu) : 0u;
+    return 0x01u;
+  }
+  int avail = 7 - rl;
+  int eb = avail < 2 ? avail : 2;
+  int fw = avail - eb;
+  uint32_t R = k >= 0 ? (((1u << (k + 1)) - 1u) << 1) : 1u;
+  return (R << avail) | ((uint32_t)(e >> (2 - eb)) << fw);
+}
+
+// Quantize table for fp32 -> bp8, indexed by the biased fp32 exponent b of |x|:
+//   mag = c_lo + (M >> sh) + ((M & ((1 << sh) - 1)) > thr)
+// with M the 23-bit fp32 mantissa.  This reproduces bposit_fast.quantize_bp8
+// (reference/bposit_fast.py:69-99): nearest=True counts the midpoints
+// (g[i] + g[i+1]) / 2 strictly below |x| (so ties go to the lower magnitude),
+// nearest=False takes the largest grid value <= |x|, and both send any nonzero
+// |x| below minpos to minpos.  `never` = 0x7FFFFF (M never exceeds it).
+struct QEntry {
+  uint32_t lo_sh;   // c_lo | sh << 8
+  uint32_t thr;
+};
+
+BP_HD double bp8_value_f64(uint32_t code) {
+  Dec d = decode_posit<8, 2>(code);
+  if (d.kind != 0) return 0.0;
+  double v = (double)((1u << d.fw) + d.fbits);
+  int s = d.scale - d.fw;
+  // exact power-of-two scaling without libm
+  while (s > 0) { v *= 2.0; --s; }
+  while (s < 0) { v *= 0.5; ++s; }
+  return d.sign ? -v : v;
+}
+
+BP_HD QEntry bp8_qentry(int b, bool nearest) {
+  const uint32_t never = 0x7FFFFFu;
+  QEntry q;
+  if (b == 0) { q.lo_sh = 0u | (23u << 8); q.thr = 0u; return q; }     // zero / subnormal
+  int E = b - 127;
+  if (b == 255 || E >= 24) { q.lo_sh = 127u | (23u << 8); q.thr = never; return q; }
+  if (E < -24) { q.lo_sh = 1u | (23u << 8); q.thr = never; return q; }
+  uint32_t clo = bp8_trunc_pow2(E);
+  double P = 1.0;
+  for (int i = 0; i < (E > 0 ? E : -E); ++i) P = E > 0 ? P * 2.0 : P * 0.5;
+  double glo = bp8_value_f64(clo);
+  double ghi = bp8_value_f64(clo + 1u);
+  if (glo == P && ghi < 2.0 * P) {
+    // regular binade: grid points P * (1 + j / 2^fw), j < 2^fw
+    double sp = ghi - glo;
+    int fw = 0;
+    while (sp * (double)(1 << fw) < P) ++fw;
+    uint32_t sh = 23u - (uint32_t)fw;
+    q.lo_sh = clo | (sh << 8);
+    q.thr = nearest ? (1u << (sh - 1)) : never;
+    return q;
+  }
+  // at most one grid point in the binade: compare with the midpoint directly
+  q.lo_sh = clo | (23u << 8);
+  if (!nearest) { q.thr = never; return q; }
+  double mid = (glo + ghi) * 0.5;
+  if (mid >= 2.0 * P) { q.thr = never; return q; }
+  double t = (mid / P - 1.0) * 8388608.0;   // exact: mid is dyadic with few bits
+  q.thr = (uint32_t)t;
+  return q;
+}
+
+// Apply a quantize entry to |x| given as (M, table entry); returns the 7-bit
+// magnitude code (0 only for x == 0).
+BP_HD uint32_t bp8_apply(QEntry q, uint32_t M) {
+  uint32_t sh = q.lo_sh >> 8;
+  uint32_t mask = (1u << sh) - 1u;
+  return (q.lo_sh & 0xFFu) + (M >> sh) + ((M & mask) > q.thr ? 1u : 0u);
+}
+
+// ---------------------------------------------------------------------------
+// fp32 -> bp16, the bit-string encoder _encode_unsigned(value, mode) of
+// reference/bposit_ref.py:382-486 on the exact value of x: regime, up to three
+// exponent bits, fraction bits, then (rtne) round up when the first dropped
+// fraction bit is set and (any later bit is set or the kept LSB is odd),
+// saturating at maxpos.  When the regime leaves no room for all exponent bits
+// the first dropped bit is still the first FRACTION bit, as in the reference.
+// NaN -> NaR (0x8000) and +-inf -> +-maxpos are extensions for inputs the
+// reference rejects.
+// ---------------------------------------------------------------------------
+BP_HD uint32_t bp16_encode_bits(uint32_t u, bool rtne) {
+  uint32_t sign = u >> 31;
+  uint32_t a = u & 0x7FFFFFFFu;
+  if (a > 0x7F800000u) return 0x8000u;
+  if (a == 0u) return 0u;
+  uint32_t field;
+  int b = (int)(a >> 23);
+  uint32_t M = a & 0x7FFFFFu;
+  int E = b - 127;
+  if (b == 0 || E < -112) field = 0x0001u;
+  else if (b == 255 || E > 112) field = 0x7FFFu;
+  else {
+    int k = E >> 3, e = E & 7;
+    int rl = k >= 0 ? k + 2 : 1 - k;
+    if (rl >= 15) {
+      field = k >= 0 ? (k >= 14 ? 0x7FFFu : 0x7FFEu) : 0x0001u;
+    } else {
+      int avail = 15 - rl;
+      int eb = avail < 3 ? avail : 3;
+      int fb = avail - eb;
+      uint32_t R = k >= 0 ? (((1u << (k + 1)) - 1u) << 1) : 1u;
+      field = (R << avail) | ((uint32_t)(e >> (3 - eb)) << fb) | (M >> (23 - fb));
+      if (rtne) {
+        uint32_t rbit = (M >> (22 - fb)) & 1u;
+        uint32_t sticky = M & ((1u << (22 - fb)) - 1u);
+        bool up = rbit && (sticky != 0u || (field & 1u));
+        if (up && field < 0x7FFFu) field += 1u;
+      }
+    }
+  }
+  if (sign) field = (0u - field) & 0x7FFFu;
+  return (sign << 15) | field;
+}
+
+// ---------------------------------------------------------------------------
+// bp32 from an exact magnitude: value = mag * 2^lsb_exp, mag = (hi:lo) 128-bit.
+// The truncating bit-string encoder of reference/bposit_ref.py:97-150 as used
+// by quire256_to_bposit32 (:703-722): total_e = floor(log2 value), regime,
+// up to three exponent bits, then fraction bits, all cut at 31 bits; clamp at
+// total_e beyond +-240; negatives take the two's complement of the field.
+// ---------------------------------------------------------------------------
+BP_HD uint32_t bp32_from_mag(bool neg, uint64_t hi, uint64_t lo, int lsb_exp) {
+  if (hi == 0u && lo == 0u) return 0u;
+  int msb = hi ? 127 - clz64(hi) : 63 - clz64(lo);
+  int te = msb + lsb_exp;
+  uint32_t field;
+  if (te > 240) field = 0x7FFFFFFFu;
+  else if (te < -240) field = 0x00000001u;
+  else {
+    int k = te >> 3, e = te & 7;
+    int rl = k >= 0 ? k + 2 : 1 - k;
+    if (rl >= 31) {
+      field = k >= 0 ? (k >= 30 ? 0x7FFFFFFFu : 0x7FFFFFFEu) : 0x00000001u;
+    } else {
+      int avail = 31 - rl;
+      int eb = avail < 3 ? avail : 3;
+      int fb = avail - eb;
+      uint32_t R = k >= 0 ? (((1u << (k + 1)) - 1u) << 1) : 1u;
+      uint32_t f = 0u;
+      if (fb > 0) {
+        // 64-bit window whose bit 63 is the msb of mag
+        uint64_t top;
+        int s = 127 - msb;                       // left shift that puts msb at bit 127
+        if (s >= 64) top = lo << (s - 64);
+        else if (s == 0) top = hi;
+        else top = (hi << s) | (lo >> (64 - s));
+        f = (uint32_t)((top << 1) >> (64 - fb));
+      }
+      field = (R << avail) | ((uint32_t)(e >> (3 - eb)) << fb) | f;
+    }
+  }
+  if (neg) field = (0u - field) & 0x7FFFFFFFu;
+  return (neg ? 0x80000000u : 0u) | field;
+}
+
+}  // namespace bp

@@ -1,0 +1,156 @@
+// bp_gemm_simt.cu -- exact quire GEMM on CUDA cores, and the per-row operand
+// statistics shared with the tensor-core path.
+//
+// out[m, n] = quire256_to_bposit32( sum_k trunc0( v(A[m,k]) * v(B[n,k]) *
+//                                   2^(sa[m,k/group] + sb[n,k/group]) * 2^96 ) )
+// which is dot_at_precision's per-term rule (reference/bposit_ref.py:1028-1035,
+// bposit_fast.dot_quire / matmul_quire reference/bposit_fast.py:102-176) with an
+// optional power-of-two group scale folded into each element's exponent.
+//
+// Every code is an exact integer form m * 2^e (|m| < 2^12).  Per row we know
+// the lowest possible set bit (emin) and the highest binade (emax), so a whole
+// dot product lives in a window of the quire that is usually far narrower
+// than 256 bits.  When that window starts at or above the quire's bit 0 (no
+// term needs truncation) and fits 127 bits with the K-term carry head-room,
+// the output is accumulated exactly in one 128-bit register pair (fast path).
+// Otherwise the thread falls back to a 512-bit quire in local memory with
+// per-term truncation toward zero (slow path; never taken for bp8 without
+// group scales).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "bp_internal.cuh"
+#include "bp_gemm_common.cuh"
+
+namespace bp {
+namespace {
+
+constexpr int TM = 16, TN = 16, KC = 32;
+
+struct ElemME {
+  int m;   // signed mantissa (0 for zero / NaR)
+  int e;   // exponent of the mantissa's bit 0, group scale included
+};
+
+template <int FMT>
+__device__ __forceinline__ ElemME load_elem(const void *base, int row, int K, int k,
+                                            const int32_t *s, int G, int group) {
+  uint32_t c = FMT == 8 ? ((const uint8_t *)base)[(size_t)row * K + k]
+                        : ((const uint16_t *)base)[(size_t)row * K + k];
+  ElemME r;
+  if (FMT == 8) posit_to_me<8, 2>(c, r.m, r.e);
+  else posit_to_me<16, 3>(c, r.m, r.e);
+  if (s && r.m) r.e += s[(size_t)row * G + k / group];
+  return r;
+}
+
+// 512-bit two's complement quire in 16 limbs: q += v * 2^sh (sh >= 0).
+__device__ void q512_add(uint32_t *q, int64_t v, int sh) {
+  if (v == 0 || sh >= 512) return;
+  int limb = sh >> 5, bit = sh & 31;
+  uint64_t uv = (uint64_t)v;
+  uint32_t fill = v < 0 ? 0xFFFFFFFFu : 0u;
+  uint32_t lo = (uint32_t)uv, hi = (uint32_t)(uv >> 32);
+  uint32_t x0 = bit ? lo << bit : lo;
+  uint32_t x1 = bit ? (hi << bit) | (lo >> (32 - bit)) : hi;
+  uint32_t x2 = bit ? (fill << bit) | (hi >> (32 - bit)) : fill;
+  uint64_t carry = 0;
+  for (int i = limb; i < 16; ++i) {
+    uint32_t t = i == limb ? x0 : (i == limb + 1 ? x1 : (i == limb + 2 ? x2 : fill));
+    uint64_t sum = (uint64_t)q[i] + t + carry;
+    q[i] = (uint32_t)sum;
+    carry = sum >> 32;
+  }
+}
+
+template <int FMT>
+__device__ void slow_output(const GemmArgs &a, int m, int n, uint32_t *out_bp32, uint32_t *out_q) {
+  uint32_t q[16];
+  for (int i = 0; i < 16; ++i) q[i] = 0u;
+  for (int k = 0; k < a.K; ++k) {
+    ElemME x = load_elem<FMT>(a.A, m, a.K, k, a.sa, a.G, a.group);
+    ElemME y = load_elem<FMT>(a.B, n, a.K, k, a.sb, a.G, a.group);
+    int64_t P = (int64_t)x.m * y.m;
+    if (!P) continue;
+    int sh = x.e + y.e + 96;
+    if (sh >= 0) {
+      q512_add(q, P, sh);
+    } else {
+      int r = -sh;
+      int64_t t = r >= 63 ? 0 : (P < 0 ? -((-P) >> r) : (P >> r));   // trunc toward zero
+      q512_add(q, t, 0);
+    }
+  }
+  *out_bp32 = bp32_from_limbs16(q);
+  if (out_q)
+    for (int i = 0; i < a.nlimbs; ++i) out_q[i] = q[i];
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(TM *TN) k_quire_gemm_simt(GemmArgs a, const int4 *__restrict__ sta,
+                                                             const int4 *__restrict__ stb) {
+  __shared__ int sAm[TM][KC + 1], sAe[TM][KC + 1];
+  __shared__ int sBm[TN][KC + 1], sBe[TN][KC + 1];
+  const int tx = threadIdx.x % TN, ty = threadIdx.x / TN;
+  const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
+  const int m = m0 + ty, n = n0 + tx;
+  const bool valid = m < a.M && n < a.N;
+  int4 ra = valid ? sta[m] : make_int4(0, 0, 0, 0);
+  int4 rb = valid ? stb[n] : make_int4(0, 0, 0, 0);
+  const bool nz = ra.z && rb.z;
+  const int base = ra.x + rb.x + 96;   // quire bit of the lowest possible term bit
+  const int width = fast_width(ra, rb, a.K, FMT);
+  const bool fast = nz && base >= 0 && width <= 127;
+  unsigned __int128 acc = 0;
+  for (int k0 = 0; k0 < a.K; k0 += KC) {
+    for (int t = threadIdx.x; t < TM * KC; t += TM * TN) {
+      int r = t / KC, kk = t % KC, k = k0 + kk;
+      ElemME x{0, 0}, y{0, 0};
+      if (k < a.K && m0 + r < a.M) x = load_elem<FMT>(a.A, m0 + r, a.K, k, a.sa, a.G, a.group);
+      if (k < a.K && n0 + r < a.N) y = load_elem<FMT>(a.B, n0 + r, a.K, k, a.sb, a.G, a.group);
+      sAm[r][kk] = x.m; sAe[r][kk] = x.e;
+      sBm[r][kk] = y.m; sBe[r][kk] = y.e;
+    }
+    __syncthreads();
+    if (fast) {
+      const int off = ra.x + rb.x;
+#pragma unroll 8
+      for (int kk = 0; kk < KC; ++kk) {
+        int P = sAm[ty][kk] * sBm[tx][kk];
+        int sh = sAe[ty][kk] + sBe[tx][kk] - off;
+        sh = min(max(sh, 0), 127);
+        acc += (unsigned __int128)(__int128)(long long)P << sh;
+      }
+    }
+    __syncthreads();
+  }
+  if (!valid) return;
+  uint32_t *ob = a.out + (size_t)m * a.ldo + n;
+  uint32_t *oq = a.quire ? a.quire + ((size_t)m * a.N + n) * a.nlimbs : nullptr;
+  if (!nz) {
+    *ob = 0u;
+    if (oq)
+      for (int i = 0; i < a.nlimbs; ++i) oq[i] = 0u;
+    return;
+  }
+  if (fast) {
+    write_fast_output(acc, base, ob, oq, a.nlimbs);
+  } else {
+    slow_output<FMT>(a, m, n, ob, oq);
+  }
+}
+
+}  // namespace
+
+int launch_row_stats(int fmt, const void *codes, int rows, int K, const int32_t *s, int group,
+                     int4 *stats, cudaStream_t st);
+
+int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s) {
+  dim3 grid((a.N + TN - 1) / TN, (a.M + TM - 1) / TM);
+  if (grid.y > 65535u) return set_error(kERange, "quire_gemm: M too large for the CUDA-core path");
+  if (a.fmt == 8) k_quire_gemm_simt<8><<<grid, TM * TN, 0, s>>>(a, sta, stb);
+  else k_quire_gemm_simt<16><<<grid, TM * TN, 0, s>>>(a, sta, stb);
+  return check_launch("quire_gemm_simt");
+}
+
+}  // namespace bp

@@ -1,0 +1,58 @@
+// bp_internal.cuh -- launch helpers shared by the library's .cu files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "bp_format.cuh"
+
+namespace bp {
+
+// Status codes (mirrored in include/bposit_b200.h).
+enum {
+  kOk = 0,
+  kEInval = -1,
+  kEFmt = -2,
+  kEAlign = -3,
+  kECuda = -4,
+  kERange = -5,
+  kENoDev = -6,
+  kEWorkspace = -7,
+};
+
+int set_error(int code, const char *fmt, ...);
+int check_launch(const char *what);
+int sm_count();   // SMs of the current device
+
+inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0u; }
+
+// ---- codec launchers (bp_codec.cu) ----
+int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t s);
+int launch_quantize_bp8(const float *x, size_t n, bool nearest, uint8_t *codes, float *values,
+                        cudaStream_t s);
+int launch_quantize_bp8_f64(const double *x, size_t n, bool nearest, uint8_t *codes, double *values,
+                            cudaStream_t s);
+int launch_encode_bp16(const float *x, size_t n, bool rtne, uint16_t *codes, cudaStream_t s);
+int launch_group_quantize_bp8(const float *x, int rows, int K, int group, bool nearest,
+                              bool compute_scales, int maxpos_log2, int32_t *exps, uint8_t *codes,
+                              cudaStream_t s);
+int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,
+                         cudaStream_t s);
+
+// ---- quire GEMM (bp_gemm_simt.cu, bp_gemm_tc.cu) ----
+struct GemmArgs {
+  int fmt;                 // 8 or 16
+  const void *A, *B;       // [M,K], [N,K] codes, K contiguous
+  int M, N, K;
+  const int32_t *sa, *sb;  // per-(row, group) exponents or null
+  int group, G;
+  uint32_t *out;           // bp32 codes, row stride ldo
+  int64_t ldo;
+  uint32_t *quire;         // optional raw quires [M, N, nlimbs]
+  int nlimbs;
+};
+
+size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo);
+int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s);
+
+}  // namespace bp

@@ -1,0 +1,157 @@
+// host_format_check.cpp -- compiles the library's format logic
+// (open-bposit_b200/csrc/bp_format.cuh, __host__ __device__ code) for the host
+// and compares it with the CPU oracle (oracle/bposit_oracle.c) over every
+// non-negative fp32 bit pattern (bp8 quantize, both modes), a strided sweep
+// of all fp32 patterns (bp16 encode, both modes), every bp8 / bp16 code
+// (decode) and random 128-bit magnitudes (bp32 round).  Test-only.
+//
+// usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
+#include <thread>
+#include <vector>
+
+#include "../open-bposit_b200/csrc/bp_format.cuh"
+
+extern "C" {
+void orc_quantize_bp8(const float *x, size_t n, int nearest, uint8_t *codes, float *values);
+uint16_t orc_encode_bp16_one(float x, int rtne);
+void orc_decode_me(int fmt_bits, uint32_t code, int64_t *mant, int *exp);
+uint32_t orc_quire_to_bp32(const uint32_t *limbs, int nlimbs);
+}
+
+static std::atomic<long long> g_bad{0};
+
+static float f_of(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+static void q8_range(uint64_t lo, uint64_t hi, bool nearest) {
+  bp::QEntry tbl[256];
+  for (int b = 0; b < 256; ++b) tbl[b] = bp::bp8_qentry(b, nearest);
+  const size_t CH = 4096;
+  float xs[CH];
+  uint8_t ref[CH];
+  long long bad = 0;
+  for (uint64_t u0 = lo; u0 < hi; u0 += CH) {
+    size_t n = (size_t)((hi - u0) < CH ? (hi - u0) : CH);
+    for (size_t i = 0; i < n; ++i) xs[i] = f_of((uint32_t)(u0 + i));
+    orc_quantize_bp8(xs, n, nearest ? 1 : 0, ref, nullptr);
+    for (size_t i = 0; i < n; ++i) {
+      uint32_t u = (uint32_t)(u0 + i);
+      uint32_t a = u & 0x7FFFFFFFu;
+      uint32_t code;
+      if (a > 0x7F800000u) code = 0x80u;
+      else {
+        uint32_t mag = bp::bp8_apply(tbl[a >> 23], a & 0x7FFFFFu);
+        code = (u >> 31) ? ((0u - mag) & 0xFFu) : mag;
+      }
+      if (code != ref[i]) {
+        if (bad < 5) fprintf(stderr, "q8 mismatch nearest=%d x=%08x dev=%02x ref=%02x\n", nearest, u, code, ref[i]);
+        ++bad;
+      }
+    }
+  }
+  g_bad += bad;
+}
+
+static void e16_range(uint64_t lo, uint64_t hi, uint64_t step, bool rtne) {
+  long long bad = 0;
+  for (uint64_t v = lo; v < hi; v += step) {
+    uint32_t u = (uint32_t)v;
+    uint32_t dev = bp::bp16_encode_bits(u, rtne);
+    uint32_t ref = orc_encode_bp16_one(f_of(u), rtne ? 1 : 0);
+    if (dev != ref) {
+      if (bad < 5) fprintf(stderr, "e16 mismatch rtne=%d x=%08x dev=%04x ref=%04x\n", rtne, u, dev, ref);
+      ++bad;
+    }
+  }
+  g_bad += bad;
+}
+
+static uint64_t rng_state = 0x9E3779B97F4A7C15ull;
+static uint64_t rnd() {
+  rng_state ^= rng_state << 13; rng_state ^= rng_state >> 7; rng_state ^= rng_state << 17;
+  return rng_state;
+}
+
+int main(int argc, char **argv) {
+  const char *what = argc > 1 ? argv[1] : "q8";
+  int nt = argc > 2 ? atoi(argv[2]) : 8;
+  if (nt < 1) nt = 1;
+  std::vector<std::thread> th;
+  if (!strcmp(what, "q8")) {
+    // every non-negative pattern and the negative half on a stride, both modes
+    for (int mode = 0; mode < 2; ++mode) {
+      for (int t = 0; t < nt; ++t) {
+        uint64_t lo = (0x80000000ull * t) / nt, hi = (0x80000000ull * (t + 1)) / nt;
+        th.emplace_back(q8_range, lo, hi, mode == 1);
+      }
+      for (auto &x : th) x.join();
+      th.clear();
+      for (uint64_t b = 0x80000000ull; b < 0x100000000ull; b += 0x01000000ull)
+        q8_range(b, b + 0x4000, mode == 1);
+    }
+  } else if (!strcmp(what, "e16")) {
+    for (int mode = 0; mode < 2; ++mode) {
+      for (int t = 0; t < nt; ++t) {
+        uint64_t lo = (0x100000000ull * t) / nt, hi = (0x100000000ull * (t + 1)) / nt;
+        th.emplace_back(e16_range, lo, hi, 13, mode == 1);
+      }
+      for (auto &x : th) x.join();
+      th.clear();
+      // dense sweeps around every binade start and the bp16 range edges
+      for (int b = 0; b < 256; ++b)
+        for (uint32_t s = 0; s < 2; ++s) {
+          uint64_t base = ((uint64_t)s << 31) | ((uint64_t)b << 23);
+          e16_range(base, base + 0x2000, 1, mode == 1);
+          e16_range(base + 0x7FFFFF - 0x2000, base + 0x800000, 1, mode == 1);
+        }
+    }
+  } else if (!strcmp(what, "dec")) {
+    long long bad = 0;
+    for (uint32_t c = 0; c < 256; ++c) {
+      int64_t m; int e; int dm, de;
+      orc_decode_me(8, c, &m, &e);
+      bp::posit_to_me<8, 2>(c, dm, de);
+      if (m != dm || (m && e != de)) { ++bad; fprintf(stderr, "bp8 decode %02x\n", c); }
+    }
+    for (uint32_t c = 0; c < 65536; ++c) {
+      int64_t m; int e; int dm, de;
+      orc_decode_me(16, c, &m, &e);
+      bp::posit_to_me<16, 3>(c, dm, de);
+      if (m != dm || (m && e != de)) { if (bad < 5) fprintf(stderr, "bp16 decode %04x\n", c); ++bad; }
+    }
+    g_bad += bad;
+  } else if (!strcmp(what, "bp32")) {
+    long long bad = 0;
+    for (int it = 0; it < 2000000; ++it) {
+      int bits = (int)(rnd() % 128) + 1;
+      uint64_t hi = rnd(), lo = rnd();
+      if (bits <= 64) { hi = 0; lo = bits == 64 ? lo : (lo & ((1ull << bits) - 1)); }
+      else hi &= bits == 128 ? ~0ull : ((1ull << (bits - 64)) - 1);
+      if (!hi && !lo) continue;
+      int shift = (int)(rnd() % 160);     // quire bit of the magnitude's bit 0
+      bool neg = rnd() & 1;
+      if (bits + shift > 250) continue;
+      // quire limbs: (mag << shift), negated if neg, 8 limbs
+      uint32_t q[8] = {0};
+      for (int i = 0; i < 128; ++i) {
+        int bit = i < 64 ? (int)((lo >> i) & 1) : (int)((hi >> (i - 64)) & 1);
+        if (bit) q[(i + shift) / 32] |= 1u << ((i + shift) % 32);
+      }
+      if (neg) {
+        uint64_t c = 1;
+        for (int i = 0; i < 8; ++i) { uint64_t s = (uint64_t)(uint32_t)~q[i] + c; q[i] = (uint32_t)s; c = s >> 32; }
+      }
+      uint32_t ref = orc_quire_to_bp32(q, 8);
+      uint32_t dev = bp::bp32_from_mag(neg, hi, lo, shift - 96);
+      if (ref != dev) { if (bad < 5) fprintf(stderr, "bp32 mismatch bits=%d shift=%d\n", bits, shift); ++bad; }
+    }
+    g_bad += bad;
+  }
+  printf("%s mismatches: %lld\n", what, (long long)g_bad.load());
+  return g_bad.load() ? 1 : 0;
+}

@@ -1,0 +1,102 @@
+"""CPU-only checks of the product library: it is built, loads, exports every
+symbol include/bposit_b200.h declares, and validates arguments on the host;
+plus an exhaustive host-compiled check of the format logic the kernels use."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import REPO
+
+HEADER = os.path.join(REPO, "include", "bposit_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?(?:unsigned\s+)?[a-z_0-9 ]+?\s*\*?\s*(bp_[a-z0-9_]+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from bposit_b200 import _lib
+    L = _lib.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+    assert set(syms) == set(_lib.EXPORTED)
+
+
+def test_version_and_error_string():
+    from bposit_b200 import _lib
+    L = _lib.lib()
+    assert L.bp_version() >= 100
+    assert isinstance(L.bp_last_error(), bytes)
+
+
+def test_host_argument_validation():
+    """Invalid arguments are rejected before any device work."""
+    from bposit_b200 import _lib
+    L = _lib.lib()
+    vp = ctypes.c_void_p
+    rc = L.bp_quire_gemm(7, None, None, 1, 1, 1, None, None, 128, vp(16), 1, None, 0, 0, None, 0, None)
+    assert rc == _lib.BP_EFMT
+    rc = L.bp_quire_gemm(8, None, None, -1, 1, 1, None, None, 128, vp(16), 1, None, 0, 0, None, 0, None)
+    assert rc == _lib.BP_EINVAL
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 3, None, 0, 0, None, 0, None)
+    assert rc == _lib.BP_EINVAL and b"ldo" in L.bp_last_error()
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, vp(16), None, 0, vp(16), 4, None, 0, 0, None, 0, None)
+    assert rc == _lib.BP_EINVAL
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, vp(16), 5, 0, None, 0, None)
+    assert rc == _lib.BP_EINVAL
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 3, None, 0, None)
+    assert rc == _lib.BP_EINVAL
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 0, vp(17), 1 << 20, None)
+    assert rc == _lib.BP_EALIGN
+    assert L.bp_decode(9, vp(16), 4, vp(16), None) == _lib.BP_EFMT
+    assert L.bp_decode(8, None, 4, vp(16), None) == _lib.BP_EINVAL
+    assert L.bp_quire_to_bp32(vp(16), 9, 1, vp(16), None) == _lib.BP_EINVAL
+    assert L.bp_quantize_bp8_grouped(vp(16), 2, 8, 0, 1, 1, 24, vp(16), vp(16), None) == _lib.BP_EINVAL
+    # zero-size calls are no-ops that succeed without touching a device
+    assert L.bp_quire_gemm(8, None, None, 0, 5, 3, None, None, 128, None, 5, None, 0, 0, None, 0, None) == 0
+    assert L.bp_quire_gemm_workspace_size(8, 16, 16, 16, 1) >= 16 * 2 * 16
+
+
+def test_python_errors_match_reference_types():
+    """Unknown formats raise KeyError (the reference's dict lookups); non-2-D
+    GEMM operands raise ValueError (reference/bposit_fast.py:147-148)."""
+    from bposit_b200 import bposit_fast, ops
+    with pytest.raises(KeyError):
+        ops.fmt_bits("bp5")
+    with pytest.raises(KeyError):
+        bposit_fast.dot_quire([1], [1], "bp4")
+    with pytest.raises(ValueError):
+        bposit_fast.matmul_quire([1, 2], [[1, 2]], "bp8")
+
+
+@pytest.fixture(scope="module")
+def host_check():
+    build = os.path.join(REPO, "tests", "_build")
+    os.makedirs(build, exist_ok=True)
+    obj = os.path.join(build, "orc.o")
+    exe = os.path.join(build, "host_format_check")
+    subprocess.run(["gcc", "-O2", "-fPIC", "-c", "-o", obj, os.path.join(REPO, "oracle", "bposit_oracle.c")],
+                   check=True)
+    subprocess.run(["g++", "-O2", "-std=c++17", "-pthread", "-o", exe,
+                    os.path.join(REPO, "tests", "host_format_check.cpp"), obj, "-lm"], check=True)
+    return exe
+
+
+@pytest.mark.parametrize("what", ["dec", "bp32", "q8", "e16"])
+def test_format_logic_matches_oracle_exhaustively(host_check, what):
+    """The kernels' format logic (bp_format.cuh) compiled for the host vs the
+    oracle: all bp8/bp16 codes; 2M random quires; every non-negative fp32
+    pattern for the bp8 quantize table (both modes); a strided full sweep of
+    fp32 patterns plus every binade edge for the bp16 encoder (both modes)."""
+    nt = max(1, min(8, len(os.sched_getaffinity(0))))
+    r = subprocess.run([host_check, what, str(nt)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "mismatches: 0" in r.stdout

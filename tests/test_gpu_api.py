@@ -1,0 +1,114 @@
+"""The reference-facing mirrors (bposit_fast / bposit_quantize / bposit_ref
+names and return types) on the GPU, checked like the reference's own
+self-tests (reference/bposit_fast.py:179-251, examples/smoke_test.sh:24-38)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def api():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from bposit_b200 import bposit_fast, bposit_quantize, bposit_ref
+    return bposit_fast, bposit_quantize, bposit_ref
+
+
+def test_quantize_bp8_values_match_reference(api, orc):
+    bf, _, _ = api
+    g = golden("fast_selftest")
+    xs = g["xs"]
+    got = bf.quantize_bp8(xs)                    # float64 in, float64 out, truncating
+    assert got.dtype == np.float64 and got.shape == xs.shape
+    exp = orc.decode_f32(g["enc_codes"], 8).astype(np.float64)
+    assert np.array_equal(got, exp)
+    q = golden("quantize_bp8")
+    x = q["x"].astype(np.float64)
+    vn = bf.quantize_bp8(x, nearest=True)
+    assert np.array_equal(np.signbit(vn), np.signbit(np.sign(x) * orc.decode_f32(q["codes_nearest"], 8)))
+    assert np.array_equal(bf.quantize_bp8_codes(x, nearest=True), q["codes_nearest"])
+
+
+def test_dot_and_dot_quire_selftest(api):
+    bf, _, _ = api
+    g = golden("fast_selftest")
+    off = g["off"]
+    for i in range(0, len(off) - 1, 7):
+        a = g["a"][off[i]:off[i + 1]].astype(np.int64)
+        b = g["b"][off[i]:off[i + 1]].astype(np.int64)
+        assert bf.dot(a, b, "bp8", "bp32") == int(g["bp32"][i])
+
+
+def test_dot_quire_rtl_vectors(api, orc):
+    bf, _, _ = api
+    g = golden("rtl_bp8")
+    for i in range(g["a"].shape[0]):
+        q = bf.dot_quire(g["a"][i].tolist(), g["b"][i].tolist(), "bp8")
+        assert q & ((1 << 256) - 1) == orc.limbs_to_int(g["quire"][i]) & ((1 << 256) - 1)
+
+
+def test_matmul_quire_vs_per_dot(api):
+    """reference/bposit_fast.py:228-238: matmul_quire == per-dot quire."""
+    bf, _, _ = api
+    rng = np.random.default_rng(0)
+    A = rng.integers(0, 256, size=(3, 200), dtype=np.int64)
+    B = rng.integers(0, 256, size=(5, 200), dtype=np.int64)
+    M = bf.matmul_quire(A, B, "bp8")
+    assert M.shape == (3, 5) and M.dtype == object
+    for i in range(3):
+        for j in range(5):
+            assert int(M[i, j]) == bf.dot_quire(A[i], B[j], "bp8")
+
+
+def test_quire256_to_bposit32(api):
+    _, _, br = api
+    g = golden("encoder_vectors")
+    qs = [int.from_bytes(g["quire"][i].tobytes(), "little", signed=True) for i in range(0, 132811, 97)]
+    got = br.quire256_to_bposit32(np.array(qs, dtype=object))
+    assert np.array_equal(got, g["bp32"][::97])
+    assert br.quire256_to_bposit32(0) == 0
+
+
+def test_code_value_and_encode_bposit16(api):
+    _, _, br = api
+    g = golden("bp16")
+    assert np.array_equal(br.encode_bposit16(g["x"], "rtne"), g["rtne"])
+    with pytest.raises(ValueError):
+        br.encode_bposit16(1.0, "nearest")
+    assert br.code_value(0x40, "bp8") == 1.0 and br.code_value(0x80, "bp8") == 0.0
+
+
+def test_quantize_w8a8_matches_reference(api):
+    """examples/smoke_test.sh:24-38 inputs: Y identical to the reference's
+    quantize_w8a8 output, and deterministic across calls."""
+    _, bq, _ = api
+    g = golden("quantize_w8a8")
+    assert np.array_equal(bq.recommended_exponents(g["W"]), g["w_exp"])
+    assert np.array_equal(bq.recommended_exponents(g["X"]), g["x_exp"])
+    y1 = bq.quantize_w8a8(g["W"], g["X"])
+    y2 = bq.quantize_w8a8(g["W"], g["X"])
+    assert np.array_equal(y1, g["Y"])
+    assert np.array_equal(y1, y2)
+
+
+def test_shuffled_tiling_reproducible(api):
+    """examples/w8a8_rounding_demo.py:80-89: identical codes across a re-run and
+    a shuffled tiling of the input."""
+    bf, _, _ = api
+    rng = np.random.default_rng(0)
+    x0 = rng.standard_normal((16, 128)) * 0.5
+    c1 = bf.quantize_bp8_codes(x0, nearest=True)
+    flat = x0.ravel()
+    idx = np.arange(flat.size)
+    rng.shuffle(idx)
+    out = np.empty(flat.size, np.uint8)
+    for s in range(0, flat.size, 97):
+        j = idx[s:s + 97]
+        out[j] = bf.quantize_bp8_codes(flat[j], nearest=True)
+    assert np.array_equal(c1, bf.quantize_bp8_codes(x0, nearest=True))
+    assert np.array_equal(c1, out.reshape(x0.shape))

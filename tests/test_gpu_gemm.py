@@ -1,0 +1,220 @@
+"""GPU parity of the exact quire GEMM (both the CUDA-core and the tensor-core
+paths, through the C ABI) against the reference's golden vectors and the
+oracle: every bposit32 output word and every raw quire bit-exact."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+ALGOS = [1, 2]   # 1 = CUDA cores, 2 = tensor cores
+
+
+@pytest.fixture(scope="module")
+def ops():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from bposit_b200 import ops as o
+    return o
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def tc_ok(ops, fmt, M, N, K):
+    from bposit_b200 import _lib
+    L = _lib.lib()
+    return L.bp_quire_gemm_workspace_size(fmt, M, N, K, 2) > L.bp_quire_gemm_workspace_size(fmt, M, N, K, 1)
+
+
+def run(ops, A, B, fmt, algo, sa=None, sb=None, group=128, quire_limbs=0):
+    out, q = ops.quire_gemm(dev(A), dev(B), fmt, sa=None if sa is None else dev(sa),
+                            sb=None if sb is None else dev(sb), group=group, quire_limbs=quire_limbs,
+                            algo=algo)
+    return out.cpu().numpy(), (None if q is None else q.cpu().numpy())
+
+
+def test_bp8_exhaustive_products(ops):
+    """reference/gen_bp8_exhaustive.py: all 65,536 bp8 x bp8 products."""
+    g = golden("bp8_exhaustive")
+    A = np.arange(256, dtype=np.uint8).reshape(256, 1)
+    out, _ = run(ops, A, A, 8, 1)
+    assert np.array_equal(out.ravel(), g["bp32"])
+
+
+def test_rtl_bp8_dots(ops):
+    """reference/gen_rtl_vectors.py: 22 bp8 dots of K=32 (quires and bp32)."""
+    g = golden("rtl_bp8")
+    for i in range(g["a"].shape[0]):
+        out, q = run(ops, g["a"][i:i + 1], g["b"][i:i + 1], 8, 1, quire_limbs=8)
+        assert np.array_equal(q[0, 0], g["quire"][i]), i
+        assert int(out[0, 0]) == int(g["bp32"][i]), i
+
+
+def test_fast_selftest_dots(ops):
+    """reference/bposit_fast.py:181-197: 300 seeded bp8 dots, K in [1, 400)."""
+    g = golden("fast_selftest")
+    off = g["off"]
+    for i in range(len(off) - 1):
+        out, _ = run(ops, g["a"][off[i]:off[i + 1]][None], g["b"][off[i]:off[i + 1]][None], 8, 1)
+        assert int(out[0, 0]) == int(g["bp32"][i]), i
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_w8a8_linear_golden(ops, algo):
+    """16x576x576 group-scaled W8A8 linear: every quire and bp32 word."""
+    g = golden("w8a8_linear")
+    if algo == 2 and not tc_ok(ops, 8, 16, 576, 576):
+        pytest.skip("tensor-core path not available for this shape")
+    out, q = run(ops, g["xc"], g["wc"], 8, algo, sa=g["sx"], sb=g["sw"], quire_limbs=8)
+    assert np.array_equal(q, g["quire"])
+    assert np.array_equal(out, g["bp32"])
+
+
+def rand_codes(rng, shape, fmt, zero_frac=0.05):
+    n = 1 << fmt
+    c = rng.integers(0, n, size=shape, dtype=np.int64)
+    c[rng.random(shape) < zero_frac] = 0
+    return c.astype(np.uint8 if fmt == 8 else np.uint16)
+
+
+SHAPES = [(1, 1, 1), (1, 1, 0), (3, 5, 7), (17, 33, 65), (64, 48, 130), (129, 131, 257), (200, 256, 512)]
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_bp8_random_vs_oracle(ops, orc, algo, M, N, K):
+    if algo == 2 and not tc_ok(ops, 8, M, N, K):
+        pytest.skip("tensor-core path not available for this shape")
+    rng = np.random.default_rng(M * 1000 + N * 10 + K)
+    A, B = rand_codes(rng, (M, K), 8), rand_codes(rng, (N, K), 8)
+    out, q = run(ops, A, B, 8, algo, quire_limbs=8)
+    rb, rq = orc.quire_gemm(A, B, 8, nlimbs=8)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("M,N,K,group", [(5, 7, 300, 128), (40, 70, 576, 128), (130, 66, 1000, 64)])
+def test_bp8_group_scaled_vs_oracle(ops, orc, algo, M, N, K, group):
+    if algo == 2 and not tc_ok(ops, 8, M, N, K):
+        pytest.skip("tensor-core path not available for this shape")
+    rng = np.random.default_rng(K + group)
+    X = (rng.standard_normal((M, K)) * np.exp2(rng.integers(-6, 6, (M, 1)))).astype(np.float32)
+    W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    sx, sw = orc.group_scales(X, group), orc.group_scales(W, group)
+    xc, wc = orc.quantize_bp8_grouped(X, sx, group), orc.quantize_bp8_grouped(W, sw, group)
+    out, q = run(ops, xc, wc, 8, algo, sa=sx, sb=sw, group=group, quire_limbs=16)
+    rb, rq = orc.quire_gemm(xc, wc, 8, sa=sx, sb=sw, group=group, nlimbs=16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+
+
+def test_bp8_truncating_terms(ops, orc):
+    """Scales that push products below 2^-96: per-term truncation toward zero
+    (the reference's int() / bposit_fast.py:125-127 branch)."""
+    rng = np.random.default_rng(11)
+    M, N, K, group = 6, 9, 200, 32
+    A, B = rand_codes(rng, (M, K), 8), rand_codes(rng, (N, K), 8)
+    G = (K + group - 1) // group
+    sa = rng.integers(-40, 5, (M, G)).astype(np.int32)
+    sb = rng.integers(-40, 5, (N, G)).astype(np.int32)
+    out, q = run(ops, A, B, 8, 1, sa=sa, sb=sb, group=group, quire_limbs=16)
+    rb, rq = orc.quire_gemm(A, B, 8, sa=sa, sb=sb, group=group, nlimbs=16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("M,N,K", [(2, 3, 5), (33, 17, 100), (128, 64, 256)])
+def test_bp16_random_vs_oracle(ops, orc, algo, M, N, K):
+    """bp16 quire GEMM on uniformly random codes (exponents up to +-112, so
+    products span 2^-224..2^224 and many terms truncate per term)."""
+    if algo == 2 and not tc_ok(ops, 16, M, N, K):
+        pytest.skip("tensor-core path not available for this shape")
+    rng = np.random.default_rng(M + N + K)
+    A, B = rand_codes(rng, (M, K), 16), rand_codes(rng, (N, K), 16)
+    out, q = run(ops, A, B, 16, algo, quire_limbs=16)
+    rb, rq = orc.quire_gemm(A, B, 16, nlimbs=16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+
+
+@pytest.mark.parametrize("algo", ALGOS)
+def test_bp16_normal_range_vs_oracle(ops, orc, algo):
+    """bp16 operands ~ N(0,1) * 2^U{-8..8} per row (the large-GEMM distribution)."""
+    from bposit_b200 import workloads
+    M, N, K = 96, 160, 1024
+    if algo == 2 and not tc_ok(ops, 16, M, N, K):
+        pytest.skip("tensor-core path not available for this shape")
+    A = orc.encode_bp16(workloads.per_row_po2(M, K, 1), True)
+    B = orc.encode_bp16(workloads.per_row_po2(N, K, 2), True)
+    out, _ = run(ops, A, B, 16, algo)
+    assert np.array_equal(out, orc.quire_gemm(A, B, 16))
+
+
+def test_column_block_output(ops, orc):
+    """ldo > N: an output shard written into its column block of a wider matrix."""
+    rng = np.random.default_rng(5)
+    A, B = rand_codes(rng, (20, 64), 8), rand_codes(rng, (30, 64), 8)
+    full = torch.zeros((20, 100), dtype=torch.uint32, device="cuda")
+    ops.quire_gemm(dev(A), dev(B), 8, out=full[:, 40:70])
+    got = full.cpu().numpy()
+    assert np.array_equal(got[:, 40:70], orc.quire_gemm(A, B, 8))
+    assert not got[:, :40].any() and not got[:, 70:].any()
+
+
+def test_zero_and_nar_only(ops):
+    A = np.array([[0, 0x80, 0], [0x80, 0x80, 0x80]], np.uint8)
+    B = np.array([[0x40, 0x7F, 0x01]], np.uint8)
+    out, q = run(ops, A, B, 8, 1, quire_limbs=8)
+    assert not out.any() and not q.any()
+
+
+def test_smollm_layer_shapes_row_subsample(ops, orc):
+    """The SmolLM2-135M-shaped projections at M=2048 (group-scaled RTN codes):
+    all outputs computed on the device, 16 rows checked against the oracle."""
+    from bposit_b200 import workloads
+    rng = np.random.default_rng(0)
+    M = 2048
+    for name, N, K in workloads.SMOLLM_SHAPES:
+        X = rng.standard_normal((M, K)).astype(np.float32)
+        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        xc, sx = ops.quantize_bp8_grouped(dev(X))
+        wc, sw = ops.quantize_bp8_grouped(dev(W))
+        out, _ = ops.quire_gemm(xc, wc, 8, sa=sx, sb=sw)
+        rows = np.sort(rng.choice(M, 16, replace=False))
+        ref = orc.quire_gemm(xc.cpu().numpy()[rows], wc.cpu().numpy(), 8, sa=sx.cpu().numpy()[rows],
+                             sb=sw.cpu().numpy())
+        assert np.array_equal(out.cpu().numpy()[rows], ref), name
+
+
+def test_large_bp8_k65536_row_subsample(ops, orc):
+    """bp8 4096 x 4096 x 65536 (operands N(0,1) * 2^U{-8..8} per row): every
+    output on the device, 2 full rows and a 64-column block checked against
+    the oracle."""
+    from bposit_b200 import workloads
+    M = N = 4096
+    K = 65536
+    torch.manual_seed(0)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+
+    def operand(rows):
+        x = torch.randn((rows, K), device="cuda", generator=gen)
+        e = torch.randint(-8, 9, (rows, 1), device="cuda", generator=gen).float()
+        return ops.quantize_bp8(x * torch.exp2(e), nearest=True)
+
+    A, B = operand(M), operand(N)
+    out, _ = ops.quire_gemm(A, B, 8)
+    o = out.cpu().numpy()
+    An, Bn = A.cpu().numpy(), B.cpu().numpy()
+    rows = np.array([0, 4095])
+    assert np.array_equal(o[rows], orc.quire_gemm(An[rows], Bn, 8))
+    cols = np.arange(1000, 1064)
+    assert np.array_equal(o[:64, cols], orc.quire_gemm(An[:64], Bn[cols], 8))
+    del A, B, out
+    torch.cuda.empty_cache()
