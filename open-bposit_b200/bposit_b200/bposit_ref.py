@@ -23,8 +23,8 @@ def code_value(code, fmt: str):
     nb = {"bp8": 8, "bp16": 16}.get(fmt)
     if nb is None:
         raise KeyError(fmt)
-    a = np.asarray(code, dtype=np.int64) & ((1 << nb) - 1)
-    t = torch.from_numpy(a.astype(np.uint8 if nb == 8 else np.uint16)).to(_device())
+    a = np.asarray(np.asarray(code, dtype=np.int64) & ((1 << nb) - 1))
+    t = torch.from_numpy(np.ascontiguousarray(a.astype(np.uint8 if nb == 8 else np.uint16)).reshape(a.shape)).to(_device())
     v = ops.decode(t, nb).cpu().numpy().astype(np.float64)
     return float(v) if v.ndim == 0 else v
 
@@ -35,7 +35,7 @@ def encode_bposit16(value, mode: str = "truncate"):
     if mode not in ("truncate", "rtne"):
         raise ValueError(f"unknown rounding mode: {mode!r}")
     a = np.asarray(value, dtype=np.float32)
-    t = torch.from_numpy(np.ascontiguousarray(a)).to(_device())
+    t = torch.from_numpy(np.ascontiguousarray(a).reshape(a.shape)).to(_device())
     c = ops.encode_bp16(t, rtne=(mode == "rtne")).cpu().numpy()
     return int(c) if c.ndim == 0 else c
 

@@ -156,9 +156,9 @@ def test_codec_sweep_full_size_properties(ops, orc):
     assert bool((sv[1:] >= sv[:-1]).all())
     c16 = ops.encode_bp16(x, rtne=True)
     r16 = orc.encode_bp16(xs, True)
-    assert np.array_equal(c16[idx].cpu().numpy(), r16)
+    assert np.array_equal(c16.view(torch.int16)[idx].cpu().numpy().view(np.uint16), r16)
     dv = ops.decode(c16)
-    assert torch.equal(ops.encode_bp16(dv, rtne=True), c16)
+    assert torch.equal(ops.encode_bp16(dv, rtne=True).view(torch.int16), c16.view(torch.int16))
     del x, codes, vals, c16, dv
     torch.cuda.empty_cache()
 
