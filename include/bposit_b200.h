@@ -112,6 +112,22 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
 /* Workspace bytes bp_quire_gemm needs for this shape and algo. */
 size_t bp_quire_gemm_workspace_size(int fmt, int M, int N, int K, int algo);
 
+/* bp_quire_gemm without any device allocation, for callers that cannot
+ * allocate: plugins whose host framework owns the whole device-memory budget,
+ * and latency-critical loops where cudaMalloc / cudaFree (which can
+ * synchronize the device) are not acceptable.  Same arguments and results as
+ * bp_quire_gemm on the CUDA-core path, minus algo and workspace.  Its scratch is
+ * a fixed 1 MiB device array inside the library (held by every GPU that loads
+ * it, until exit), so M + N must not exceed 65,536 rows (BP_ERANGE otherwise).
+ * The first call on each device looks up that array's device address; make it
+ * before any stream capture.  All calls on a device share the array: calls
+ * that overlap on the GPU race and must be serialized by the caller.
+ * No counterpart in the reference (it has no device memory at all). */
+int bp_quire_gemm_noalloc(int fmt, const void *A, const void *B, int M, int N, int K,
+                          const int32_t *sa, const int32_t *sb, int group,
+                          uint32_t *out_bp32, int64_t ldo, uint32_t *out_quire, int quire_limbs,
+                          void *stream);
+
 /* bposit32 codes -> float64 values times 2^(row_exp[m] + col_exp[n]) for an
  * [M, N] matrix (row/col exponents may be NULL = 0); NaR -> 0.0 as in
  * _bp32_to_float.  Exact (unless the scaled value leaves the float64 range): bp32

@@ -1,0 +1,94 @@
+// bp_noalloc.cu -- bp_quire_gemm_noalloc: the exact quire GEMM for callers
+// that must not allocate device memory.
+//
+// Who cannot allocate: a plugin running inside a host framework that owns the
+// whole device-memory budget (every byte comes from the host's own pools), and
+// latency-critical loops where a cudaMalloc / cudaFree -- which can
+// synchronize the device -- is not acceptable.  They still pass their own
+// inputs and outputs; this entry point needs nothing else.
+//
+// Its only scratch (the per-row operand statistics of the CUDA-core GEMM) lives
+// in a fixed file-scope device array of kNoAllocScratchBytes, which every GPU
+// that loads this library holds until the process exits.  In host code the
+// array's name is only a host-side stand-in, so the device address is looked up
+// once per device with cudaGetSymbolAddress (with that device current) and
+// cached; the first call on each device does that set-up and should therefore
+// come before any stream capture.  All calls on a device share the one array
+// and it keeps the last call's contents: every byte a call reads is written by
+// the same call first, but calls that overlap on the GPU (different streams,
+// or threads racing on one device) race on it and must be serialized.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "../../include/bposit_b200.h"
+#include "bp_internal.cuh"
+
+namespace bp {
+int launch_row_stats(int fmt, const void *codes, int rows, int K, const int32_t *s, int group,
+                     int4 *stats, cudaStream_t st);
+int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
+}  // namespace bp
+
+using namespace bp;
+
+// 1 MiB: one 16-byte statistics record per row of A and of B, so M + N <= 65536.
+static constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void *g_noalloc_addr[128];
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+static int noalloc_scratch(void **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(kENoDev, "bp_quire_gemm_noalloc: no CUDA device: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 128) return set_error(kENoDev, "bp_quire_gemm_noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void *p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(kECuda, "bp_quire_gemm_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return kOk;
+}
+
+extern "C" int bp_quire_gemm_noalloc(int fmt, const void *A, const void *B, int M, int N, int K,
+                                     const int32_t *sa, const int32_t *sb, int group, uint32_t *out_bp32,
+                                     int64_t ldo, uint32_t *out_quire, int quire_limbs, void *stream) {
+  if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_noalloc: fmt must be 8 or 16 (got %d)", fmt);
+  if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_noalloc: negative size");
+  if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_noalloc: group must be > 0 with scales");
+  if (ldo < N) return set_error(kEInval, "bp_quire_gemm_noalloc: ldo (%lld) < N (%d)", (long long)ldo, N);
+  if (out_quire && quire_limbs != 8 && quire_limbs != 12 && quire_limbs != 16)
+    return set_error(kEInval, "bp_quire_gemm_noalloc: quire_limbs must be 8, 12 or 16");
+  size_t need = ((size_t)M + (size_t)N) * sizeof(int4);
+  if (need > kNoAllocScratchBytes)
+    return set_error(kERange,
+                     "bp_quire_gemm_noalloc: M + N = %lld rows exceeds the fixed scratch limit of %zu rows "
+                     "(use bp_quire_gemm with a workspace)",
+                     (long long)M + N, kNoAllocScratchBytes / sizeof(int4));
+  if (M == 0 || N == 0) return kOk;
+  if (!out_bp32 || (K > 0 && (!A || !B))) return set_error(kEInval, "bp_quire_gemm_noalloc: null pointer");
+  void *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != kOk) return rc;
+  GemmArgs a{};
+  a.fmt = fmt; a.A = A; a.B = B; a.M = M; a.N = N; a.K = K;
+  a.sa = sa; a.sb = sb; a.group = group > 0 ? group : 1;
+  a.G = group > 0 ? (K + group - 1) / group : 1;
+  a.out = out_bp32; a.ldo = ldo; a.quire = out_quire; a.nlimbs = out_quire ? quire_limbs : 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  int4 *sta = (int4 *)scratch;
+  int4 *stb = sta + M;
+  rc = launch_row_stats(fmt, A, M, K, sa, a.group, sta, s);
+  if (rc != kOk) return rc;
+  rc = launch_row_stats(fmt, B, N, K, sb, a.group, stb, s);
+  if (rc != kOk) return rc;
+  return launch_gemm_simt(a, sta, stb, s);
+}
