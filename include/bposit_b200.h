@@ -46,6 +46,12 @@ const char *bp_last_error(void);
  * all threads).  Diagnostic; no reference counterpart. */
 unsigned long long bp_launch_count(void);
 
+/* Reads and clears the current device's kernel error word: nonzero when a
+ * bounded wait inside a tensor-core GEMM kernel gave up (the kernel then left
+ * its outputs unwritten and returned).  Synchronizes with the device.
+ * Diagnostic; no reference counterpart. */
+int bp_device_error(int *out);
+
 /* Decode n codes to their exact fp32 values; zero and NaR give +0.0.
  * Replaces bposit_ref.code_value (reference/bposit_ref.py:1022-1025) and the
  * (mantissa, exponent) LUT of bposit_fast._lut (reference/bposit_fast.py:27-43).

@@ -60,6 +60,7 @@ def lib() -> ctypes.CDLL:
             "bp_version": ([], i32),
             "bp_last_error": ([], ctypes.c_char_p),
             "bp_launch_count": ([], ctypes.c_ulonglong),
+            "bp_device_error": ([vp], i32),
             "bp_decode": ([i32, vp, sz, vp, vp], i32),
             "bp_quantize_bp8": ([vp, sz, i32, vp, vp, vp], i32),
             "bp_quantize_bp8_f64": ([vp, sz, i32, vp, vp, vp], i32),
@@ -81,7 +82,7 @@ def lib() -> ctypes.CDLL:
 
 
 EXPORTED = (
-    "bp_version", "bp_last_error", "bp_launch_count", "bp_decode", "bp_quantize_bp8", "bp_quantize_bp8_f64",
+    "bp_version", "bp_last_error", "bp_launch_count", "bp_device_error", "bp_decode", "bp_quantize_bp8", "bp_quantize_bp8_f64",
     "bp_quantize_bp8_grouped", "bp_encode_bp16", "bp_quire_to_bp32", "bp_quire_gemm",
     "bp_quire_gemm_workspace_size", "bp_quire_gemm_noalloc", "bp_bp32_to_f64",
 )

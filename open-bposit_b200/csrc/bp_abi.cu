@@ -65,6 +65,7 @@ static int check_device() {
   return kOk;
 }
 
+int tc_device_error(int *out);
 int launch_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
                        double *out, cudaStream_t s);
 
@@ -87,6 +88,13 @@ int bp_version(void) { return BP_VERSION; }
 const char *bp_last_error(void) { return g_err; }
 
 unsigned long long bp_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int bp_device_error(int *out) {
+  g_err[0] = 0;
+  if (!out) return set_error(kEInval, "bp_device_error: null pointer");
+  TRY(check_device());
+  return tc_device_error(out);
+}
 
 int bp_decode(int fmt, const void *codes, size_t n, float *out, void *stream) {
   g_err[0] = 0;

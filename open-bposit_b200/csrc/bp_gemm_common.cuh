@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "bp_format.cuh"
+#include "bp_internal.cuh"
 
 namespace bp {
 
@@ -75,6 +76,66 @@ __device__ __forceinline__ void write_fast_output(unsigned __int128 acc, int bas
       oq[i] = v;
     }
   }
+}
+
+// ---- exact per-element form and the slow (512-bit, per-term truncating) path ----
+struct ElemME {
+  int m;   // signed mantissa (0 for zero / NaR)
+  int e;   // exponent of the mantissa's bit 0, group scale included
+};
+
+template <int FMT>
+__device__ __forceinline__ ElemME load_elem(const void *base, int row, int K, int k,
+                                            const int32_t *s, int G, int group) {
+  uint32_t c = FMT == 8 ? ((const uint8_t *)base)[(size_t)row * K + k]
+                        : ((const uint16_t *)base)[(size_t)row * K + k];
+  ElemME r;
+  if (FMT == 8) posit_to_me<8, 2>(c, r.m, r.e);
+  else posit_to_me<16, 3>(c, r.m, r.e);
+  if (s && r.m) r.e += s[(size_t)row * G + k / group];
+  return r;
+}
+
+// 512-bit two's complement quire in 16 limbs: q += v * 2^sh (sh >= 0).
+__device__ inline void q512_add(uint32_t *q, int64_t v, int sh) {
+  if (v == 0 || sh >= 512) return;
+  int limb = sh >> 5, bit = sh & 31;
+  uint64_t uv = (uint64_t)v;
+  uint32_t fill = v < 0 ? 0xFFFFFFFFu : 0u;
+  uint32_t lo = (uint32_t)uv, hi = (uint32_t)(uv >> 32);
+  uint32_t x0 = bit ? lo << bit : lo;
+  uint32_t x1 = bit ? (hi << bit) | (lo >> (32 - bit)) : hi;
+  uint32_t x2 = bit ? (fill << bit) | (hi >> (32 - bit)) : fill;
+  uint64_t carry = 0;
+  for (int i = limb; i < 16; ++i) {
+    uint32_t t = i == limb ? x0 : (i == limb + 1 ? x1 : (i == limb + 2 ? x2 : fill));
+    uint64_t sum = (uint64_t)q[i] + t + carry;
+    q[i] = (uint32_t)sum;
+    carry = sum >> 32;
+  }
+}
+
+template <int FMT>
+__device__ inline void slow_output(const GemmArgs &a, int m, int n, uint32_t *out_bp32, uint32_t *out_q) {
+  uint32_t q[16];
+  for (int i = 0; i < 16; ++i) q[i] = 0u;
+  for (int k = 0; k < a.K; ++k) {
+    ElemME x = load_elem<FMT>(a.A, m, a.K, k, a.sa, a.G, a.group);
+    ElemME y = load_elem<FMT>(a.B, n, a.K, k, a.sb, a.G, a.group);
+    int64_t P = (int64_t)x.m * y.m;
+    if (!P) continue;
+    int sh = x.e + y.e + 96;
+    if (sh >= 0) {
+      q512_add(q, P, sh);
+    } else {
+      int r = -sh;
+      int64_t t = r >= 63 ? 0 : (P < 0 ? -((-P) >> r) : (P >> r));   // trunc toward zero
+      q512_add(q, t, 0);
+    }
+  }
+  *out_bp32 = bp32_from_limbs16(q);
+  if (out_q)
+    for (int i = 0; i < a.nlimbs; ++i) out_q[i] = q[i];
 }
 
 }  // namespace bp
