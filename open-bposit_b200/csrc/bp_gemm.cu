@@ -9,8 +9,7 @@
 namespace bp {
 
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
-int launch_gemm_tc(const GemmArgs &a, const int4 *sta, const int4 *stb, void *ws, size_t ws_bytes,
-                   cudaStream_t s);
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, cudaStream_t s);
 size_t gemm_tc_workspace(int fmt, int M, int N, int K);
 bool gemm_tc_supported(int fmt, int M, int N, int K);
 
@@ -86,15 +85,15 @@ int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cu
   if (ws_bytes < need_stats) return set_error(kEWorkspace, "quire_gemm: workspace too small");
   int4 *sta = (int4 *)ws;
   int4 *stb = sta + a.M;
-  int rc = launch_row_stats(a.fmt, a.A, a.M, a.K, a.sa, a.group, sta, s);
-  if (rc) return rc;
-  rc = launch_row_stats(a.fmt, a.B, a.N, a.K, a.sb, a.group, stb, s);
-  if (rc) return rc;
-  if (use_tc(a, algo)) {
+  if (use_tc(a, algo)) {   // the tensor-core prep computes the row statistics itself
     size_t need = gemm_tc_workspace(a.fmt, a.M, a.N, a.K);
     if (ws_bytes < need_stats + need) return set_error(kEWorkspace, "quire_gemm: workspace too small");
     return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, s);
   }
+  int rc = launch_row_stats(a.fmt, a.A, a.M, a.K, a.sa, a.group, sta, s);
+  if (rc) return rc;
+  rc = launch_row_stats(a.fmt, a.B, a.N, a.K, a.sb, a.group, stb, s);
+  if (rc) return rc;
   return launch_gemm_simt(a, sta, stb, s);
 }
 

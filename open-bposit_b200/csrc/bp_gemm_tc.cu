@@ -6,26 +6,28 @@
 // reference/bposit_fast.py:102-176, reference/bposit_ref.py:703-722), computed by
 // exponent-sliced integer MMAs:
 //
-//  1. Per row r of an operand (row stats: min lsb exponent la_r, max binade
-//     hb_r) choose a main base L_r = max(la_r, hb_r - SPAN + 1).  Every element
-//     with lsb >= L_r is an integer X = v / 2^L_r with |X| < 2^SPAN, recoded
-//     into S signed 8-bit digits X = sum_s d_s 256^s (d_s in [-128, 127]) and
-//     stored as S int8 planes [S][rows][Kp] (k_tc_prep).  bp8: S = 3,
-//     SPAN = 21; bp16: S = 4, SPAN = 29.
-//  2. Elements below L_r (the rare far tail of a row) are left out of the
-//     planes and added back exactly by k_tc_corr on CUDA cores:
+//  1. k_tc_prep, one block per operand row r: row statistics (min lsb exponent
+//     la_r, max binade hb_r), then a main base L_r = max(la_r, hb_r - SPAN + 1).
+//     Every element with lsb >= L_r is an integer X = v / 2^L_r, |X| < 2^SPAN,
+//     recoded into S signed base-128 digits X = sum_s d_s 128^s (low digits in
+//     [-64, 63], top digit |d| <= 65) and stored as S int8 planes
+//     [S][rows][Kp].  bp8: S = 3, SPAN = 20; bp16: S = 4, SPAN = 27.  The rare
+//     elements below L_r (a row's far tail) are listed instead.
+//  2. k_tc_corr adds the tails back exactly on CUDA cores:
 //     A_tail * B + A_main * B_tail, one 128-bit sum per touched output.
-//  3. The GEMM (k_quire_gemm_tc) issues, per 128-deep K block, S*S*4 int8
-//     MMAs (128 x BN x 32) and accumulates digit pair (s, t) into TMEM
-//     accumulator d = s + t.  K is cut into chunks of at most 32768 so every
-//     int32 diagonal sum is exact (|sum| <= K * 49152 < 2^31).
-//  4. The epilogue reads the 2S-1 diagonals, forms
-//     Q = sum_d acc_d * 256^d (exact, 128-bit), moves it to the output's lsb
-//     base la_i + la_j, adds the tail correction and rounds once to bposit32
-//     (or stores Q per chunk for k_tc_reduce when K needed several chunks).
-//  5. Outputs whose exact window exceeds 128 bits or that need per-term
-//     truncation (products below 2^-96) are recomputed by k_tc_fixup with the
-//     512-bit quire of the CUDA-core slow path.
+//  3. k_quire_gemm_tc issues, per 128-deep K block, S*S*4 int8 MMAs
+//     (128 x BN x 32) and accumulates digit pair (s, t) into TMEM accumulator
+//     d = s + t; the S MMAs sharing an A digit plane reuse it from the tensor
+//     core's A collector.  With base-128 digits a diagonal grows by at most
+//     12416 (bp8) / 16512 (bp16) per k, so int32 stays exact for K up to
+//     KCHUNK; longer K is cut into chunks summed by k_tc_reduce.
+//  4. The epilogue reads the 2S-1 diagonals, forms Q = sum_d acc_d * 128^d
+//     (exact, 128-bit), moves it to the output's lsb base la_i + la_j, adds the
+//     tail correction and rounds once to bposit32.
+//  5. Outputs whose exact window exceeds 128 bits, that need per-term
+//     truncation (products below 2^-96), or whose tail list overflowed are
+//     recomputed by k_tc_fixup with the 512-bit quire of the CUDA-core slow
+//     path (it exits at once when global row bounds show there are none).
 //
 // Warp roles in the GEMM (128 threads, one CTA per SM, 512 TMEM columns):
 // warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues MMAs, all four warps
@@ -49,13 +51,30 @@ __device__ int g_tc_error;   // nonzero after a bounded wait gave up
 namespace {
 
 constexpr int BM = 128, BK = 128, STAGES = 2, THREADS = 128;
-constexpr int KCHUNK = 32768;                 // K per exact int32 chunk
-constexpr long long WAIT_LIMIT = 4000000000LL; // cycles (~2 s) before a wait gives up
+constexpr long long WAIT_LIMIT = 4000000000LL;   // cycles (~2 s) before a wait gives up
+constexpr int TAILCAP = 1024;                    // listed tail elements per row (more -> fixup)
+constexpr int BIG = 1 << 20;                     // offset that makes max-reductions find a minimum
 
 template <int S>
 struct Cfg {
   static constexpr int BN = S == 3 ? 96 : 64;
   static constexpr int D = 2 * S - 1;
+  static constexpr int SPAN = 7 * S - 1;
+  static constexpr int TOP = (1 << (SPAN - 7 * (S - 1))) + 1;   // bound of |top digit|
+  static constexpr long long digit_max(int s) { return s == S - 1 ? TOP : 64; }
+  static constexpr long long diag_bound(int d) {
+    long long b = 0;
+    for (int s = 0; s < S; ++s)
+      if (d - s >= 0 && d - s < S) b += digit_max(s) * digit_max(d - s);
+    return b;
+  }
+  static constexpr long long max_diag() {
+    long long m = 0;
+    for (int d = 0; d < D; ++d) m = diag_bound(d) > m ? diag_bound(d) : m;
+    return m;
+  }
+  // K per chunk with every int32 diagonal sum exact, a multiple of BK
+  static constexpr int KCHUNK = (int)((0x7FFFFFFFLL / max_diag()) / BK * BK);
   static constexpr int A_BYTES = S * BM * BK;
   static constexpr int B_BYTES = S * BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -64,6 +83,15 @@ struct Cfg {
                                     ((uint32_t)(BM >> 4) << 24);
   static_assert(D * BN <= 512, "TMEM budget");
   static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
+  static_assert(TOP <= 127, "top digit must fit int8");
+};
+
+// Per-operand device counters, zeroed before each call:
+//   v[0] correction slots used, v[1] tail-list entries used,
+//   v[2] BIG - min la over nonzero rows, v[3] max (hb - la), v[4] any row whose
+//   tail could not be listed, v[5] any nonzero row.
+struct TcCounters {
+  int v[16];
 };
 
 struct TcParams {
@@ -146,12 +174,26 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// D[tmem] (+)= A[adesc] . B[bdesc]^T, int8 x int8 -> int32.  COL selects the
+// A-collector use: 0 load A and keep it, 1 reuse the kept A, 2 reuse and release.
+template <int COL>
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  if (COL == 0)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8.collector::a::fill [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  else if (COL == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8.collector::a::use [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -274,7 +316,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int t = 0; t < S; ++t) {
               const int d = s + t;
               uint64_t bd = sw128_desc(b0 + t * C::BN * BK + ks * 32);
-              umma_i8(tmem + d * C::BN, ad, bd, C::IDESC, (init >> d) & 1u);
+              const uint32_t acc = (init >> d) & 1u;
+              if (t == 0) umma_i8<0>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+              else if (t == S - 1) umma_i8<2>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+              else umma_i8<1>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
               init |= 1u << d;
             }
           }
@@ -313,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       unsigned __int128 Q = 0;
 #pragma unroll
       for (int d = 0; d < C::D; ++d)
-        Q += (unsigned __int128)(__int128)(long long)(int)v[d][jj] << (8 * d);
+        Q += (unsigned __int128)(__int128)(long long)(int)v[d][jj] << (7 * d);
       if (p.nchunks > 1) {
         p.partial[((size_t)chunk * p.M + i) * p.N + j] = make_ulonglong2((unsigned long long)Q,
                                                                           (unsigned long long)(Q >> 64));
@@ -354,119 +399,199 @@ __device__ __forceinline__ uint32_t load_code(const void *codes, size_t idx) {
   return FMT == 8 ? (uint32_t)((const uint8_t *)codes)[idx] : (uint32_t)((const uint16_t *)codes)[idx];
 }
 
-// One warp per row: main base L, S digit planes (4 bytes per lane per plane
-// per step), tail count, and a correction slot for rows with a tail.
+// 16 bytes of codes: 16 bp8 or 8 bp16 codes into c[].
+template <int FMT>
+__device__ __forceinline__ void load_codes16(const void *codes, size_t idx, uint32_t *c) {
+  uint4 w = *(const uint4 *)((const uint8_t *)codes + idx * (FMT / 8));
+  uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  if (FMT == 8) {
+#pragma unroll
+    for (int q = 0; q < 16; ++q) c[q] = (ws[q >> 2] >> (8 * (q & 3))) & 0xFFu;
+  } else {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) c[q] = (ws[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+  }
+}
+
+__device__ __forceinline__ int block_min(int v, int *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = min(r, red[w]);
+  return r;
+}
+
+__device__ __forceinline__ int block_max(int v, int *red) { return -block_min(-v, red); }
+
+// One block per row: statistics, main base L, S digit planes, tail list and
+// correction slot.  Pass 2 re-reads the row, which is still in L2.
 template <int FMT, int S>
 __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes, int rows, int K, int Kp,
                                                  const int32_t *__restrict__ sc, int G, int group,
-                                                 const int4 *__restrict__ stats, int8_t *__restrict__ planes,
+                                                 int4 *__restrict__ stats, int8_t *__restrict__ planes,
                                                  int *__restrict__ Lr, int *__restrict__ slot,
-                                                 int *__restrict__ slot_row, int *__restrict__ counter, int cap) {
-  constexpr int SPAN = 8 * S - 3;
-  const int lane = threadIdx.x & 31;
-  const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
-  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;
+                                                 int4 *__restrict__ seg, int *__restrict__ tails, int pool_cap,
+                                                 int cap, TcCounters *__restrict__ ctr) {
+  constexpr int SPAN = Cfg<S>::SPAN;
+  constexpr int EPT = FMT == 8 ? 16 : 8;   // elements per 16-byte load
+  __shared__ int s_tail[TAILCAP];
+  __shared__ int red[8];
+  __shared__ int s_nt, s_off, s_slot;
   const size_t plane = (size_t)rows * Kp;
-  for (long long r = warp; r < rows; r += nw) {
-    int4 st = stats[r];
-    int L = st.z ? max(st.x, st.y - (SPAN - 1)) : 0;
-    int ntail = 0;
+  const bool vec = (K % EPT) == 0 && (((uintptr_t)codes) & 15u) == 0;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const size_t rb = (size_t)r * K;
+    // pass 1: statistics
+    int lo = 0x3FFFFFFF, hi = -0x3FFFFFFF, nz = 0;
+    if (vec) {
+      for (int k0 = threadIdx.x * EPT; k0 < K; k0 += blockDim.x * EPT) {
+        uint32_t c[EPT];
+        load_codes16<FMT>(codes, rb + k0, c);
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          Dec d = FMT == 8 ? decode_posit<8, 2>(c[q]) : decode_posit<16, 3>(c[q]);
+          if (d.kind != 0) continue;
+          int sc_ = sc ? sc[(size_t)r * G + (k0 + q) / group] : 0;
+          lo = min(lo, d.scale - d.fw + sc_);
+          hi = max(hi, d.scale + sc_);
+          nz = 1;
+        }
+      }
+    } else {
+      for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        uint32_t c = load_code<FMT>(codes, rb + k);
+        Dec d = FMT == 8 ? decode_posit<8, 2>(c) : decode_posit<16, 3>(c);
+        if (d.kind != 0) continue;
+        int sc_ = sc ? sc[(size_t)r * G + k / group] : 0;
+        lo = min(lo, d.scale - d.fw + sc_);
+        hi = max(hi, d.scale + sc_);
+        nz = 1;
+      }
+    }
+    lo = block_min(lo, red);
+    hi = block_max(hi, red);
+    nz = block_max(nz, red);
+    const int L = nz ? max(lo, hi - (SPAN - 1)) : 0;
+    if (threadIdx.x == 0) {
+      stats[r] = make_int4(nz ? lo : 0, nz ? hi : 0, nz, 0);
+      Lr[r] = L;
+      s_nt = 0;
+      if (nz) {
+        atomicMax(&ctr->v[2], BIG - lo);
+        atomicMax(&ctr->v[3], hi - lo);
+        atomicMax(&ctr->v[5], 1);
+      }
+    }
+    __syncthreads();
+    // pass 2: digit planes and tail list
     int8_t *row = planes + (size_t)r * Kp;
-    for (int k0 = lane * 4; k0 < Kp; k0 += 128) {
-      uint32_t w[S];
+    for (int k0 = threadIdx.x * EPT; k0 < Kp; k0 += blockDim.x * EPT) {
+      uint32_t c[EPT];
+      if (vec && k0 < K) {
+        load_codes16<FMT>(codes, rb + k0, c);
+      } else {
 #pragma unroll
-      for (int s = 0; s < S; ++s) w[s] = 0u;
+        for (int q = 0; q < EPT; ++q) c[q] = k0 + q < K ? load_code<FMT>(codes, rb + k0 + q) : 0u;
+      }
+      uint32_t w[S][EPT / 4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        int k = k0 + q;
-        if (k >= K) break;
-        ElemME x = decode_scaled<FMT>(load_code<FMT>(codes, (size_t)r * K + k), sc, (int)r, k, G, group);
-        if (!x.m) continue;
+      for (int s = 0; s < S; ++s)
+#pragma unroll
+        for (int q = 0; q < EPT / 4; ++q) w[s][q] = 0u;
+#pragma unroll
+      for (int q = 0; q < EPT; ++q) {
+        const int k = k0 + q;
+        ElemME x;
+        if (FMT == 8) posit_to_me<8, 2>(c[q], x.m, x.e);
+        else posit_to_me<16, 3>(c[q], x.m, x.e);
+        if (!x.m || k >= K) continue;
+        if (sc) x.e += sc[(size_t)r * G + k / group];
         if (x.e < L) {
-          ++ntail;
+          int pos = atomicAdd(&s_nt, 1);
+          if (pos < TAILCAP) s_tail[pos] = k;
           continue;
         }
         int t = x.m * (1 << (x.e - L));
 #pragma unroll
-        for (int s = 0; s < S; ++s) {
-          int d = (int)(int8_t)(uint8_t)(t & 0xFF);
-          w[s] |= ((uint32_t)(uint8_t)d) << (8 * q);
-          t = (t - d) >> 8;
+        for (int s = 0; s < S - 1; ++s) {
+          int dg = ((t + 64) & 127) - 64;
+          w[s][q >> 2] |= ((uint32_t)(uint8_t)dg) << (8 * (q & 3));
+          t = (t - dg) >> 7;
+        }
+        w[S - 1][q >> 2] |= ((uint32_t)(uint8_t)t) << (8 * (q & 3));
+      }
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        if (EPT == 16) *(uint4 *)(row + s * plane + k0) = make_uint4(w[s][0], w[s][1], w[s][2], w[s][3]);
+        else *(uint2 *)(row + s * plane + k0) = make_uint2(w[s][0], w[s][1]);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int nt = s_nt;
+      int sl = -1, off = 0;
+      if (nt) {
+        sl = atomicAdd(&ctr->v[0], 1);
+        bool fits = nt <= TAILCAP;
+        if (fits) {
+          off = atomicAdd(&ctr->v[1], nt);
+          fits = off + nt <= pool_cap;
+        }
+        if (sl < cap) seg[sl] = make_int4(off, fits ? nt : 0, r, 0);
+        if (sl >= cap || !fits) {
+          sl = -2;
+          atomicMax(&ctr->v[4], 1);
         }
       }
-#pragma unroll
-      for (int s = 0; s < S; ++s) *(uint32_t *)(row + s * plane + k0) = w[s];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ntail += __shfl_xor_sync(0xFFFFFFFFu, ntail, o);
-    if (lane == 0) {
-      int sl = -1;
-      if (ntail) {
-        sl = atomicAdd(counter, 1);
-        if (sl < cap) slot_row[sl] = (int)r;
-        else sl = -2;
-      }
-      Lr[r] = L;
       slot[r] = sl;
+      s_slot = sl;
+      s_off = off;
     }
+    __syncthreads();
+    if (s_slot >= 0)
+      for (int t = threadIdx.x; t < s_nt; t += blockDim.x) tails[s_off + t] = s_tail[t];
+    __syncthreads();
   }
 }
 
 // ------------------------------------------------------- tail correction ---
-// For each tail row x of operand X (slot s), over all rows y of operand Y:
-//   C[s][y] = sum over tail elements (x, k) of X:  v(X[x,k]) * v(Y[y,k])
+// For each listed tail row x of operand X (slot s), over all rows y of Y:
+//   C[s][y] = sum over its tail elements (x, k):  v(X[x,k]) * v(Y[y,k])
 // exactly, in units of 2^(la_x + la_y).  When YL is given, Y's own tail
-// elements (lsb below YL[y]) are skipped (they were counted from Y's side).
+// elements (lsb below YL[y]) are skipped (they are counted from Y's side).
 template <int FMT>
 __global__ void __launch_bounds__(256) k_tc_corr(const void *__restrict__ X, const void *__restrict__ Y, int Yrows,
                                                  int K, const int32_t *__restrict__ xs, const int32_t *__restrict__ ys,
                                                  int G, int group, const int4 *__restrict__ xst,
-                                                 const int4 *__restrict__ yst, const int *__restrict__ XL,
-                                                 const int *__restrict__ YL, const int *__restrict__ slot_row,
-                                                 const int *__restrict__ counter, int cap,
+                                                 const int4 *__restrict__ yst, const int *__restrict__ YL,
+                                                 const int4 *__restrict__ seg, const int *__restrict__ tails,
+                                                 const TcCounters *__restrict__ ctr, int cap,
                                                  ulonglong2 *__restrict__ Cout) {
-  __shared__ int sk[256], sm[256], se[256];
-  __shared__ int cnt;
-  const int nslots = min(*counter, cap);
+  const int nslots = min(ctr->v[0], cap);
   for (int sl = blockIdx.x; sl < nslots; sl += gridDim.x) {
-    const int x = slot_row[sl];
-    const int4 sx = xst[x];
-    const int Lx = XL[x];
+    const int4 sg = seg[sl];
+    const int x = sg.z;
+    const int la_x = xst[x].x;
     for (int y0 = blockIdx.y * 256; y0 < Yrows; y0 += gridDim.y * 256) {
       const int y = y0 + threadIdx.x;
-      const bool valid = y < Yrows;
-      const int4 sy = valid ? yst[y] : make_int4(0, 0, 0, 0);
-      const int Ly = (YL && valid) ? YL[y] : -0x3FFFFFFF;
+      if (y >= Yrows) continue;
+      const int la_y = yst[y].x;
+      const int Ly = YL ? YL[y] : -0x3FFFFFFF;
       unsigned __int128 acc = 0;
-      for (int k0 = 0; k0 < K; k0 += 256) {
-        if (threadIdx.x == 0) cnt = 0;
-        __syncthreads();
-        int k = k0 + threadIdx.x;
-        if (k < K) {
-          ElemME e = decode_scaled<FMT>(load_code<FMT>(X, (size_t)x * K + k), xs, x, k, G, group);
-          if (e.m && e.e < Lx) {
-            int pos = atomicAdd(&cnt, 1);
-            sk[pos] = k;
-            sm[pos] = e.m;
-            se[pos] = e.e;
-          }
-        }
-        __syncthreads();
-        const int n = cnt;
-        if (valid) {
-          for (int t = 0; t < n; ++t) {
-            const int kk = sk[t];
-            ElemME f = decode_scaled<FMT>(load_code<FMT>(Y, (size_t)y * K + kk), ys, y, kk, G, group);
-            if (!f.m || f.e < Ly) continue;
-            long long P = (long long)sm[t] * f.m;
-            int sh = se[t] + f.e - (sx.x + sy.x);
-            sh = min(max(sh, 0), 127);
-            acc += (unsigned __int128)(__int128)P << sh;
-          }
-        }
-        __syncthreads();
+      for (int t = 0; t < sg.y; ++t) {
+        const int k = tails[sg.x + t];
+        ElemME e = decode_scaled<FMT>(load_code<FMT>(X, (size_t)x * K + k), xs, x, k, G, group);
+        ElemME f = decode_scaled<FMT>(load_code<FMT>(Y, (size_t)y * K + k), ys, y, k, G, group);
+        if (!f.m || f.e < Ly) continue;
+        long long P = (long long)e.m * f.m;
+        int sh = e.e + f.e - (la_x + la_y);
+        sh = min(max(sh, 0), 127);
+        acc += (unsigned __int128)(__int128)P << sh;
       }
-      if (valid) Cout[(size_t)sl * Yrows + y] = make_ulonglong2((unsigned long long)acc, (unsigned long long)(acc >> 64));
+      Cout[(size_t)sl * Yrows + y] = make_ulonglong2((unsigned long long)acc, (unsigned long long)(acc >> 64));
     }
   }
 }
@@ -475,7 +600,14 @@ __global__ void __launch_bounds__(256) k_tc_corr(const void *__restrict__ X, con
 template <int FMT>
 __global__ void __launch_bounds__(256) k_tc_fixup(GemmArgs a, const int4 *__restrict__ sta,
                                                   const int4 *__restrict__ stb, const int *__restrict__ slotA,
-                                                  const int *__restrict__ slotB) {
+                                                  const int *__restrict__ slotB, const TcCounters *__restrict__ cA,
+                                                  const TcCounters *__restrict__ cB) {
+  // Every output is 0 when an operand has no nonzero row; and when the
+  // global bounds already make every pair exact there is nothing to redo.
+  if (!cA->v[5] || !cB->v[5]) return;
+  const int min_la = (BIG - cA->v[2]) + (BIG - cB->v[2]);
+  const int max_w = cA->v[3] + cB->v[3] + 2 + ceil_log2_int(a.K) + 1;
+  if (min_la + 96 >= 0 && max_w <= 127 && !cA->v[4] && !cB->v[4]) return;
   size_t n = (size_t)a.M * a.N;
   for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < n; o += (size_t)gridDim.x * blockDim.x) {
     int i = (int)(o / a.N), j = (int)(o % a.N);
@@ -518,12 +650,12 @@ int make_plane_map(CUtensorMap *m, void *base, int Kp, int rows, int S, int box_
 inline size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
 struct TcLayout {
-  int S, Kp, nkb, nchunks, capA, capB;
-  size_t planesA, planesB, LA, LB, slotA, slotB, rowA, rowB, ctr, CA, CB, part, total;
+  int S, Kp, nkb, kbc, nchunks, capA, capB, pool;
+  size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, part, total;
 };
 
-// Correction buffers hold at most this many bytes per side; rows with a tail
-// beyond the cap are finished by the fixup kernel instead.
+// Correction buffers hold at most this many bytes per side; tail rows beyond
+// the cap are finished by the fixup kernel instead.
 constexpr size_t kCorrBudget = size_t(512) << 20;
 
 TcLayout tc_layout(int fmt, int M, int N, int K) {
@@ -531,10 +663,11 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.S = fmt == 8 ? 3 : 4;
   L.Kp = (K + BK - 1) / BK * BK;
   L.nkb = L.Kp / BK;
-  const int kbc = KCHUNK / BK;
-  L.nchunks = (L.nkb + kbc - 1) / kbc;
+  L.kbc = (L.S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
+  L.nchunks = (L.nkb + L.kbc - 1) / L.kbc;
   L.capA = (int)std::min<size_t>((size_t)M, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(N, 1))));
   L.capB = (int)std::min<size_t>((size_t)N, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(M, 1))));
+  L.pool = std::max(65536, 8 * std::max(M, N));
   size_t o = 0;
   L.planesA = o; o += al((size_t)L.S * M * L.Kp);
   L.planesB = o; o += al((size_t)L.S * N * L.Kp);
@@ -542,8 +675,10 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.LB = o; o += al(4 * (size_t)N);
   L.slotA = o; o += al(4 * (size_t)M);
   L.slotB = o; o += al(4 * (size_t)N);
-  L.rowA = o; o += al(4 * (size_t)M);
-  L.rowB = o; o += al(4 * (size_t)N);
+  L.segA = o; o += al(16 * (size_t)L.capA);
+  L.segB = o; o += al(16 * (size_t)L.capB);
+  L.tailA = o; o += al(4 * (size_t)L.pool);
+  L.tailB = o; o += al(4 * (size_t)L.pool);
   L.ctr = o; o += 256;
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
@@ -577,60 +712,60 @@ bool gemm_tc_supported(int fmt, int M, int N, int K) {
 
 size_t gemm_tc_workspace(int fmt, int M, int N, int K) { return tc_layout(fmt, M, N, K).total; }
 
-int launch_gemm_tc(const GemmArgs &a, const int4 *sta, const int4 *stb, void *ws, size_t ws_bytes, cudaStream_t s) {
+// sta / stb are outputs here: the prep kernels write the row statistics.
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, cudaStream_t s) {
   TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K);
   if (ws_bytes < L.total) return set_error(kEWorkspace, "quire_gemm: tensor-core workspace too small");
   char *w = (char *)ws;
   int8_t *planesA = (int8_t *)(w + L.planesA), *planesB = (int8_t *)(w + L.planesB);
   int *LA = (int *)(w + L.LA), *LB = (int *)(w + L.LB);
   int *slotA = (int *)(w + L.slotA), *slotB = (int *)(w + L.slotB);
-  int *rowA = (int *)(w + L.rowA), *rowB = (int *)(w + L.rowB);
-  int *ctr = (int *)(w + L.ctr);
+  int4 *segA = (int4 *)(w + L.segA), *segB = (int4 *)(w + L.segB);
+  int *tailA = (int *)(w + L.tailA), *tailB = (int *)(w + L.tailB);
+  TcCounters *cA = (TcCounters *)(w + L.ctr);
+  TcCounters *cB = cA + 1;
   ulonglong2 *CA = (ulonglong2 *)(w + L.CA), *CB = (ulonglong2 *)(w + L.CB);
   ulonglong2 *part = L.nchunks > 1 ? (ulonglong2 *)(w + L.part) : nullptr;
 
-  cudaError_t e = cudaMemsetAsync(ctr, 0, 256, s);
+  cudaError_t e = cudaMemsetAsync(cA, 0, 2 * sizeof(TcCounters), s);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(e));
   const int sms = sm_count();
-  auto prep = [&](const void *codes, int rows, const int32_t *sc, const int4 *st, int8_t *planes, int *Lr,
-                  int *slot, int *srow, int *counter, int cap) {
-    long long blocks = ((long long)rows * 32 + 255) / 256;
-    int g = (int)std::min<long long>(blocks, (long long)sms * 8);
+  auto prep = [&](const void *codes, int rows, const int32_t *sc, int4 *st, int8_t *planes, int *Lr, int *slot,
+                  int4 *seg, int *tails, int cap, TcCounters *c) {
+    int g = std::min(rows, sms * 4);
     if (a.fmt == 8)
-      k_tc_prep<8, 3><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, srow,
-                                        counter, cap);
+      k_tc_prep<8, 3><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, seg, tails,
+                                        L.pool, cap, c);
     else
-      k_tc_prep<16, 4><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, srow,
-                                         counter, cap);
+      k_tc_prep<16, 4><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, seg,
+                                         tails, L.pool, cap, c);
     return check_launch("tc_prep");
   };
-  int rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, rowA, ctr, L.capA);
+  int rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA);
   if (rc) return rc;
-  rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, rowB, ctr + 1, L.capB);
+  rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB);
   if (rc) return rc;
 
   // tail corrections (the kernels read the tail-row counts on the device)
-  {
-    dim3 ga((unsigned)std::min(L.capA, sms * 2), (unsigned)std::min((a.N + 255) / 256, 64));
-    dim3 gb((unsigned)std::min(L.capB, sms * 2), (unsigned)std::min((a.M + 255) / 256, 64));
-    if (a.fmt == 8) {
-      k_tc_corr<8><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, LA, nullptr, rowA,
-                                      ctr, L.capA, CA);
-      rc = check_launch("tc_corr");
-      if (rc) return rc;
-      k_tc_corr<8><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LB, LA, rowB,
-                                      ctr + 1, L.capB, CB);
-    } else {
-      k_tc_corr<16><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, LA, nullptr, rowA,
-                                       ctr, L.capA, CA);
-      rc = check_launch("tc_corr");
-      if (rc) return rc;
-      k_tc_corr<16><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LB, LA, rowB,
-                                       ctr + 1, L.capB, CB);
-    }
+  dim3 ga((unsigned)std::min(L.capA, sms * 2), (unsigned)std::min((a.N + 255) / 256, 64));
+  dim3 gb((unsigned)std::min(L.capB, sms * 2), (unsigned)std::min((a.M + 255) / 256, 64));
+  if (a.fmt == 8) {
+    k_tc_corr<8><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA, cA,
+                                    L.capA, CA);
     rc = check_launch("tc_corr");
     if (rc) return rc;
+    k_tc_corr<8><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB, cB,
+                                    L.capB, CB);
+  } else {
+    k_tc_corr<16><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
+                                     cA, L.capA, CA);
+    rc = check_launch("tc_corr");
+    if (rc) return rc;
+    k_tc_corr<16><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB, cB,
+                                     L.capB, CB);
   }
+  rc = check_launch("tc_corr");
+  if (rc) return rc;
 
   int S = L.S;
   int bn = S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
@@ -642,7 +777,7 @@ int launch_gemm_tc(const GemmArgs &a, const int4 *sta, const int4 *stb, void *ws
 
   TcParams p{};
   p.M = a.M; p.N = a.N; p.K = a.K; p.Kp = L.Kp; p.nkb = L.nkb;
-  p.kb_per_chunk = KCHUNK / BK; p.nchunks = L.nchunks;
+  p.kb_per_chunk = L.kbc; p.nchunks = L.nchunks;
   p.sta = sta; p.stb = stb; p.LA = LA; p.LB = LB; p.slotA = slotA; p.slotB = slotB;
   p.CA = CA; p.CB = CB;
   p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.partial = part;
@@ -655,8 +790,8 @@ int launch_gemm_tc(const GemmArgs &a, const int4 *sta, const int4 *stb, void *ws
     rc = check_launch("tc_reduce");
     if (rc) return rc;
   }
-  if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB);
-  else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB);
+  if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
+  else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   return check_launch("tc_fixup");
 }
 

@@ -218,3 +218,62 @@ def test_large_bp8_k65536_row_subsample(ops, orc):
     assert np.array_equal(o[:64, cols], orc.quire_gemm(An[:64], Bn[cols], 8))
     del A, B, out
     torch.cuda.empty_cache()
+
+
+def _device_error():
+    import ctypes
+    from bposit_b200 import _lib
+    v = ctypes.c_int(0)
+    assert _lib.lib().bp_device_error(ctypes.byref(v)) == 0
+    return v.value
+
+
+@pytest.mark.parametrize("fmt", [8, 16])
+def test_tc_listed_tails(ops, orc, fmt):
+    """Rows whose values span more than the tensor-core digit window: a few
+    tiny elements per row become listed tails, corrected exactly on CUDA cores."""
+    rng = np.random.default_rng(40 + fmt)
+    M, N, K = 150, 170, 1000
+    X = rng.standard_normal((M, K)).astype(np.float32)
+    Y = rng.standard_normal((N, K)).astype(np.float32)
+    for Z in (X, Y):
+        rows = np.repeat(np.arange(Z.shape[0]), 3)
+        cols = rng.integers(0, K, rows.size)
+        Z[rows, cols] = (rng.standard_normal(rows.size) * (2.0 ** -22 if fmt == 8 else 2.0 ** -60)).astype(np.float32)
+    if fmt == 8:
+        A, B = orc.quantize_bp8(X)[0], orc.quantize_bp8(Y)[0]
+    else:
+        A, B = orc.encode_bp16(X, True), orc.encode_bp16(Y, True)
+    out, q = run(ops, A, B, fmt, 2, quire_limbs=16)
+    rb, rq = orc.quire_gemm(A, B, fmt, nlimbs=16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+    assert _device_error() == 0
+
+
+def test_tc_tail_overflow_goes_to_fixup(ops, orc):
+    """More tail elements in a row than the tail list holds: that row's
+    outputs are recomputed by the exact fixup kernel."""
+    rng = np.random.default_rng(9)
+    M, N, K = 40, 50, 3000
+    A = orc.quantize_bp8(rng.standard_normal((M, K)).astype(np.float32))[0]
+    B = orc.quantize_bp8(rng.standard_normal((N, K)).astype(np.float32))[0]
+    A[3, :2000] = 0x01          # 2000 x minpos
+    A[3, 2000] = 0x7F           # maxpos: the row's window cannot reach minpos
+    B[7, ::2] = 0xFF            # -minpos
+    B[7, 1] = 0x7E
+    out, _ = run(ops, A, B, 8, 2)
+    assert np.array_equal(out, orc.quire_gemm(A, B, 8))
+    assert _device_error() == 0
+
+
+def test_tc_split_k(ops, orc):
+    """K beyond one exact int32 chunk: per-chunk 128-bit partial sums."""
+    rng = np.random.default_rng(10)
+    M, N, K = 64, 96, 200000
+    A = orc.quantize_bp8(rng.standard_normal((M, K)).astype(np.float32))[0]
+    B = orc.quantize_bp8(rng.standard_normal((N, K)).astype(np.float32))[0]
+    out, _ = run(ops, A, B, 8, 2)
+    rows = np.array([0, 17, 63])
+    assert np.array_equal(out[rows], orc.quire_gemm(A[rows], B, 8))
+    assert _device_error() == 0
