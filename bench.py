@@ -44,54 +44,91 @@ def load_peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler for the timed region."""
+    """SM clock and throttle reasons sampled every 20 ms by an NVML thread
+    during the timed region (nvidia-smi at 200 ms is the fallback)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"bposit_clocks_{os.getpid()}.csv")
+    def __init__(self, cuda_index: int):
+        import threading
+        self.idx = cuda_index
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = self.idx
+        if vis:
+            parts = [v.strip() for v in vis.split(",") if v.strip()]
+            if self.idx < len(parts) and parts[self.idx].isdigit():
+                idx = int(parts[self.idx])
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(idx)
+
+    def _run(self, nv, h):
+        bits = [(name, getattr(nv, attr, 0)) for name, attr in self.REASONS]
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                for name, b in bits:
+                    if b and (r & b):
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.02)
 
     def start(self):
+        import threading
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
-        except (OSError, ValueError):
-            self.proc = None
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
+            self._thread.start()
+        except Exception:
+            try:
+                self._path = os.path.join("/tmp", f"bposit_clocks_{os.getpid()}.csv")
+                self._fh = open(self._path, "w")
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.idx}", "--query-gpu=clocks.sm,clocks.max.sm,"
+                     "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                     "--format=csv,noheader,nounits", "-lms", "200"], stdout=self._fh, stderr=subprocess.DEVNULL)
+            except (OSError, ValueError):
+                self._proc = None
 
     def stop(self):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.fh.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+        elif self._proc is not None:
+            self._proc.terminate()
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.path)
-        if not sm:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._fh.close()
+            for line in open(self._path):
+                f = [x.strip() for x in line.split(",")]
+                try:
+                    self.samples.append(float(f[0]))
+                    self.max_mhz = float(f[1])
+                except (ValueError, IndexError):
+                    continue
+                for (name, _), v in zip(self.REASONS, f[2:6]):
+                    if v.lower() == "active":
+                        self.reasons.add(name)
+            os.unlink(self._path)
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def make_operand(ops, torch, rows, K, gen, device):
@@ -298,6 +335,8 @@ def run_ours(args):
     per_rank_ops = 2.0 * M_ * (n1 - n0) * K_
     k_tops = per_rank_ops / (kms * 1e-3) / 1e12
     int8_peak = 2.0 * peaks["bf16_tflops"]
+    from bposit_b200 import ops as _ops
+    slice_pairs = 9 if _ops.gemm_workspace_size(8, M_, n1 - n0, K_, 2) and args.algo != 1 else None
 
     # end to end through the public API with host buffers (pinned)
     hA = A.cpu().pin_memory()
@@ -366,7 +405,11 @@ def run_ours(args):
             "roofline": {"bound": "tensor", "achieved": round(k_tops, 3), "peak": round(int8_peak, 1),
                          "unit": "TOPS", "frac": round(k_tops / int8_peak, 5), "traffic": traffic,
                          "peak_source": f"int8 dense = 2 x {peak_src} bf16 {peaks['bf16_tflops']} TF/s",
-                         "kernel": "quire GEMM (row stats + GEMM launches)", "kernel_ms": round(kms, 3)},
+                         "kernel": "quire GEMM (all launches of one bp_quire_gemm call)",
+                         "kernel_ms": round(kms, 3),
+                         "issued_int8_TOPS": round(k_tops * slice_pairs, 1) if slice_pairs else None,
+                         "issued_frac": round(k_tops * slice_pairs / int8_peak, 4) if slice_pairs else None,
+                         "slice_pairs_per_useful_mac": slice_pairs},
             "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS", "ms_per_step": round(ems, 3),
                     "h2d_bytes_per_step": int(M_ * K_ + (n1 - n0) * K_),
                     "d2h_bytes_per_step": int(M_ * N_ * 4)},
@@ -385,7 +428,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
