@@ -426,8 +426,24 @@ __device__ __forceinline__ int block_min(int v, int *red) {
 
 __device__ __forceinline__ int block_max(int v, int *red) { return -block_min(-v, red); }
 
+// Decoded element: lsb exponent (group scale folded in) and signed mantissa.
+template <int FMT>
+__device__ __forceinline__ ElemME prep_decode(uint32_t c, const int4 *s_dec) {
+  ElemME x;
+  if (FMT == 8) {
+    int4 t = s_dec[c];
+    x.m = t.z;
+    x.e = t.x;
+  } else {
+    posit_to_me<16, 3>(c, x.m, x.e);
+  }
+  return x;
+}
+
 // One block per row: statistics, main base L, S digit planes, tail list and
-// correction slot.  Pass 2 re-reads the row, which is still in L2.
+// correction slot.  Pass 2 re-reads the row, which is still in L2.  bp8 codes
+// are decoded through a 256-entry table; for unscaled bp8 rows pass 2 also
+// uses a per-row table of each code's packed digits (bit 31 marks a tail).
 template <int FMT, int S>
 __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes, int rows, int K, int Kp,
                                                  const int32_t *__restrict__ sc, int G, int group,
@@ -437,37 +453,52 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
                                                  int cap, TcCounters *__restrict__ ctr) {
   constexpr int SPAN = Cfg<S>::SPAN;
   constexpr int EPT = FMT == 8 ? 16 : 8;   // elements per 16-byte load
+  constexpr bool LUT_DIGITS = FMT == 8 && S <= 4;
   __shared__ int s_tail[TAILCAP];
+  __shared__ int4 s_dec[FMT == 8 ? 256 : 1];     // {lsb, binade, mantissa, 0}
+  __shared__ uint32_t s_dig[FMT == 8 ? 256 : 1];
   __shared__ int red[8];
   __shared__ int s_nt, s_off, s_slot;
+  if (FMT == 8) {
+    for (int c = threadIdx.x; c < 256; c += blockDim.x) {
+      int m, e;
+      posit_to_me<8, 2>((uint32_t)c, m, e);
+      int hb = m ? e + 31 - __clz(m < 0 ? -m : m) : 0;
+      s_dec[c] = make_int4(e, hb, m, 0);
+    }
+    __syncthreads();
+  }
   const size_t plane = (size_t)rows * Kp;
   const bool vec = (K % EPT) == 0 && (((uintptr_t)codes) & 15u) == 0;
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const size_t rb = (size_t)r * K;
     // pass 1: statistics
     int lo = 0x3FFFFFFF, hi = -0x3FFFFFFF, nz = 0;
-    if (vec) {
-      for (int k0 = threadIdx.x * EPT; k0 < K; k0 += blockDim.x * EPT) {
-        uint32_t c[EPT];
+    for (int k0 = threadIdx.x * EPT; k0 < K; k0 += blockDim.x * EPT) {
+      uint32_t c[EPT];
+      if (vec) {
         load_codes16<FMT>(codes, rb + k0, c);
+      } else {
 #pragma unroll
-        for (int q = 0; q < EPT; ++q) {
-          Dec d = FMT == 8 ? decode_posit<8, 2>(c[q]) : decode_posit<16, 3>(c[q]);
-          if (d.kind != 0) continue;
-          int sc_ = sc ? sc[(size_t)r * G + (k0 + q) / group] : 0;
-          lo = min(lo, d.scale - d.fw + sc_);
-          hi = max(hi, d.scale + sc_);
-          nz = 1;
-        }
+        for (int q = 0; q < EPT; ++q) c[q] = k0 + q < K ? load_code<FMT>(codes, rb + k0 + q) : 0u;
       }
-    } else {
-      for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        uint32_t c = load_code<FMT>(codes, rb + k);
-        Dec d = FMT == 8 ? decode_posit<8, 2>(c) : decode_posit<16, 3>(c);
-        if (d.kind != 0) continue;
-        int sc_ = sc ? sc[(size_t)r * G + k / group] : 0;
-        lo = min(lo, d.scale - d.fw + sc_);
-        hi = max(hi, d.scale + sc_);
+#pragma unroll
+      for (int q = 0; q < EPT; ++q) {
+        int l, h;
+        if (FMT == 8) {
+          int4 t = s_dec[c[q]];
+          if (!t.z) continue;
+          l = t.x;
+          h = t.y;
+        } else {
+          Dec d = decode_posit<16, 3>(c[q]);
+          if (d.kind != 0) continue;
+          l = d.scale - d.fw;
+          h = d.scale;
+        }
+        int sc_ = sc ? sc[(size_t)r * G + (k0 + q) / group] : 0;
+        lo = min(lo, l + sc_);
+        hi = max(hi, h + sc_);
         nz = 1;
       }
     }
@@ -483,6 +514,28 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
         atomicMax(&ctr->v[2], BIG - lo);
         atomicMax(&ctr->v[3], hi - lo);
         atomicMax(&ctr->v[5], 1);
+      }
+    }
+    const bool lut = LUT_DIGITS && sc == nullptr;
+    if (lut) {
+      for (int cc = threadIdx.x; cc < 256; cc += blockDim.x) {
+        int4 t = s_dec[cc];
+        uint32_t v = 0u;
+        if (t.z) {
+          if (t.x < L) {
+            v = 0x80000000u;
+          } else {
+            int x = t.z * (1 << (t.x - L));
+#pragma unroll
+            for (int s = 0; s < S - 1; ++s) {
+              int dg = ((x + 64) & 127) - 64;
+              v |= ((uint32_t)(uint8_t)dg) << (8 * s);
+              x = (x - dg) >> 7;
+            }
+            v |= ((uint32_t)(uint8_t)x) << (8 * (S - 1));
+          }
+        }
+        s_dig[cc] = v;
       }
     }
     __syncthreads();
@@ -504,9 +557,18 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
 #pragma unroll
       for (int q = 0; q < EPT; ++q) {
         const int k = k0 + q;
-        ElemME x;
-        if (FMT == 8) posit_to_me<8, 2>(c[q], x.m, x.e);
-        else posit_to_me<16, 3>(c[q], x.m, x.e);
+        if (lut) {
+          uint32_t v = s_dig[c[q]];
+          if (v & 0x80000000u) {
+            int pos = atomicAdd(&s_nt, 1);
+            if (pos < TAILCAP) s_tail[pos] = k;
+            continue;
+          }
+#pragma unroll
+          for (int s = 0; s < S; ++s) w[s][q >> 2] |= ((v >> (8 * s)) & 0xFFu) << (8 * (q & 3));
+          continue;
+        }
+        ElemME x = prep_decode<FMT>(c[q], s_dec);
         if (!x.m || k >= K) continue;
         if (sc) x.e += sc[(size_t)r * G + k / group];
         if (x.e < L) {
