@@ -15,7 +15,7 @@
 //     elements below L_r (a row's far tail) are listed instead.
 //  2. k_tc_corr adds the tails back exactly on CUDA cores:
 //     A_tail * B + A_main * B_tail, one 128-bit sum per touched output.
-//  3. k_quire_gemm_tc issues, per 128-deep K block, S*S*4 int8 MMAs
+//  3. k_quire_gemm_tc issues, per 64-deep K block, S*S*2 int8 MMAs
 //     (128 x BN x 32) and accumulates digit pair (s, t) into TMEM accumulator
 //     d = s + t; the S MMAs sharing an A digit plane reuse it from the tensor
 //     core's A collector.  With base-128 digits a diagonal grows by at most
@@ -50,7 +50,10 @@ __device__ int g_tc_error;   // nonzero after a bounded wait gave up
 
 namespace {
 
-constexpr int BM = 128, BK = 128, STAGES = 2, THREADS = 128;
+#ifndef BP_TC_BK
+#define BP_TC_BK 64
+#endif
+constexpr int BM = 128, BK = BP_TC_BK, THREADS = 128;
 constexpr long long WAIT_LIMIT = 4000000000LL;   // cycles (~2 s) before a wait gives up
 constexpr int TAILCAP = 1024;                    // listed tail elements per row (more -> fixup)
 constexpr int BIG = 1 << 20;                     // offset that makes max-reductions find a minimum
@@ -78,6 +81,7 @@ struct Cfg {
   static constexpr int A_BYTES = S * BM * BK;
   static constexpr int B_BYTES = S * BN * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = BK == 128 ? 2 : (S == 3 ? 5 : 4);
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + BN * 32;
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                     ((uint32_t)(BM >> 4) << 24);
@@ -166,40 +170,58 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// K-major operand tile with 128-byte swizzle: rows of 128 bytes, 8-row atoms
-// 1024 bytes apart (SBO), leading offset 16 bytes (unused by the swizzle),
-// descriptor version 1, layout SWIZZLE_128B.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+// K-major operand tile with 64-byte swizzle: rows of 64 bytes (BK int8),
+// 8-row atoms 512 bytes apart (SBO), leading offset 16 bytes (unused by the
+// swizzle), descriptor version 1, layout SWIZZLE_64B.
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  if (BK == 128)
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)32 << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
 }
 
-// D[tmem] (+)= A[adesc] . B[bdesc]^T, int8 x int8 -> int32.  COL selects the
-// A-collector use: 0 load A and keep it, 1 reuse the kept A, 2 reuse and release.
+// D[tmem] (+)= A[adesc] . B[bdesc]^T, int8 x int8 -> int32, issued by one
+// lane elected from the calling (converged) warp so that the whole issue loop
+// stays warp-uniform.  COL selects the A-collector use: 0 load A and keep it,
+// 1 reuse the kept A, 2 reuse and release, 3 no collector.
+#define BP_UMMA_ASM(QUAL)                                                                   \
+  asm volatile(                                                                             \
+      "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"    \
+      "@e tcgen05.mma.cta_group::1.kind::i8" QUAL " [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d), \
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate))
+
 template <int COL>
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
-  if (COL == 0)
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8.collector::a::fill [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-  else if (COL == 1)
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8.collector::a::use [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-  else
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8.collector::a::lastuse [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+  if (COL == 0) BP_UMMA_ASM(".collector::a::fill");
+  else if (COL == 1) BP_UMMA_ASM(".collector::a::use");
+  else if (COL == 2) BP_UMMA_ASM(".collector::a::lastuse");
+  else BP_UMMA_ASM("");
+}
+#undef BP_UMMA_ASM
+
+// Arrive on `bar` once every tcgen05 operation this warp issued so far has
+// completed (one elected lane commits).
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
+      : "memory");
 }
 
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
+// Warp-uniform bounded wait: every lane leaves together once any lane has
+// seen the phase complete (completion is monotonic).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int code) {
+  long long t0 = clock64();
+  while (true) {
+    bool done = mbar_try_wait(bar, parity);
+    if (__any_sync(0xFFFFFFFFu, done)) return true;
+    if (clock64() - t0 > WAIT_LIMIT) {
+      if ((threadIdx.x & 31) == 0) atomicOr(&g_tc_error, code);
+      return false;
+    }
+  }
 }
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
@@ -249,11 +271,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   using C = Cfg<S>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t *full = (uint64_t *)(smem + STAGES * C::STAGE_BYTES);
-  uint64_t *empty = full + STAGES;
-  uint64_t *tfull = empty + STAGES;
+  uint64_t *full = (uint64_t *)(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *empty = full + C::STAGES;
+  uint64_t *tfull = empty + C::STAGES;
   uint32_t *tmem_slot = (uint32_t *)(tfull + 1);
-  int4 *sstat = (int4 *)(smem + STAGES * C::STAGE_BYTES + 256);          // [BN] B-row stats
+  int4 *sstat = (int4 *)(smem + C::STAGES * C::STAGE_BYTES + 256);          // [BN] B-row stats
   int2 *sLs = (int2 *)(sstat + C::BN);                                    // [BN] {L, slot}
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -263,7 +285,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int nkb = kb1 - kb0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -285,8 +307,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       for (int it = 0; it < nkb && ok; ++it) {
-        int st = it % STAGES;
-        uint32_t round = (uint32_t)(it / STAGES);
+        int st = it % C::STAGES;
+        uint32_t round = (uint32_t)(it / C::STAGES);
         ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1);
         if (!ok) break;
         uint8_t *sa = smem + st * C::STAGE_BYTES;
@@ -297,12 +319,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
+    {   // the whole warp runs the issue loop; one elected lane issues each MMA
       uint32_t init = 0u;
       for (int it = 0; it < nkb && ok; ++it) {
-        int st = it % STAGES;
-        uint32_t round = (uint32_t)(it / STAGES);
-        ok = mbar_wait(&full[st], round & 1u, 2);
+        int st = it % C::STAGES;
+        uint32_t round = (uint32_t)(it / C::STAGES);
+        ok = mbar_wait_warp(&full[st], round & 1u, 2);
         if (!ok) break;
         tc_fence_after();
         uint32_t a0 = smem_u32(smem + st * C::STAGE_BYTES);
@@ -311,11 +333,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int ks = 0; ks < BK / 32; ++ks) {
 #pragma unroll
           for (int s = 0; s < S; ++s) {
-            uint64_t ad = sw128_desc(a0 + s * BM * BK + ks * 32);
+            uint64_t ad = sw64_desc(a0 + s * BM * BK + ks * 32);
 #pragma unroll
             for (int t = 0; t < S; ++t) {
               const int d = s + t;
-              uint64_t bd = sw128_desc(b0 + t * C::BN * BK + ks * 32);
+              uint64_t bd = sw64_desc(b0 + t * C::BN * BK + ks * 32);
               const uint32_t acc = (init >> d) & 1u;
               if (t == 0) umma_i8<0>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
               else if (t == S - 1) umma_i8<2>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
@@ -695,7 +717,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [S][rows][Kp] int8 planes; box {128 (K), box_rows, S}; 128-byte swizzle.
+// [S][rows][Kp] int8 planes; box {BK (K), box_rows, S}; 64-byte swizzle.
 int make_plane_map(CUtensorMap *m, void *base, int Kp, int rows, int S, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return set_error(kECuda, "quire_gemm: cuTensorMapEncodeTiled unavailable");
@@ -704,7 +726,7 @@ int make_plane_map(CUtensorMap *m, void *base, int Kp, int rows, int S, int box_
   cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, (cuuint32_t)S};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  BK == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(kECuda, "quire_gemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
   return kOk;
 }
@@ -723,7 +745,7 @@ constexpr size_t kCorrBudget = size_t(512) << 20;
 TcLayout tc_layout(int fmt, int M, int N, int K) {
   TcLayout L{};
   L.S = fmt == 8 ? 3 : 4;
-  L.Kp = (K + BK - 1) / BK * BK;
+  L.Kp = (K + 127) / 128 * 128;
   L.nkb = L.Kp / BK;
   L.kbc = (L.S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
   L.nchunks = (L.nkb + L.kbc - 1) / L.kbc;
