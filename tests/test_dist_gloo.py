@@ -1,0 +1,78 @@
+"""Host logic of the N-sharded quire GEMM (bposit_b200/dist.py) on 2 CPU ranks
+over gloo: shard bounds, the all-gather of column shards and the assembly into
+[M, N] are checked bit-exactly against the unsharded oracle GEMM, including N
+not divisible by the rank count and a rank that owns no columns.  The oracle
+stands in for the device GEMM on CPU ranks (the GPU run of the same class is
+tests/test_gpu_dist.py)."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, cases, q):
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "open-bposit_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from bposit_b200.dist import ShardedQuireGemm
+    from oracle import oracle
+    try:
+        for (M, N, K, seed) in cases:
+            rng = np.random.default_rng(seed)
+            A = rng.integers(0, 256, (M, K), dtype=np.uint8)
+            B = rng.integers(0, 256, (N, K), dtype=np.uint8)
+
+            def cpu_gemm(a, b, out_view, sa, sb):
+                out_view.copy_(torch.from_numpy(oracle.quire_gemm(a.numpy(), b.numpy(), 8, nthreads=1).view(np.int32)).view(torch.uint32))
+
+            g = ShardedQuireGemm(M, N, torch.device("cpu"), gemm_fn=cpu_gemm)
+            n0, n1 = g.plan.bounds
+            out = g(torch.from_numpy(A), torch.from_numpy(B[n0:n1].copy()))
+            if rank == 0:
+                ref = oracle.quire_gemm(A, B, 8, nthreads=1)
+                q.put(((M, N, K), bool(np.array_equal(out.numpy(), ref))))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_sharded_gemm_gloo(world):
+    cases = [(5, 8, 33, 1), (7, 7, 64, 2), (3, 1, 16, 3), (9, 13, 100, 4)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cases, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [q.get(timeout=5) for _ in cases]
+    assert all(ok for _, ok in res), res
+
+
+def test_shard_bounds():
+    from bposit_b200.dist import shard_bounds
+    for N in (0, 1, 7, 8, 4096):
+        for world in (1, 2, 3, 4, 8):
+            spans = [shard_bounds(N, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == N
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert all(0 <= n0 <= n1 <= N for n0, n1 in spans)
