@@ -448,14 +448,23 @@ __device__ __forceinline__ int block_min(int v, int *red) {
 
 __device__ __forceinline__ int block_max(int v, int *red) { return -block_min(-v, red); }
 
+// bp8 decode table entry: lsb exponent, binade and signed mantissa packed in
+// 10 + 10 + 12 bits (bp8: |lsb|, |binade| <= 24, |mantissa| <= 15).
+__device__ __forceinline__ uint32_t dec_pack(int lsb, int hb, int m) {
+  return (uint32_t)(lsb + 512) | ((uint32_t)(hb + 512) << 10) | ((uint32_t)(m + 2048) << 20);
+}
+__device__ __forceinline__ int dec_lsb(uint32_t t) { return (int)(t & 1023u) - 512; }
+__device__ __forceinline__ int dec_hb(uint32_t t) { return (int)((t >> 10) & 1023u) - 512; }
+__device__ __forceinline__ int dec_m(uint32_t t) { return (int)(t >> 20) - 2048; }
+
 // Decoded element: lsb exponent (group scale folded in) and signed mantissa.
 template <int FMT>
-__device__ __forceinline__ ElemME prep_decode(uint32_t c, const int4 *s_dec) {
+__device__ __forceinline__ ElemME prep_decode(uint32_t c, const uint32_t *s_dec) {
   ElemME x;
   if (FMT == 8) {
-    int4 t = s_dec[c];
-    x.m = t.z;
-    x.e = t.x;
+    uint32_t t = s_dec[c];
+    x.m = dec_m(t);
+    x.e = dec_lsb(t);
   } else {
     posit_to_me<16, 3>(c, x.m, x.e);
   }
@@ -477,7 +486,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
   constexpr int EPT = FMT == 8 ? 16 : 8;   // elements per 16-byte load
   constexpr bool LUT_DIGITS = FMT == 8 && S <= 4;
   __shared__ int s_tail[TAILCAP];
-  __shared__ int4 s_dec[FMT == 8 ? 256 : 1];     // {lsb, binade, mantissa, 0}
+  __shared__ uint32_t s_dec[FMT == 8 ? 256 : 1];  // packed lsb | binade | mantissa (dec_* below)
   __shared__ uint32_t s_dig[FMT == 8 ? 256 : 1];
   __shared__ int red[8];
   __shared__ int s_nt, s_off, s_slot;
@@ -486,7 +495,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
       int m, e;
       posit_to_me<8, 2>((uint32_t)c, m, e);
       int hb = m ? e + 31 - __clz(m < 0 ? -m : m) : 0;
-      s_dec[c] = make_int4(e, hb, m, 0);
+      s_dec[c] = dec_pack(e, hb, m);
     }
     __syncthreads();
   }
@@ -508,10 +517,10 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
       for (int q = 0; q < EPT; ++q) {
         int l, h;
         if (FMT == 8) {
-          int4 t = s_dec[c[q]];
-          if (!t.z) continue;
-          l = t.x;
-          h = t.y;
+          uint32_t t = s_dec[c[q]];
+          if (!dec_m(t)) continue;
+          l = dec_lsb(t);
+          h = dec_hb(t);
         } else {
           Dec d = decode_posit<16, 3>(c[q]);
           if (d.kind != 0) continue;
@@ -541,13 +550,13 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
     const bool lut = LUT_DIGITS && sc == nullptr;
     if (lut) {
       for (int cc = threadIdx.x; cc < 256; cc += blockDim.x) {
-        int4 t = s_dec[cc];
+        uint32_t t = s_dec[cc];
         uint32_t v = 0u;
-        if (t.z) {
-          if (t.x < L) {
+        if (dec_m(t)) {
+          if (dec_lsb(t) < L) {
             v = 0x80000000u;
           } else {
-            int x = t.z * (1 << (t.x - L));
+            int x = dec_m(t) * (1 << (dec_lsb(t) - L));
 #pragma unroll
             for (int s = 0; s < S - 1; ++s) {
               int dg = ((x + 64) & 127) - 64;
@@ -742,13 +751,39 @@ struct TcLayout {
 // the cap are finished by the fixup kernel instead.
 constexpr size_t kCorrBudget = size_t(512) << 20;
 
+// K blocks per CTA task: at most one exact int32 chunk, and split further
+// when that fills the machine's waves better (cost model: waves x K blocks per
+// task, plus the partial-sum traffic of the split).
+void choose_split(TcLayout &L, int M, int N) {
+  const int exact = (L.S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
+  const int bn = L.S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
+  const long long tiles = (long long)((N + bn - 1) / bn) * ((M + BM - 1) / BM);
+  const int sms = sm_count();
+  const double t_kb = (L.S == 3 ? 18 * 48 : 32 * 48) / 1.9e3;   // microseconds per K block
+  const int min_chunks = (L.nkb + exact - 1) / exact;
+  double best = 1e300;
+  L.kbc = exact;
+  for (int s = min_chunks; s <= min_chunks * 8; ++s) {
+    int kb = (L.nkb + s - 1) / s;
+    if (s > min_chunks && kb < 16) break;
+    int se = (L.nkb + kb - 1) / kb;
+    long long waves = (tiles * se + sms - 1) / sms;
+    double t = (double)waves * (kb * t_kb + 4.0);
+    if (se > 1) t += (double)se * M * N * 32.0 / 5e6 + 5.0;
+    if (t < best * 0.98) {
+      best = t;
+      L.kbc = kb;
+    }
+  }
+  L.nchunks = (L.nkb + L.kbc - 1) / L.kbc;
+}
+
 TcLayout tc_layout(int fmt, int M, int N, int K) {
   TcLayout L{};
   L.S = fmt == 8 ? 3 : 4;
   L.Kp = (K + 127) / 128 * 128;
   L.nkb = L.Kp / BK;
-  L.kbc = (L.S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
-  L.nchunks = (L.nkb + L.kbc - 1) / L.kbc;
+  choose_split(L, M, N);
   L.capA = (int)std::min<size_t>((size_t)M, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(N, 1))));
   L.capB = (int)std::min<size_t>((size_t)N, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(M, 1))));
   L.pool = std::max(65536, 8 * std::max(M, N));
@@ -816,7 +851,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   const int sms = sm_count();
   auto prep = [&](const void *codes, int rows, const int32_t *sc, int4 *st, int8_t *planes, int *Lr, int *slot,
                   int4 *seg, int *tails, int cap, TcCounters *c) {
-    int g = std::min(rows, sms * 4);
+    int g = std::min(rows, sms * 8);
     if (a.fmt == 8)
       k_tc_prep<8, 3><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, seg, tails,
                                         L.pool, cap, c);
