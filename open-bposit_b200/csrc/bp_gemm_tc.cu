@@ -503,8 +503,12 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
   const bool vec = (K % EPT) == 0 && (((uintptr_t)codes) & 15u) == 0;
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const size_t rb = (size_t)r * K;
-    // pass 1: statistics
+    // pass 1: statistics.  A posit's lsb exponent and binade are both
+    // non-decreasing in its magnitude, so the row's min lsb and max binade are
+    // those of its smallest and largest nonzero code magnitude (per group
+    // chunk when group scales are present).
     int lo = 0x3FFFFFFF, hi = -0x3FFFFFFF, nz = 0;
+    const bool chunk_groups = sc != nullptr && (group % EPT) == 0;
     for (int k0 = threadIdx.x * EPT; k0 < K; k0 += blockDim.x * EPT) {
       uint32_t c[EPT];
       if (vec) {
@@ -513,24 +517,51 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
 #pragma unroll
         for (int q = 0; q < EPT; ++q) c[q] = k0 + q < K ? load_code<FMT>(codes, rb + k0 + q) : 0u;
       }
+      if (sc == nullptr || chunk_groups) {
+        uint32_t mn = 0xFFFFFFFFu, mx = 0u;
 #pragma unroll
-      for (int q = 0; q < EPT; ++q) {
-        int l, h;
-        if (FMT == 8) {
-          uint32_t t = s_dec[c[q]];
-          if (!dec_m(t)) continue;
-          l = dec_lsb(t);
-          h = dec_hb(t);
-        } else {
-          Dec d = decode_posit<16, 3>(c[q]);
-          if (d.kind != 0) continue;
-          l = d.scale - d.fw;
-          h = d.scale;
+        for (int q = 0; q < EPT; ++q) {
+          const uint32_t sb = FMT == 8 ? 0x80u : 0x8000u;
+          uint32_t mag = (c[q] & sb) ? (2u * sb - c[q]) : c[q];
+          bool v = (c[q] & (sb - 1u)) != 0u;          // not zero, not NaR
+          mn = v ? min(mn, mag) : mn;
+          mx = v ? max(mx, mag) : mx;
         }
-        int sc_ = sc ? sc[(size_t)r * G + (k0 + q) / group] : 0;
-        lo = min(lo, l + sc_);
-        hi = max(hi, h + sc_);
-        nz = 1;
+        if (mx) {
+          int sc_ = sc ? sc[(size_t)r * G + k0 / group] : 0;
+          int l, h;
+          if (FMT == 8) {
+            l = dec_lsb(s_dec[mn]);
+            h = dec_hb(s_dec[mx]);
+          } else {
+            Dec d0 = decode_posit<16, 3>(mn), d1 = decode_posit<16, 3>(mx);
+            l = d0.scale - d0.fw;
+            h = d1.scale;
+          }
+          lo = min(lo, l + sc_);
+          hi = max(hi, h + sc_);
+          nz = 1;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          int l, h;
+          if (FMT == 8) {
+            uint32_t t = s_dec[c[q]];
+            if (!dec_m(t)) continue;
+            l = dec_lsb(t);
+            h = dec_hb(t);
+          } else {
+            Dec d = decode_posit<16, 3>(c[q]);
+            if (d.kind != 0) continue;
+            l = d.scale - d.fw;
+            h = d.scale;
+          }
+          int sc_ = sc[(size_t)r * G + (k0 + q) / group];
+          lo = min(lo, l + sc_);
+          hi = max(hi, h + sc_);
+          nz = 1;
+        }
       }
     }
     lo = block_min(lo, red);
