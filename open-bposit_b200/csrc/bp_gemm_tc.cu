@@ -603,54 +603,95 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
     __syncthreads();
     // pass 2: digit planes and tail list
     int8_t *row = planes + (size_t)r * Kp;
-    for (int k0 = threadIdx.x * EPT; k0 < Kp; k0 += blockDim.x * EPT) {
-      uint32_t c[EPT];
-      if (vec && k0 < K) {
-        load_codes16<FMT>(codes, rb + k0, c);
-      } else {
+    if (lut && vec) {
+      // unscaled bp8: every code's S digits come packed in one table word
+      // (bit 31 = tail); plane words are assembled with byte permutes
+      for (int k0 = threadIdx.x * 16; k0 < Kp; k0 += blockDim.x * 16) {
+        uint32_t v[16];
+        uint32_t any = 0u;
+        if (k0 < K) {
+          uint4 cw = *(const uint4 *)((const uint8_t *)codes + rb + k0);
+          uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-        for (int q = 0; q < EPT; ++q) c[q] = k0 + q < K ? load_code<FMT>(codes, rb + k0 + q) : 0u;
+          for (int q = 0; q < 16; ++q) {
+            v[q] = s_dig[(ws[q >> 2] >> (8 * (q & 3))) & 0xFFu];
+            any |= v[q];
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 16; ++q) v[q] = 0u;
+        }
+        if (any & 0x80000000u) {
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (v[q] & 0x80000000u) {
+              int pos = atomicAdd(&s_nt, 1);
+              if (pos < TAILCAP) s_tail[pos] = k0 + q;
+            }
+        }
+#pragma unroll
+        for (int sd = 0; sd < S; ++sd) {
+          const uint32_t sel = (uint32_t)sd | ((uint32_t)(4 + sd) << 4);
+          uint32_t wd[4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint32_t lo2 = __byte_perm(v[4 * g], v[4 * g + 1], sel);
+            uint32_t hi2 = __byte_perm(v[4 * g + 2], v[4 * g + 3], sel);
+            wd[g] = __byte_perm(lo2, hi2, 0x5410);
+          }
+          *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+        }
       }
-      uint32_t w[S][EPT / 4];
+    } else {
+      for (int k0 = threadIdx.x * EPT; k0 < Kp; k0 += blockDim.x * EPT) {
+        uint32_t c[EPT];
+        if (vec && k0 < K) {
+          load_codes16<FMT>(codes, rb + k0, c);
+        } else {
 #pragma unroll
-      for (int s = 0; s < S; ++s)
+          for (int q = 0; q < EPT; ++q) c[q] = k0 + q < K ? load_code<FMT>(codes, rb + k0 + q) : 0u;
+        }
+        uint32_t w[S][EPT / 4];
 #pragma unroll
-        for (int q = 0; q < EPT / 4; ++q) w[s][q] = 0u;
+        for (int sd = 0; sd < S; ++sd)
 #pragma unroll
-      for (int q = 0; q < EPT; ++q) {
-        const int k = k0 + q;
-        if (lut) {
-          uint32_t v = s_dig[c[q]];
-          if (v & 0x80000000u) {
+          for (int q = 0; q < EPT / 4; ++q) w[sd][q] = 0u;
+#pragma unroll
+        for (int q = 0; q < EPT; ++q) {
+          const int k = k0 + q;
+          if (lut) {
+            uint32_t v = s_dig[c[q]];
+            if (v & 0x80000000u) {
+              int pos = atomicAdd(&s_nt, 1);
+              if (pos < TAILCAP) s_tail[pos] = k;
+              continue;
+            }
+#pragma unroll
+            for (int sd = 0; sd < S; ++sd) w[sd][q >> 2] |= ((v >> (8 * sd)) & 0xFFu) << (8 * (q & 3));
+            continue;
+          }
+          ElemME x = prep_decode<FMT>(c[q], s_dec);
+          if (!x.m || k >= K) continue;
+          if (sc) x.e += sc[(size_t)r * G + k / group];
+          if (x.e < L) {
             int pos = atomicAdd(&s_nt, 1);
             if (pos < TAILCAP) s_tail[pos] = k;
             continue;
           }
+          int t = x.m * (1 << (x.e - L));
 #pragma unroll
-          for (int s = 0; s < S; ++s) w[s][q >> 2] |= ((v >> (8 * s)) & 0xFFu) << (8 * (q & 3));
-          continue;
+          for (int sd = 0; sd < S - 1; ++sd) {
+            int dg = ((t + 64) & 127) - 64;
+            w[sd][q >> 2] |= ((uint32_t)(uint8_t)dg) << (8 * (q & 3));
+            t = (t - dg) >> 7;
+          }
+          w[S - 1][q >> 2] |= ((uint32_t)(uint8_t)t) << (8 * (q & 3));
         }
-        ElemME x = prep_decode<FMT>(c[q], s_dec);
-        if (!x.m || k >= K) continue;
-        if (sc) x.e += sc[(size_t)r * G + k / group];
-        if (x.e < L) {
-          int pos = atomicAdd(&s_nt, 1);
-          if (pos < TAILCAP) s_tail[pos] = k;
-          continue;
-        }
-        int t = x.m * (1 << (x.e - L));
 #pragma unroll
-        for (int s = 0; s < S - 1; ++s) {
-          int dg = ((t + 64) & 127) - 64;
-          w[s][q >> 2] |= ((uint32_t)(uint8_t)dg) << (8 * (q & 3));
-          t = (t - dg) >> 7;
+        for (int sd = 0; sd < S; ++sd) {
+          if (EPT == 16) *(uint4 *)(row + sd * plane + k0) = make_uint4(w[sd][0], w[sd][1], w[sd][2], w[sd][3]);
+          else *(uint2 *)(row + sd * plane + k0) = make_uint2(w[sd][0], w[sd][1]);
         }
-        w[S - 1][q >> 2] |= ((uint32_t)(uint8_t)t) << (8 * (q & 3));
-      }
-#pragma unroll
-      for (int s = 0; s < S; ++s) {
-        if (EPT == 16) *(uint4 *)(row + s * plane + k0) = make_uint4(w[s][0], w[s][1], w[s][2], w[s][3]);
-        else *(uint2 *)(row + s * plane + k0) = make_uint2(w[s][0], w[s][1]);
       }
     }
     __syncthreads();
