@@ -4,7 +4,8 @@
 Headline (one JSON line on rank 0): bit-exact bp8 quire-GEMM throughput in
 TOPS (2*M*N*K / time) on the large bp8 GEMM M=4096, N=4096, K=65536 with
 operands N(0,1) * 2^U{-8..8} per row (seeded, synthetic), the output dimension
-N sharded over the ranks and the bposit32 result all-gathered over NCCL.
+N sharded over the ranks and the bposit32 result all-gathered by the GEMM
+epilogue itself (NVLink peer stores; --gather nccl for an NCCL all-gather).
 The same line carries the encode/decode sweep (2^28 fp32 per rank) in GB/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -31,7 +32,7 @@ for _p in (REPO, os.path.join(REPO, "open-bposit_b200")):
 M_, N_, K_ = 4096, 4096, 65536
 METRIC = "bit-exact bp8 W8A8 quire-GEMM TOPS (bp8 4096x4096x65536, N-sharded)"
 WORKLOAD = ("bp8 exact quire GEMM M=4096 N=4096 K=65536, operands N(0,1)*2^U{-8..8} per row, "
-            "RTN-quantized; one bposit32 round per output; N sharded over ranks + NCCL all-gather")
+            "RTN-quantized; one bposit32 round per output; N sharded over ranks, result all-gathered")
 
 
 def load_peaks():
@@ -265,7 +266,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from bposit_b200 import _lib, ops
-    from bposit_b200.dist import ShardedQuireGemm
+    from bposit_b200.dist import FusedShardedQuireGemm, ShardedQuireGemm, assemble
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -280,11 +281,37 @@ def run_ours(args):
     gen = torch.Generator(device=device).manual_seed(0)
     A = make_operand(ops, torch, M_, K_, gen, device)
     B = make_operand(ops, torch, N_, K_, gen, device)
-    g = ShardedQuireGemm(M_, N_, device, algo=args.algo)
+    fused = args.gather == "fused"
+    g = (FusedShardedQuireGemm if fused else ShardedQuireGemm)(M_, N_, device, algo=args.algo)
     n0, n1 = g.plan.bounds
     Bs = B[n0:n1].contiguous()
     del B
     torch.cuda.empty_cache()
+    ws = torch.empty(max(256, ops.gemm_workspace_size(8, M_, n1 - n0, K_, args.algo)), dtype=torch.uint8,
+                     device=device)
+
+    def shard_step(A_, B_, ev=None):
+        """One N-sharded GEMM + all-gather; `ev` brackets the GEMM launches."""
+        if fused and world > 1:
+            dist.all_reduce(g.flag)
+        if ev is not None:
+            ev[0].record(stream)
+        if fused:
+            ops.quire_gemm_multi(A_, B_, g.result[:, n0:n1], g.peer_ptrs, n0, fmt=8, algo=args.algo,
+                                 workspace=ws)
+        else:
+            ops.quire_gemm(A_, B_, 8, out=g.local[:, :n1 - n0] if world > 1 else g.result, algo=args.algo,
+                           workspace=ws)
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            if fused:
+                dist.all_reduce(g.flag)
+            else:
+                dist.all_gather_into_tensor(g.gathered.view(-1).view(torch.int32),
+                                            g.local.view(-1).view(torch.int32))
+                assemble(g.gathered, g.plan, g.result)
+        return g.result
 
     def sync_all():
         torch.cuda.synchronize()
@@ -296,18 +323,7 @@ def run_ours(args):
            for _ in range(args.steps)]
 
     def gemm_only(i=None):
-        if i is not None:
-            kev[i][0].record(stream)
-        out_view = g.local[:, :n1 - n0] if world > 1 else g.result
-        g.gemm_fn(A, Bs, out_view, None, None)
-        if i is not None:
-            kev[i][1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(g.gathered.view(-1).view(torch.int32),
-                                        g.local.view(-1).view(torch.int32))
-            from bposit_b200.dist import assemble
-            assemble(g.gathered, g.plan, g.result)
-        return g.result
+        return shard_step(A, Bs, None if i is None else kev[i])
 
     for _ in range(args.warmup):
         gemm_only()
@@ -348,12 +364,7 @@ def run_ours(args):
     def e2e_step():
         dA.copy_(hA, non_blocking=True)
         dB.copy_(hB, non_blocking=True)
-        out_view = g.local[:, :n1 - n0] if world > 1 else g.result
-        g.gemm_fn(dA, dB, out_view, None, None)
-        if world > 1:
-            dist.all_gather_into_tensor(g.gathered.view(-1).view(torch.int32), g.local.view(-1).view(torch.int32))
-            from bposit_b200.dist import assemble
-            assemble(g.gathered, g.plan, g.result)
+        shard_step(dA, dB)
         hOut.copy_(g.result, non_blocking=True)
 
     e2e_steps = max(1, min(args.steps, 5))
@@ -400,7 +411,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": M_, "N": N_, "K": K_, "fmt": "bp8",
-                       "parallelism": f"N-shard x{world} + NCCL all-gather",
+                       "parallelism": (f"N-shard x{world} + " + ("all-gather fused into the GEMM epilogue "
+                                       "(NVLink peer stores)" if fused else "NCCL all-gather")),
                        "l2": "inputs 512 MiB > L2 (no flush needed)", "algo": args.algo},
             "roofline": {"bound": "tensor", "achieved": round(k_tops, 3), "peak": round(int8_peak, 1),
                          "unit": "TOPS", "frac": round(k_tops / int8_peak, 5), "traffic": traffic,
@@ -419,6 +431,8 @@ def run_ours(args):
             "encode_decode": codec,
         }
         print(json.dumps(line), flush=True)
+    if fused:
+        g.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -433,6 +447,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                    help="all-gather of the N-shards: in the GEMM epilogue (peer stores) or NCCL")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

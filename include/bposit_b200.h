@@ -115,6 +115,42 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
                   uint32_t *out_bp32, int64_t ldo, uint32_t *out_quire, int quire_limbs,
                   int algo, void *workspace, size_t workspace_bytes, void *stream);
 
+/* bp_quire_gemm whose bposit32 results are also stored, by the GEMM epilogue
+ * itself, into n_peer further [M, ldo] matrices at column peer_col0 -- on a
+ * multi-GPU node, the full result matrices of the other ranks, reached over
+ * NVLink (mapped with bp_ipc_open; peer access from bp_enable_peer_access).  One call both
+ * computes this rank's N-shard and all-gathers it: after every rank's call has
+ * completed (e.g. behind a collective barrier), every rank holds the whole
+ * [M, N_total] bposit32 matrix.  out_bp32 points at this rank's block
+ * (its full matrix + peer_col0).  n_peer <= 8; no raw-quire output.
+ * Replaces the reference's matmul_quire (reference/bposit_fast.py:136-176)
+ * for an N-sharded GEMM; the fused all-gather has no reference counterpart. */
+int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int K,
+                        const int32_t *sa, const int32_t *sb, int group,
+                        uint32_t *out_bp32, int64_t ldo, uint32_t *const *peer_outs, int n_peer,
+                        int64_t peer_col0, int algo, void *workspace, size_t workspace_bytes,
+                        void *stream);
+
+/* Enable direct access from the current device to peer_device's memory
+ * (idempotent).  Multi-GPU plumbing; no reference counterpart. */
+int bp_enable_peer_access(int peer_device);
+
+/* Device memory shared between the processes of one node (CUDA IPC), for the
+ * result buffers that bp_quire_gemm_multi writes across GPUs.
+ *   bp_ipc_alloc  -- zeroed allocation on the current device plus its
+ *                    BP_IPC_HANDLE_BYTES-byte handle (pass it to the peers);
+ *   bp_ipc_open   -- map a peer's handle into the current device's context
+ *                    (peer access enabled as needed); *ptr is a device address
+ *                    the current device's kernels may load from and store to;
+ *   bp_ipc_close  -- unmap what bp_ipc_open returned;
+ *   bp_ipc_free   -- free what bp_ipc_alloc returned (after every peer closed).
+ * Multi-GPU plumbing; no reference counterpart. */
+#define BP_IPC_HANDLE_BYTES 64
+int bp_ipc_alloc(size_t bytes, void **ptr, void *handle_out);
+int bp_ipc_free(void *ptr);
+int bp_ipc_open(const void *handle, void **ptr);
+int bp_ipc_close(void *ptr);
+
 /* Workspace bytes bp_quire_gemm needs for this shape and algo. */
 size_t bp_quire_gemm_workspace_size(int fmt, int M, int N, int K, int algo);
 

@@ -1,11 +1,19 @@
 """Multi-GPU quire GEMM: the output dimension N is sharded across ranks (one
-process per GPU) and the bposit32 result is all-gathered over NCCL.
+process per GPU) and every rank ends with the whole bposit32 result.
 
 Each rank holds all of A[M,K] and its row block B[n0:n1, K] of B[N,K] and
 computes out[:, n0:n1] exactly; outputs are column-disjoint and no partial sum
 ever crosses a rank, so the result is bit-identical for every rank count.
-The gather is one all_gather_into_tensor of the [M, N/p] uint32 shards into a
-[p, M, N/p] buffer followed by a local transpose into [M, N].
+
+Two ways to all-gather the blocks:
+  ShardedQuireGemm       -- one NCCL all_gather_into_tensor of the [M, N/p]
+                            uint32 shards into [p, M, N/p], then a local
+                            transpose into [M, N];
+  FusedShardedQuireGemm  -- the GEMM epilogue stores every finished bposit32
+                            straight into all ranks' [M, N] result buffers over
+                            NVLink (peer stores into CUDA-IPC-shared memory);
+                            two one-word NCCL all-reduces order the call
+                            against the ranks' previous and next use of them.
 """
 from __future__ import annotations
 
@@ -94,3 +102,81 @@ class ShardedQuireGemm:
         dist.all_gather_into_tensor(self.gathered.view(-1).view(torch.int32),
                                     self.local.view(-1).view(torch.int32), group=self.group)
         return assemble(self.gathered, self.plan, self.result)
+
+
+class FusedShardedQuireGemm:
+    """N-sharded quire GEMM with the all-gather fused into the GEMM epilogue.
+
+    Every rank allocates one [M, N] uint32 result in CUDA-IPC-shareable memory
+    and maps every peer's result into its own device context; each rank's
+    GEMM writes its column block [n0, n1) into its own result and, over
+    NVLink, into every peer's.  A call is
+        all_reduce(1 word)   -- no rank still reads its previous result
+        GEMM + peer stores   -- bp_quire_gemm_multi
+        all_reduce(1 word)   -- every peer's stores into this result are done
+    all on the current stream.  The returned tensor stays valid until the
+    next call.  Needs one node with peer access between all its GPUs and at
+    most 9 ranks; call close() on every rank before destroying the group.
+    """
+
+    def __init__(self, M: int, N: int, device, group=None, fmt: int = 8, algo: int = 0,
+                 group_size: int = 128):
+        from . import ops
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world - 1 > 8:
+            raise ValueError("FusedShardedQuireGemm supports at most 9 ranks")
+        self.plan = ShardPlan(M, N, self.world, self.rank)
+        self.fmt, self.algo, self.group_size = fmt, algo, group_size
+        dev = torch.device(device)
+        self.device = dev
+        self.result, handle, self._own = ops.ipc_alloc((M, N), dev)
+        self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.peer_ptrs: list[int] = []
+        if self.world > 1:
+            objs = [None] * self.world
+            dist.all_gather_object(objs, (dev.index, handle), group=group)
+            with torch.cuda.device(dev):
+                for r, (pdev, h) in enumerate(objs):
+                    if r != self.rank:
+                        ops.enable_peer_access(pdev)
+                        self.peer_ptrs.append(ops.ipc_open(h))
+        self.workspace = None
+
+    def __call__(self, A: torch.Tensor, B_shard: torch.Tensor, sa=None, sb_shard=None) -> torch.Tensor:
+        from . import ops
+        if self.result is None:
+            raise RuntimeError("FusedShardedQuireGemm is closed")
+        n0, n1 = self.plan.bounds
+        if B_shard.shape[0] != n1 - n0:
+            raise ValueError(f"B shard has {B_shard.shape[0]} rows, rank {self.rank} owns {n1 - n0}")
+        if self.world > 1:
+            dist.all_reduce(self.flag, group=self.group)
+        if n1 > n0:
+            if self.workspace is None:
+                need = ops.gemm_workspace_size(self.fmt, A.shape[0], n1 - n0, A.shape[1], self.algo)
+                self.workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=A.device)
+            ops.quire_gemm_multi(A, B_shard, self.result[:, n0:n1], self.peer_ptrs, n0, fmt=self.fmt, sa=sa,
+                                 sb=sb_shard, group=self.group_size, algo=self.algo, workspace=self.workspace)
+        if self.world > 1:
+            dist.all_reduce(self.flag, group=self.group)
+        return self.result
+
+    def close(self) -> None:
+        """Unmap the peers' results and free this rank's once no rank writes
+        into them any more.  Collective: every rank calls it."""
+        from . import ops
+        if self.result is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self.peer_ptrs:
+                ops.ipc_close(p)
+        self.peer_ptrs = []
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.result = None
+        ops.ipc_free(self._own)

@@ -137,6 +137,82 @@ def quire_gemm(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, gro
     return out, q
 
 
+def quire_gemm_multi(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_ptrs, peer_col0: int,
+                     fmt=None, sa=None, sb=None, group: int = 128, algo: int = 0, workspace=None):
+    """quire_gemm whose bp32 results are also stored into every matrix in
+    `peer_ptrs` (device addresses of [M, ldo] uint32 matrices, normally other
+    GPUs' result buffers) at column `peer_col0`, by the GEMM epilogue itself.
+    `out` is this rank's [M, N] column block (row stride ldo)."""
+    f = fmt_bits(fmt) if fmt is not None else (8 if A.dtype == torch.uint8 else 16)
+    a = _dev(A, "A", _CODE_DTYPE[f])
+    b = _dev(B, "B", _CODE_DTYPE[f])
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("quire_gemm_multi expects A[M,K] and B[N,K]")
+    M, K = a.shape
+    N = b.shape[0]
+    if out.dtype != torch.uint32 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out must be a [M, N] uint32 view with unit column stride")
+    sa_ = None if sa is None else _dev(sa, "sa", torch.int32)
+    sb_ = None if sb is None else _dev(sb, "sb", torch.int32)
+    ptrs = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[int(x) for x in peer_ptrs])
+    need = gemm_workspace_size(f, M, N, K, algo)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.device)
+    _lib.check(_lib.lib().bp_quire_gemm_multi(f, _p(a), _p(b), M, N, K, _p(sa_), _p(sb_), group, _p(out),
+                                              out.stride(0), ptrs, len(peer_ptrs), peer_col0, algo,
+                                              _p(workspace), workspace.numel(), _stream()))
+    return out
+
+
+def enable_peer_access(peer_device: int) -> None:
+    """Let the current device read and write `peer_device`'s memory directly."""
+    _lib.check(_lib.lib().bp_enable_peer_access(int(peer_device)))
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class _DeviceBuffer:
+    """__cuda_array_interface__ view of memory the library allocated (no ownership)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 2, "strides": None}
+
+
+def ipc_alloc(shape, device) -> tuple[torch.Tensor, bytes, int]:
+    """Zeroed uint32 tensor in memory that other processes can map (CUDA IPC):
+    (tensor, handle, device address).  The tensor does not own the memory;
+    release it with ipc_free(address) once no process uses it."""
+    numel = 1
+    for d in shape:
+        numel *= int(d)
+    with torch.cuda.device(device):
+        ptr = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _lib.check(_lib.lib().bp_ipc_alloc(max(4, numel * 4), ctypes.byref(ptr), handle))
+        t = torch.as_tensor(_DeviceBuffer(ptr.value, shape, "<i4"), device=device).view(torch.uint32)
+    return t, handle.raw, int(ptr.value)
+
+
+def ipc_free(ptr: int) -> None:
+    _lib.check(_lib.lib().bp_ipc_free(ctypes.c_void_p(ptr)))
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's ipc_alloc memory into the current device's
+    context; returns its device address here."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("bad IPC handle")
+    ptr = ctypes.c_void_p()
+    _lib.check(_lib.lib().bp_ipc_open(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _lib.check(_lib.lib().bp_ipc_close(ctypes.c_void_p(ptr)))
+
+
 def bp32_to_f64(codes: torch.Tensor, row_exp=None, col_exp=None) -> torch.Tensor:
     """[M, N] bp32 codes -> float64 values * 2^(row_exp[m] + col_exp[n])."""
     c = _dev(codes, "codes", torch.uint32)

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdint.h>
+#include <string.h>
 #include <stdio.h>
 
 #include <atomic>
@@ -184,6 +185,122 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K, co
   cudaError_t f = cudaFreeAsync(ws, s);
   if (rc == kOk && f != cudaSuccess) rc = set_error(kECuda, "bp_quire_gemm: workspace free: %s", cudaGetErrorString(f));
   return rc;
+}
+
+int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
+                        const int32_t *sb, int group, uint32_t *out_bp32, int64_t ldo,
+                        uint32_t *const *peer_outs, int n_peer, int64_t peer_col0, int algo, void *workspace,
+                        size_t workspace_bytes, void *stream) {
+  g_err[0] = 0;
+  if (n_peer < 0 || n_peer > kMaxExtraOut)
+    return set_error(kEInval, "bp_quire_gemm_multi: n_peer must be in [0, %d]", kMaxExtraOut);
+  if (n_peer && (!peer_outs || peer_col0 < 0 || peer_col0 + N > ldo))
+    return set_error(kEInval, "bp_quire_gemm_multi: bad peer outputs");
+  for (int e = 0; e < n_peer; ++e)
+    if (!peer_outs[e]) return set_error(kEInval, "bp_quire_gemm_multi: null peer output %d", e);
+  if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_multi: fmt must be 8 or 16 (got %d)", fmt);
+  if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_multi: negative size");
+  if (algo < 0 || algo > 2) return set_error(kEInval, "bp_quire_gemm_multi: algo must be 0, 1 or 2");
+  if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_multi: group must be > 0 with scales");
+  if (ldo < N) return set_error(kEInval, "bp_quire_gemm_multi: ldo (%lld) < N (%d)", (long long)ldo, N);
+  if (M == 0 || N == 0) return kOk;
+  if (!out_bp32 || (K > 0 && (!A || !B))) return set_error(kEInval, "bp_quire_gemm_multi: null pointer");
+  if (workspace && ((uintptr_t)workspace & 255u)) return set_error(kEAlign, "bp_quire_gemm_multi: workspace not 256-byte aligned");
+  TRY(check_device());
+  GemmArgs a{};
+  a.fmt = fmt; a.A = A; a.B = B; a.M = M; a.N = N; a.K = K;
+  a.sa = sa; a.sb = sb; a.group = group > 0 ? group : 1;
+  a.G = group > 0 ? (K + group - 1) / group : 1;
+  a.out = out_bp32; a.ldo = ldo; a.quire = nullptr; a.nlimbs = 0;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool tc = gemm_uses_tc(a, algo);
+  if (tc) {
+    a.n_extra = n_peer; a.extra_col0 = peer_col0;
+    for (int e = 0; e < n_peer; ++e) a.extra_out[e] = peer_outs[e];
+  }
+  size_t need = gemm_workspace_size(fmt, M, N, K, algo);
+  void *ws = workspace;
+  if (ws && workspace_bytes < need)
+    return set_error(kEWorkspace, "bp_quire_gemm_multi: workspace %zu bytes < %zu needed", workspace_bytes, need);
+  if (!ws) {
+    cudaError_t e = cudaMallocAsync(&ws, need, s);
+    if (e != cudaSuccess) return set_error(kECuda, "bp_quire_gemm_multi: workspace allocation: %s", cudaGetErrorString(e));
+  }
+  int rc = launch_quire_gemm(a, algo, ws, need, s);
+  if (rc == kOk && !tc) {   // CUDA-core path: copy the finished block to each peer
+    for (int e = 0; e < n_peer && rc == kOk; ++e) {
+      cudaError_t ce = cudaMemcpy2DAsync(peer_outs[e] + peer_col0, (size_t)ldo * 4, out_bp32, (size_t)ldo * 4,
+                                         (size_t)N * 4, (size_t)M, cudaMemcpyDeviceToDevice, s);
+      if (ce != cudaSuccess) rc = set_error(kECuda, "bp_quire_gemm_multi: peer copy: %s", cudaGetErrorString(ce));
+    }
+  }
+  if (!workspace) cudaFreeAsync(ws, s);
+  return rc;
+}
+
+int bp_enable_peer_access(int peer_device) {
+  g_err[0] = 0;
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return set_error(kENoDev, "bp_enable_peer_access: no device");
+  if (peer_device == cur) return kOk;
+  int can = 0;
+  cudaError_t e = cudaDeviceCanAccessPeer(&can, cur, peer_device);
+  if (e != cudaSuccess) return set_error(kECuda, "bp_enable_peer_access: %s", cudaGetErrorString(e));
+  if (!can) return set_error(kENoDev, "bp_enable_peer_access: device %d cannot access device %d", cur, peer_device);
+  e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return kOk;
+  }
+  if (e != cudaSuccess) return set_error(kECuda, "bp_enable_peer_access: %s", cudaGetErrorString(e));
+  return kOk;
+}
+
+int bp_ipc_alloc(size_t bytes, void **ptr, void *handle_out) {
+  g_err[0] = 0;
+  if (!ptr || !handle_out || bytes == 0) return set_error(kEInval, "bp_ipc_alloc: bad arguments");
+  TRY(check_device());
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return set_error(kECuda, "bp_ipc_alloc: cudaMalloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_error(kECuda, "bp_ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == BP_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle_out, &h, sizeof(h));
+  *ptr = p;
+  return kOk;
+}
+
+int bp_ipc_free(void *ptr) {
+  g_err[0] = 0;
+  if (!ptr) return kOk;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? kOk : set_error(kECuda, "bp_ipc_free: %s", cudaGetErrorString(e));
+}
+
+int bp_ipc_open(const void *handle, void **ptr) {
+  g_err[0] = 0;
+  if (!handle || !ptr) return set_error(kEInval, "bp_ipc_open: null argument");
+  TRY(check_device());
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void *p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(kECuda, "bp_ipc_open: %s", cudaGetErrorString(e));
+  *ptr = p;
+  return kOk;
+}
+
+int bp_ipc_close(void *ptr) {
+  g_err[0] = 0;
+  if (!ptr) return kOk;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? kOk : set_error(kECuda, "bp_ipc_close: %s", cudaGetErrorString(e));
 }
 
 int bp_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *row_exp, const int32_t *col_exp,

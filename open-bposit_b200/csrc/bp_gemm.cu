@@ -74,6 +74,8 @@ static bool use_tc(const GemmArgs &a, int algo) {
   return (long long)a.M * a.N >= 128LL * 128 * 8 && a.K >= 64;
 }
 
+bool gemm_uses_tc(const GemmArgs &a, int algo) { return use_tc(a, algo); }
+
 size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo) {
   size_t ws = stats_bytes(M, N);
   if (algo != 1 && gemm_tc_supported(fmt, M, N, K)) ws += gemm_tc_workspace(fmt, M, N, K);

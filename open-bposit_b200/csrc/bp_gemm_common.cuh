@@ -58,13 +58,15 @@ __device__ __forceinline__ int fast_width(int4 ra, int4 rb, int K, int) {
 }
 
 // Writes one output from an exact 128-bit sum `acc` whose bit 0 sits at quire
-// bit `base` (units of 2^-96): the bp32 code and, optionally, `nlimbs` limbs of
-// the raw quire (two's complement, truncated to nlimbs*32 bits).
-__device__ __forceinline__ void write_fast_output(unsigned __int128 acc, int base, uint32_t *ob,
-                                                  uint32_t *oq, int nlimbs) {
+// bit `base` (units of 2^-96): the bp32 code (returned, and stored at `ob`
+// unless it is null) and, optionally, `nlimbs` limbs of the raw quire (two's
+// complement, truncated to nlimbs*32 bits).
+__device__ __forceinline__ uint32_t write_fast_output(unsigned __int128 acc, int base, uint32_t *ob,
+                                                      uint32_t *oq, int nlimbs) {
   bool neg = (uint64_t)(acc >> 127) != 0u;
   unsigned __int128 mag = neg ? (unsigned __int128)0 - acc : acc;
-  *ob = bp32_from_mag(neg, (uint64_t)(mag >> 64), (uint64_t)mag, base - 96);
+  const uint32_t code = bp32_from_mag(neg, (uint64_t)(mag >> 64), (uint64_t)mag, base - 96);
+  if (ob) *ob = code;
   if (oq) {
     for (int i = 0; i < nlimbs; ++i) {
       int o = 32 * i - base;
@@ -76,6 +78,7 @@ __device__ __forceinline__ void write_fast_output(unsigned __int128 acc, int bas
       oq[i] = v;
     }
   }
+  return code;
 }
 
 // ---- exact per-element form and the slow (512-bit, per-term truncating) path ----

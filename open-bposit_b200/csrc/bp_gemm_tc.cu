@@ -108,6 +108,9 @@ struct TcParams {
   uint32_t *quire;
   int nlimbs;
   ulonglong2 *partial;         // [chunk][M][N] when nchunks > 1
+  uint32_t *extra_out[kMaxExtraOut];   // peer result matrices (row stride ldo)
+  int n_extra;
+  int64_t extra_col0;
 };
 
 // ---------------------------------------------------------------- PTX ---
@@ -244,23 +247,34 @@ __device__ __forceinline__ bool tc_exact(int4 ra, int4 rb, int slot_i, int slot_
   return ra.x + rb.x + 96 >= 0 && fast_width(ra, rb, K, 0) <= 127 && slot_i != -2 && slot_j != -2;
 }
 
-// Final value of one output from its main-part sum Q (lsb base L_i + L_j).
-__device__ __forceinline__ void finish_output(const TcParams &p, int i, int j, unsigned __int128 Q, int4 ra,
-                                              int4 rb, int Li, int Lj, int slot_i, int slot_j) {
-  uint32_t *ob = p.out + (size_t)i * p.ldo + j;
+// Final bposit32 of output (i, j) from its main-part sum Q (lsb base L_i +
+// L_j); the raw quire limbs, when requested, are stored here too.  Returns
+// false when the output is left to k_tc_fixup.
+__device__ __forceinline__ bool finish_code(const TcParams &p, int i, int j, unsigned __int128 Q, int4 ra,
+                                            int4 rb, int Li, int Lj, int slot_i, int slot_j, uint32_t &code) {
   uint32_t *oq = p.quire ? p.quire + ((size_t)i * p.N + j) * p.nlimbs : nullptr;
   if (!(ra.z && rb.z)) {
-    *ob = 0u;
     if (oq)
       for (int t = 0; t < p.nlimbs; ++t) oq[t] = 0u;
-    return;
+    code = 0u;
+    return true;
   }
-  if (!tc_exact(ra, rb, slot_i, slot_j, p.K)) return;
+  if (!tc_exact(ra, rb, slot_i, slot_j, p.K)) return false;
   int sh = (Li - ra.x) + (Lj - rb.x);
   unsigned __int128 tot = Q << sh;
   if (slot_i >= 0) tot += u128(p.CA[(size_t)slot_i * p.N + j]);
   if (slot_j >= 0) tot += u128(p.CB[(size_t)slot_j * p.M + i]);
-  write_fast_output(tot, ra.x + rb.x + 96, ob, oq, p.nlimbs);
+  code = write_fast_output(tot, ra.x + rb.x + 96, nullptr, oq, p.nlimbs);
+  return true;
+}
+
+// finish_code stored to the output and to every extra output.
+__device__ __forceinline__ void finish_output(const TcParams &p, int i, int j, unsigned __int128 Q, int4 ra,
+                                              int4 rb, int Li, int Lj, int slot_i, int slot_j) {
+  uint32_t code;
+  if (!finish_code(p, i, j, Q, ra, rb, Li, Lj, slot_i, slot_j, code)) return;
+  p.out[(size_t)i * p.ldo + j] = code;
+  for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
 }
 
 // ----------------------------------------------------------------- GEMM ---
@@ -366,6 +380,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     slot_i = p.slotA[i];
   }
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  // Finished codes are staged per warp in the (now idle) pipeline buffers --
+  // [32 rows][BN + 1] words, conflict-free both ways -- with a per-row mask of
+  // the outputs this kernel owns, then stored row by row with consecutive
+  // lanes on consecutive columns, so each warp store is one 128-byte line
+  // (also across NVLink, for the extra outputs).
+  constexpr int MW = C::BN / 32;
+  static_assert(C::BN % 32 == 0, "BN must be a multiple of 32");
+  static_assert(THREADS * (C::BN + 1 + MW) * 4 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
+  uint32_t *stg = (uint32_t *)smem + warp * 32 * (C::BN + 1);
+  uint32_t *smask = (uint32_t *)smem + THREADS * (C::BN + 1) + warp * 32 * MW;
+  uint32_t vm[MW];
+#pragma unroll
+  for (int q = 0; q < MW; ++q) vm[q] = 0u;
 #pragma unroll 1
   for (int c0 = 0; c0 < C::BN; c0 += 16) {
     uint32_t v[C::D][16];
@@ -386,10 +413,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                                                                           (unsigned long long)(Q >> 64));
       } else {
         int2 ls = sLs[c0 + jj];
-        finish_output(p, i, j, Q, ra, sstat[c0 + jj], Li, ls.x, slot_i, ls.y);
+        uint32_t code;
+        if (finish_code(p, i, j, Q, ra, sstat[c0 + jj], Li, ls.x, slot_i, ls.y, code)) {
+          stg[lane * (C::BN + 1) + c0 + jj] = code;
+          vm[(c0 + jj) >> 5] |= 1u << ((c0 + jj) & 31);
+        }
       }
     }
   }
+  if (p.nchunks == 1) {
+#pragma unroll
+    for (int q = 0; q < MW; ++q) smask[lane * MW + q] = vm[q];
+    __syncwarp();
+#pragma unroll 1
+    for (int rr = 0; rr < 32; ++rr) {
+      const int ii = m0 + warp * 32 + rr;
+      if (ii >= p.M) break;
+#pragma unroll
+      for (int q = 0; q < MW; ++q) {
+        const int cc = q * 32 + lane;
+        if ((smask[rr * MW + q] >> lane) & 1u) {
+          const uint32_t code = stg[rr * (C::BN + 1) + cc];
+          p.out[(size_t)ii * p.ldo + n0 + cc] = code;
+          for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)ii * p.ldo + p.extra_col0 + n0 + cc] = code;
+        }
+      }
+    }
+  }
+  if (p.n_extra) __threadfence_system();   // peer stores complete before the kernel does
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 512);
@@ -404,6 +455,7 @@ __global__ void __launch_bounds__(256) k_tc_reduce(TcParams p) {
     for (int c = 0; c < p.nchunks; ++c) Q += u128(p.partial[(size_t)c * n + o]);
     finish_output(p, i, j, Q, p.sta[i], p.stb[j], p.LA[i], p.LB[j], p.slotA[i], p.slotB[j]);
   }
+  if (p.n_extra) __threadfence_system();
 }
 
 // ----------------------------------------------------------- digit planes ---
@@ -779,9 +831,11 @@ __global__ void __launch_bounds__(256) k_tc_fixup(GemmArgs a, const int4 *__rest
     int4 ra = sta[i], rb = stb[j];
     if (!(ra.z && rb.z)) continue;
     if (tc_exact(ra, rb, slotA[i], slotB[j], a.K)) continue;
-    slow_output<FMT>(a, i, j, a.out + (size_t)i * a.ldo + j,
-                     a.quire ? a.quire + ((size_t)i * a.N + j) * a.nlimbs : nullptr);
+    uint32_t *ob = a.out + (size_t)i * a.ldo + j;
+    slow_output<FMT>(a, i, j, ob, a.quire ? a.quire + ((size_t)i * a.N + j) * a.nlimbs : nullptr);
+    for (int e = 0; e < a.n_extra; ++e) a.extra_out[e][(size_t)i * a.ldo + a.extra_col0 + j] = *ob;
   }
+  if (a.n_extra) __threadfence_system();
 }
 
 // ------------------------------------------------------------ host side ---
@@ -972,6 +1026,8 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   p.sta = sta; p.stb = stb; p.LA = LA; p.LB = LB; p.slotA = slotA; p.slotB = slotB;
   p.CA = CA; p.CB = CB;
   p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.partial = part;
+  p.n_extra = a.n_extra; p.extra_col0 = a.extra_col0;
+  for (int e = 0; e < a.n_extra; ++e) p.extra_out[e] = a.extra_out[e];
   rc = S == 3 ? launch_tc_gemm_kernel<3>(ma, mb, p, s) : launch_tc_gemm_kernel<4>(ma, mb, p, s);
   if (rc) return rc;
   size_t outs = (size_t)a.M * a.N;

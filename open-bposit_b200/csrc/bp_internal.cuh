@@ -40,6 +40,7 @@ int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *
                          cudaStream_t s);
 
 // ---- quire GEMM (bp_gemm_simt.cu, bp_gemm_tc.cu) ----
+constexpr int kMaxExtraOut = 8;
 struct GemmArgs {
   int fmt;                 // 8 or 16
   const void *A, *B;       // [M,K], [N,K] codes, K contiguous
@@ -48,11 +49,18 @@ struct GemmArgs {
   int group, G;
   uint32_t *out;           // bp32 codes, row stride ldo
   int64_t ldo;
+  // Extra destinations (tensor-core path): every bp32 word is also stored at
+  // extra_out[r][i * ldo + extra_col0 + j] -- e.g. the full result matrices of
+  // peer GPUs, written over NVLink by the GEMM epilogue.
+  uint32_t *extra_out[kMaxExtraOut];
+  int n_extra;
+  int64_t extra_col0;
   uint32_t *quire;         // optional raw quires [M, N, nlimbs]
   int nlimbs;
 };
 
 size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo);
+bool gemm_uses_tc(const GemmArgs &a, int algo);
 int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s);
 
 }  // namespace bp

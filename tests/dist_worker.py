@@ -1,8 +1,9 @@
 """One rank of the multi-GPU quire GEMM check (launched by tests/test_gpu_dist.py
 through torch.distributed.run, one process per GPU, NCCL).  Every rank computes
-its N-shard on the tensor cores, the shards are all-gathered, and rank 0
-compares the gathered bposit32 matrix with an unsharded single-GPU GEMM:
-the quire result must be bit-identical for any rank count."""
+its N-shard on the tensor cores, the shards are all-gathered (NCCL, and the
+fused epilogue peer stores), and every rank compares its whole bposit32 matrix
+with an unsharded single-GPU GEMM: the quire result must be bit-identical for
+any rank count."""
 from __future__ import annotations
 
 import datetime
@@ -17,7 +18,7 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [REPO, os.path.join(REPO, "open-bposit_b200")]
 
 from bposit_b200 import ops  # noqa: E402
-from bposit_b200.dist import ShardedQuireGemm  # noqa: E402
+from bposit_b200.dist import FusedShardedQuireGemm, ShardedQuireGemm  # noqa: E402
 
 
 def main():
@@ -27,7 +28,9 @@ def main():
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
     results = []
-    for (M, N, K, group) in ((512, 1001, 4096, 0), (300, 777, 1000, 128)):
+    cases = ((512, 1001, 4096, 0), (300, 777, 1000, 128), (2048, 1536, 4096, 0), (2048, 1536, 2048, 128),
+             (256, max(1, world - 1), 512, 0))   # the last one leaves the last rank an empty shard
+    for (M, N, K, group) in cases:
         g = torch.Generator(device=dev).manual_seed(123)
         X = torch.randn((M, K), device=dev, generator=g)
         W = torch.randn((N, K), device=dev, generator=g) * 0.02
@@ -39,13 +42,28 @@ def main():
             B, sb = ops.quantize_bp8(W), None
         sg = ShardedQuireGemm(M, N, dev, group_size=group or 128)
         n0, n1 = sg.plan.bounds
-        out = sg(A, B[n0:n1].contiguous(), sa, None if sb is None else sb[n0:n1].contiguous())
+        Bs = B[n0:n1].contiguous()
+        sbs = None if sb is None else sb[n0:n1].contiguous()
+        out = sg(A, Bs, sa, sbs).clone()
+        # Fused epilogue all-gather (peer stores); two calls on different A so
+        # the second one overwrites a live result buffer.
+        fg = FusedShardedQuireGemm(M, N, dev, group_size=group or 128)
+        A2 = A.flip(0).contiguous()
+        sa2 = None if sa is None else sa.flip(0).contiguous()
+        fused1 = fg(A, Bs, sa, sbs).clone()
+        fused2 = fg(A2, Bs, sa2, sbs).clone()
         torch.cuda.synchronize()
+        fg.close()
+        ref, _ = ops.quire_gemm(A, B, 8, sa=sa, sb=sb, group=group or 128)
+        ref2, _ = ops.quire_gemm(A2, B, 8, sa=sa2, sb=sb, group=group or 128)
+        torch.cuda.synchronize()
+        eq = lambda x, y: bool(torch.equal(x.view(torch.int32), y.view(torch.int32)))  # noqa: E731
+        ok = [eq(out, ref), eq(fused1, ref), eq(fused2, ref2)]
+        flags = torch.tensor([int(all(ok))], device=dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
         if rank == 0:
-            ref, _ = ops.quire_gemm(A, B, 8, sa=sa, sb=sb, group=group or 128)
-            torch.cuda.synchronize()
-            results.append({"shape": [M, N, K], "group": group,
-                            "equal": bool(torch.equal(out.view(torch.int32), ref.view(torch.int32)))})
+            results.append({"shape": [M, N, K], "group": group, "gather": ok[0], "fused": ok[1:],
+                            "equal": bool(flags.item())})
     dist.barrier()
     if rank == 0:
         print(json.dumps({"world": world, "results": results}), flush=True)

@@ -23,7 +23,8 @@ def test_sharded_gemm_matches_single_gpu():
            f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", "--master-port", "29533",
            os.path.join(REPO, "tests", "dist_worker.py")]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=400)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    errors = [ln for ln in r.stderr.splitlines() if "rror" in ln and "frame #" not in ln][:20]
+    assert r.returncode == 0, "\n".join(errors) + "\n" + r.stdout[-2000:] + r.stderr[-3000:]
     line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
     res = json.loads(line)
     assert res["world"] == n and all(x["equal"] for x in res["results"]), res
