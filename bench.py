@@ -401,8 +401,8 @@ def run_ours(args):
         with open(tp) as f:
             tj = json.load(f)
         ent = tj.get("quire_gemm_" + ("tc" if args.algo != 1 else "simt"))
-        if ent and "bytes_per_mac" in ent:
-            traffic = ent["bytes_per_mac"] * M_ * (n1 - n0) * K_
+        if ent and ent.get("shape") == [M_, n1 - n0, K_]:
+            traffic = ent["dram_bytes_per_call"]
 
     if rank == 0:
         line = {
@@ -419,6 +419,8 @@ def run_ours(args):
                          "peak_source": f"int8 dense = 2 x {peak_src} bf16 {peaks['bf16_tflops']} TF/s",
                          "kernel": "quire GEMM (all launches of one bp_quire_gemm call)",
                          "kernel_ms": round(kms, 3),
+                         "traffic_note": ("DRAM bytes read+written by one bp_quire_gemm call (6 launches), one ncu "
+                                          "capture at this shape" if traffic else "no capture at this shape"),
                          "issued_int8_TOPS": round(k_tops * slice_pairs, 1) if slice_pairs else None,
                          "issued_frac": round(k_tops * slice_pairs / int8_peak, 4) if slice_pairs else None,
                          "slice_pairs_per_useful_mac": slice_pairs},

@@ -1,0 +1,103 @@
+"""Run one workload of the library on the current GPU and print its timing.
+
+    python -m bposit_b200.run gemm M N K [--fmt bp8|bp16] [--group 128] [--calls 3] [--algo 0]
+    python -m bposit_b200.run codec N [--fmt bp8|bp16] [--calls 3]
+
+``gemm`` times bp_quire_gemm on operands N(0,1) * 2^U{-8..8} per row (the
+large-GEMM workload's distribution), quantized on the device; ``codec`` times
+the encode and decode kernels on the codec-sweep value mix.  Each runs
+`--calls` untimed calls and then `--calls` calls timed with CUDA events, so a
+profiler can capture a fixed, small number of launches (e.g. ``ncu -k
+regex:k_quire_gemm_tc -c 1``).
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+
+import torch
+
+from . import ops
+from .workloads import codec_sweep
+
+
+def _operand(rows: int, K: int, fmt: int, gen: torch.Generator, group: int):
+    x = torch.randn((rows, K), device="cuda", generator=gen)
+    e = torch.randint(-8, 9, (rows, 1), device="cuda", generator=gen).float()
+    x = x * torch.exp2(e)
+    if group:
+        if fmt != 8:
+            raise SystemExit("group scales are a bp8 feature")
+        return ops.quantize_bp8_grouped(x, group=group)
+    if fmt == 8:
+        return ops.quantize_bp8(x, nearest=True), None
+    return ops.encode_bp16(x), None
+
+
+def _time(fn, calls: int) -> float:
+    for _ in range(calls):
+        fn()
+    torch.cuda.synchronize()
+    s, t = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(calls):
+        fn()
+    t.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(t) / calls
+
+
+def run_gemm(a) -> str:
+    fmt = ops.fmt_bits(a.fmt)
+    gen = torch.Generator(device="cuda").manual_seed(a.seed)
+    A, sa = _operand(a.M, a.K, fmt, gen, a.group)
+    B, sb = _operand(a.N, a.K, fmt, gen, a.group)
+    ws = torch.empty(max(256, ops.gemm_workspace_size(fmt, a.M, a.N, a.K, a.algo)), dtype=torch.uint8,
+                     device="cuda")
+    out = torch.empty((a.M, a.N), dtype=torch.uint32, device="cuda")
+    ms = _time(lambda: ops.quire_gemm(A, B, fmt, sa=sa, sb=sb, group=a.group or 128, out=out, algo=a.algo,
+                                      workspace=ws), a.calls)
+    return (f"gemm {a.fmt} M={a.M} N={a.N} K={a.K} group={a.group}: {ms:.3f} ms/call, "
+            f"{2.0 * a.M * a.N * a.K / ms / 1e9:.1f} TOPS")
+
+
+def run_codec(a) -> str:
+    fmt = ops.fmt_bits(a.fmt)
+    x = torch.from_numpy(codec_sweep(a.n, a.fmt, a.seed)).cuda()
+    if fmt == 8:
+        codes = torch.empty(a.n, dtype=torch.uint8, device="cuda")
+        enc = _time(lambda: ops.quantize_bp8(x, nearest=True, out=codes), a.calls)
+    else:
+        codes = torch.empty(a.n, dtype=torch.uint16, device="cuda")
+        enc = _time(lambda: ops.encode_bp16(x, out=codes), a.calls)
+    dec = _time(lambda: ops.decode(codes, a.fmt), a.calls)
+    b = fmt // 8 + 4
+    return (f"codec {a.fmt} n={a.n}: encode {enc:.3f} ms ({a.n * b / enc / 1e6:.0f} GB/s), "
+            f"decode {dec:.3f} ms ({a.n * b / dec / 1e6:.0f} GB/s)")
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m bposit_b200.run")
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("M", type=int)
+    g.add_argument("N", type=int)
+    g.add_argument("K", type=int)
+    g.add_argument("--fmt", default="bp8", choices=["bp8", "bp16"])
+    g.add_argument("--group", type=int, default=0, help="per-group power-of-two scales (bp8)")
+    g.add_argument("--algo", type=int, default=0)
+    c = sub.add_parser("codec")
+    c.add_argument("n", type=int)
+    c.add_argument("--fmt", default="bp8", choices=["bp8", "bp16"])
+    for p in (g, c):
+        p.add_argument("--calls", type=int, default=3)
+        p.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("no CUDA device")
+    print(run_gemm(a) if a.what == "gemm" else run_codec(a), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
