@@ -30,9 +30,10 @@
 //     path (it exits at once when global row bounds show there are none).
 //
 // Warp roles in the GEMM (128 threads, one CTA per SM, 512 TMEM columns):
-// warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues MMAs, all four warps
-// run the epilogue (warp w reads TMEM lanes 32w..32w+31 = tile rows).  All
-// mbarrier waits are bounded; a timeout sets an error word and unwinds.
+// warp 0 lane 0 issues TMA loads, warps 1 and 2 issue the MMAs of alternate
+// K blocks, all four warps run the epilogue (warp w reads TMEM lanes
+// 32w..32w+31 = tile rows).  All mbarrier waits are bounded; a timeout sets an
+// error word and unwinds.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -140,11 +141,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Bounded wait: false (and the error word set) if the phase never completes.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code) {
+// Bounded wait.  A timeout records `code` in g_tc_error and raises the CTA's
+// abort word, which makes every other bounded wait of the CTA give up at once.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code,
+                                          volatile int *abort = nullptr) {
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
+    if (abort && *abort) return false;
     if (clock64() - t0 > WAIT_LIMIT) {
       atomicOr(&g_tc_error, code);
+      if (abort) *abort = 1;
       return false;
     }
   }
@@ -215,13 +221,18 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
 
 // Warp-uniform bounded wait: every lane leaves together once any lane has
 // seen the phase complete (completion is monotonic).
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int code) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int code,
+                                               volatile int *abort = nullptr) {
   long long t0 = clock64();
   while (true) {
     bool done = mbar_try_wait(bar, parity);
     if (__any_sync(0xFFFFFFFFu, done)) return true;
+    if (abort && __any_sync(0xFFFFFFFFu, *abort != 0)) return false;
     if (clock64() - t0 > WAIT_LIMIT) {
-      if ((threadIdx.x & 31) == 0) atomicOr(&g_tc_error, code);
+      if ((threadIdx.x & 31) == 0) {
+        atomicOr(&g_tc_error, code);
+        if (abort) *abort = 1;
+      }
       return false;
     }
   }
@@ -289,6 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *empty = full + C::STAGES;
   uint64_t *tfull = empty + C::STAGES;
   uint32_t *tmem_slot = (uint32_t *)(tfull + 1);
+  volatile int *abort = (volatile int *)(tmem_slot + 1);                  // set by a timed-out wait
   int4 *sstat = (int4 *)(smem + C::STAGES * C::STAGE_BYTES + 256);          // [BN] B-row stats
   int2 *sLs = (int2 *)(sstat + C::BN);                                    // [BN] {L, slot}
 
@@ -303,7 +315,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 1);
+    mbar_init(tfull, 2);   // one commit from each issuing warp
+    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   for (int c = threadIdx.x; c < C::BN; c += THREADS) {
@@ -323,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int it = 0; it < nkb && ok; ++it) {
         int st = it % C::STAGES;
         uint32_t round = (uint32_t)(it / C::STAGES);
-        ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1);
+        ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1, abort);
         if (!ok) break;
         uint8_t *sa = smem + st * C::STAGE_BYTES;
         mbar_expect_tx(&full[st], C::STAGE_BYTES);
@@ -332,15 +345,26 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    {   // the whole warp runs the issue loop; one elected lane issues each MMA
-      uint32_t init = 0u;
-      for (int it = 0; it < nkb && ok; ++it) {
-        int st = it % C::STAGES;
-        uint32_t round = (uint32_t)(it / C::STAGES);
-        ok = mbar_wait_warp(&full[st], round & 1u, 2);
-        if (!ok) break;
+  } else if (warp == 1 || warp == 2) {
+    // Two issuing warps take alternate K blocks.  A warp waits for its block's
+    // data while the other warp issues, then takes the hand-off (named barrier
+    // 1 or 2 between the two warps, bracketed by tcgen05 fences so the MMAs of
+    // consecutive blocks stay ordered in the tensor pipe): the full-barrier
+    // poll, which stalls MMA issue for ~200 cycles when the issuing warp does
+    // it, is off the critical path.  Every iteration takes the same hand-off
+    // steps whether or not its wait succeeded, so a timeout cannot strand the
+    // partner at a named barrier.
+    const int me = warp - 1;
+    uint32_t init = me ? (1u << C::D) - 1u : 0u;   // block 0 (warp 1) initialises every diagonal
+    for (int it = me; it < nkb; it += 2) {
+      const int st = it % C::STAGES;
+      const uint32_t round = (uint32_t)(it / C::STAGES);
+      if (ok) ok = mbar_wait_warp(&full[st], round & 1u, 2, abort);
+      if (it > 0) {
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + me) : "memory");
         tc_fence_after();
+      }
+      if (ok) {
         uint32_t a0 = smem_u32(smem + st * C::STAGE_BYTES);
         uint32_t b0 = a0 + C::A_BYTES;
 #pragma unroll
@@ -362,13 +386,17 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         umma_commit(&empty[st]);
       }
-      umma_commit(tfull);
+      if (it + 1 < nkb) {
+        tc_fence_before();
+        asm volatile("bar.arrive %0, 64;" ::"r"(1 + (me ^ 1)) : "memory");
+      }
     }
+    umma_commit(tfull);
     __syncwarp();
   }
 
   // ---------------------------------------------------------------- epilogue
-  ok = mbar_wait(tfull, 0, 4) && ok;
+  ok = mbar_wait(tfull, 0, 4, abort) && ok;
   tc_fence_after();
   const int r = warp * 32 + lane;
   const int i = m0 + r;
