@@ -54,7 +54,7 @@ namespace {
 #ifndef BP_TC_BK
 #define BP_TC_BK 64
 #endif
-constexpr int BM = 128, BK = BP_TC_BK, THREADS = 128;
+constexpr int BM = 128, BK = BP_TC_BK, THREADS = 256;
 constexpr long long WAIT_LIMIT = 4000000000LL;   // cycles (~2 s) before a wait gives up
 constexpr int TAILCAP = 1024;                    // listed tail elements per row (more -> fixup)
 constexpr int BIG = 1 << 20;                     // offset that makes max-reductions find a minimum
@@ -144,9 +144,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Bounded wait.  A timeout records `code` in g_tc_error and raises the CTA's
 // abort word, which makes every other bounded wait of the CTA give up at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code,
-                                          volatile int *abort = nullptr) {
+                                          volatile int *abort = nullptr, bool nap = false) {
   long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
+    if (nap) __nanosleep(256);   // idle warps keep off the shared-memory pipe
     if (abort && *abort) return false;
     if (clock64() - t0 > WAIT_LIMIT) {
       atomicOr(&g_tc_error, code);
@@ -396,9 +397,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   // ---------------------------------------------------------------- epilogue
-  ok = mbar_wait(tfull, 0, 4, abort) && ok;
+  // Eight warps: warp w reads TMEM lane quarter w & 3 (tile rows 32q..32q+31,
+  // the only lanes its tcgen05.ld may touch) and column half w >> 2.
+  ok = mbar_wait(tfull, 0, 4, abort, warp > 2) && ok;
   tc_fence_after();
-  const int r = warp * 32 + lane;
+  const int q4 = warp & 3, half = warp >> 2;
+  const int r = q4 * 32 + lane;
   const int i = m0 + r;
   int4 ra = make_int4(0, 0, 0, 0);
   int Li = 0, slot_i = -1;
@@ -407,22 +411,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     Li = p.LA[i];
     slot_i = p.slotA[i];
   }
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-  // Finished codes are staged per warp in the (now idle) pipeline buffers --
-  // [32 rows][BN + 1] words, conflict-free both ways -- with a per-row mask of
-  // the outputs this kernel owns, then stored row by row with consecutive
-  // lanes on consecutive columns, so each warp store is one 128-byte line
-  // (also across NVLink, for the extra outputs).
-  constexpr int MW = C::BN / 32;
-  static_assert(C::BN % 32 == 0, "BN must be a multiple of 32");
-  static_assert(THREADS * (C::BN + 1 + MW) * 4 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
-  uint32_t *stg = (uint32_t *)smem + warp * 32 * (C::BN + 1);
-  uint32_t *smask = (uint32_t *)smem + THREADS * (C::BN + 1) + warp * 32 * MW;
-  uint32_t vm[MW];
-#pragma unroll
-  for (int q = 0; q < MW; ++q) vm[q] = 0u;
+  const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+  // Finished codes are staged per lane quarter in the (now idle) pipeline
+  // buffers -- [32 rows][BN + 1] words, conflict-free both ways -- then stored
+  // row by row with consecutive lanes on consecutive columns, so each warp
+  // store is one 128-byte line (also across NVLink, for the extra outputs).
+  // Outputs left to k_tc_fixup are staged as 0; the fixup, later on the same
+  // stream, overwrites them everywhere.
+  constexpr int CW = C::BN / 2;
+  static_assert(C::BN % 32 == 0 && CW % 16 == 0, "BN must be a multiple of 32");
+  static_assert(4 * 32 * (C::BN + 1) * 4 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
+  uint32_t *stg = (uint32_t *)smem + q4 * 32 * (C::BN + 1);
 #pragma unroll 1
-  for (int c0 = 0; c0 < C::BN; c0 += 16) {
+  for (int c0 = half * CW; c0 < half * CW + CW; c0 += 16) {
     uint32_t v[C::D][16];
 #pragma unroll
     for (int d = 0; d < C::D; ++d) tmem_ld16(trow + d * C::BN + c0, v[d]);
@@ -432,35 +433,41 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int jj = 0; jj < 16; ++jj) {
       const int j = n0 + c0 + jj;
       if (j >= p.N) continue;
-      unsigned __int128 Q = 0;
+      // |acc_d| < 2^31, so sum_d acc_d 128^d is below 2^60: exact in 64 bits
+      long long Q = 0;
 #pragma unroll
-      for (int d = 0; d < C::D; ++d)
-        Q += (unsigned __int128)(__int128)(long long)(int)v[d][jj] << (7 * d);
+      for (int d = 0; d < C::D; ++d) Q += (long long)(int)v[d][jj] * (1ll << (7 * d));
       if (p.nchunks > 1) {
-        p.partial[((size_t)chunk * p.M + i) * p.N + j] = make_ulonglong2((unsigned long long)Q,
-                                                                          (unsigned long long)(Q >> 64));
+        p.partial[((size_t)chunk * p.M + i) * p.N + j] =
+            make_ulonglong2((unsigned long long)Q, Q < 0 ? ~0ull : 0ull);
       } else {
-        int2 ls = sLs[c0 + jj];
-        uint32_t code;
-        if (finish_code(p, i, j, Q, ra, sstat[c0 + jj], Li, ls.x, slot_i, ls.y, code)) {
-          stg[lane * (C::BN + 1) + c0 + jj] = code;
-          vm[(c0 + jj) >> 5] |= 1u << ((c0 + jj) & 31);
+        const int2 ls = sLs[c0 + jj];
+        const int4 rb = sstat[c0 + jj];
+        uint32_t code = 0u;
+        if (!p.quire && slot_i < 0 && ls.y < 0 && ra.z && rb.z) {
+          // no tail correction, no raw quire: round Q * 2^(L_i + L_j) directly
+          if (tc_exact(ra, rb, slot_i, ls.y, p.K)) {
+            const bool neg = Q < 0;
+            code = bp32_from_mag(neg, 0u, neg ? 0ull - (unsigned long long)Q : (unsigned long long)Q, Li + ls.x);
+          }
+        } else if (!finish_code(p, i, j, (unsigned __int128)(__int128)Q, ra, rb, Li, ls.x, slot_i, ls.y, code)) {
+          code = 0u;
         }
+        stg[lane * (C::BN + 1) + c0 + jj] = code;
       }
     }
   }
   if (p.nchunks == 1) {
-#pragma unroll
-    for (int q = 0; q < MW; ++q) smask[lane * MW + q] = vm[q];
-    __syncwarp();
+    // the two warps of a lane quarter meet, then each stores half of its rows
+    asm volatile("bar.sync %0, 64;" ::"r"(3 + q4) : "memory");
 #pragma unroll 1
-    for (int rr = 0; rr < 32; ++rr) {
-      const int ii = m0 + warp * 32 + rr;
+    for (int rr = half * 16; rr < half * 16 + 16; ++rr) {
+      const int ii = m0 + q4 * 32 + rr;
       if (ii >= p.M) break;
 #pragma unroll
-      for (int q = 0; q < MW; ++q) {
-        const int cc = q * 32 + lane;
-        if ((smask[rr * MW + q] >> lane) & 1u) {
+      for (int qq = 0; qq < C::BN / 32; ++qq) {
+        const int cc = qq * 32 + lane;
+        if (n0 + cc < p.N) {
           const uint32_t code = stg[rr * (C::BN + 1) + cc];
           p.out[(size_t)ii * p.ldo + n0 + cc] = code;
           for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)ii * p.ldo + p.extra_col0 + n0 + cc] = code;
