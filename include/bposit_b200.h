@@ -102,7 +102,8 @@ int bp_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,
  * sb (optional, may be NULL) are int32 per-(row, group) exponents
  * [rows, ceil(K/group)].  If out_quire is non-NULL, the raw quires are also
  * written as [M, N, quire_limbs] (quire_limbs 8, 12 or 16; truncated two's
- * complement).  algo: 0 = auto, 1 = CUDA cores, 2 = tensor cores (tcgen05).
+ * complement).  algo: 0 = auto, 1 = CUDA cores, 2 = tensor cores (tcgen05; paired SMs,
+ * cta_group::2, when M > 128), 3 = tensor cores with one SM per output tile.
  * workspace: device memory of at least bp_quire_gemm_workspace_size() bytes,
  * 256-byte aligned; NULL lets the library take it stream-ordered from the
  * device's default memory pool for the duration of the call.

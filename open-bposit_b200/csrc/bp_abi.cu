@@ -157,7 +157,7 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K, co
   g_err[0] = 0;
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm: negative size");
-  if (algo < 0 || algo > 2) return set_error(kEInval, "bp_quire_gemm: algo must be 0, 1 or 2");
+  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm: algo must be 0, 1, 2 or 3");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm: group must be > 0 with scales");
   if (ldo < N) return set_error(kEInval, "bp_quire_gemm: ldo (%lld) < N (%d)", (long long)ldo, N);
   if (out_quire && quire_limbs != 8 && quire_limbs != 12 && quire_limbs != 16)
@@ -200,7 +200,7 @@ int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int
     if (!peer_outs[e]) return set_error(kEInval, "bp_quire_gemm_multi: null peer output %d", e);
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_multi: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_multi: negative size");
-  if (algo < 0 || algo > 2) return set_error(kEInval, "bp_quire_gemm_multi: algo must be 0, 1 or 2");
+  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_multi: algo must be 0, 1, 2 or 3");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_multi: group must be > 0 with scales");
   if (ldo < N) return set_error(kEInval, "bp_quire_gemm_multi: ldo (%lld) < N (%d)", (long long)ldo, N);
   if (M == 0 || N == 0) return kOk;

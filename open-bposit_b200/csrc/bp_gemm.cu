@@ -9,7 +9,8 @@
 namespace bp {
 
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
-int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, cudaStream_t s);
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
+                   cudaStream_t s);
 size_t gemm_tc_workspace(int fmt, int M, int N, int K);
 bool gemm_tc_supported(int fmt, int M, int N, int K);
 
@@ -69,7 +70,7 @@ static size_t stats_bytes(int M, int N) { return align_up((size_t)(M + N) * size
 static bool use_tc(const GemmArgs &a, int algo) {
   if (algo == 1) return false;
   if (!gemm_tc_supported(a.fmt, a.M, a.N, a.K)) return false;
-  if (algo == 2) return true;
+  if (algo == 2 || algo == 3) return true;
   // auto: tensor cores once there is enough work to fill the machine
   return (long long)a.M * a.N >= 128LL * 128 * 8 && a.K >= 64;
 }
@@ -90,7 +91,7 @@ int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cu
   if (use_tc(a, algo)) {   // the tensor-core prep computes the row statistics itself
     size_t need = gemm_tc_workspace(a.fmt, a.M, a.N, a.K);
     if (ws_bytes < need_stats + need) return set_error(kEWorkspace, "quire_gemm: workspace too small");
-    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, s);
+    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo == 3, s);
   }
   int rc = launch_row_stats(a.fmt, a.A, a.M, a.K, a.sa, a.group, sta, s);
   if (rc) return rc;

@@ -59,9 +59,14 @@ constexpr long long WAIT_LIMIT = 4000000000LL;   // cycles (~2 s) before a wait 
 constexpr int TAILCAP = 1024;                    // listed tail elements per row (more -> fixup)
 constexpr int BIG = 1 << 20;                     // offset that makes max-reductions find a minimum
 
-template <int S>
+// Tile configuration.  PAIR: the 2-SM form -- a cluster of two CTAs issues
+// M = 256 MMAs (tcgen05 cta_group::2); each CTA holds its own 128 rows of A and
+// half of the tile's B rows, and owns 128 rows of the output tile.
+template <int S, bool PAIR = false>
 struct Cfg {
   static constexpr int BN = S == 3 ? 96 : 64;
+  static constexpr int BNB = PAIR ? BN / 2 : BN;   // B rows (tile columns) staged by one CTA
+  static constexpr int MM = PAIR ? 2 * BM : BM;    // rows of one MMA
   static constexpr int D = 2 * S - 1;
   static constexpr int SPAN = 7 * S - 1;
   static constexpr int TOP = (1 << (SPAN - 7 * (S - 1))) + 1;   // bound of |top digit|
@@ -80,15 +85,20 @@ struct Cfg {
   // K per chunk with every int32 diagonal sum exact, a multiple of BK
   static constexpr int KCHUNK = (int)((0x7FFFFFFFLL / max_diag()) / BK * BK);
   static constexpr int A_BYTES = S * BM * BK;
-  static constexpr int B_BYTES = S * BN * BK;
+  static constexpr int B_BYTES = S * BNB * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BK == 128 ? 2 : (S == 3 ? 5 : 4);
+  static constexpr int STAGES = PAIR ? (S == 3 ? 6 : 5) : (BK == 128 ? 2 : (S == 3 ? 5 : 4));
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + BN * 32;
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                                    ((uint32_t)(BM >> 4) << 24);
+                                    ((uint32_t)(MM >> 4) << 24);
   static_assert(D * BN <= 512, "TMEM budget");
-  static_assert(BN % 16 == 0 && BN <= 256, "UMMA N");
+  static_assert(BN % 32 == 0 && BN <= 256, "UMMA N");
+  static_assert(BNB % 8 == 0, "B rows per CTA in whole 8-row swizzle atoms");
+  static_assert(!PAIR || BK == 64, "the paired form uses 64-deep K blocks");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1 KB aligned");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
   static_assert(TOP <= 127, "top digit must fit int8");
+  static_assert(KCHUNK >= BK, "at least one K block per exact chunk");
 };
 
 // Per-operand device counters, zeroed before each call:
@@ -140,7 +150,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false (and the error word set) if the phase never completes.
 // Bounded wait.  A timeout records `code` in g_tc_error and raises the CTA's
 // abort word, which makes every other bounded wait of the CTA give up at once.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int code,
@@ -167,14 +176,54 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
-               "r"(ncols));
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+// The TMA load of the paired form: the destination is this CTA's shared
+// memory, the completion goes to `bar`, a shared::cluster address (the pair
+// leader's barrier).  No multicast.
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar, int x, int y,
+                                                 int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
 }
 
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of both CTAs of the cluster; release/acquire orders shared
+// memory (barrier initialisation, epilogue reads) across the pair.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of `p`'s counterpart in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_smem(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void tmem_alloc_t(uint32_t *slot, uint32_t ncols) {
+  if (PAIR) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  } else {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+}
+
+template <bool PAIR>
+__device__ __forceinline__ void tmem_dealloc_t(uint32_t taddr, uint32_t ncols) {
+  if (PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+  else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -195,19 +244,26 @@ __device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
 // lane elected from the calling (converged) warp so that the whole issue loop
 // stays warp-uniform.  COL selects the A-collector use: 0 load A and keep it,
 // 1 reuse the kept A, 2 reuse and release, 3 no collector.
-#define BP_UMMA_ASM(QUAL)                                                                   \
+#define BP_UMMA_ASM(GROUP, QUAL)                                                            \
   asm volatile(                                                                             \
       "{\n\t.reg .pred p, e;\n\telect.sync _|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"    \
-      "@e tcgen05.mma.cta_group::1.kind::i8" QUAL " [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d), \
+      "@e tcgen05.mma.cta_group::" GROUP ".kind::i8" QUAL " [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d), \
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate))
 
-template <int COL>
+template <int COL, bool PAIR = false>
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                         uint32_t accumulate) {
-  if (COL == 0) BP_UMMA_ASM(".collector::a::fill");
-  else if (COL == 1) BP_UMMA_ASM(".collector::a::use");
-  else if (COL == 2) BP_UMMA_ASM(".collector::a::lastuse");
-  else BP_UMMA_ASM("");
+  if (PAIR) {
+    if (COL == 0) BP_UMMA_ASM("2", ".collector::a::fill");
+    else if (COL == 1) BP_UMMA_ASM("2", ".collector::a::use");
+    else if (COL == 2) BP_UMMA_ASM("2", ".collector::a::lastuse");
+    else BP_UMMA_ASM("2", "");
+  } else {
+    if (COL == 0) BP_UMMA_ASM("1", ".collector::a::fill");
+    else if (COL == 1) BP_UMMA_ASM("1", ".collector::a::use");
+    else if (COL == 2) BP_UMMA_ASM("1", ".collector::a::lastuse");
+    else BP_UMMA_ASM("1", "");
+  }
 }
 #undef BP_UMMA_ASM
 
@@ -217,6 +273,17 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+// The paired form's commit: arrive on `bar` in both CTAs of the pair (the
+// same shared-memory offset in each; cta mask 0b11) once every tcgen05
+// operation this warp issued so far has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}\n"
+      ::"r"(smem_u32(bar)), "h"((unsigned short)3)
       : "memory");
 }
 
@@ -290,11 +357,14 @@ __device__ __forceinline__ void finish_output(const TcParams &p, int i, int j, u
 }
 
 // ----------------------------------------------------------------- GEMM ---
-template <int S>
+// One CTA per SM.  PAIR: launched in clusters of two; CTA rank 0 (the leader)
+// issues M = 256 MMAs that read A from both CTAs (128 rows each) and B from
+// both (half of the tile's columns each) and write each CTA's own TMEM.
+template <int S, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     k_quire_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     TcParams p) {
-  using C = Cfg<S>;
+  using C = Cfg<S, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t *full = (uint64_t *)(smem + C::STAGES * C::STAGE_BYTES);
@@ -306,7 +376,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   int2 *sLs = (int2 *)(sstat + C::BN);                                    // [BN] {L, slot}
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * C::BN, m0 = blockIdx.y * BM, chunk = blockIdx.z;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;      // 0: issues the pair's MMAs
+  const int n0 = (PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x) * C::BN;
+  const int m0 = blockIdx.y * C::MM + (int)rank * BM, chunk = blockIdx.z;
   const int kb0 = chunk * p.kb_per_chunk;
   const int kb1 = min(p.nkb, kb0 + p.kb_per_chunk);
   const int nkb = kb1 - kb0;
@@ -316,16 +388,17 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(tfull, 2);   // one commit from each issuing warp
+    mbar_init(tfull, 2);   // one commit from each issuing warp (of the leader, when paired)
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (PAIR) cluster_sync_all();   // the peer's barriers exist before anything reaches them
   for (int c = threadIdx.x; c < C::BN; c += THREADS) {
     int j = n0 + c;
     sstat[c] = j < p.N ? p.stb[j] : make_int4(0, 0, 0, 0);
     sLs[c] = j < p.N ? make_int2(p.LB[j], p.slotB[j]) : make_int2(0, -1);
   }
-  if (warp == 0) tmem_alloc(tmem_slot, 512);
+  if (warp == 0) tmem_alloc_t<PAIR>(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -340,13 +413,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1, abort);
         if (!ok) break;
         uint8_t *sa = smem + st * C::STAGE_BYTES;
-        mbar_expect_tx(&full[st], C::STAGE_BYTES);
-        tma_load_3d(sa, &tmA, &full[st], (kb0 + it) * BK, m0, 0);
-        tma_load_3d(sa + C::A_BYTES, &tmB, &full[st], (kb0 + it) * BK, n0, 0);
+        if (PAIR) {
+          // both CTAs' loads complete on the leader's barrier, which expects both
+          if (rank == 0) mbar_expect_tx(&full[st], 2 * C::STAGE_BYTES);
+          const uint32_t fb = cluster_smem(&full[st], 0);
+          tma_load_3d_pair(sa, &tmA, fb, (kb0 + it) * BK, m0, 0);
+          tma_load_3d_pair(sa + C::A_BYTES, &tmB, fb, (kb0 + it) * BK, n0 + (int)rank * C::BNB, 0);
+        } else {
+          mbar_expect_tx(&full[st], C::STAGE_BYTES);
+          tma_load_3d(sa, &tmA, &full[st], (kb0 + it) * BK, m0, 0);
+          tma_load_3d(sa + C::A_BYTES, &tmB, &full[st], (kb0 + it) * BK, n0, 0);
+        }
       }
     }
     __syncwarp();
-  } else if (warp == 1 || warp == 2) {
+  } else if ((warp == 1 || warp == 2) && rank == 0) {
     // Two issuing warps take alternate K blocks.  A warp waits for its block's
     // data while the other warp issues, then takes the hand-off (named barrier
     // 1 or 2 between the two warps, bracketed by tcgen05 fences so the MMAs of
@@ -376,30 +457,38 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int t = 0; t < S; ++t) {
               const int d = s + t;
-              uint64_t bd = sw64_desc(b0 + t * C::BN * BK + ks * 32);
+              uint64_t bd = sw64_desc(b0 + t * C::BNB * BK + ks * 32);
               const uint32_t acc = (init >> d) & 1u;
-              if (t == 0) umma_i8<0>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
-              else if (t == S - 1) umma_i8<2>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
-              else umma_i8<1>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+              if (t == 0) umma_i8<0, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+              else if (t == S - 1) umma_i8<2, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+              else umma_i8<1, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
               init |= 1u << d;
             }
           }
         }
-        umma_commit(&empty[st]);
+        if (PAIR) {   // the slot is free in both CTAs
+          umma_commit_pair(&empty[st]);
+        } else {
+          umma_commit(&empty[st]);
+        }
       }
       if (it + 1 < nkb) {
         tc_fence_before();
         asm volatile("bar.arrive %0, 64;" ::"r"(1 + (me ^ 1)) : "memory");
       }
     }
-    umma_commit(tfull);
+    if (PAIR) {
+      umma_commit_pair(tfull);
+    } else {
+      umma_commit(tfull);
+    }
     __syncwarp();
   }
 
   // ---------------------------------------------------------------- epilogue
   // Eight warps: warp w reads TMEM lane quarter w & 3 (tile rows 32q..32q+31,
   // the only lanes its tcgen05.ld may touch) and column half w >> 2.
-  ok = mbar_wait(tfull, 0, 4, abort, warp > 2) && ok;
+  ok = mbar_wait(tfull, 0, 4, abort, true) && ok;
   tc_fence_after();
   const int q4 = warp & 3, half = warp >> 2;
   const int r = q4 * 32 + lane;
@@ -477,8 +566,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (p.n_extra) __threadfence_system();   // peer stores complete before the kernel does
   tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 512);
+  if (PAIR) cluster_sync_all();   // both CTAs are done with the pair's TMEM
+  else __syncthreads();
+  if (warp == 0) tmem_dealloc_t<PAIR>(tmem, 512);
+  if (PAIR) cluster_sync_all();   // neither CTA leaves while the other still deallocates
 }
 
 // ----------------------------------------------------------- split-K sum ---
@@ -967,19 +1058,37 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   return L;
 }
 
-template <int S>
+template <int S, bool PAIR>
 int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const TcParams &p, cudaStream_t s) {
-  using C = Cfg<S>;
+  using C = Cfg<S, PAIR>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(k_quire_gemm_tc<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr_err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   });
   if (attr_err != cudaSuccess)
     return set_error(kECuda, "quire_gemm: cannot set shared memory size: %s", cudaGetErrorString(attr_err));
-  dim3 grid((p.N + C::BN - 1) / C::BN, (p.M + BM - 1) / BM, p.nchunks);
+  const unsigned nt = (unsigned)((p.N + C::BN - 1) / C::BN);
+  dim3 grid(PAIR ? 2 * nt : nt, (unsigned)((p.M + C::MM - 1) / C::MM), (unsigned)p.nchunks);
   if (grid.y > 65535u || grid.z > 65535u) return set_error(kERange, "quire_gemm: grid too large");
-  k_quire_gemm_tc<S><<<grid, THREADS, C::SMEM, s>>>(ma, mb, p);
+  if (!PAIR) {
+    k_quire_gemm_tc<S, false><<<grid, THREADS, C::SMEM, s>>>(ma, mb, p);
+    return check_launch("quire_gemm_tc");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_quire_gemm_tc<S, true>, ma, mb, p);
+  if (e != cudaSuccess) return set_error(kECuda, "quire_gemm_tc (paired): %s", cudaGetErrorString(e));
   return check_launch("quire_gemm_tc");
 }
 
@@ -993,7 +1102,8 @@ bool gemm_tc_supported(int fmt, int M, int N, int K) {
 size_t gemm_tc_workspace(int fmt, int M, int N, int K) { return tc_layout(fmt, M, N, K).total; }
 
 // sta / stb are outputs here: the prep kernels write the row statistics.
-int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, cudaStream_t s) {
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
+                   cudaStream_t s) {
   TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K);
   if (ws_bytes < L.total) return set_error(kEWorkspace, "quire_gemm: tensor-core workspace too small");
   char *w = (char *)ws;
@@ -1048,11 +1158,13 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   if (rc) return rc;
 
   int S = L.S;
-  int bn = S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
+  // Paired SMs whenever the tile has a second 128-row half to work on.
+  const bool pair = !single_sm && BK == 64 && a.M > BM;
+  const int bnb = S == 3 ? (pair ? Cfg<3, true>::BNB : Cfg<3>::BNB) : (pair ? Cfg<4, true>::BNB : Cfg<4>::BNB);
   CUtensorMap ma, mb;
   rc = make_plane_map(&ma, planesA, L.Kp, a.M, S, BM);
   if (rc) return rc;
-  rc = make_plane_map(&mb, planesB, L.Kp, a.N, S, bn);
+  rc = make_plane_map(&mb, planesB, L.Kp, a.N, S, bnb);
   if (rc) return rc;
 
   TcParams p{};
@@ -1063,7 +1175,8 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.partial = part;
   p.n_extra = a.n_extra; p.extra_col0 = a.extra_col0;
   for (int e = 0; e < a.n_extra; ++e) p.extra_out[e] = a.extra_out[e];
-  rc = S == 3 ? launch_tc_gemm_kernel<3>(ma, mb, p, s) : launch_tc_gemm_kernel<4>(ma, mb, p, s);
+  if (S == 3) rc = pair ? launch_tc_gemm_kernel<3, true>(ma, mb, p, s) : launch_tc_gemm_kernel<3, false>(ma, mb, p, s);
+  else rc = pair ? launch_tc_gemm_kernel<4, true>(ma, mb, p, s) : launch_tc_gemm_kernel<4, false>(ma, mb, p, s);
   if (rc) return rc;
   size_t outs = (size_t)a.M * a.N;
   int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);

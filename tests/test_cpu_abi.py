@@ -52,8 +52,8 @@ def test_host_argument_validation():
     assert rc == _lib.BP_EINVAL
     rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, vp(16), 5, 0, None, 0, None)
     assert rc == _lib.BP_EINVAL
-    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 3, None, 0, None)
-    assert rc == _lib.BP_EINVAL
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 4, None, 0, None)
+    assert rc == _lib.BP_EINVAL   # algo 0..3
     rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 0, vp(17), 1 << 20, None)
     assert rc == _lib.BP_EALIGN
     assert L.bp_decode(9, vp(16), 4, vp(16), None) == _lib.BP_EFMT

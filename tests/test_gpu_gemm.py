@@ -11,7 +11,7 @@ from conftest import golden
 
 pytestmark = pytest.mark.gpu
 
-ALGOS = [1, 2]   # 1 = CUDA cores, 2 = tensor cores
+ALGOS = [1, 2, 3]   # 1 = CUDA cores, 2 = tensor cores (paired SMs when M > 128), 3 = tensor cores, one SM per tile
 
 
 @pytest.fixture(scope="module")
@@ -68,7 +68,7 @@ def test_fast_selftest_dots(ops):
 def test_w8a8_linear_golden(ops, algo):
     """16x576x576 group-scaled W8A8 linear: every quire and bp32 word."""
     g = golden("w8a8_linear")
-    if algo == 2 and not tc_ok(ops, 8, 16, 576, 576):
+    if algo in (2, 3) and not tc_ok(ops, 8, 16, 576, 576):
         pytest.skip("tensor-core path not available for this shape")
     out, q = run(ops, g["xc"], g["wc"], 8, algo, sa=g["sx"], sb=g["sw"], quire_limbs=8)
     assert np.array_equal(q, g["quire"])
@@ -88,7 +88,7 @@ SHAPES = [(1, 1, 1), (1, 1, 0), (3, 5, 7), (17, 33, 65), (64, 48, 130), (129, 13
 @pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_bp8_random_vs_oracle(ops, orc, algo, M, N, K):
-    if algo == 2 and not tc_ok(ops, 8, M, N, K):
+    if algo in (2, 3) and not tc_ok(ops, 8, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(M * 1000 + N * 10 + K)
     A, B = rand_codes(rng, (M, K), 8), rand_codes(rng, (N, K), 8)
@@ -101,7 +101,7 @@ def test_bp8_random_vs_oracle(ops, orc, algo, M, N, K):
 @pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("M,N,K,group", [(5, 7, 300, 128), (40, 70, 576, 128), (130, 66, 1000, 64)])
 def test_bp8_group_scaled_vs_oracle(ops, orc, algo, M, N, K, group):
-    if algo == 2 and not tc_ok(ops, 8, M, N, K):
+    if algo in (2, 3) and not tc_ok(ops, 8, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(K + group)
     X = (rng.standard_normal((M, K)) * np.exp2(rng.integers(-6, 6, (M, 1)))).astype(np.float32)
@@ -134,7 +134,7 @@ def test_bp8_truncating_terms(ops, orc):
 def test_bp16_random_vs_oracle(ops, orc, algo, M, N, K):
     """bp16 quire GEMM on uniformly random codes (exponents up to +-112, so
     products span 2^-224..2^224 and many terms truncate per term)."""
-    if algo == 2 and not tc_ok(ops, 16, M, N, K):
+    if algo in (2, 3) and not tc_ok(ops, 16, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(M + N + K)
     A, B = rand_codes(rng, (M, K), 16), rand_codes(rng, (N, K), 16)
@@ -149,7 +149,7 @@ def test_bp16_normal_range_vs_oracle(ops, orc, algo):
     """bp16 operands ~ N(0,1) * 2^U{-8..8} per row (the large-GEMM distribution)."""
     from bposit_b200 import workloads
     M, N, K = 96, 160, 1024
-    if algo == 2 and not tc_ok(ops, 16, M, N, K):
+    if algo in (2, 3) and not tc_ok(ops, 16, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     A = orc.encode_bp16(workloads.per_row_po2(M, K, 1), True)
     B = orc.encode_bp16(workloads.per_row_po2(N, K, 2), True)
