@@ -95,6 +95,19 @@ int bp_encode_bp16(const float *x, size_t n, int rtne, uint16_t *codes, void *st
  * Replaces bposit_ref.quire256_to_bposit32 (reference/bposit_ref.py:703-722). */
 int bp_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out, void *stream);
 
+/* Round n quires once to bposit16 (truncating, saturating at +-maxpos).
+ * Replaces bposit_ref.quire256_to_bposit16 (reference/bposit_ref.py:620-635),
+ * the out_fmt="bp16" round of dot / dot_at_precision / mixed_precision_sum
+ * (reference/bposit_ref.py:989-992, reference/bposit_fast.py:131-133). */
+int bp_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, void *stream);
+
+/* bposit32 codes produced by a quire round (bp_quire_gemm, bp_quire_to_bp32)
+ * to the bposit16 round of the same quires.  Both rounds truncate the same
+ * regime/exponent/fraction bit string (es = 3 in both), so this is exact:
+ * bp16 = top 15 bits of the bp32 field, saturated the way bp16 saturates.
+ * The bp16 output of an exact GEMM is bp_quire_gemm followed by this. */
+int bp_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, void *stream);
+
 /* Exact quire GEMM: for m < M, n < N
  *   q[m,n] = sum_k trunc0( v(A[m,k]) * v(B[n,k]) * 2^(sa[m,k/group] + sb[n,k/group]) * 2^96 )
  *   out_bp32[m * ldo + n] = bposit32 of q[m,n] (one truncating round)

@@ -105,15 +105,21 @@ def dot_quire(a_codes, b_codes, fmt: str) -> int:
     return int(_limbs_to_ints(q.cpu().numpy())[0, 0])
 
 
+_OUT_FMTS = ("bp16", "bp32")   # reference/bposit_ref.py:989-992
+
+
 def dot(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
-    """Exact dot rounded once to out_fmt (reference/bposit_fast.py:131-133)."""
-    if out_fmt != "bp32":
+    """Exact dot rounded once to out_fmt, "bp32" or "bp16"
+    (reference/bposit_fast.py:131-133)."""
+    if out_fmt not in _OUT_FMTS:
         raise KeyError(out_fmt)
     nb = _nbits(fmt)
     a = _codes_to_dev(a_codes, nb).reshape(1, -1)
     b = _codes_to_dev(b_codes, nb).reshape(1, -1)
     a, b = _broadcast(a, b)
     out, _ = ops.quire_gemm(a, b, nb)
+    if out_fmt == "bp16":
+        out = ops.bp32_to_bp16(out)
     return int(out.cpu().numpy()[0, 0])
 
 
@@ -127,6 +133,17 @@ def matmul_quire(A_codes, B_codes, fmt: str):
     B = _codes_to_dev(B_codes, nb)
     _, q = ops.quire_gemm(A, B, nb, quire_limbs=16)
     return _limbs_to_ints(q.cpu().numpy())
+
+
+def matmul_bp16(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,
+                algo: int = 0):
+    """As matmul_bp32, every output rounded once to bposit16 instead
+    (quire256_to_bposit16, reference/bposit_ref.py:620-635).  uint16 codes."""
+    out = matmul_bp32(_codes_to_dev(A_codes, _nbits(fmt)), _codes_to_dev(B_codes, _nbits(fmt)), fmt,
+                      a_exps=a_exps, b_exps=b_exps, group=group, algo=algo)
+    out = ops.bp32_to_bp16(out)
+    on_dev = isinstance(A_codes, torch.Tensor) and A_codes.is_cuda
+    return out if on_dev else out.cpu().numpy()
 
 
 def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,

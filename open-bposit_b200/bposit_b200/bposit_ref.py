@@ -55,3 +55,13 @@ def quire256_to_bposit32(q):
     limbs = torch.from_numpy(_ints_to_limbs(qs)).to(_device())
     out = ops.quire_to_bp32(limbs).cpu().numpy()
     return int(out[0]) if scalar else out.reshape(np.shape(q))
+
+
+def quire256_to_bposit16(q):
+    """Single round of exact quire(s) (Python ints, 96 fraction bits) to
+    bposit16, truncating (reference/bposit_ref.py:620-635)."""
+    scalar = np.ndim(q) == 0
+    qs = [q] if scalar else list(np.asarray(q, dtype=object).ravel())
+    limbs = torch.from_numpy(_ints_to_limbs(qs)).to(_device())
+    out = ops.quire_to_bp16(limbs).cpu().numpy()
+    return int(out[0]) if scalar else out.reshape(np.shape(q))

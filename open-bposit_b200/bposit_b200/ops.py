@@ -100,6 +100,23 @@ def quire_to_bp32(limbs: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def quire_to_bp16(limbs: torch.Tensor) -> torch.Tensor:
+    """[..., nlimbs] quire limbs -> bposit16 codes (quire256_to_bposit16)."""
+    q = _dev(limbs, "limbs", torch.uint32)
+    nl = q.shape[-1]
+    out = torch.empty(q.shape[:-1], dtype=torch.uint16, device=q.device)
+    _lib.check(_lib.lib().bp_quire_to_bp16(_p(q), nl, out.numel(), _p(out), _stream()))
+    return out
+
+
+def bp32_to_bp16(codes: torch.Tensor) -> torch.Tensor:
+    """bposit32 codes of quire rounds -> the bposit16 rounds of the same quires."""
+    c = _dev(codes, "codes", torch.uint32)
+    out = torch.empty(c.shape, dtype=torch.uint16, device=c.device)
+    _lib.check(_lib.lib().bp_bp32_to_bp16(_p(c), c.numel(), _p(out), _stream()))
+    return out
+
+
 def gemm_workspace_size(fmt, M: int, N: int, K: int, algo: int = 0) -> int:
     return int(_lib.lib().bp_quire_gemm_workspace_size(fmt_bits(fmt), M, N, K, algo))
 

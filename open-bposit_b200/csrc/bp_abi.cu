@@ -146,6 +146,22 @@ int bp_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,
   return launch_quire_to_bp32(limbs, nlimbs, n, out, (cudaStream_t)stream);
 }
 
+int bp_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, void *stream) {
+  g_err[0] = 0;
+  if (nlimbs != 8 && nlimbs != 12 && nlimbs != 16)
+    return set_error(kEInval, "bp_quire_to_bp16: nlimbs must be 8, 12 or 16 (got %d)", nlimbs);
+  if (n && (!limbs || !out)) return set_error(kEInval, "bp_quire_to_bp16: null pointer");
+  TRY(check_device());
+  return launch_quire_to_bp16(limbs, nlimbs, n, out, (cudaStream_t)stream);
+}
+
+int bp_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, void *stream) {
+  g_err[0] = 0;
+  if (n && (!codes || !out)) return set_error(kEInval, "bp_bp32_to_bp16: null pointer");
+  TRY(check_device());
+  return launch_bp32_to_bp16(codes, n, out, (cudaStream_t)stream);
+}
+
 size_t bp_quire_gemm_workspace_size(int fmt, int M, int N, int K, int algo) {
   if ((fmt != 8 && fmt != 16) || M < 0 || N < 0 || K < 0) return 0;
   return gemm_workspace_size(fmt, M, N, K, algo);

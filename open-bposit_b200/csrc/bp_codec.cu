@@ -253,6 +253,28 @@ __global__ void __launch_bounds__(kThreads) k_quire_to_bp32(const uint32_t *__re
   }
 }
 
+// quire256_to_bposit16 of [n, NL] limbs: the bp16 prefix of the bposit32
+// round (bp16_from_bp32).
+template <int NL>
+__global__ void __launch_bounds__(kThreads) k_quire_to_bp16(const uint32_t *__restrict__ limbs, size_t n,
+                                                            uint16_t *__restrict__ out) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) {
+    uint32_t q[NL];
+#pragma unroll
+    for (int j = 0; j < NL; ++j) q[j] = limbs[i * NL + j];
+    out[i] = bp16_from_bp32(bp32_from_limbs<NL>(q));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_bp32_to_bp16(const uint32_t *__restrict__ codes, size_t n,
+                                                           uint16_t *__restrict__ out) {
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) out[i] = bp16_from_bp32(codes[i]);
+}
+
 }  // namespace
 
 // --------------------------------------------------------------- launchers ---
@@ -304,6 +326,24 @@ int launch_group_quantize_bp8(const float *x, int rows, int K, int group, bool n
   else
     k_group_quantize_bp8<false><<<g, kThreads, 0, s>>>(x, rows, K, group, G, compute_scales, maxpos_log2, exps, codes);
   return check_launch("group_quantize_bp8");
+}
+
+int launch_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, cudaStream_t s) {
+  if (n == 0) return kOk;
+  int g = grid_for(n);
+  switch (nlimbs) {
+    case 8: k_quire_to_bp16<8><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    case 12: k_quire_to_bp16<12><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    case 16: k_quire_to_bp16<16><<<g, kThreads, 0, s>>>(limbs, n, out); break;
+    default: return set_error(kEInval, "quire_to_bp16: nlimbs must be 8, 12 or 16 (got %d)", nlimbs);
+  }
+  return check_launch("quire_to_bp16");
+}
+
+int launch_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, cudaStream_t s) {
+  if (n == 0) return kOk;
+  k_bp32_to_bp16<<<grid_for(n), kThreads, 0, s>>>(codes, n, out);
+  return check_launch("bp32_to_bp16");
 }
 
 int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out, cudaStream_t s) {

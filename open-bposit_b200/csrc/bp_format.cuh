@@ -264,4 +264,20 @@ BP_HD uint32_t bp32_from_mag(bool neg, uint64_t hi, uint64_t lo, int lsb_exp) {
   return (neg ? 0x80000000u : 0u) | field;
 }
 
+// quire256_to_bposit16 from the bposit32 of the same quire.  Both rounds
+// truncate (reference/bposit_ref.py:97-135 for bp32; 382-486, mode
+// "truncate", for bp16) the same bit string -- regime, three exponent bits
+// (es = 3 in both formats), fraction -- so the 15-bit bp16 field is the top 15
+// bits of the 31-bit bp32 field.  The formats differ only where bp16
+// saturates: total exponent above 112 already gives 15 leading ones; below
+// -112 the top 15 bits are zero and bp16 returns minpos (never zero).
+BP_HD uint16_t bp16_from_bp32(uint32_t c) {
+  if (c == 0u) return 0;
+  const bool neg = (c >> 31) != 0u;
+  const uint32_t f32 = neg ? (0u - c) & 0x7FFFFFFFu : c & 0x7FFFFFFFu;
+  uint32_t f16 = f32 >> 16;
+  if (f16 == 0u) f16 = 1u;
+  return (uint16_t)(neg ? 0x8000u | ((0u - f16) & 0x7FFFu) : f16);
+}
+
 }  // namespace bp

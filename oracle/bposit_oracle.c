@@ -385,6 +385,58 @@ void orc_quire_to_bp32_batch(const uint32_t *limbs, int nlimbs, size_t n, uint32
     for (size_t i = 0; i < n; i++) out[i] = orc_quire_to_bp32(limbs + i * (size_t)nlimbs, nlimbs);
 }
 
+/* quire256_to_bposit16 (reference/bposit_ref.py:620-635): |q| / 2^96 through
+ * encode_bposit16 in its default "truncate" mode, _encode_unsigned
+ * (reference/bposit_ref.py:382-486): regime, up to three exponent bits
+ * (MSB first), fraction bits, cut to the 15-bit field; total_e > 112 ->
+ * maxpos 0x7FFF, total_e < -112 -> minpos 0x0001; negative values take the
+ * two's complement of the field (reference/bposit_ref.py:503-507). */
+static uint16_t q_to_bp16(const quire_t *qin)
+{
+    quire_t q = *qin;
+    int nz = 0;
+    for (int i = 0; i < QL; i++) nz |= q.w[i] != 0;
+    if (!nz) return 0;
+    int sign = q_is_neg(&q);
+    if (sign) q_neg(&q);
+    int msb = -1;
+    for (int i = QL * 32 - 1; i >= 0; i--) if (q_bit(&q, i)) { msb = i; break; }
+    int total_e = msb - QFRAC;
+    uint32_t field;
+    if (total_e > 112) field = 0x7FFF;
+    else if (total_e < -112) field = 0x0001;
+    else {
+        int k = total_e >> 3, e = total_e & 7;
+        int bits[40]; int nb = 0;
+        if (k >= 0) { for (int i = 0; i < k + 1; i++) bits[nb++] = 1; bits[nb++] = 0; }
+        else { for (int i = 0; i < -k; i++) bits[nb++] = 0; bits[nb++] = 1; }
+        if (nb >= 15) nb = 15;
+        else {
+            for (int i = 2; i >= 0; i--) { bits[nb++] = (e >> i) & 1; if (nb == 15) break; }
+            int pos = msb - 1;
+            while (nb < 16) { bits[nb++] = pos >= 0 ? q_bit(&q, pos) : 0; pos--; }
+            nb = 15;
+        }
+        uint32_t out = 0;
+        for (int i = 0; i < nb; i++) out = (out << 1) | (uint32_t)bits[i];
+        out <<= (15 - nb);
+        field = out & 0x7FFF;
+    }
+    if (sign) field = ((~field) + 1u) & 0x7FFF;
+    return (uint16_t)(((uint32_t)sign << 15) | field);
+}
+
+void orc_quire_to_bp16_batch(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out)
+{
+    for (size_t i = 0; i < n; i++) {
+        const uint32_t *l = limbs + i * (size_t)nlimbs;
+        quire_t q;
+        uint32_t fill = (l[nlimbs - 1] >> 31) ? 0xFFFFFFFFu : 0u;
+        for (int j = 0; j < QL; j++) q.w[j] = j < nlimbs ? l[j] : fill;
+        out[i] = q_to_bp16(&q);
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* Per-group power-of-two scale: s = ceil(log2(absmax / maxpos_bp8)) with    */
 /* maxpos_bp8 = 2^24 (reference/bposit_ref.py:226-227), i.e.                 */

@@ -38,6 +38,7 @@ def lib() -> ctypes.CDLL:
         L.orc_quantize_bp8_f64.argtypes = [vp, sz, i32, vp]
         L.orc_encode_bp16.argtypes = [vp, sz, i32, vp]
         L.orc_quire_to_bp32_batch.argtypes = [vp, i32, sz, vp]
+        L.orc_quire_to_bp16_batch.argtypes = [vp, i32, sz, vp]
         L.orc_group_scales.argtypes = [vp, i32, i32, i32, i32, vp]
         L.orc_quantize_bp8_grouped.argtypes = [vp, i32, i32, i32, vp, i32, vp]
         L.orc_quire_gemm.argtypes = [i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, i32, i32]
@@ -106,6 +107,16 @@ def quire_to_bp32(limbs: np.ndarray) -> np.ndarray:
     n, nl = limbs.shape
     out = np.empty(n, np.uint32)
     lib().orc_quire_to_bp32_batch(_p(limbs), nl, n, _p(out))
+    return out
+
+
+def quire_to_bp16(limbs: np.ndarray) -> np.ndarray:
+    """quire256_to_bposit16 (reference/bposit_ref.py:620-635) over [n, nlimbs]
+    little-endian uint32 two's-complement limbs."""
+    limbs = np.ascontiguousarray(limbs, dtype=np.uint32)
+    n, nl = limbs.shape
+    out = np.empty(n, np.uint16)
+    lib().orc_quire_to_bp16_batch(_p(limbs), nl, n, _p(out))
     return out
 
 

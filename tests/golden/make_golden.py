@@ -25,6 +25,8 @@ Fixtures
                        rule of dot_at_precision and quire256_to_bposit32
   quantize_w8a8.npz    bposit_quantize.quantize_w8a8 on examples/smoke_test.sh's
                        W[16,32] / X[4,32] (seeds 0 / 1)
+  quire_bp16.npz       quire256_to_bposit16 on the encoder-vector quires plus
+                       saturation / regime-edge / seeded quires
 """
 from __future__ import annotations
 
@@ -248,6 +250,28 @@ def main():
         np.savez_compressed(HERE / "w8a8_linear.npz", X=X, W=W, sx=sx, sw=sw, xc=xc, wc=wc,
                             bp32=out, quire=quires)
         print("w8a8_linear", out.shape, f"{time.time()-t0:.1f}s")
+
+    if want("quire_bp16"):
+        # the encoder-vector quires are already in encoder_vectors.npz: store
+        # only their bp16 rounds, plus the extra quires with theirs
+        ev = np.load(HERE / "encoder_vectors.npz")
+        qs = [sum(int(w) << (32 * i) for i, w in enumerate(row)) for row in ev["quire"]]
+        qs = [q - (1 << 256) if q >> 255 else q for q in qs]
+        ev16 = np.array([bp.quire256_to_bposit16(q) & 0xFFFF for q in qs], np.uint16)
+        rng = random.Random(16)
+        extra = [0, 1, -1, (1 << 255) - 1, -(1 << 255)]
+        for t in range(0, 255):             # every power of two and its neighbours (all fit 256 bits)
+            for d in (-1, 0, 1):
+                v = (1 << t) + d
+                extra += [v, -v]
+        for _ in range(6000):               # seeded magnitudes over the whole quire
+            nb = rng.randrange(1, 256)
+            v = rng.getrandbits(nb)
+            extra.append(-v if rng.random() < 0.5 else v)
+        out = np.array([bp.quire256_to_bposit16(q) & 0xFFFF for q in extra], np.uint16)
+        limbs = np.array([to_limbs(q & ((1 << 256) - 1), 8) for q in extra], np.uint32)
+        np.savez_compressed(HERE / "quire_bp16.npz", ev_bp16=ev16, quire=limbs, bp16=out)
+        print("quire_bp16", len(qs) + len(extra), f"{time.time()-t0:.1f}s")
 
     if want("quantize_w8a8"):
         W = np.random.default_rng(0).standard_normal((16, 32)) * 0.05

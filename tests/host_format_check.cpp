@@ -3,7 +3,8 @@
 // and compares it with the CPU oracle (oracle/bposit_oracle.c) over every
 // non-negative fp32 bit pattern (bp8 quantize, both modes), a strided sweep
 // of all fp32 patterns (bp16 encode, both modes), every bp8 / bp16 code
-// (decode) and random 128-bit magnitudes (bp32 round).  Test-only.
+// (decode) and random 128-bit magnitudes (bp32 round, and the bp16 round
+// derived from it).  Test-only.
 //
 // usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32
 #include <stdint.h>
@@ -22,6 +23,7 @@ void orc_quantize_bp8(const float *x, size_t n, int nearest, uint8_t *codes, flo
 uint16_t orc_encode_bp16_one(float x, int rtne);
 void orc_decode_me(int fmt_bits, uint32_t code, int64_t *mant, int *exp);
 uint32_t orc_quire_to_bp32(const uint32_t *limbs, int nlimbs);
+void orc_quire_to_bp16_batch(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out);
 }
 
 static std::atomic<long long> g_bad{0};
@@ -133,7 +135,7 @@ int main(int argc, char **argv) {
       if (bits <= 64) { hi = 0; lo = bits == 64 ? lo : (lo & ((1ull << bits) - 1)); }
       else hi &= bits == 128 ? ~0ull : ((1ull << (bits - 64)) - 1);
       if (!hi && !lo) continue;
-      int shift = (int)(rnd() % 160);     // quire bit of the magnitude's bit 0
+      int shift = (int)(rnd() % 200);     // quire bit of the magnitude's bit 0
       bool neg = rnd() & 1;
       if (bits + shift > 250) continue;
       // quire limbs: (mag << shift), negated if neg, 8 limbs
@@ -149,6 +151,13 @@ int main(int argc, char **argv) {
       uint32_t ref = orc_quire_to_bp32(q, 8);
       uint32_t dev = bp::bp32_from_mag(neg, hi, lo, shift - 96);
       if (ref != dev) { if (bad < 5) fprintf(stderr, "bp32 mismatch bits=%d shift=%d\n", bits, shift); ++bad; }
+      // the bp16 round of the same quire, derived from the bp32 code
+      uint16_t ref16;
+      orc_quire_to_bp16_batch(q, 8, 1, &ref16);
+      if (ref16 != bp::bp16_from_bp32(dev)) {
+        if (bad < 5) fprintf(stderr, "bp16 mismatch bits=%d shift=%d\n", bits, shift);
+        ++bad;
+      }
     }
     g_bad += bad;
   }

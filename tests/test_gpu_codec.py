@@ -199,6 +199,32 @@ def test_quire_to_bp32_encoder_vectors(ops):
         assert np.array_equal(ops.quire_to_bp32(dev(wide)).cpu().numpy(), g["bp32"])
 
 
+def test_quire_to_bp16_golden(ops):
+    """quire256_to_bposit16 (reference/bposit_ref.py:620-635) on the encoder-vector
+    quires and the extra saturation / power-of-two / seeded quires, directly from
+    the limbs and through the bposit32 round."""
+    g = golden("quire_bp16")
+    ev = golden("encoder_vectors")
+    assert np.array_equal(ops.quire_to_bp16(dev(ev["quire"])).cpu().numpy(), g["ev_bp16"])
+    assert np.array_equal(ops.bp32_to_bp16(dev(ev["bp32"])).cpu().numpy(), g["ev_bp16"])
+    assert np.array_equal(ops.quire_to_bp16(dev(g["quire"])).cpu().numpy(), g["bp16"])
+    assert np.array_equal(ops.bp32_to_bp16(ops.quire_to_bp32(dev(g["quire"]))).cpu().numpy(), g["bp16"])
+
+
+def test_dot_out_fmt_bp16(orc):
+    """dot(..., out_fmt="bp16") and matmul_bp16 against the oracle's quires."""
+    from bposit_b200 import bposit_fast as bf
+    rng = np.random.default_rng(5)
+    A = rng.integers(0, 256, (7, 300), dtype=np.uint8)
+    B = rng.integers(0, 256, (5, 300), dtype=np.uint8)
+    _, q = orc.quire_gemm(A, B, 8, nlimbs=16)
+    ref = orc.quire_to_bp16(q.reshape(-1, 16)).reshape(7, 5)
+    assert np.array_equal(bf.matmul_bp16(A, B, "bp8"), ref)
+    assert bf.dot(A[2], B[3], "bp8", out_fmt="bp16") == int(ref[2, 3])
+    with pytest.raises(KeyError):
+        bf.dot(A[0], B[0], "bp8", out_fmt="bp8")
+
+
 def test_bp32_to_f64(ops, orc):
     g = golden("bp32_decode")
     c = g["codes"]

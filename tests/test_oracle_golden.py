@@ -115,3 +115,12 @@ def test_w8a8_linear_group_scaled(orc):
 def test_quantize_w8a8_fixture_present():
     g = golden("quantize_w8a8")
     assert g["Y"].shape == (4, 16)
+
+
+def test_quire_to_bp16(orc):
+    """quire256_to_bposit16 (reference/bposit_ref.py:620-635): the encoder-vector
+    quires plus power-of-two, saturation and seeded quires."""
+    g = golden("quire_bp16")
+    ev = golden("encoder_vectors")
+    assert np.array_equal(orc.quire_to_bp16(ev["quire"]), g["ev_bp16"])
+    assert np.array_equal(orc.quire_to_bp16(g["quire"]), g["bp16"])
