@@ -91,6 +91,22 @@ int bp_quantize_bp8_grouped(const float *x, int rows, int K, int group, int near
  * (reference/bposit_ref.py:382-507).  NaN -> NaR (0x8000), +-inf -> +-maxpos. */
 int bp_encode_bp16(const float *x, size_t n, int rtne, uint16_t *codes, void *stream);
 
+/* Truncating encode of float64 values to the small rungs, one code per byte:
+ * fmt 4 = bposit4 (es 1, encode range 2^+-2), fmt 5 = AI-posit5 (es 1,
+ * 2^+-4).  Replaces encode_bposit4 / encode_aiposit5 on floats and
+ * quantize_vec (reference/bposit_ref.py:852-866, 899-925, 1017-1019),
+ * including the float entry's limit_denominator(10**8) zero cut.  NaN -> NaR. */
+int bp_quantize_small(int fmt, const double *x, size_t n, uint8_t *codes, void *stream);
+
+/* Exact transcode of codes to a wider format: fmt_in 4 or 5 (one code per
+ * byte) or 8, fmt_out 8 (uint8) or 16 (uint16), fmt_out > fmt_in.  Every
+ * value of the narrower formats is a value of the wider one; NaR -> NaR.
+ * With it the bp8 / bp16 quire GEMM computes the reference's small-rung and
+ * mixed-rung quires: dot_at_precision / dot_quire / matmul_quire for bp4 and
+ * aip5 and mixed_precision_sum (reference/bposit_ref.py:995-1035,
+ * reference/bposit_fast.py:22,102-176). */
+int bp_transcode(int fmt_in, int fmt_out, const void *codes, size_t n, void *out, void *stream);
+
 /* Round n quires (nlimbs = 8, 12 or 16 limbs each) once to bposit32.
  * Replaces bposit_ref.quire256_to_bposit32 (reference/bposit_ref.py:703-722). */
 int bp_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out, void *stream);
@@ -192,6 +208,13 @@ int bp_quire_gemm_noalloc(int fmt, const void *A, const void *B, int M, int N, i
  * (reference/bposit_quantize.py:66-68, 88). */
 int bp_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *row_exp,
                    const int32_t *col_exp, double *out, void *stream);
+
+/* The same values plus an optional fp32 column bias [N], each rounded once to
+ * the nearest-even fp32: the hand-off from an exact W8A8 GEMM to the next
+ * fp32 op of a model (the nn.Linear drop-in).  No reference counterpart (the
+ * reference stops at float64). */
+int bp_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *row_exp, const int32_t *col_exp,
+                   const float *bias, float *out, void *stream);
 
 #ifdef __cplusplus
 }

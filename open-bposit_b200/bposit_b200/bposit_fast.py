@@ -7,9 +7,10 @@ computed by the library's sm_100a kernels.
 
 Inputs may be numpy arrays / lists (copied to the current CUDA device, results
 returned as numpy / Python ints like the reference) or CUDA tensors (kept on
-the device, except where the reference returns Python ints).  Formats: "bp8"
-and "bp16" (the reference's fast path has bp4 / aip5 / bp8; the low rungs are
-not part of the B200 path and raise KeyError, as an unknown format does).
+the device, except where the reference returns Python ints).  Formats: the
+reference's "bp4", "aip5" and "bp8", plus "bp16".  Every bp4 / AI-posit5 value
+is a bp8 value, so those codes are widened to bp8 on the device (exactly) and
+go through the bp8 quire GEMM; the quires are the same numbers.
 """
 from __future__ import annotations
 
@@ -19,7 +20,7 @@ import torch
 from . import ops
 
 QUIRE_FRAC_BITS = 96
-_NBITS = {"bp8": 8, "bp16": 16}
+_NBITS = {"bp4": 4, "aip5": 5, "bp8": 8, "bp16": 16}
 
 
 def _nbits(fmt: str) -> int:
@@ -33,15 +34,22 @@ def _device():
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def _gemm_bits(nb: int) -> int:
+    """The quire-GEMM format that carries codes of nb bits (bp4 / aip5 -> bp8)."""
+    return 8 if nb <= 8 else 16
+
+
 def _codes_to_dev(c, nb: int) -> torch.Tensor:
-    dt = torch.uint8 if nb == 8 else torch.uint16
+    """Codes (any integer array-like or CUDA tensor) masked to nb bits, on the
+    device in the GEMM format (_gemm_bits)."""
+    dt = torch.uint8 if nb <= 8 else torch.uint16
     if isinstance(c, torch.Tensor) and c.is_cuda:
-        if c.dtype == dt:
-            return c.contiguous()
-        return (c.to(torch.int64) & ((1 << nb) - 1)).to(dt)
-    a = np.asarray(c, dtype=np.int64) & ((1 << nb) - 1)      # the reference's `& mask`
-    a = a.astype(np.uint8 if nb == 8 else np.uint16)
-    return torch.from_numpy(np.ascontiguousarray(a)).to(_device())
+        t = c.contiguous() if c.dtype == dt and nb in (8, 16) else (c.to(torch.int64) & ((1 << nb) - 1)).to(dt)
+    else:
+        a = np.asarray(c, dtype=np.int64) & ((1 << nb) - 1)      # the reference's `& mask`
+        a = a.astype(np.uint8 if nb <= 8 else np.uint16)
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(_device())
+    return ops.transcode(t, nb, 8) if nb < 8 else t
 
 
 def _limbs_to_ints(q: np.ndarray) -> np.ndarray:
@@ -101,7 +109,7 @@ def dot_quire(a_codes, b_codes, fmt: str) -> int:
     a = _codes_to_dev(a_codes, nb).reshape(1, -1)
     b = _codes_to_dev(b_codes, nb).reshape(1, -1)
     a, b = _broadcast(a, b)
-    _, q = ops.quire_gemm(a, b, nb, quire_limbs=16)
+    _, q = ops.quire_gemm(a, b, _gemm_bits(nb), quire_limbs=16)
     return int(_limbs_to_ints(q.cpu().numpy())[0, 0])
 
 
@@ -117,7 +125,7 @@ def dot(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
     a = _codes_to_dev(a_codes, nb).reshape(1, -1)
     b = _codes_to_dev(b_codes, nb).reshape(1, -1)
     a, b = _broadcast(a, b)
-    out, _ = ops.quire_gemm(a, b, nb)
+    out, _ = ops.quire_gemm(a, b, _gemm_bits(nb))
     if out_fmt == "bp16":
         out = ops.bp32_to_bp16(out)
     return int(out.cpu().numpy()[0, 0])
@@ -131,7 +139,7 @@ def matmul_quire(A_codes, B_codes, fmt: str):
         raise ValueError("matmul_quire expects A[T,K] and B[N,K]")
     A = _codes_to_dev(A_codes, nb)
     B = _codes_to_dev(B_codes, nb)
-    _, q = ops.quire_gemm(A, B, nb, quire_limbs=16)
+    _, q = ops.quire_gemm(A, B, _gemm_bits(nb), quire_limbs=16)
     return _limbs_to_ints(q.cpu().numpy())
 
 
@@ -139,11 +147,10 @@ def matmul_bp16(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None,
                 algo: int = 0):
     """As matmul_bp32, every output rounded once to bposit16 instead
     (quire256_to_bposit16, reference/bposit_ref.py:620-635).  uint16 codes."""
-    out = matmul_bp32(_codes_to_dev(A_codes, _nbits(fmt)), _codes_to_dev(B_codes, _nbits(fmt)), fmt,
-                      a_exps=a_exps, b_exps=b_exps, group=group, algo=algo)
-    out = ops.bp32_to_bp16(out)
-    on_dev = isinstance(A_codes, torch.Tensor) and A_codes.is_cuda
-    return out if on_dev else out.cpu().numpy()
+    out = matmul_bp32(A_codes, B_codes, fmt, a_exps=a_exps, b_exps=b_exps, group=group, algo=algo)
+    on_dev = isinstance(out, torch.Tensor)
+    r = ops.bp32_to_bp16(out if on_dev else torch.from_numpy(out).to(_device()))
+    return r if on_dev else r.cpu().numpy()
 
 
 def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,
@@ -158,5 +165,5 @@ def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None,
     B = _codes_to_dev(B_codes, nb)
     sa = None if a_exps is None else torch.as_tensor(a_exps, dtype=torch.int32).to(A.device).contiguous()
     sb = None if b_exps is None else torch.as_tensor(b_exps, dtype=torch.int32).to(A.device).contiguous()
-    out, _ = ops.quire_gemm(A, B, nb, sa=sa, sb=sb, group=group, algo=algo)
+    out, _ = ops.quire_gemm(A, B, _gemm_bits(nb), sa=sa, sb=sb, group=group, algo=algo)
     return out if on_dev else out.cpu().numpy()

@@ -8,6 +8,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .bposit_quantize import _LIMIT_ZERO
 
 QUIRE_FRAC_BITS = 96   # reference/bposit_ref.py:541
 QUIRE_BITS = 256
@@ -17,16 +18,87 @@ def _device():
     return torch.device("cuda", torch.cuda.current_device())
 
 
+_RUNG_BITS = {"bp4": 4, "aip5": 5, "bp8": 8, "bp16": 16}
+
+
+def _codes_dev(code, nb: int) -> torch.Tensor:
+    """Code(s) masked to nb bits on the device, widened to bp8 for bp4 / aip5."""
+    a = np.asarray(np.asarray(code, dtype=np.int64) & ((1 << nb) - 1))
+    t = torch.from_numpy(np.ascontiguousarray(a.astype(np.uint8 if nb <= 8 else np.uint16)).reshape(a.shape))
+    t = t.to(_device())
+    return ops.transcode(t, nb, 8) if nb < 8 else t
+
+
 def code_value(code, fmt: str):
-    """Exact value of bp8 / bp16 code(s), 0 for zero and NaR
+    """Exact value of bp4 / aip5 / bp8 / bp16 code(s), 0 for zero and NaR
     (reference/bposit_ref.py:1022-1025), as float (exact)."""
-    nb = {"bp8": 8, "bp16": 16}.get(fmt)
+    nb = _RUNG_BITS.get(fmt)
     if nb is None:
         raise KeyError(fmt)
-    a = np.asarray(np.asarray(code, dtype=np.int64) & ((1 << nb) - 1))
-    t = torch.from_numpy(np.ascontiguousarray(a.astype(np.uint8 if nb == 8 else np.uint16)).reshape(a.shape)).to(_device())
-    v = ops.decode(t, nb).cpu().numpy().astype(np.float64)
+    v = ops.decode(_codes_dev(code, nb), 8 if nb <= 8 else 16).cpu().numpy().astype(np.float64)
     return float(v) if v.ndim == 0 else v
+
+
+def quantize_vec(vals, fmt: str) -> list:
+    """Truncating encode of float values to bp4 / aip5 / bp8 codes
+    (reference/bposit_ref.py:1017-1019, the encoders' float entries)."""
+    x = torch.from_numpy(np.ascontiguousarray(np.asarray(vals, dtype=np.float64).ravel())).to(_device())
+    if fmt in ("bp4", "aip5"):
+        c = ops.quantize_small(x, fmt)
+    elif fmt == "bp8":
+        c = ops.quantize_bp8(x, nearest=False)
+        c = torch.where(x.abs() <= _LIMIT_ZERO, torch.zeros_like(c), c)   # limit_denominator(10**8)
+    else:
+        raise KeyError(fmt)
+    return [int(v) for v in c.cpu().numpy()]
+
+
+def _round_out(q_bp32: torch.Tensor, out_fmt: str):
+    if out_fmt == "bp32":
+        return q_bp32
+    if out_fmt == "bp16":
+        return ops.bp32_to_bp16(q_bp32)
+    raise KeyError(out_fmt)
+
+
+def dot_at_precision(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
+    """Exact dot of two code vectors of bp4 / aip5 / bp8, one quire, rounded once
+    to out_fmt (reference/bposit_ref.py:1028-1035)."""
+    nb = {"bp4": 4, "aip5": 5, "bp8": 8}.get(fmt)
+    if nb is None:
+        raise KeyError(fmt)
+    a = _codes_dev(list(a_codes), nb).reshape(1, -1)
+    b = _codes_dev(list(b_codes), nb).reshape(1, -1)
+    n = min(a.shape[1], b.shape[1])                     # zip() semantics
+    out, _ = ops.quire_gemm(a[:, :n].contiguous(), b[:, :n].contiguous(), 8)
+    return int(_round_out(out, out_fmt).cpu().numpy()[0, 0])
+
+
+def mixed_precision_sum(items, out_fmt: str) -> int:
+    """Exact sum of [(code, fmt), ...] over bp4 / aip5 / bp8 / bp16 in one quire,
+    rounded once to out_fmt (reference/bposit_ref.py:995-1002): every item is
+    widened to bp16 and the row is one bp16 quire dot against 1.0."""
+    items = list(items)
+    if not items:
+        return 0
+    dev = _device()
+    fmts = [f for _, f in items]
+    for f in set(fmts):
+        if f not in _RUNG_BITS:
+            raise KeyError(f)
+    row = np.zeros(len(items), np.uint16)
+    for f in set(fmts):
+        nb = _RUNG_BITS[f]
+        idx = np.array([i for i, g in enumerate(fmts) if g == f])
+        c = np.array([int(items[i][0]) & ((1 << nb) - 1) for i in idx], np.int64)
+        if nb == 16:
+            row[idx] = c.astype(np.uint16)
+        else:
+            t = torch.from_numpy(c.astype(np.uint8)).to(dev)
+            row[idx] = ops.transcode(t, nb, 16).cpu().numpy()
+    ones = torch.full((1, len(items)), 0x4000, dtype=torch.uint16, device=dev)   # bp16 1.0
+    out, _ = ops.quire_gemm(torch.from_numpy(row).to(dev).reshape(1, -1), ones, 16)
+    return int(_round_out(out, out_fmt).cpu().numpy()[0, 0])
 
 
 def encode_bposit16(value, mode: str = "truncate"):

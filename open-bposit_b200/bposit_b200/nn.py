@@ -1,0 +1,147 @@
+"""torch.nn drop-in: a Linear layer computed as a bp8 W8A8 exact-quire GEMM.
+
+    lin = BpositLinear.from_linear(torch.nn.Linear(896, 4864).cuda())
+    y = lin(x)                       # x [..., 896] float -> y [..., 4864] float32
+
+Two scale recipes:
+
+* ``scales="w8a8"`` (default) -- the reference's W8A8 recipe
+  (reference/bposit_quantize.py:46-89): one power-of-two exponent per row of
+  W and of X (round(log2(ref)), ref = RMS or the 95th percentile of |x| when
+  that exceeds twice the RMS), truncating bp8 encode of the scaled rows, the
+  exact quire GEMM, one bposit32 round per output, then value * 2^(e_x + e_w)
+  (+ bias) rounded once to the nearest fp32.  The weight exponents come from
+  the host numpy rule (``bposit_quantize.recommended_exponents``); the
+  activation exponents are the same rule in float64 on the device (numpy's
+  summation order is not reproduced: an exponent can differ only when ref lies
+  within an ulp of 2^(k + 1/2), or the 95th percentile within an ulp of twice
+  the RMS).
+* ``scales="group128"`` -- the per-(row, 128-group) power-of-two scales of the
+  benchmark's W8A8 linear: s = ceil(log2(absmax)) - 24, round-to-nearest
+  encode, scales folded into the GEMM's element exponents.  This maps each
+  group's largest value to bp8's maxpos, where the format has no fraction bits,
+  so it is the benchmark's definition rather than an accurate recipe.
+
+The weight is encoded once, on first use or by ``quantize_weight()``.  The
+reference itself has no module API; this wraps its recipe for torch models.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import ops
+from .bposit_quantize import _LIMIT_ZERO, _encode_rows, recommended_exponents
+
+
+def row_exponents(x: torch.Tensor) -> torch.Tensor:
+    """recommended_exponents (reference/bposit_quantize.py:46-63) of the rows of
+    x [rows, K] on the device, float64: int32 [rows]."""
+    v = x.double()
+    K = v.shape[1]
+    rms = torch.sqrt(torch.mean(v * v, dim=1))
+    a = v.abs()
+    # numpy percentile, 'linear': position 0.95 (K - 1) between sorted a[lo], a[lo + 1]
+    pos = 0.95 * (K - 1)
+    lo = int(np.floor(pos))
+    t = pos - lo
+    top = torch.topk(a, K - lo, dim=1, largest=True, sorted=True).values
+    a_lo = top[:, -1]
+    a_hi = top[:, -2] if K - lo >= 2 else a_lo
+    d = a_hi - a_lo
+    p95 = a_hi - d * (1.0 - t) if t >= 0.5 else a_lo + d * t
+    ref = torch.where((p95 > 0) & (p95 > 2 * rms), p95, rms)
+    ex = torch.round(torch.log2(torch.where(rms > 0, ref, torch.ones_like(ref))))
+    return torch.where(rms > 0, ex, torch.zeros_like(ex)).to(torch.int32)
+
+
+def _encode_scaled(x: torch.Tensor, ex: torch.Tensor) -> torch.Tensor:
+    """Truncating bp8 encode of x / 2^ex[row] in float64, with the float entry's
+    limit_denominator(10**8) zero cut (encode_bposit8, reference/bposit_ref.py:258-270)."""
+    xs = x.double() / torch.exp2(ex.to(torch.float64))[:, None]   # exact: power-of-two scale
+    c = ops.quantize_bp8(xs.contiguous(), nearest=False)
+    return torch.where(xs.abs() <= _LIMIT_ZERO, torch.zeros_like(c), c)
+
+
+class BpositLinear(torch.nn.Module):
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, group: int = 128,
+                 scales: str = "w8a8", device=None, dtype=torch.float32):
+        super().__init__()
+        if scales not in ("w8a8", "group128"):
+            raise ValueError(f"unknown scale recipe {scales!r}")
+        self.in_features, self.out_features, self.group, self.scales = in_features, out_features, group, scales
+        self.weight = torch.nn.Parameter(torch.empty((out_features, in_features), device=device, dtype=dtype),
+                                         requires_grad=False)
+        self.bias = (torch.nn.Parameter(torch.zeros(out_features, device=device, dtype=dtype), requires_grad=False)
+                     if bias else None)
+        self._wq = None          # (codes [N, K] uint8, exponents [N, G] int32)
+        self._ws = None          # GEMM workspace, grown on demand
+        self._ws_key = None
+
+    @classmethod
+    def from_linear(cls, lin: torch.nn.Linear, group: int = 128, scales: str = "w8a8") -> "BpositLinear":
+        m = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, group=group, scales=scales,
+                device=lin.weight.device, dtype=torch.float32)
+        with torch.no_grad():
+            m.weight.copy_(lin.weight.float())
+            if lin.bias is not None:
+                m.bias.copy_(lin.bias.float())
+        return m
+
+    @torch.no_grad()
+    def quantize_weight(self):
+        """Encode the weight with the module's scale recipe; call again after
+        changing ``weight``.  Returns (codes [N, K] uint8, exponents int32)."""
+        W = self.weight.float().contiguous()
+        if self.scales == "group128":
+            self._wq = ops.quantize_bp8_grouped(W, group=self.group)
+        else:
+            Wn = W.double().cpu().numpy()
+            ew = recommended_exponents(Wn)
+            self._wq = (_encode_rows(Wn, ew, W.device), torch.from_numpy(ew.astype(np.int32)).to(W.device))
+        return self._wq
+
+    def _workspace(self, M: int, device):
+        key = (M, self.out_features, self.in_features)
+        if self._ws_key != key:
+            need = ops.gemm_workspace_size(8, M, self.out_features, self.in_features)
+            if self._ws is None or self._ws.numel() < need:
+                self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
+            self._ws_key = key
+        return self._ws
+
+    @torch.no_grad()
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"expected last dimension {self.in_features}, got {x.shape[-1]}")
+        if self._wq is None:
+            self.quantize_weight()
+        wc, ws = self._wq
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.in_features).float().contiguous()
+        M = x2.shape[0]
+        bias = None if self.bias is None else self.bias.float().contiguous()
+        if self.scales == "group128":
+            xc, xs = ops.quantize_bp8_grouped(x2, group=self.group)
+            codes, _ = ops.quire_gemm(xc, wc, 8, sa=xs, sb=ws, group=self.group,
+                                      workspace=self._workspace(M, x2.device))
+            y = ops.bp32_to_f32(codes, bias=bias)
+        else:
+            ex = row_exponents(x2)
+            codes, _ = ops.quire_gemm(_encode_scaled(x2, ex), wc, 8, workspace=self._workspace(M, x2.device))
+            y = ops.bp32_to_f32(codes, row_exp=ex, col_exp=ws, bias=bias)
+        return y.reshape(*lead, self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"bias={self.bias is not None}, scales={self.scales}, arithmetic=bp8 W8A8 exact quire")
+
+
+def bpositify(module: torch.nn.Module, group: int = 128, scales: str = "w8a8") -> torch.nn.Module:
+    """Replace every torch.nn.Linear inside `module` by a BpositLinear (in place)."""
+    for name, child in list(module.named_children()):
+        if isinstance(child, torch.nn.Linear):
+            setattr(module, name, BpositLinear.from_linear(child, group=group, scales=scales))
+        else:
+            bpositify(child, group=group, scales=scales)
+    return module

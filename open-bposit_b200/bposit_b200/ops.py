@@ -100,6 +100,30 @@ def quire_to_bp32(limbs: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def quantize_small(x: torch.Tensor, fmt) -> torch.Tensor:
+    """Truncating float64 -> bposit4 ("bp4"/4) or AI-posit5 ("aip5"/5) codes, uint8."""
+    f = {"bp4": 4, "aip5": 5, 4: 4, 5: 5}.get(fmt)
+    if f is None:
+        raise KeyError(fmt)
+    xx = _dev(x, "x", torch.float64)
+    codes = torch.empty(xx.shape, dtype=torch.uint8, device=xx.device)
+    _lib.check(_lib.lib().bp_quantize_small(f, _p(xx), xx.numel(), _p(codes), _stream()))
+    return codes
+
+
+def transcode(codes: torch.Tensor, fmt_in, fmt_out) -> torch.Tensor:
+    """Exact widening of codes: bp4 / aip5 (uint8, one code per byte) or bp8 to
+    bp8 (uint8) or bp16 (uint16); NaR -> NaR."""
+    fi = {"bp4": 4, "aip5": 5, "bp8": 8, 4: 4, 5: 5, 8: 8}.get(fmt_in)
+    fo = {"bp8": 8, "bp16": 16, 8: 8, 16: 16}.get(fmt_out)
+    if fi is None or fo is None or fo <= fi:
+        raise KeyError(f"{fmt_in} -> {fmt_out}")
+    c = _dev(codes, "codes", torch.uint8)
+    out = torch.empty(c.shape, dtype=torch.uint8 if fo == 8 else torch.uint16, device=c.device)
+    _lib.check(_lib.lib().bp_transcode(fi, fo, _p(c), c.numel(), _p(out), _stream()))
+    return out
+
+
 def quire_to_bp16(limbs: torch.Tensor) -> torch.Tensor:
     """[..., nlimbs] quire limbs -> bposit16 codes (quire256_to_bposit16)."""
     q = _dev(limbs, "limbs", torch.uint32)
@@ -228,6 +252,24 @@ def ipc_open(handle: bytes) -> int:
 
 def ipc_close(ptr: int) -> None:
     _lib.check(_lib.lib().bp_ipc_close(ctypes.c_void_p(ptr)))
+
+
+def bp32_to_f32(codes: torch.Tensor, row_exp=None, col_exp=None, bias=None, out=None) -> torch.Tensor:
+    """[M,N] bp32 codes -> fp32 of value * 2^(row_exp[m] + col_exp[n]) + bias[n],
+    rounded once (nearest-even) from the exact value."""
+    c = _dev(codes, "codes", torch.uint32)
+    if c.dim() != 2:
+        raise ValueError("codes must be [M, N]")
+    M, N = c.shape
+    re = None if row_exp is None else _dev(row_exp, "row_exp", torch.int32)
+    ce = None if col_exp is None else _dev(col_exp, "col_exp", torch.int32)
+    b = None if bias is None else _dev(bias, "bias", torch.float32)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=c.device)
+    elif out.dtype != torch.float32 or out.shape != (M, N) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [M, N] float32 tensor")
+    _lib.check(_lib.lib().bp_bp32_to_f32(_p(c), M, N, _p(re), _p(ce), _p(b), _p(out), _stream()))
+    return out
 
 
 def bp32_to_f64(codes: torch.Tensor, row_exp=None, col_exp=None) -> torch.Tensor:

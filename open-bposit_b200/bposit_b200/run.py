@@ -2,10 +2,12 @@
 
     python -m bposit_b200.run gemm M N K [--fmt bp8|bp16] [--group 128] [--calls 3] [--algo 0]
     python -m bposit_b200.run codec N [--fmt bp8|bp16] [--calls 3]
+    python -m bposit_b200.run qwen05 [--batch 8] [--seq 1024] [--layers 24] [--fp32]
 
 ``gemm`` times bp_quire_gemm on operands N(0,1) * 2^U{-8..8} per row (the
 large-GEMM workload's distribution), quantized on the device; ``codec`` times
-the encode and decode kernels on the codec-sweep value mix.  Each runs
+the encode and decode kernels on the codec-sweep value mix; ``qwen05`` times
+the Qwen2.5-0.5B-shaped decoder forward with every linear a BpositLinear.  Each runs
 `--calls` untimed calls and then `--calls` calls timed with CUDA events, so a
 profiler can capture a fixed, small number of launches (e.g. ``ncu -k
 regex:k_quire_gemm_tc -c 1``).
@@ -76,6 +78,17 @@ def run_codec(a) -> str:
             f"decode {dec:.3f} ms ({a.n * b / dec / 1e6:.0f} GB/s)")
 
 
+def run_qwen05(a) -> str:
+    from .forward import qwen05, synthetic_ids
+    model = qwen05(layers=a.layers, bposit=not a.fp32)
+    ids = synthetic_ids(a.batch, a.seq, seed=a.seed)
+    ms = _time(lambda: model(ids), a.calls)
+    tok = a.batch * a.seq
+    return (f"qwen05-shaped forward ({'fp32 torch linears' if a.fp32 else 'bp8 W8A8 exact-quire linears'}) "
+            f"batch={a.batch} seq={a.seq} layers={a.layers}: {ms:.2f} ms, {tok / ms * 1e3:.0f} tokens/s, "
+            f"linears {model.linear_ops(tok) / ms / 1e9:.1f} TOPS over the whole forward")
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m bposit_b200.run")
     sub = ap.add_subparsers(dest="what", required=True)
@@ -89,13 +102,19 @@ def main(argv=None) -> int:
     c = sub.add_parser("codec")
     c.add_argument("n", type=int)
     c.add_argument("--fmt", default="bp8", choices=["bp8", "bp16"])
-    for p in (g, c):
+    w = sub.add_parser("qwen05")
+    w.add_argument("--batch", type=int, default=8)
+    w.add_argument("--seq", type=int, default=1024)
+    w.add_argument("--layers", type=int, default=24)
+    w.add_argument("--fp32", action="store_true", help="plain torch fp32 linears, for comparison")
+    for p in (g, c, w):
         p.add_argument("--calls", type=int, default=3)
         p.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("no CUDA device")
-    print(run_gemm(a) if a.what == "gemm" else run_codec(a), flush=True)
+    fn = {"gemm": run_gemm, "codec": run_codec, "qwen05": run_qwen05}[a.what]
+    print(fn(a), flush=True)
     return 0
 
 

@@ -162,6 +162,23 @@ int bp_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, void *stream
   return launch_bp32_to_bp16(codes, n, out, (cudaStream_t)stream);
 }
 
+int bp_quantize_small(int fmt, const double *x, size_t n, uint8_t *codes, void *stream) {
+  g_err[0] = 0;
+  if (fmt != 4 && fmt != 5) return set_error(kEFmt, "bp_quantize_small: fmt must be 4 or 5 (got %d)", fmt);
+  if (n && (!x || !codes)) return set_error(kEInval, "bp_quantize_small: null pointer");
+  TRY(check_device());
+  return launch_quantize_small(fmt, x, n, codes, (cudaStream_t)stream);
+}
+
+int bp_transcode(int fmt_in, int fmt_out, const void *codes, size_t n, void *out, void *stream) {
+  g_err[0] = 0;
+  if ((fmt_in != 4 && fmt_in != 5 && fmt_in != 8) || (fmt_out != 8 && fmt_out != 16) || fmt_out <= fmt_in)
+    return set_error(kEFmt, "bp_transcode: unsupported %d -> %d (4, 5 -> 8, 16; 8 -> 16)", fmt_in, fmt_out);
+  if (n && (!codes || !out)) return set_error(kEInval, "bp_transcode: null pointer");
+  TRY(check_device());
+  return launch_transcode(fmt_in, fmt_out, codes, n, out, (cudaStream_t)stream);
+}
+
 size_t bp_quire_gemm_workspace_size(int fmt, int M, int N, int K, int algo) {
   if ((fmt != 8 && fmt != 16) || M < 0 || N < 0 || K < 0) return 0;
   return gemm_workspace_size(fmt, M, N, K, algo);
@@ -326,6 +343,15 @@ int bp_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *row_exp, 
   if ((size_t)M * N != 0 && (!codes || !out)) return set_error(kEInval, "bp_bp32_to_f64: null pointer");
   TRY(check_device());
   return launch_bp32_to_f64(codes, M, N, row_exp, col_exp, out, (cudaStream_t)stream);
+}
+
+int bp_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *row_exp, const int32_t *col_exp,
+                   const float *bias, float *out, void *stream) {
+  g_err[0] = 0;
+  if (M < 0 || N < 0) return set_error(kEInval, "bp_bp32_to_f32: negative size");
+  if ((size_t)M * N != 0 && (!codes || !out)) return set_error(kEInval, "bp_bp32_to_f32: null pointer");
+  TRY(check_device());
+  return launch_bp32_to_f32(codes, M, N, row_exp, col_exp, bias, out, (cudaStream_t)stream);
 }
 
 }  // extern "C"

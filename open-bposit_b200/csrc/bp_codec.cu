@@ -385,7 +385,39 @@ __global__ void __launch_bounds__(256) k_bp32_to_f64(const uint32_t *__restrict_
   }
 }
 
+// The same exact value (plus an optional fp32 column bias), rounded once to
+// the nearest-even fp32 -- the hand-off to the next fp32 op of a model.
+__global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict__ codes, int M, int N,
+                                                     const int32_t *__restrict__ re,
+                                                     const int32_t *__restrict__ ce,
+                                                     const float *__restrict__ bias,
+                                                     float *__restrict__ out) {
+  size_t n = (size_t)M * N;
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = tid; i < n; i += stride) {
+    Dec d = decode_posit<32, 3>(codes[i]);
+    double v = 0.0;
+    if (d.kind == 0) {
+      int ex = d.scale - d.fw + (re ? re[i / N] : 0) + (ce ? ce[i % N] : 0);
+      v = scalbn((double)((1u << d.fw) + d.fbits), ex);
+      if (d.sign) v = -v;
+    }
+    if (bias) v += (double)bias[i % N];
+    out[i] = __double2float_rn(v);
+  }
+}
+
 }  // namespace
+
+int launch_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
+                       const float *bias, float *out, cudaStream_t s) {
+  size_t n = (size_t)M * N;
+  if (n == 0) return kOk;
+  size_t blocks = (n + 255) / 256, cap = (size_t)sm_count() * 8;
+  k_bp32_to_f32<<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(codes, M, N, re, ce, bias, out);
+  return check_launch("bp32_to_f32");
+}
 
 int launch_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
                        double *out, cudaStream_t s) {

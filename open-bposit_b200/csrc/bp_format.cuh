@@ -8,6 +8,7 @@
 // fewer than eS bits.  Every helper here is integer-only.
 #pragma once
 #include <stdint.h>
+#include <string.h>
 
 #ifdef __CUDACC__
 #define BP_HD __host__ __device__ __forceinline__
@@ -262,6 +263,63 @@ BP_HD uint32_t bp32_from_mag(bool neg, uint64_t hi, uint64_t lo, int lsb_exp) {
   }
   if (neg) field = (0u - field) & 0x7FFFFFFFu;
   return (neg ? 0x80000000u : 0u) | field;
+}
+
+// ---- the small rungs: bposit4 (es 1, encode range 2^+-2) and AI-posit5
+// (es 1, 2^+-4) (reference/bposit_ref.py:879-940) --------------------------
+// Fraction(x).limit_denominator(10**8) is 0 exactly when |x| < 1/(2*10**8);
+// this is the largest double below that bound (the float entry of the
+// truncating encoders, reference/bposit_ref.py:258-270, 852-856).
+#define BP_LIMIT_ZERO 0x1.5798ee2308c39p-28
+
+// Truncating encode of a double with the reference's generic
+// _encode_unsigned_gen + _encode_gen (reference/bposit_ref.py:806-866):
+// floor(log2|x|) above MAXE -> maxpos, below -MAXE -> minpos, else regime,
+// ES exponent bits (MSB first) and fraction bits cut to the NB-1 bit field;
+// negative values take the field's two's complement.  NaN -> NaR.
+template <int NB, int ES, int MAXE>
+BP_HD uint32_t small_encode(double x) {
+  constexpr int F = NB - 1;
+  constexpr uint32_t fmask = (1u << F) - 1u;
+  if (x != x) return 1u << F;
+  const bool neg = x < 0.0;
+  const double a = neg ? -x : x;
+  if (a <= BP_LIMIT_ZERO) return 0u;
+  uint32_t field;
+  uint64_t u;
+  memcpy(&u, &a, 8);
+  const int be = (int)((u >> 52) & 0x7FF);
+  if (be == 0x7FF) {
+    field = fmask;                      // +-inf
+  } else {
+    const int te = be - 1023;           // a >= 2^-28: normal, floor(log2 a) exact
+    if (te > MAXE) field = fmask;
+    else if (te < -MAXE) field = 1u;
+    else {
+      const int k = te >> ES, e = te & ((1 << ES) - 1);
+      uint32_t bits = 0;
+      int nb = 0;
+      auto push = [&](uint32_t b) {
+        if (nb < F) bits = (bits << 1) | b;
+        ++nb;
+      };
+      if (k >= 0) {
+        for (int i = 0; i <= k; ++i) push(1u);
+        push(0u);
+      } else {
+        for (int i = 0; i < -k; ++i) push(0u);
+        push(1u);
+      }
+      if (nb < F) {
+        for (int i = ES - 1; i >= 0 && nb < F; --i) push((uint32_t)(e >> i) & 1u);
+        for (int i = 51; i >= 0 && nb < F; --i) push((uint32_t)(u >> i) & 1u);   // fraction, truncated
+      }
+      const int kept = nb < F ? nb : F;
+      field = (bits << (F - kept)) & fmask;
+    }
+  }
+  if (neg) field = (0u - field) & fmask;
+  return (neg ? 1u << F : 0u) | field;
 }
 
 // quire256_to_bposit16 from the bposit32 of the same quire.  Both rounds

@@ -36,6 +36,10 @@ int launch_encode_bp16(const float *x, size_t n, bool rtne, uint16_t *codes, cud
 int launch_group_quantize_bp8(const float *x, int rows, int K, int group, bool nearest,
                               bool compute_scales, int maxpos_log2, int32_t *exps, uint8_t *codes,
                               cudaStream_t s);
+int launch_quantize_small(int fmt, const double *x, size_t n, uint8_t *codes, cudaStream_t s);
+int launch_transcode(int fmt_in, int fmt_out, const void *codes, size_t n, void *out, cudaStream_t s);
+int launch_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
+                       const float *bias, float *out, cudaStream_t s);
 int launch_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, cudaStream_t s);
 int launch_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, cudaStream_t s);
 int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,

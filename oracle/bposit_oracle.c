@@ -78,10 +78,15 @@ static int decode_field(uint32_t p, int nbits, int es, int *sign_out, int64_t *m
 
 /* code -> (signed mantissa, exponent); zero and NaR -> mant 0, like code_value
  * (reference/bposit_ref.py:1022-1025) and the bp8 ROM of gen_rtl_vectors.py:289-298. */
+static int es_of(int fmt_bits)
+{
+    return fmt_bits <= 5 ? 1 : (fmt_bits == 8 ? 2 : 3);   /* bp4/aip5: 1, bp8: 2, bp16/bp32: 3 */
+}
+
 void orc_decode_me(int fmt_bits, uint32_t code, int64_t *mant, int *exp)
 {
     int s;
-    int es = fmt_bits == 8 ? 2 : 3;
+    int es = es_of(fmt_bits);
     int r = decode_field(code, fmt_bits, es, &s, mant, exp);
     if (r <= 0) { *mant = 0; *exp = 0; }
 }
@@ -434,6 +439,84 @@ void orc_quire_to_bp16_batch(const uint32_t *limbs, int nlimbs, size_t n, uint16
         uint32_t fill = (l[nlimbs - 1] >> 31) ? 0xFFFFFFFFu : 0u;
         for (int j = 0; j < QL; j++) q.w[j] = j < nlimbs ? l[j] : fill;
         out[i] = q_to_bp16(&q);
+    }
+}
+
+/* Small rungs: _encode_unsigned_gen + _encode_gen (reference/bposit_ref.py:806-866)
+ * in truncate mode for bposit4 (nbits 4, es 1, max_e 2) and AI-posit5
+ * (nbits 5, es 1, max_e 4) on float64 input: |x| whose limit_denominator(10**8)
+ * is 0 gives code 0; floor(log2|x|) > max_e -> maxpos field, < -max_e -> minpos;
+ * else regime bits, es exponent bits, fraction bits cut to nbits-1 bits; the
+ * sign takes the field's two's complement. */
+static uint32_t small_encode_one(double x, int nbits, int es, int max_e)
+{
+    int F = nbits - 1;
+    uint32_t fmask = (1u << F) - 1u;
+    if (x != x) return 1u << F;
+    int sign = x < 0;
+    double a = fabs(x);
+    /* limit_denominator(10**8) is 0 iff a < 1/(2*10^8); the largest double
+     * below that rational is 0x1.5798ee2308c39p-28 */
+    if (a <= 0x1.5798ee2308c39p-28) return 0;
+    uint32_t field;
+    if (isinf(a)) field = fmask;
+    else {
+        int te;
+        double m = frexp(a, &te);   /* a = m 2^te, m in [0.5, 1) */
+        te -= 1;                    /* floor(log2 a) */
+        if (te > max_e) field = fmask;
+        else if (te < -max_e) field = 1u;
+        else {
+            int k = te >= 0 ? te >> es : -((-te + (1 << es) - 1) >> es);   /* floor(te / 2^es) */
+            int e = te - k * (1 << es);
+            int bits[64]; int nb = 0;
+            if (k >= 0) { for (int i = 0; i < k + 1; i++) bits[nb++] = 1; bits[nb++] = 0; }
+            else { for (int i = 0; i < -k; i++) bits[nb++] = 0; bits[nb++] = 1; }
+            if (nb >= F) nb = F;
+            else {
+                for (int i = es - 1; i >= 0; i--) { bits[nb++] = (e >> i) & 1; if (nb == F) break; }
+                double f = 2.0 * m - 1.0;      /* fraction of a / 2^te in [0, 1), exact */
+                while (nb < F + 1) { f *= 2.0; if (f >= 1.0) { bits[nb++] = 1; f -= 1.0; } else bits[nb++] = 0; }
+                nb = F;
+            }
+            uint32_t out = 0;
+            for (int i = 0; i < nb; i++) out = (out << 1) | (uint32_t)bits[i];
+            out <<= (F - nb);
+            field = out & fmask;
+        }
+    }
+    if (sign) field = ((~field) + 1u) & fmask;
+    return ((uint32_t)sign << F) | field;
+}
+
+void orc_quantize_small(int nbits, const double *x, size_t n, uint8_t *codes)
+{
+    int max_e = nbits == 4 ? 2 : 4;
+    for (size_t i = 0; i < n; i++) codes[i] = (uint8_t)small_encode_one(x[i], nbits, 1, max_e);
+}
+
+/* Exact transcode to a wider format: the code of the same value (NaR -> NaR). */
+void orc_transcode(int fmt_in, int fmt_out, const uint8_t *in, size_t n, void *out)
+{
+    int es_in = es_of(fmt_in), es_out = es_of(fmt_out);
+    uint32_t lut[256];
+    for (uint32_t c = 0; c < (1u << fmt_in); c++) {
+        int s; int64_t m; int e;
+        int r = decode_field(c, fmt_in, es_in, &s, &m, &e);
+        uint32_t nar_out = 1u << (fmt_out - 1);
+        if (r == 0) { lut[c] = 0; continue; }
+        if (r < 0) { lut[c] = nar_out; continue; }
+        double v = ldexp((double)m, e);
+        lut[c] = nar_out;
+        for (uint32_t d = 1; d < (1u << fmt_out); d++) {
+            int s2; int64_t m2; int e2;
+            if (decode_field(d, fmt_out, es_out, &s2, &m2, &e2) > 0 && ldexp((double)m2, e2) == v) { lut[c] = d; break; }
+        }
+    }
+    for (size_t i = 0; i < n; i++) {
+        uint32_t v = lut[in[i] & ((1u << fmt_in) - 1u)];
+        if (fmt_out == 8) ((uint8_t *)out)[i] = (uint8_t)v;
+        else ((uint16_t *)out)[i] = (uint16_t)v;
     }
 }
 

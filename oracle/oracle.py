@@ -39,6 +39,8 @@ def lib() -> ctypes.CDLL:
         L.orc_encode_bp16.argtypes = [vp, sz, i32, vp]
         L.orc_quire_to_bp32_batch.argtypes = [vp, i32, sz, vp]
         L.orc_quire_to_bp16_batch.argtypes = [vp, i32, sz, vp]
+        L.orc_quantize_small.argtypes = [i32, vp, sz, vp]
+        L.orc_transcode.argtypes = [i32, i32, vp, sz, vp]
         L.orc_group_scales.argtypes = [vp, i32, i32, i32, i32, vp]
         L.orc_quantize_bp8_grouped.argtypes = [vp, i32, i32, i32, vp, i32, vp]
         L.orc_quire_gemm.argtypes = [i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, i32, i32]
@@ -117,6 +119,24 @@ def quire_to_bp16(limbs: np.ndarray) -> np.ndarray:
     n, nl = limbs.shape
     out = np.empty(n, np.uint16)
     lib().orc_quire_to_bp16_batch(_p(limbs), nl, n, _p(out))
+    return out
+
+
+def quantize_small(x: np.ndarray, nbits: int) -> np.ndarray:
+    """Truncating float64 -> bposit4 (nbits 4) / AI-posit5 (nbits 5) codes, one per
+    byte (encode_bposit4 / encode_aiposit5, reference/bposit_ref.py:806-925)."""
+    x = np.ascontiguousarray(x, dtype=np.float64)
+    out = np.empty(x.shape, np.uint8)
+    lib().orc_quantize_small(nbits, _p(x), x.size, _p(out))
+    return out
+
+
+def transcode(codes: np.ndarray, fmt_in: int, fmt_out: int) -> np.ndarray:
+    """Codes of fmt_in (4, 5 or 8 bits, one per byte) to the fmt_out (8 or 16)
+    codes of the same values (exact; NaR -> NaR)."""
+    c = np.ascontiguousarray(codes, dtype=np.uint8)
+    out = np.empty(c.shape, np.uint8 if fmt_out == 8 else np.uint16)
+    lib().orc_transcode(fmt_in, fmt_out, _p(c), c.size, _p(out))
     return out
 
 

@@ -27,6 +27,9 @@ Fixtures
                        W[16,32] / X[4,32] (seeds 0 / 1)
   quire_bp16.npz       quire256_to_bposit16 on the encoder-vector quires plus
                        saturation / regime-edge / seeded quires
+  rungs.npz            bposit4 / AI-posit5: code values, quantize_vec on edge and
+                       seeded floats, dot_at_precision (bp4, aip5, bp8 -> bp32,
+                       bp16) and mixed_precision_sum over bp4/aip5/bp8/bp16 items
 """
 from __future__ import annotations
 
@@ -272,6 +275,46 @@ def main():
         limbs = np.array([to_limbs(q & ((1 << 256) - 1), 8) for q in extra], np.uint32)
         np.savez_compressed(HERE / "quire_bp16.npz", ev_bp16=ev16, quire=limbs, bp16=out)
         print("quire_bp16", len(qs) + len(extra), f"{time.time()-t0:.1f}s")
+
+    if want("rungs"):
+        rng = np.random.default_rng(45)
+        res = {}
+        for fmt, nb in (("bp4", 4), ("aip5", 5)):
+            res[f"{fmt}_values"] = np.array([float(bp.code_value(c, fmt)) for c in range(1 << nb)])
+        edges = [0.0, -0.0, 1.0, 1.5, 3.0, 3.9, 4.0, 7.99, 8.0, 16.0, 17.0, 64.0, 100.0, 1e30, 0.25, 0.2, 0.0625,
+                 0.05, 0.015625, 0.01, 1e-9, 5e-9, 4.999999999999999e-09, 1.0 / 3, 0.375, 0.74, 0.75, 2.0 ** -30]
+        vals = np.array(edges + [-v for v in edges] +
+                        list(rng.standard_normal(3000) * np.exp2(rng.integers(-8, 8, 3000))), np.float64)
+        res["q_in"] = vals
+        for fmt in ("bp4", "aip5", "bp8"):
+            res[f"q_{fmt}"] = np.array(bp.quantize_vec([float(v) for v in vals], fmt), np.uint8)
+        # dot_at_precision on random code vectors
+        for fmt, nb in (("bp4", 4), ("aip5", 5), ("bp8", 8)):
+            L = 40
+            lens = rng.integers(1, 300, L)
+            a = [rng.integers(0, 1 << nb, n) for n in lens]
+            b = [rng.integers(0, 1 << nb, n) for n in lens]
+            res[f"dot_{fmt}_len"] = lens
+            res[f"dot_{fmt}_a"] = np.concatenate(a).astype(np.uint8)
+            res[f"dot_{fmt}_b"] = np.concatenate(b).astype(np.uint8)
+            for of in ("bp32", "bp16"):
+                res[f"dot_{fmt}_{of}"] = np.array(
+                    [bp.dot_at_precision(list(map(int, x)), list(map(int, y)), fmt, of) for x, y in zip(a, b)],
+                    np.uint32)
+        # mixed_precision_sum over all four rungs
+        fm = ("bp4", "aip5", "bp8", "bp16")
+        nbs = (4, 5, 8, 16)
+        lens = rng.integers(1, 200, 60)
+        fi = [rng.integers(0, 4, n) for n in lens]
+        codes = [np.array([rng.integers(0, 1 << nbs[j]) for j in f]) for f in fi]
+        res["mix_len"] = lens
+        res["mix_fmt"] = np.concatenate(fi).astype(np.uint8)
+        res["mix_code"] = np.concatenate(codes).astype(np.uint16)
+        for of in ("bp32", "bp16"):
+            res[f"mix_{of}"] = np.array([bp.mixed_precision_sum([(int(c), fm[j]) for c, j in zip(cs, f)], of)
+                                         for cs, f in zip(codes, fi)], np.uint32)
+        np.savez_compressed(HERE / "rungs.npz", **res)
+        print("rungs", f"{time.time()-t0:.1f}s")
 
     if want("quantize_w8a8"):
         W = np.random.default_rng(0).standard_normal((16, 32)) * 0.05

@@ -6,7 +6,8 @@
 // (decode) and random 128-bit magnitudes (bp32 round, and the bp16 round
 // derived from it).  Test-only.
 //
-// usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32
+// usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32 | small
+#include <math.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -24,6 +25,7 @@ uint16_t orc_encode_bp16_one(float x, int rtne);
 void orc_decode_me(int fmt_bits, uint32_t code, int64_t *mant, int *exp);
 uint32_t orc_quire_to_bp32(const uint32_t *limbs, int nlimbs);
 void orc_quire_to_bp16_batch(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out);
+void orc_quantize_small(int nbits, const double *x, size_t n, uint8_t *codes);
 }
 
 static std::atomic<long long> g_bad{0};
@@ -157,6 +159,33 @@ int main(int argc, char **argv) {
       if (ref16 != bp::bp16_from_bp32(dev)) {
         if (bad < 5) fprintf(stderr, "bp16 mismatch bits=%d shift=%d\n", bits, shift);
         ++bad;
+      }
+    }
+    g_bad += bad;
+  } else if (!strcmp(what, "small")) {
+    // bposit4 / AI-posit5 truncating encode: every fp32 pattern on a stride
+    // (as double) plus random doubles around every binade in range
+    long long bad = 0;
+    std::vector<double> xs;
+    for (uint64_t u = 0; u < 0x100000000ull; u += 4099) xs.push_back((double)f_of((uint32_t)u));
+    for (int it = 0; it < 2000000; ++it) {
+      int e = (int)(rnd() % 24) - 12;
+      double m = 1.0 + (double)(rnd() >> 11) * 0x1p-53;
+      double x = ldexp(m, e);
+      if (rnd() & 1) x = -x;
+      xs.push_back(x);
+    }
+    xs.push_back(0x1.5798ee2308c39p-28);
+    xs.push_back(0x1.5798ee2308c3ap-28);
+    std::vector<uint8_t> ref(xs.size());
+    for (int nb = 4; nb <= 5; ++nb) {
+      orc_quantize_small(nb, xs.data(), xs.size(), ref.data());
+      for (size_t i = 0; i < xs.size(); ++i) {
+        uint32_t dev = nb == 4 ? bp::small_encode<4, 1, 2>(xs[i]) : bp::small_encode<5, 1, 4>(xs[i]);
+        if (dev != ref[i]) {
+          if (bad < 5) fprintf(stderr, "small%d mismatch x=%a dev=%02x ref=%02x\n", nb, xs[i], dev, ref[i]);
+          ++bad;
+        }
       }
     }
     g_bad += bad;

@@ -72,7 +72,7 @@ def test_python_errors_match_reference_types():
     with pytest.raises(KeyError):
         ops.fmt_bits("bp5")
     with pytest.raises(KeyError):
-        bposit_fast.dot_quire([1], [1], "bp4")
+        bposit_fast.dot_quire([1], [1], "bp6")
     with pytest.raises(ValueError):
         bposit_fast.matmul_quire([1, 2], [[1, 2]], "bp8")
 
@@ -90,12 +90,13 @@ def host_check():
     return exe
 
 
-@pytest.mark.parametrize("what", ["dec", "bp32", "q8", "e16"])
+@pytest.mark.parametrize("what", ["dec", "bp32", "q8", "e16", "small"])
 def test_format_logic_matches_oracle_exhaustively(host_check, what):
     """The kernels' format logic (bp_format.cuh) compiled for the host vs the
     oracle: all bp8/bp16 codes; 2M random quires; every non-negative fp32
     pattern for the bp8 quantize table (both modes); a strided full sweep of
-    fp32 patterns plus every binade edge for the bp16 encoder (both modes)."""
+    fp32 patterns plus every binade edge for the bp16 encoder (both modes); a
+    strided fp32 sweep and 2M random doubles for the bposit4 / AI-posit5 encoders."""
     nt = max(1, min(8, len(os.sched_getaffinity(0))))
     r = subprocess.run([host_check, what, str(nt)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr

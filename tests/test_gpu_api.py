@@ -114,3 +114,44 @@ def test_shuffled_tiling_reproducible(api):
         out[j] = bf.quantize_bp8_codes(flat[j], nearest=True)
     assert np.array_equal(c1, bf.quantize_bp8_codes(x0, nearest=True))
     assert np.array_equal(c1, out.reshape(x0.shape))
+
+
+def test_small_rungs_against_reference_vectors():
+    """bposit4 / AI-posit5 through the reference-named API: code_value,
+    quantize_vec, dot_at_precision (bp32 and bp16 out), mixed_precision_sum
+    over bp4/aip5/bp8/bp16, and bposit_fast.matmul_quire / dot for bp4 and aip5."""
+    from bposit_b200 import bposit_fast as bf
+    from bposit_b200 import bposit_ref as br
+    g = golden("rungs")
+    for fmt, nb in (("bp4", 4), ("aip5", 5)):
+        assert np.array_equal(br.code_value(np.arange(1 << nb), fmt), g[f"{fmt}_values"])
+    x = g["q_in"]
+    for fmt in ("bp4", "aip5", "bp8"):
+        assert br.quantize_vec(x, fmt) == [int(v) for v in g[f"q_{fmt}"]], fmt
+    for fmt in ("bp4", "aip5", "bp8"):
+        lens = g[f"dot_{fmt}_len"]
+        off = np.concatenate([[0], np.cumsum(lens)])
+        for i in range(0, len(lens), 3):
+            a = g[f"dot_{fmt}_a"][off[i]:off[i + 1]]
+            b = g[f"dot_{fmt}_b"][off[i]:off[i + 1]]
+            assert br.dot_at_precision(a, b, fmt, "bp32") == int(g[f"dot_{fmt}_bp32"][i])
+            assert br.dot_at_precision(a, b, fmt, "bp16") == int(g[f"dot_{fmt}_bp16"][i])
+            if fmt != "bp8":
+                assert bf.dot(a, b, fmt) == int(g[f"dot_{fmt}_bp32"][i])
+    fm = ("bp4", "aip5", "bp8", "bp16")
+    lens = g["mix_len"]
+    off = np.concatenate([[0], np.cumsum(lens)])
+    for i in range(0, len(lens), 2):
+        items = [(int(c), fm[f]) for c, f in zip(g["mix_code"][off[i]:off[i + 1]], g["mix_fmt"][off[i]:off[i + 1]])]
+        assert br.mixed_precision_sum(items, "bp32") == int(g["mix_bp32"][i]), i
+        assert br.mixed_precision_sum(items, "bp16") == int(g["mix_bp16"][i]), i
+    # matmul_quire on bp4 codes equals the bp8 GEMM of the widened codes
+    rng = np.random.default_rng(3)
+    A = rng.integers(0, 16, (5, 70))
+    B = rng.integers(0, 16, (4, 70))
+    q4 = bf.matmul_quire(A, B, "bp4")
+    from oracle import oracle as orc
+    _, q = orc.quire_gemm(orc.transcode(A.astype(np.uint8), 4, 8), orc.transcode(B.astype(np.uint8), 4, 8), 8,
+                          nlimbs=16)
+    assert all(int(q4[i, j]) == int.from_bytes(q[i, j].tobytes(), "little", signed=True)
+               for i in range(5) for j in range(4))

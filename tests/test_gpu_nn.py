@@ -1,0 +1,84 @@
+"""The torch.nn drop-in (BpositLinear) and the Qwen2.5-0.5B-shaped forward built
+on it, against the oracle: every checked output equals the oracle's W8A8
+quire GEMM (the reference's per-row recipe, or the per-group-128 one), one
+bposit32 round, exact value * scale + bias rounded to the nearest fp32."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def oracle_linear(orc, X: np.ndarray, W: np.ndarray, bias, scales: str = "w8a8", group: int = 128) -> np.ndarray:
+    """The oracle's output of BpositLinear for rows X[M, K] (fp32 values)."""
+    if scales == "group128":
+        xs = orc.group_scales(X, group)
+        ws = orc.group_scales(W, group)
+        xc = orc.quantize_bp8_grouped(X, xs, group, True)
+        wc = orc.quantize_bp8_grouped(W, ws, group, True)
+        v = orc.bp32_to_double(orc.quire_gemm(xc, wc, 8, sa=xs, sb=ws, group=group))
+    else:
+        from bposit_b200.bposit_quantize import recommended_exponents
+        X64, W64 = X.astype(np.float64), W.astype(np.float64)
+        ex, ew = recommended_exponents(X64), recommended_exponents(W64)
+
+        def enc(M, e):
+            s = M / np.exp2(e.astype(np.float64))[:, None]
+            c = orc.quantize_bp8_f64(s, nearest=False)
+            return np.where(np.abs(s) <= 4.999999999999999e-09, 0, c).astype(np.uint8)
+
+        v = orc.bp32_to_double(orc.quire_gemm(enc(X64, ex), enc(W64, ew), 8))
+        v = v * np.exp2((ex[:, None] + ew[None, :]).astype(np.float64))
+    if bias is not None:
+        v = v + np.asarray(bias, np.float64)[None, :]
+    return v.astype(np.float32)
+
+
+@pytest.mark.parametrize("scales", ["w8a8", "group128"])
+@pytest.mark.parametrize("M,K,N,bias", [(37, 576, 200, True), (5, 1536, 576, False), (130, 896, 1152, True)])
+def test_bposit_linear_matches_oracle(orc, M, K, N, bias, scales):
+    from bposit_b200.bposit_quantize import recommended_exponents
+    from bposit_b200.nn import BpositLinear, row_exponents
+    torch.manual_seed(M)
+    lin = torch.nn.Linear(K, N, bias=bias).cuda()
+    x = torch.randn(M, K, device="cuda")
+    x[torch.rand(M, K, device="cuda") < 0.01] *= 20.0
+    y = BpositLinear.from_linear(lin, scales=scales)(x)
+    xn = x.cpu().numpy()
+    assert np.array_equal(row_exponents(x).cpu().numpy(), recommended_exponents(xn.astype(np.float64)))
+    ref = oracle_linear(orc, xn, lin.weight.detach().cpu().numpy(),
+                        None if not bias else lin.bias.detach().cpu().numpy(), scales)
+    assert y.dtype == torch.float32
+    assert np.array_equal(y.cpu().numpy(), ref)
+
+
+def test_qwen_shaped_forward_linears_match_oracle(orc):
+    from bposit_b200.forward import qwen05, synthetic_ids
+    from bposit_b200.nn import BpositLinear
+    model = qwen05(layers=2)
+    ids = synthetic_ids(1, 48, seed=1)
+    captured = []
+
+    def hook(mod, inp, out):
+        captured.append((mod, inp[0].detach().reshape(-1, mod.in_features).clone(),
+                         out.detach().reshape(-1, mod.out_features).clone()))
+
+    hs = [m.register_forward_hook(hook) for m in model.modules() if isinstance(m, BpositLinear)]
+    h = model(ids)
+    for x in hs:
+        x.remove()
+    assert torch.isfinite(h).all()
+    assert len(captured) == 8            # qkv, o, gate_up, down per layer
+    rng = np.random.default_rng(0)
+    for mod, x, y in captured:
+        rows = rng.choice(x.shape[0], 6, replace=False)
+        ref = oracle_linear(orc, x[rows].cpu().numpy(), mod.weight.cpu().numpy(),
+                            None if mod.bias is None else mod.bias.cpu().numpy(), mod.scales)
+        assert np.array_equal(y[rows].cpu().numpy(), ref)
+    # sanity against the fp32 model with the same weights (not a parity claim)
+    ref_model = qwen05(layers=2, bposit=False)
+    h32 = ref_model(ids)
+    cos = torch.nn.functional.cosine_similarity(h.flatten(), h32.flatten(), dim=0).item()
+    assert cos > 0.97

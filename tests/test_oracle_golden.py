@@ -124,3 +124,66 @@ def test_quire_to_bp16(orc):
     ev = golden("encoder_vectors")
     assert np.array_equal(orc.quire_to_bp16(ev["quire"]), g["ev_bp16"])
     assert np.array_equal(orc.quire_to_bp16(g["quire"]), g["bp16"])
+
+
+NB = {"bp4": 4, "aip5": 5, "bp8": 8, "bp16": 16}
+
+
+def test_rungs_values_and_transcode(orc):
+    """Every bposit4 / AI-posit5 code: its value (code_value) is the value of its
+    bp8 and bp16 transcodes."""
+    g = golden("rungs")
+    for fmt in ("bp4", "aip5"):
+        codes = np.arange(1 << NB[fmt], dtype=np.uint8)
+        for out in (8, 16):
+            t = orc.transcode(codes, NB[fmt], out)
+            v = orc.decode_f32(t, out).astype(np.float64)
+            assert np.array_equal(v, g[f"{fmt}_values"]), (fmt, out)
+
+
+def test_rungs_quantize(orc):
+    """quantize_vec (reference/bposit_ref.py:1017-1019) for bp4, aip5 and bp8."""
+    g = golden("rungs")
+    x = g["q_in"]
+    assert np.array_equal(orc.quantize_small(x, 4), g["q_bp4"])
+    assert np.array_equal(orc.quantize_small(x, 5), g["q_aip5"])
+    c8 = orc.quantize_bp8_f64(x, nearest=False)
+    c8 = np.where(np.abs(x) <= 4.999999999999999e-09, 0, c8)   # limit_denominator(10**8) zero cut
+    assert np.array_equal(c8, g["q_bp8"])
+
+
+def test_rungs_dot_at_precision(orc):
+    """dot_at_precision (reference/bposit_ref.py:1028-1035) for bp4, aip5, bp8 with
+    bp32 and bp16 outputs: the bp8 quire GEMM on transcoded codes."""
+    g = golden("rungs")
+    for fmt in ("bp4", "aip5", "bp8"):
+        lens = g[f"dot_{fmt}_len"]
+        off = np.concatenate([[0], np.cumsum(lens)])
+        for i in range(len(lens)):
+            a = g[f"dot_{fmt}_a"][off[i]:off[i + 1]]
+            b = g[f"dot_{fmt}_b"][off[i]:off[i + 1]]
+            if fmt != "bp8":
+                a, b = orc.transcode(a, NB[fmt], 8), orc.transcode(b, NB[fmt], 8)
+            out, q = orc.quire_gemm(a[None, :], b[None, :], 8, nlimbs=16)
+            assert int(out[0, 0]) == int(g[f"dot_{fmt}_bp32"][i]), (fmt, i)
+            assert int(orc.quire_to_bp16(q.reshape(1, 16))[0]) == int(g[f"dot_{fmt}_bp16"][i]), (fmt, i)
+
+
+def test_rungs_mixed_precision_sum(orc):
+    """mixed_precision_sum (reference/bposit_ref.py:995-1002) over bp4/aip5/bp8/bp16
+    items: every item transcoded to bp16, one bp16 quire row against 1.0."""
+    g = golden("rungs")
+    fm = (4, 5, 8, 16)
+    lens = g["mix_len"]
+    off = np.concatenate([[0], np.cumsum(lens)])
+    for i in range(len(lens)):
+        f = g["mix_fmt"][off[i]:off[i + 1]]
+        c = g["mix_code"][off[i]:off[i + 1]]
+        row = np.empty(len(c), np.uint16)
+        for j in range(4):
+            m = f == j
+            row[m] = c[m] if fm[j] == 16 else orc.transcode(c[m].astype(np.uint8), fm[j], 16)
+        ones = np.full((1, len(c)), 0x4000, np.uint16)
+        out, q = orc.quire_gemm(row[None, :], ones, 16, nlimbs=16)
+        assert int(out[0, 0]) == int(g["mix_bp32"][i]), i
+        assert int(orc.quire_to_bp16(q.reshape(1, 16))[0]) == int(g["mix_bp16"][i]), i
