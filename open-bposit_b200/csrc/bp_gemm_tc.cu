@@ -40,6 +40,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "bp_gemm_common.cuh"
@@ -110,7 +111,9 @@ struct TcCounters {
 };
 
 struct TcParams {
-  int M, N, K, Kp, nkb, kb_per_chunk, nchunks;
+  int M, N, K, Kp, nkb, kb_per_chunk;
+  int tile0, ntn;              // first linear tile of this launch; tiles along N
+  int split;                   // K chunks per tile in this launch (1: whole tiles)
   const int4 *sta, *stb;
   const int *LA, *LB, *slotA, *slotB;
   const ulonglong2 *CA, *CB;   // tail corrections [slot][other dim], 128-bit
@@ -118,7 +121,7 @@ struct TcParams {
   int64_t ldo;
   uint32_t *quire;
   int nlimbs;
-  ulonglong2 *partial;         // [chunk][M][N] when nchunks > 1
+  ulonglong2 *partial;         // split launch: [tile - tile0][chunk][MM rows][BN cols], 128-bit
   uint32_t *extra_out[kMaxExtraOut];   // peer result matrices (row stride ldo)
   int n_extra;
   int64_t extra_col0;
@@ -377,8 +380,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;      // 0: issues the pair's MMAs
-  const int n0 = (PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x) * C::BN;
-  const int m0 = blockIdx.y * C::MM + (int)rank * BM, chunk = blockIdx.z;
+  // linear tiles, N fastest (consecutive CTAs share an A row block); y = K chunk
+  const int tile = p.tile0 + (PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x);
+  const int n0 = (tile % p.ntn) * C::BN;
+  const int m0 = (tile / p.ntn) * C::MM + (int)rank * BM, chunk = blockIdx.y;
   const int kb0 = chunk * p.kb_per_chunk;
   const int kb1 = min(p.nkb, kb0 + p.kb_per_chunk);
   const int nkb = kb1 - kb0;
@@ -526,8 +531,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       long long Q = 0;
 #pragma unroll
       for (int d = 0; d < C::D; ++d) Q += (long long)(int)v[d][jj] * (1ll << (7 * d));
-      if (p.nchunks > 1) {
-        p.partial[((size_t)chunk * p.M + i) * p.N + j] =
+      if (p.split > 1) {
+        p.partial[(((size_t)(tile - p.tile0) * p.split + chunk) * C::MM + rank * BM + r) * C::BN + c0 + jj] =
             make_ulonglong2((unsigned long long)Q, Q < 0 ? ~0ull : 0ull);
       } else {
         const int2 ls = sLs[c0 + jj];
@@ -546,7 +551,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   }
-  if (p.nchunks == 1) {
+  if (p.split == 1) {
     // the two warps of a lane quarter meet, then each stores half of its rows
     asm volatile("bar.sync %0, 64;" ::"r"(3 + q4) : "memory");
 #pragma unroll 1
@@ -573,12 +578,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 }
 
 // ----------------------------------------------------------- split-K sum ---
-__global__ void __launch_bounds__(256) k_tc_reduce(TcParams p) {
-  size_t n = (size_t)p.M * p.N;
+// Sums the K chunks of the tiles of a split launch and finishes their outputs.
+template <int MM, int BN>
+__global__ void __launch_bounds__(256) k_tc_reduce(TcParams p, int ntiles) {
+  const size_t per_tile = (size_t)MM * BN;
+  const size_t n = (size_t)ntiles * per_tile;
   for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < n; o += (size_t)gridDim.x * blockDim.x) {
-    int i = (int)(o / p.N), j = (int)(o % p.N);
+    const int tl = (int)(o / per_tile);
+    const int rc = (int)(o % per_tile);
+    const int tile = p.tile0 + tl;
+    const int i = (tile / p.ntn) * MM + rc / BN, j = (tile % p.ntn) * BN + rc % BN;
+    if (i >= p.M || j >= p.N) continue;
     unsigned __int128 Q = 0;
-    for (int c = 0; c < p.nchunks; ++c) Q += u128(p.partial[(size_t)c * n + o]);
+    for (int c = 0; c < p.split; ++c) Q += u128(p.partial[((size_t)tl * p.split + c) * per_tile + rc]);
     finish_output(p, i, j, Q, p.sta[i], p.stb[j], p.LA[i], p.LB[j], p.slotA[i], p.slotB[j]);
   }
   if (p.n_extra) __threadfence_system();
@@ -995,7 +1007,7 @@ int make_plane_map(CUtensorMap *m, void *base, int Kp, int rows, int S, int box_
 inline size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
 struct TcLayout {
-  int S, Kp, nkb, kbc, nchunks, capA, capB, pool;
+  int S, Kp, nkb, capA, capB, pool;
   size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, part, total;
 };
 
@@ -1003,31 +1015,46 @@ struct TcLayout {
 // the cap are finished by the fixup kernel instead.
 constexpr size_t kCorrBudget = size_t(512) << 20;
 
-// K blocks per CTA task: at most one exact int32 chunk, and split further
-// when that fills the machine's waves better (cost model: waves x K blocks per
-// task, plus the partial-sum traffic of the split).
-void choose_split(TcLayout &L, int M, int N) {
-  const int exact = (L.S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
-  const int bn = L.S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
-  const long long tiles = (long long)((N + bn - 1) / bn) * ((M + BM - 1) / BM);
-  const int sms = sm_count();
-  const double t_kb = (L.S == 3 ? 18 * 48 : 32 * 48) / 1.9e3;   // microseconds per K block
-  const int min_chunks = (L.nkb + exact - 1) / exact;
-  double best = 1e300;
-  L.kbc = exact;
-  for (int s = min_chunks; s <= min_chunks * 8; ++s) {
-    int kb = (L.nkb + s - 1) / s;
-    if (s > min_chunks && kb < 16) break;
-    int se = (L.nkb + kb - 1) / kb;
-    long long waves = (tiles * se + sms - 1) / sms;
-    double t = (double)waves * (kb * t_kb + 4.0);
-    if (se > 1) t += (double)se * M * N * 32.0 / 5e6 + 5.0;
-    if (t < best * 0.98) {
-      best = t;
-      L.kbc = kb;
-    }
+// Which tiles run whole and which are split along K.  Tiles are linear (N
+// fastest); tiles [0, whole) run whole, tiles [whole, ntiles) in `split`
+// chunks of kbc K blocks each, their 128-bit partials summed by k_tc_reduce.
+//  * K longer than one exact int32 chunk: every tile is split (the minimum).
+//  * otherwise the full waves run whole and only the last, partial wave is
+//    split -- as many ways as fit in one wave -- so the machine stays full to
+//    the end instead of idling through a mostly empty last wave.
+struct TcSchedule {
+  int MM, BN, ntn, ntiles, whole, split, kbc;
+};
+
+int tc_wave_capacity(bool pair);
+
+TcSchedule tc_schedule(int S, int M, int N, int nkb, bool pair) {
+  TcSchedule sc{};
+  sc.MM = pair ? 2 * BM : BM;
+  sc.BN = S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
+  sc.ntn = (N + sc.BN - 1) / sc.BN;
+  sc.ntiles = sc.ntn * ((M + sc.MM - 1) / sc.MM);
+  const int exact = (S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
+  const int min_split = (nkb + exact - 1) / exact;
+  const int P = std::max(1, tc_wave_capacity(pair));
+  if (min_split > 1) {
+    sc.whole = 0;
+    sc.split = min_split;
+  } else {
+    const int R = sc.ntiles % P;
+    int sp = R ? P / R : 1;
+    sp = std::min(sp, std::max(1, nkb / 16));   // keep at least 16 K blocks per chunk
+    sc.split = sp;
+    sc.whole = sp > 1 ? sc.ntiles - R : sc.ntiles;
   }
-  L.nchunks = (L.nkb + L.kbc - 1) / L.kbc;
+  sc.kbc = (nkb + sc.split - 1) / sc.split;
+  sc.split = (nkb + sc.kbc - 1) / sc.kbc;   // every chunk non-empty
+  if (sc.split == 1) sc.whole = sc.ntiles;
+  return sc;
+}
+
+size_t tc_partial_bytes(const TcSchedule &sc) {
+  return sc.whole < sc.ntiles ? 16 * (size_t)(sc.ntiles - sc.whole) * sc.split * sc.MM * sc.BN : 0;
 }
 
 TcLayout tc_layout(int fmt, int M, int N, int K) {
@@ -1035,7 +1062,6 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.S = fmt == 8 ? 3 : 4;
   L.Kp = (K + 127) / 128 * 128;
   L.nkb = L.Kp / BK;
-  choose_split(L, M, N);
   L.capA = (int)std::min<size_t>((size_t)M, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(N, 1))));
   L.capB = (int)std::min<size_t>((size_t)N, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(M, 1))));
   L.pool = std::max(65536, 8 * std::max(M, N));
@@ -1053,43 +1079,107 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.ctr = o; o += 256;
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
-  L.part = o; o += L.nchunks > 1 ? al(16 * (size_t)L.nchunks * M * N) : 0;
+  // room for either form's split tiles (the form is chosen at launch)
+  L.part = o;
+  o += al(std::max(tc_partial_bytes(tc_schedule(L.S, M, N, L.nkb, false)),
+                   tc_partial_bytes(tc_schedule(L.S, M, N, L.nkb, M > BM && BK == 64))));
   L.total = o;
   return L;
 }
 
 template <int S, bool PAIR>
-int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const TcParams &p, cudaStream_t s) {
-  using C = Cfg<S, PAIR>;
+cudaError_t tc_kernel_attr() {
   static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
+  static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg<S, PAIR>::SMEM);
   });
-  if (attr_err != cudaSuccess)
-    return set_error(kECuda, "quire_gemm: cannot set shared memory size: %s", cudaGetErrorString(attr_err));
-  const unsigned nt = (unsigned)((p.N + C::BN - 1) / C::BN);
-  dim3 grid(PAIR ? 2 * nt : nt, (unsigned)((p.M + C::MM - 1) / C::MM), (unsigned)p.nchunks);
-  if (grid.y > 65535u || grid.z > 65535u) return set_error(kERange, "quire_gemm: grid too large");
-  if (!PAIR) {
-    k_quire_gemm_tc<S, false><<<grid, THREADS, C::SMEM, s>>>(ma, mb, p);
-    return check_launch("quire_gemm_tc");
-  }
+  return err;
+}
+
+cudaLaunchConfig_t pair_config(dim3 grid, cudaStream_t s, size_t smem, cudaLaunchAttribute *attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(THREADS);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Tiles (CTAs, or CTA pairs) resident at once: the SM count, or the number of
+// co-resident 2-CTA clusters of the paired kernel on this device (cached).
+int tc_wave_capacity(bool pair) {
+  const int sms = sm_count();
+  if (!pair) return sms;
+  static std::atomic<int> cache[128];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return sms / 2;
+  int v = cache[dev].load();
+  if (v > 0) return v;
+  int n = 0;
+  if (tc_kernel_attr<3, true>() == cudaSuccess) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = pair_config(dim3(2 * 1024, 1, 1), nullptr, Cfg<3, true>::SMEM, attr);
+    if (cudaOccupancyMaxActiveClusters(&n, k_quire_gemm_tc<3, true>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  v = n > 0 ? n : sms / 2;
+  cache[dev].store(v);
+  return v;
+}
+
+// One launch over `ntiles` linear tiles starting at p.tile0, p.split K chunks each.
+template <int S, bool PAIR>
+int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const TcParams &p, int ntiles,
+                          cudaStream_t s) {
+  using C = Cfg<S, PAIR>;
+  cudaError_t attr_err = tc_kernel_attr<S, PAIR>();
+  if (attr_err != cudaSuccess)
+    return set_error(kECuda, "quire_gemm: cannot set shared memory size: %s", cudaGetErrorString(attr_err));
+  dim3 grid((unsigned)((PAIR ? 2 : 1) * ntiles), (unsigned)p.split, 1);
+  if (grid.y > 65535u) return set_error(kERange, "quire_gemm: too many K chunks");
+  if (!PAIR) {
+    k_quire_gemm_tc<S, false><<<grid, THREADS, C::SMEM, s>>>(ma, mb, p);
+    return check_launch("quire_gemm_tc");
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_config(grid, s, C::SMEM, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_quire_gemm_tc<S, true>, ma, mb, p);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm_tc (paired): %s", cudaGetErrorString(e));
   return check_launch("quire_gemm_tc");
+}
+
+template <int S, bool PAIR>
+int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
+                       int grid_reduce, cudaStream_t s) {
+  int rc = kOk;
+  p.ntn = sc.ntn;
+  if (sc.whole > 0) {
+    p.tile0 = 0;
+    p.split = 1;
+    p.kb_per_chunk = p.nkb;
+    rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.whole, s);
+    if (rc) return rc;
+  }
+  if (sc.whole < sc.ntiles) {
+    p.tile0 = sc.whole;
+    p.split = sc.split;
+    p.kb_per_chunk = sc.kbc;
+    rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.ntiles - sc.whole, s);
+    if (rc) return rc;
+    k_tc_reduce<Cfg<S, PAIR>::MM, Cfg<S, PAIR>::BN><<<grid_reduce, 256, 0, s>>>(p, sc.ntiles - sc.whole);
+    rc = check_launch("tc_reduce");
+  }
+  return rc;
 }
 
 }  // namespace
@@ -1115,7 +1205,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   TcCounters *cA = (TcCounters *)(w + L.ctr);
   TcCounters *cB = cA + 1;
   ulonglong2 *CA = (ulonglong2 *)(w + L.CA), *CB = (ulonglong2 *)(w + L.CB);
-  ulonglong2 *part = L.nchunks > 1 ? (ulonglong2 *)(w + L.part) : nullptr;
+  ulonglong2 *part = (ulonglong2 *)(w + L.part);
 
   cudaError_t e = cudaMemsetAsync(cA, 0, 2 * sizeof(TcCounters), s);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(e));
@@ -1169,22 +1259,20 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
 
   TcParams p{};
   p.M = a.M; p.N = a.N; p.K = a.K; p.Kp = L.Kp; p.nkb = L.nkb;
-  p.kb_per_chunk = L.kbc; p.nchunks = L.nchunks;
   p.sta = sta; p.stb = stb; p.LA = LA; p.LB = LB; p.slotA = slotA; p.slotB = slotB;
   p.CA = CA; p.CB = CB;
   p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.partial = part;
   p.n_extra = a.n_extra; p.extra_col0 = a.extra_col0;
   for (int e = 0; e < a.n_extra; ++e) p.extra_out[e] = a.extra_out[e];
-  if (S == 3) rc = pair ? launch_tc_gemm_kernel<3, true>(ma, mb, p, s) : launch_tc_gemm_kernel<3, false>(ma, mb, p, s);
-  else rc = pair ? launch_tc_gemm_kernel<4, true>(ma, mb, p, s) : launch_tc_gemm_kernel<4, false>(ma, mb, p, s);
-  if (rc) return rc;
+  const TcSchedule sc = tc_schedule(S, a.M, a.N, L.nkb, pair);
+  if (tc_partial_bytes(sc) > L.total - L.part) return set_error(kEWorkspace, "quire_gemm: split buffer too small");
   size_t outs = (size_t)a.M * a.N;
   int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);
-  if (L.nchunks > 1) {
-    k_tc_reduce<<<g, 256, 0, s>>>(p);
-    rc = check_launch("tc_reduce");
-    if (rc) return rc;
-  }
+  if (S == 3)
+    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, g, s) : launch_tc_schedule<3, false>(ma, mb, p, sc, g, s);
+  else
+    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, g, s) : launch_tc_schedule<4, false>(ma, mb, p, sc, g, s);
+  if (rc) return rc;
   if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   return check_launch("tc_fixup");

@@ -212,12 +212,25 @@ def test_large_bp8_k65536_row_subsample(ops, orc):
     out, _ = ops.quire_gemm(A, B, 8)
     o = out.cpu().numpy()
     An, Bn = A.cpu().numpy(), B.cpu().numpy()
-    rows = np.array([0, 4095])
+    rows = np.array([0, 3900, 4095])   # the last tiles (last M block, both halves) run K-split
     assert np.array_equal(o[rows], orc.quire_gemm(An[rows], Bn, 8))
     cols = np.arange(1000, 1064)
     assert np.array_equal(o[:64, cols], orc.quire_gemm(An[:64], Bn[cols], 8))
     del A, B, out
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("algo", [2, 3])
+def test_balanced_last_wave(ops, orc, algo):
+    """96 paired (192 single) tiles: one full wave runs whole, the remaining tiles
+    run split along K with 128-bit partials; rows in whole and split tiles."""
+    M, N, K = 2048, 1152, 4096
+    rng = np.random.default_rng(11)
+    A = rand_codes(rng, (M, K), 8)
+    B = rand_codes(rng, (N, K), 8)
+    out, _ = run(ops, A, B, 8, algo)
+    rows = np.array([0, 1000, 1600, 1800, 2000, 2047])
+    assert np.array_equal(out[rows], orc.quire_gemm(A[rows], B, 8))
 
 
 def _device_error():
