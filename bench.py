@@ -3,9 +3,10 @@
 
 Headline (one JSON line on rank 0): bit-exact bp8 quire-GEMM throughput in
 TOPS (2*M*N*K / time) on the large bp8 GEMM M=4096, N=4096, K=65536 with
-operands N(0,1) * 2^U{-8..8} per row (seeded, synthetic), the output dimension
-N sharded over the ranks and the bposit32 result all-gathered by the GEMM
-epilogue itself (NVLink peer stores; --gather nccl for an NCCL all-gather).
+operands N(0,1) * 2^U{-8..8} per row (seeded, synthetic), the output split into
+blocks over a pm x pn grid of ranks (chosen by dist.choose_grid) and the
+bposit32 result all-gathered by the GEMM epilogue itself (NVLink peer stores;
+--gather nccl for N shards and an NCCL all-gather).
 The same line carries the encode/decode sweep (2^28 fp32 per rank) in GB/s.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
@@ -30,9 +31,10 @@ for _p in (REPO, os.path.join(REPO, "open-bposit_b200")):
         sys.path.insert(0, _p)
 
 M_, N_, K_ = 4096, 4096, 65536
-METRIC = "bit-exact bp8 W8A8 quire-GEMM TOPS (bp8 4096x4096x65536, N-sharded)"
+METRIC = "bit-exact bp8 W8A8 quire-GEMM TOPS (bp8 4096x4096x65536)"
 WORKLOAD = ("bp8 exact quire GEMM M=4096 N=4096 K=65536, operands N(0,1)*2^U{-8..8} per row, "
-            "RTN-quantized; one bposit32 round per output; N sharded over ranks, result all-gathered")
+            "RTN-quantized; one bposit32 round per output; output blocks sharded over ranks (pm x pn grid), "
+            "result all-gathered")
 
 
 def load_peaks():
@@ -282,22 +284,30 @@ def run_ours(args):
     A = make_operand(ops, torch, M_, K_, gen, device)
     B = make_operand(ops, torch, N_, K_, gen, device)
     fused = args.gather == "fused"
-    g = (FusedShardedQuireGemm if fused else ShardedQuireGemm)(M_, N_, device, algo=args.algo)
-    n0, n1 = g.plan.bounds
+    if fused:
+        g = FusedShardedQuireGemm(M_, N_, device, algo=args.algo, K=K_)
+        m0, m1, n0, n1 = g.block
+        grid = g.grid
+    else:
+        g = ShardedQuireGemm(M_, N_, device, algo=args.algo)
+        (n0, n1), (m0, m1), grid = g.plan.bounds, (0, M_), (1, world)
+    A_full = A
+    A = A_full[m0:m1].contiguous()
     Bs = B[n0:n1].contiguous()
     del B
     torch.cuda.empty_cache()
-    ws = torch.empty(max(256, ops.gemm_workspace_size(8, M_, n1 - n0, K_, args.algo)), dtype=torch.uint8,
+    ws = torch.empty(max(256, ops.gemm_workspace_size(8, m1 - m0, n1 - n0, K_, args.algo)), dtype=torch.uint8,
                      device=device)
+    peers = [p + 4 * m0 * N_ for p in g.peer_ptrs] if fused else []
 
     def shard_step(A_, B_, ev=None):
-        """One N-sharded GEMM + all-gather; `ev` brackets the GEMM launches."""
+        """One sharded GEMM + all-gather; `ev` brackets the GEMM launches."""
         if fused and world > 1:
             dist.all_reduce(g.flag)
         if ev is not None:
             ev[0].record(stream)
         if fused:
-            ops.quire_gemm_multi(A_, B_, g.result[:, n0:n1], g.peer_ptrs, n0, fmt=8, algo=args.algo,
+            ops.quire_gemm_multi(A_, B_, g.result[m0:m1, n0:n1], peers, n0, fmt=8, algo=args.algo,
                                  workspace=ws)
         else:
             ops.quire_gemm(A_, B_, 8, out=g.local[:, :n1 - n0] if world > 1 else g.result, algo=args.algo,
@@ -348,11 +358,11 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms, kms = float(tt[0]), float(tt[1])
     tops = 2.0 * M_ * N_ * K_ / (ms * 1e-3) / 1e12
-    per_rank_ops = 2.0 * M_ * (n1 - n0) * K_
+    per_rank_ops = 2.0 * (m1 - m0) * (n1 - n0) * K_
     k_tops = per_rank_ops / (kms * 1e-3) / 1e12
     int8_peak = 2.0 * peaks["bf16_tflops"]
     from bposit_b200 import ops as _ops
-    slice_pairs = 9 if _ops.gemm_workspace_size(8, M_, n1 - n0, K_, 2) and args.algo != 1 else None
+    slice_pairs = 9 if _ops.gemm_workspace_size(8, m1 - m0, n1 - n0, K_, 2) and args.algo != 1 else None
 
     # end to end through the public API with host buffers (pinned)
     hA = A.cpu().pin_memory()
@@ -389,7 +399,7 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = max(1, len(os.sched_getaffinity(0)))
-        An = A[:max(64, 4 * threads)].cpu().numpy()
+        An = A_full[:max(64, 4 * threads)].cpu().numpy()
         Bn = Bs.cpu().numpy()
         v, rows, dt = cpu_reference(An, Bn, 15.0, threads)
         cpu = {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
@@ -401,7 +411,7 @@ def run_ours(args):
         with open(tp) as f:
             tj = json.load(f)
         ent = tj.get("quire_gemm_" + ("tc" if args.algo != 1 else "simt"))
-        if ent and ent.get("shape") == [M_, n1 - n0, K_]:
+        if ent and ent.get("shape") == [m1 - m0, n1 - n0, K_]:
             traffic = ent["dram_bytes_per_call"]
 
     if rank == 0:
@@ -411,8 +421,9 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": M_, "N": N_, "K": K_, "fmt": "bp8",
-                       "parallelism": (f"N-shard x{world} + " + ("all-gather fused into the GEMM epilogue "
-                                       "(NVLink peer stores)" if fused else "NCCL all-gather")),
+                       "parallelism": (f"{grid[0]}x{grid[1]} (M x N) block grid over {world} ranks + " +
+                                       ("all-gather fused into the GEMM epilogue (NVLink peer stores)" if fused
+                                        else "NCCL all-gather")),
                        "l2": "inputs 512 MiB > L2 (no flush needed)", "algo": args.algo},
             "roofline": {"bound": "tensor", "achieved": round(k_tops, 3), "peak": round(int8_peak, 1),
                          "unit": "TOPS", "frac": round(k_tops / int8_peak, 5), "traffic": traffic,
@@ -425,7 +436,7 @@ def run_ours(args):
                          "issued_frac": round(k_tops * slice_pairs / int8_peak, 4) if slice_pairs else None,
                          "slice_pairs_per_useful_mac": slice_pairs},
             "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS", "ms_per_step": round(ems, 3),
-                    "h2d_bytes_per_step": int(M_ * K_ + (n1 - n0) * K_),
+                    "h2d_bytes_per_step": int((m1 - m0) * K_ + (n1 - n0) * K_),
                     "d2h_bytes_per_step": int(M_ * N_ * 4)},
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
@@ -450,7 +461,8 @@ def main():
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
-                    help="all-gather of the N-shards: in the GEMM epilogue (peer stores) or NCCL")
+                    help="all-gather of the output blocks: in the GEMM epilogue (peer stores, M x N rank grid) "
+                         "or NCCL (N shards)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

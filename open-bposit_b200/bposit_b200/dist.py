@@ -14,6 +14,9 @@ Two ways to all-gather the blocks:
                             NVLink (peer stores into CUDA-IPC-shared memory);
                             two one-word NCCL all-reduces order the call
                             against the ranks' previous and next use of them.
+                            The ranks may also form a pm x pn grid over
+                            (M, N) blocks (choose_grid), which splits the
+                            per-rank operand preparation of A as well.
 """
 from __future__ import annotations
 
@@ -104,6 +107,41 @@ class ShardedQuireGemm:
         return assemble(self.gathered, self.plan, self.result)
 
 
+def block_bounds(M: int, N: int, grid: tuple[int, int], rank: int) -> tuple[int, int, int, int]:
+    """Output block (m0, m1, n0, n1) of `rank` on a pm x pn rank grid (rank =
+    rm * pn + rn); blocks of ceil(M / pm) rows and ceil(N / pn) columns."""
+    pm, pn = grid
+    m0, m1 = shard_bounds(M, pm, rank // pn)
+    n0, n1 = shard_bounds(N, pn, rank % pn)
+    return m0, m1, n0, n1
+
+
+def choose_grid(world: int, M: int, N: int, K: int, fmt: int = 8, wave: int = 74) -> tuple[int, int]:
+    """The pm x pn rank grid with the smallest modelled per-rank time: every rank
+    prepares its M/pm rows of A and N/pn rows of B (time ~ rows * K), then runs
+    its block's tiles (256 x 96 for bp8, 256 x 64 for bp16) in waves of `wave`
+    tile pairs, the last partial wave split along K across the machine."""
+    bn = 96 if fmt == 8 else 64
+    slices = 9 if fmt == 8 else 16
+    nkb = max(1, -(-K // 128) * 2)
+    best, best_cost = (1, world), None
+    for pm in range(1, world + 1):
+        if world % pm:
+            continue
+        pn = world // pm
+        mr, nr = -(-M // pm), -(-N // pn)
+        prep = (mr + nr) * K * 1.05e-9                    # ~0.28 ms per 4096 x 65536 operand
+        tiles = -(-mr // 256) * -(-nr // bn)
+        W, R = divmod(tiles, wave)
+        sp = min(wave // R, max(1, nkb // 16)) if R else 1
+        waves = W + ((1.0 / sp) if (R and sp > 1) else (1.0 if R else 0.0))
+        gemm = waves * K * slices * bn / 96 * 8.8e-7 / 9      # ~0.52 ms per bp8 tile at K = 65536
+        cost = prep + gemm
+        if best_cost is None or cost < best_cost * 0.995:
+            best, best_cost = (pm, pn), cost
+    return best
+
+
 class FusedShardedQuireGemm:
     """N-sharded quire GEMM with the all-gather fused into the GEMM epilogue.
 
@@ -120,13 +158,20 @@ class FusedShardedQuireGemm:
     """
 
     def __init__(self, M: int, N: int, device, group=None, fmt: int = 8, algo: int = 0,
-                 group_size: int = 128):
+                 group_size: int = 128, grid: Optional[tuple[int, int]] = None, K: Optional[int] = None):
         from . import ops
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if self.world - 1 > 8:
             raise ValueError("FusedShardedQuireGemm supports at most 9 ranks")
+        if grid is None:
+            grid = choose_grid(self.world, M, N, K, fmt) if K else (1, self.world)
+        if grid[0] * grid[1] != self.world:
+            raise ValueError(f"grid {grid} does not cover {self.world} ranks")
+        self.grid = tuple(grid)
+        self.M, self.N = M, N
+        self.block = block_bounds(M, N, self.grid, self.rank)   # (m0, m1, n0, n1)
         self.plan = ShardPlan(M, N, self.world, self.rank)
         self.fmt, self.algo, self.group_size = fmt, algo, group_size
         dev = torch.device(device)
@@ -144,21 +189,26 @@ class FusedShardedQuireGemm:
                         self.peer_ptrs.append(ops.ipc_open(h))
         self.workspace = None
 
-    def __call__(self, A: torch.Tensor, B_shard: torch.Tensor, sa=None, sb_shard=None) -> torch.Tensor:
+    def __call__(self, A_block: torch.Tensor, B_block: torch.Tensor, sa=None, sb=None) -> torch.Tensor:
+        """A_block = A[m0:m1], B_block = B[n0:n1] (and their group exponents) for
+        this rank's block (m0, m1, n0, n1) = self.block; with a 1 x world grid
+        A_block is all of A."""
         from . import ops
         if self.result is None:
             raise RuntimeError("FusedShardedQuireGemm is closed")
-        n0, n1 = self.plan.bounds
-        if B_shard.shape[0] != n1 - n0:
-            raise ValueError(f"B shard has {B_shard.shape[0]} rows, rank {self.rank} owns {n1 - n0}")
+        m0, m1, n0, n1 = self.block
+        if A_block.shape[0] != m1 - m0 or B_block.shape[0] != n1 - n0:
+            raise ValueError(f"rank {self.rank} owns rows [{m0}, {m1}) of A and [{n0}, {n1}) of B, got "
+                             f"{A_block.shape[0]} and {B_block.shape[0]}")
         if self.world > 1:
             dist.all_reduce(self.flag, group=self.group)
-        if n1 > n0:
+        if m1 > m0 and n1 > n0:
             if self.workspace is None:
-                need = ops.gemm_workspace_size(self.fmt, A.shape[0], n1 - n0, A.shape[1], self.algo)
-                self.workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=A.device)
-            ops.quire_gemm_multi(A, B_shard, self.result[:, n0:n1], self.peer_ptrs, n0, fmt=self.fmt, sa=sa,
-                                 sb=sb_shard, group=self.group_size, algo=self.algo, workspace=self.workspace)
+                need = ops.gemm_workspace_size(self.fmt, m1 - m0, n1 - n0, A_block.shape[1], self.algo)
+                self.workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=A_block.device)
+            peers = [p + 4 * m0 * self.N for p in self.peer_ptrs]     # row m0 of every peer's result
+            ops.quire_gemm_multi(A_block, B_block, self.result[m0:m1, n0:n1], peers, n0, fmt=self.fmt, sa=sa,
+                                 sb=sb, group=self.group_size, algo=self.algo, workspace=self.workspace)
         if self.world > 1:
             dist.all_reduce(self.flag, group=self.group)
         return self.result

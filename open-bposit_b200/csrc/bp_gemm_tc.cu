@@ -699,6 +699,32 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
     // chunk when group scales are present).
     int lo = 0x3FFFFFFF, hi = -0x3FFFFFFF, nz = 0;
     const bool chunk_groups = sc != nullptr && (group % EPT) == 0;
+    if (FMT == 8 && sc == nullptr && vec) {
+      // unscaled bp8: running byte-wise min / max of the code magnitudes, four
+      // codes per SIMD op; zero and NaR (low 7 bits 0) count as 0xFF for the
+      // minimum and 0 for the maximum.  Decoded once at the end.
+      uint32_t mnw = 0xFFFFFFFFu, mxw = 0u;
+      for (int k0 = threadIdx.x * 16; k0 < K; k0 += blockDim.x * 16) {
+        const uint4 cw = *(const uint4 *)((const uint8_t *)codes + rb + k0);
+        const uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t w = ws[q];
+          const uint32_t neg = __vcmpgeu4(w, 0x80808080u);
+          const uint32_t mag = __vsub4(w ^ neg, neg);
+          const uint32_t inv = __vcmpeq4(w & 0x7F7F7F7Fu, 0u);
+          mnw = __vminu4(mnw, mag | inv);
+          mxw = __vmaxu4(mxw, mag & ~inv);
+        }
+      }
+      const uint32_t mn = min(min(mnw & 0xFFu, (mnw >> 8) & 0xFFu), min((mnw >> 16) & 0xFFu, mnw >> 24));
+      const uint32_t mx = max(max(mxw & 0xFFu, (mxw >> 8) & 0xFFu), max((mxw >> 16) & 0xFFu, mxw >> 24));
+      if (mx) {
+        lo = dec_lsb(s_dec[mn]);
+        hi = dec_hb(s_dec[mx]);
+        nz = 1;
+      }
+    } else
     for (int k0 = threadIdx.x * EPT; k0 < K; k0 += blockDim.x * EPT) {
       uint32_t c[EPT];
       if (vec) {
@@ -819,17 +845,35 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
               if (pos < TAILCAP) s_tail[pos] = k0 + q;
             }
         }
-#pragma unroll
-        for (int sd = 0; sd < S; ++sd) {
-          const uint32_t sel = (uint32_t)sd | ((uint32_t)(4 + sd) << 4);
-          uint32_t wd[4];
+        if (S == 3) {
+          // 4 x 3 byte transpose per 4 codes: 7 permutes for the three plane words
+          uint32_t wd[3][4];
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
-            uint32_t lo2 = __byte_perm(v[4 * g], v[4 * g + 1], sel);
-            uint32_t hi2 = __byte_perm(v[4 * g + 2], v[4 * g + 3], sel);
-            wd[g] = __byte_perm(lo2, hi2, 0x5410);
+            const uint32_t a01 = __byte_perm(v[4 * g], v[4 * g + 1], 0x5140);      // d0 d0' d1 d1'
+            const uint32_t a23 = __byte_perm(v[4 * g + 2], v[4 * g + 3], 0x5140);
+            const uint32_t b01 = __byte_perm(v[4 * g], v[4 * g + 1], 0x0062);      // d2 d2'
+            const uint32_t b23 = __byte_perm(v[4 * g + 2], v[4 * g + 3], 0x0062);
+            wd[0][g] = __byte_perm(a01, a23, 0x5410);
+            wd[1][g] = __byte_perm(a01, a23, 0x7632);
+            wd[2][g] = __byte_perm(b01, b23, 0x5410);
           }
-          *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+#pragma unroll
+          for (int sd = 0; sd < 3; ++sd)
+            *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[sd][0], wd[sd][1], wd[sd][2], wd[sd][3]);
+        } else {
+#pragma unroll
+          for (int sd = 0; sd < S; ++sd) {
+            const uint32_t sel = (uint32_t)sd | ((uint32_t)(4 + sd) << 4);
+            uint32_t wd[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint32_t lo2 = __byte_perm(v[4 * g], v[4 * g + 1], sel);
+              uint32_t hi2 = __byte_perm(v[4 * g + 2], v[4 * g + 3], sel);
+              wd[g] = __byte_perm(lo2, hi2, 0x5410);
+            }
+            *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+          }
         }
       }
     } else {

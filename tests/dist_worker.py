@@ -46,19 +46,35 @@ def main():
         sbs = None if sb is None else sb[n0:n1].contiguous()
         out = sg(A, Bs, sa, sbs).clone()
         # Fused epilogue all-gather (peer stores); two calls on different A so
-        # the second one overwrites a live result buffer.
-        fg = FusedShardedQuireGemm(M, N, dev, group_size=group or 128)
+        # the second one overwrites a live result buffer; an N-shard grid and,
+        # where the rank count allows, an M x N block grid.
         A2 = A.flip(0).contiguous()
         sa2 = None if sa is None else sa.flip(0).contiguous()
-        fused1 = fg(A, Bs, sa, sbs).clone()
-        fused2 = fg(A2, Bs, sa2, sbs).clone()
-        torch.cuda.synchronize()
-        fg.close()
+        fused1 = fused2 = None
+        grids = [(1, world)] + ([(2, world // 2)] if world % 2 == 0 and world > 2 else []) + \
+                ([(world, 1)] if world > 1 else [])
+        fused_ok = True
+        for grid in grids:
+            fg = FusedShardedQuireGemm(M, N, dev, group_size=group or 128, grid=grid)
+            m0, m1, n0g, n1g = fg.block
+
+            def blk(t, lo, hi):
+                return None if t is None else t[lo:hi].contiguous()
+
+            r1 = fg(blk(A, m0, m1), blk(B, n0g, n1g), blk(sa, m0, m1), blk(sb, n0g, n1g)).clone()
+            r2 = fg(blk(A2, m0, m1), blk(B, n0g, n1g), blk(sa2, m0, m1), blk(sb, n0g, n1g)).clone()
+            torch.cuda.synchronize()
+            fg.close()
+            if fused1 is None:
+                fused1, fused2 = r1, r2
+            else:
+                fused_ok = fused_ok and torch.equal(r1.view(torch.int32), fused1.view(torch.int32)) and \
+                    torch.equal(r2.view(torch.int32), fused2.view(torch.int32))
         ref, _ = ops.quire_gemm(A, B, 8, sa=sa, sb=sb, group=group or 128)
         ref2, _ = ops.quire_gemm(A2, B, 8, sa=sa2, sb=sb, group=group or 128)
         torch.cuda.synchronize()
         eq = lambda x, y: bool(torch.equal(x.view(torch.int32), y.view(torch.int32)))  # noqa: E731
-        ok = [eq(out, ref), eq(fused1, ref), eq(fused2, ref2)]
+        ok = [eq(out, ref), eq(fused1, ref), eq(fused2, ref2), fused_ok]
         flags = torch.tensor([int(all(ok))], device=dev)
         dist.all_reduce(flags, op=dist.ReduceOp.MIN)
         if rank == 0:

@@ -76,3 +76,20 @@ def test_shard_bounds():
             assert spans[0][0] == 0 and spans[-1][1] == N
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert all(0 <= n0 <= n1 <= N for n0, n1 in spans)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 6, 8])
+def test_block_grid_covers_output_once(world):
+    """Every pm x pn grid (and the chosen one) tiles [M, N] exactly once."""
+    from bposit_b200.dist import block_bounds, choose_grid
+    for M, N in ((4096, 4096), (300, 777), (5, 3), (1, 64)):
+        grids = [(pm, world // pm) for pm in range(1, world + 1) if world % pm == 0]
+        chosen = choose_grid(world, M, N, 65536)
+        assert chosen in grids
+        for grid in grids:
+            cover = np.zeros((M, N), np.int32)
+            for r in range(world):
+                m0, m1, n0, n1 = block_bounds(M, N, grid, r)
+                assert 0 <= m0 <= m1 <= M and 0 <= n0 <= n1 <= N
+                cover[m0:m1, n0:n1] += 1
+            assert (cover == 1).all()
