@@ -364,7 +364,8 @@ def run_ours(args):
     from bposit_b200 import ops as _ops
     slice_pairs = 9 if _ops.gemm_workspace_size(8, m1 - m0, n1 - n0, K_, 2) and args.algo != 1 else None
 
-    # end to end through the public API with host buffers (pinned)
+    # end to end with host buffers (pinned): one GPU through bp_quire_gemm_host;
+    # several through H2D of each rank's blocks, the sharded step and a D2H of the result
     hA = A.cpu().pin_memory()
     hB = Bs.cpu().pin_memory()
     hOut = torch.empty((M_, N_), dtype=torch.uint32).pin_memory()
@@ -372,6 +373,10 @@ def run_ours(args):
     dB = torch.empty_like(Bs)
 
     def e2e_step():
+        if world == 1:
+            # the host-buffer C ABI: B streamed in chunks, copies overlapped with the GEMM
+            ops.quire_gemm_host(hA, hB, 8, out=hOut, algo=args.algo)
+            return
         dA.copy_(hA, non_blocking=True)
         dB.copy_(hB, non_blocking=True)
         shard_step(dA, dB)

@@ -145,6 +145,18 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
                   uint32_t *out_bp32, int64_t ldo, uint32_t *out_quire, int quire_limbs,
                   int algo, void *workspace, size_t workspace_bytes, void *stream);
 
+/* bp_quire_gemm on HOST buffers: A, B, sa, sb and out_bp32 are host pointers
+ * (page-locked memory gives full PCIe bandwidth; pageable memory works,
+ * slower).  B is streamed to the device in row chunks while earlier chunks
+ * are multiplied and their bposit32 blocks copied back, so the copies in,
+ * the tensor-core work and the copies out overlap; A is prepared once.  The
+ * call is asynchronous on `stream` like every other entry point: out_bp32 is
+ * complete when the stream is.  Same results as bp_quire_gemm.  Replaces
+ * matmul_quire + quire256_to_bposit32 on numpy arrays
+ * (reference/bposit_fast.py:136-176, reference/bposit_ref.py:703-722). */
+int bp_quire_gemm_host(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
+                       const int32_t *sb, int group, uint32_t *out_bp32, int64_t ldo, int algo, void *stream);
+
 /* bp_quire_gemm whose bposit32 results are also stored, by the GEMM epilogue
  * itself, into n_peer further [M, ldo] matrices at column peer_col0 -- on a
  * multi-GPU node, the full result matrices of the other ranks, reached over

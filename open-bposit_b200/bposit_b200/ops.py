@@ -178,6 +178,37 @@ def quire_gemm(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, gro
     return out, q
 
 
+def quire_gemm_host(A, B, fmt=None, sa=None, sb=None, group: int = 128, out=None, algo: int = 0):
+    """Exact quire GEMM on host arrays (CPU tensors or numpy; page-locked CPU
+    tensors copy fastest): the library streams B to the device in chunks and
+    overlaps the copies with the tensor-core work.  Returns the [M, N] uint32
+    bposit32 codes as a CPU tensor (`out`, if given), complete once the
+    current CUDA stream is synchronized."""
+    def host(x, dtype):
+        t = torch.as_tensor(x)
+        if t.is_cuda:
+            raise ValueError("quire_gemm_host takes host arrays")
+        return t.contiguous() if t.dtype == dtype else t.to(dtype).contiguous()
+    f = fmt_bits(fmt) if fmt is not None else (8 if torch.as_tensor(A).dtype == torch.uint8 else 16)
+    a = host(A, _CODE_DTYPE[f])
+    b = host(B, _CODE_DTYPE[f])
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("quire_gemm_host expects A[M,K] and B[N,K]")
+    M, K = a.shape
+    N = b.shape[0]
+    sa_ = None if sa is None else host(sa, torch.int32)
+    sb_ = None if sb is None else host(sb, torch.int32)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.uint32, pin_memory=True)
+    elif out.is_cuda or out.dtype != torch.uint32 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out must be a host [M, N] uint32 tensor with unit column stride")
+    _lib.check(_lib.lib().bp_quire_gemm_host(f, a.data_ptr(), b.data_ptr(), M, N, K,
+                                             None if sa_ is None else sa_.data_ptr(),
+                                             None if sb_ is None else sb_.data_ptr(), group,
+                                             out.data_ptr(), out.stride(0), algo, _stream()))
+    return out
+
+
 def quire_gemm_multi(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_ptrs, peer_col0: int,
                      fmt=None, sa=None, sb=None, group: int = 128, algo: int = 0, workspace=None):
     """quire_gemm whose bp32 results are also stored into every matrix in

@@ -271,6 +271,20 @@ int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int
   return rc;
 }
 
+int bp_quire_gemm_host(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
+                       const int32_t *sb, int group, uint32_t *out_bp32, int64_t ldo, int algo, void *stream) {
+  g_err[0] = 0;
+  if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_host: fmt must be 8 or 16 (got %d)", fmt);
+  if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_host: negative size");
+  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_host: algo must be 0, 1, 2 or 3");
+  if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_host: group must be > 0 with scales");
+  if (ldo < N) return set_error(kEInval, "bp_quire_gemm_host: ldo (%lld) < N (%d)", (long long)ldo, N);
+  if (M == 0 || N == 0) return kOk;
+  if (!out_bp32 || (K > 0 && (!A || !B))) return set_error(kEInval, "bp_quire_gemm_host: null pointer");
+  TRY(check_device());
+  return launch_quire_gemm_host(fmt, A, B, M, N, K, sa, sb, group, out_bp32, ldo, algo, (cudaStream_t)stream);
+}
+
 int bp_enable_peer_access(int peer_device) {
   g_err[0] = 0;
   int cur = 0;

@@ -10,7 +10,7 @@ namespace bp {
 
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
 int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
-                   cudaStream_t s);
+                   int a_mode, cudaStream_t s);
 size_t gemm_tc_workspace(int fmt, int M, int N, int K);
 bool gemm_tc_supported(int fmt, int M, int N, int K);
 
@@ -83,7 +83,7 @@ size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo) {
   return ws;
 }
 
-int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s) {
+int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s, int a_mode) {
   size_t need_stats = stats_bytes(a.M, a.N);
   if (ws_bytes < need_stats) return set_error(kEWorkspace, "quire_gemm: workspace too small");
   int4 *sta = (int4 *)ws;
@@ -91,8 +91,9 @@ int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cu
   if (use_tc(a, algo)) {   // the tensor-core prep computes the row statistics itself
     size_t need = gemm_tc_workspace(a.fmt, a.M, a.N, a.K);
     if (ws_bytes < need_stats + need) return set_error(kEWorkspace, "quire_gemm: workspace too small");
-    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo == 3, s);
+    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo == 3, a_mode, s);
   }
+  if (a_mode == 2) return kOk;   // the CUDA-core path prepares nothing ahead
   int rc = launch_row_stats(a.fmt, a.A, a.M, a.K, a.sa, a.group, sta, s);
   if (rc) return rc;
   rc = launch_row_stats(a.fmt, a.B, a.N, a.K, a.sb, a.group, stb, s);

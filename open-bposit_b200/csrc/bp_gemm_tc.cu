@@ -1236,8 +1236,14 @@ bool gemm_tc_supported(int fmt, int M, int N, int K) {
 size_t gemm_tc_workspace(int fmt, int M, int N, int K) { return tc_layout(fmt, M, N, K).total; }
 
 // sta / stb are outputs here: the prep kernels write the row statistics.
+// A's preparation (statistics in sta, digit planes, bases, tail lists,
+// counters) can be done alone (a_mode 2) and reused by later calls with the
+// same A, M, K and workspace layout (the same N) that prepare only B (a_mode 1).
 int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
-                   cudaStream_t s) {
+                   int a_mode, cudaStream_t s) {
+  // a_mode 0: prepare A and B and multiply; 1: A already prepared (reuse);
+  // 2: prepare A only
+  const bool reuse_a = a_mode == 1, a_only = a_mode == 2;
   TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K);
   if (ws_bytes < L.total) return set_error(kEWorkspace, "quire_gemm: tensor-core workspace too small");
   char *w = (char *)ws;
@@ -1251,7 +1257,8 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   ulonglong2 *CA = (ulonglong2 *)(w + L.CA), *CB = (ulonglong2 *)(w + L.CB);
   ulonglong2 *part = (ulonglong2 *)(w + L.part);
 
-  cudaError_t e = cudaMemsetAsync(cA, 0, 2 * sizeof(TcCounters), s);
+  cudaError_t e = reuse_a ? cudaMemsetAsync(cB, 0, sizeof(TcCounters), s)
+                          : cudaMemsetAsync(cA, 0, (a_only ? 1 : 2) * sizeof(TcCounters), s);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(e));
   const int sms = sm_count();
   auto prep = [&](const void *codes, int rows, const int32_t *sc, int4 *st, int8_t *planes, int *Lr, int *slot,
@@ -1265,8 +1272,11 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
                                          tails, L.pool, cap, c);
     return check_launch("tc_prep");
   };
-  int rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA);
-  if (rc) return rc;
+  int rc = kOk;
+  if (!reuse_a) {
+    rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA);
+    if (rc || a_only) return rc;
+  }
   rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB);
   if (rc) return rc;
 

@@ -40,6 +40,9 @@ int launch_quantize_small(int fmt, const double *x, size_t n, uint8_t *codes, cu
 int launch_transcode(int fmt_in, int fmt_out, const void *codes, size_t n, void *out, cudaStream_t s);
 int launch_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
                        const float *bias, float *out, cudaStream_t s);
+int launch_quire_gemm_host(int fmt, const void *A_h, const void *B_h, int M, int N, int K, const int32_t *sa_h,
+                           const int32_t *sb_h, int group, uint32_t *out_h, int64_t ldo, int algo,
+                           cudaStream_t s);
 int launch_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, cudaStream_t s);
 int launch_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, cudaStream_t s);
 int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,
@@ -67,6 +70,9 @@ struct GemmArgs {
 
 size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo);
 bool gemm_uses_tc(const GemmArgs &a, int algo);
-int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s);
+// a_mode (tensor-core path): 0 prepare A and B, then multiply; 1 reuse A's
+// preparation from an earlier call on the same workspace; 2 prepare A only.
+int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s,
+                      int a_mode = 0);
 
 }  // namespace bp

@@ -155,3 +155,37 @@ def test_small_rungs_against_reference_vectors():
                           nlimbs=16)
     assert all(int(q4[i, j]) == int.from_bytes(q[i, j].tobytes(), "little", signed=True)
                for i in range(5) for j in range(4))
+
+
+@pytest.mark.parametrize("case", ["chunked", "chunked_groups", "bp16_small", "pageable"])
+def test_quire_gemm_host_buffers(case):
+    """bp_quire_gemm_host (host buffers, B streamed in chunks, A prepared once)
+    gives exactly the device GEMM's codes."""
+    from bposit_b200 import ops
+    rng = np.random.default_rng(7)
+    group = 128
+    if case in ("chunked", "chunked_groups", "pageable"):
+        M, N, K, fmt = 2048, 3000, 16384, 8      # 82 MB of codes: 4 chunks of 768 rows, the last padded
+    else:
+        M, N, K, fmt = 200, 300, 1000, 16
+    dt = np.uint8 if fmt == 8 else np.uint16
+    if case == "chunked_groups":
+        X = torch.randn(M, K, device="cuda")
+        W = torch.randn(N, K, device="cuda") * 0.02
+        A, sa = ops.quantize_bp8_grouped(X, group=group)
+        B, sb = ops.quantize_bp8_grouped(W, group=group)
+    else:
+        A = torch.from_numpy(rng.integers(0, 1 << fmt, (M, K)).astype(dt)).cuda()
+        B = torch.from_numpy(rng.integers(0, 1 << fmt, (N, K)).astype(dt)).cuda()
+        sa = sb = None
+    ref, _ = ops.quire_gemm(A, B, fmt, sa=sa, sb=sb, group=group)
+    if case == "pageable":
+        hA, hB = A.cpu().numpy(), B.cpu().numpy()
+        out = ops.quire_gemm_host(hA, hB, fmt)
+    else:
+        hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
+        hsa = None if sa is None else sa.cpu().pin_memory()
+        hsb = None if sb is None else sb.cpu().pin_memory()
+        out = ops.quire_gemm_host(hA, hB, fmt, sa=hsa, sb=hsb, group=group)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out.view(torch.int32), ref.cpu().view(torch.int32))
