@@ -91,6 +91,17 @@ int bp_quantize_bp8_grouped(const float *x, int rows, int K, int group, int near
  * (reference/bposit_ref.py:382-507).  NaN -> NaR (0x8000), +-inf -> +-maxpos. */
 int bp_encode_bp16(const float *x, size_t n, int rtne, uint16_t *codes, void *stream);
 
+/* The activation side of the reference's W8A8 recipe, per row of x[rows, K]
+ * (fp32): exps[r] = recommended_exponents (round(log2(ref)), ref = the row's
+ * RMS, or its 95th percentile of |x| when that exceeds twice the RMS; 0 for an
+ * all-zero row), computed in float64 on the device, and codes[r, :] = the
+ * truncating bp8 encode of x[r, :] * 2^-exps[r] with encode_bposit8's float
+ * entry zero cut (reference/bposit_quantize.py:46-89,
+ * reference/bposit_ref.py:258-270).  The float64 sum of squares is reduced in
+ * a different order than numpy's, which can change an exponent only when ref
+ * is within an ulp of 2^(k + 1/2) or the percentile within an ulp of 2 RMS. */
+int bp_w8a8_encode_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, void *stream);
+
 /* Truncating encode of float64 values to the small rungs, one code per byte:
  * fmt 4 = bposit4 (es 1, encode range 2^+-2), fmt 5 = AI-posit5 (es 1,
  * 2^+-4).  Replaces encode_bposit4 / encode_aiposit5 on floats and

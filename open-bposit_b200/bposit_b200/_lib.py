@@ -77,6 +77,7 @@ def lib() -> ctypes.CDLL:
             "bp_quantize_small": ([i32, vp, sz, vp, vp], i32),
             "bp_bp32_to_f32": ([vp, i32, i32, vp, vp, vp, vp, vp], i32),
             "bp_quire_gemm_host": ([i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, i64, i32, vp], i32),
+            "bp_w8a8_encode_rows": ([vp, i32, i32, vp, vp, vp], i32),
             "bp_transcode": ([i32, i32, vp, sz, vp, vp], i32),
             "bp_bp32_to_bp16": ([vp, sz, vp, vp], i32),
             "bp_ipc_alloc": ([sz, vp, vp], i32),
@@ -98,6 +99,7 @@ EXPORTED = (
     "bp_version", "bp_last_error", "bp_launch_count", "bp_device_error", "bp_decode", "bp_quantize_bp8", "bp_quantize_bp8_f64",
     "bp_quantize_bp8_grouped", "bp_encode_bp16", "bp_quire_to_bp32", "bp_quire_to_bp16", "bp_bp32_to_bp16",
     "bp_quantize_small", "bp_transcode", "bp_bp32_to_f32", "bp_quire_gemm_host",
+    "bp_w8a8_encode_rows",
     "bp_quire_gemm",
     "bp_quire_gemm_workspace_size", "bp_quire_gemm_multi", "bp_enable_peer_access",
     "bp_ipc_alloc", "bp_ipc_free", "bp_ipc_open", "bp_ipc_close", "bp_quire_gemm_noalloc",

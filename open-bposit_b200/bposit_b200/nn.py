@@ -12,10 +12,11 @@ Two scale recipes:
   exact quire GEMM, one bposit32 round per output, then value * 2^(e_x + e_w)
   (+ bias) rounded once to the nearest fp32.  The weight exponents come from
   the host numpy rule (``bposit_quantize.recommended_exponents``); the
-  activation exponents are the same rule in float64 on the device (numpy's
-  summation order is not reproduced: an exponent can differ only when ref lies
-  within an ulp of 2^(k + 1/2), or the 95th percentile within an ulp of twice
-  the RMS).
+  activations go through one kernel per forward (``ops.w8a8_encode_rows``:
+  the same rule in float64 on the device, then the encode; numpy's summation
+  order is not reproduced, so an exponent can differ only when ref lies within
+  an ulp of 2^(k + 1/2), or the 95th percentile within an ulp of twice the
+  RMS).
 * ``scales="group128"`` -- the per-(row, 128-group) power-of-two scales of the
   benchmark's W8A8 linear: s = ceil(log2(absmax)) - 24, round-to-nearest
   encode, scales folded into the GEMM's element exponents.  This maps each
@@ -127,8 +128,8 @@ class BpositLinear(torch.nn.Module):
                                       workspace=self._workspace(M, x2.device))
             y = ops.bp32_to_f32(codes, bias=bias)
         else:
-            ex = row_exponents(x2)
-            codes, _ = ops.quire_gemm(_encode_scaled(x2, ex), wc, 8, workspace=self._workspace(M, x2.device))
+            xc, ex = ops.w8a8_encode_rows(x2)
+            codes, _ = ops.quire_gemm(xc, wc, 8, workspace=self._workspace(M, x2.device))
             y = ops.bp32_to_f32(codes, row_exp=ex, col_exp=ws, bias=bias)
         return y.reshape(*lead, self.out_features)
 

@@ -100,6 +100,20 @@ def quire_to_bp32(limbs: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def w8a8_encode_rows(x: torch.Tensor):
+    """The reference W8A8 recipe's activation side for x[rows, K] (fp32): per-row
+    exponents (recommended_exponents, float64 on the device) and the truncating
+    bp8 codes of x / 2^e.  Returns (codes [rows, K] uint8, exps [rows] int32)."""
+    xx = _dev(x, "x", torch.float32)
+    if xx.dim() != 2:
+        raise ValueError("x must be 2-D [rows, K]")
+    rows, K = xx.shape
+    codes = torch.empty((rows, K), dtype=torch.uint8, device=xx.device)
+    exps = torch.empty(rows, dtype=torch.int32, device=xx.device)
+    _lib.check(_lib.lib().bp_w8a8_encode_rows(_p(xx), rows, K, _p(exps), _p(codes), _stream()))
+    return codes, exps
+
+
 def quantize_small(x: torch.Tensor, fmt) -> torch.Tensor:
     """Truncating float64 -> bposit4 ("bp4"/4) or AI-posit5 ("aip5"/5) codes, uint8."""
     f = {"bp4": 4, "aip5": 5, 4: 4, 5: 5}.get(fmt)

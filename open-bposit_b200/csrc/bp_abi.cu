@@ -285,6 +285,14 @@ int bp_quire_gemm_host(int fmt, const void *A, const void *B, int M, int N, int 
   return launch_quire_gemm_host(fmt, A, B, M, N, K, sa, sb, group, out_bp32, ldo, algo, (cudaStream_t)stream);
 }
 
+int bp_w8a8_encode_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, void *stream) {
+  g_err[0] = 0;
+  if (rows < 0 || K < 0) return set_error(kEInval, "bp_w8a8_encode_rows: negative size");
+  if ((size_t)rows * K != 0 && (!x || !exps || !codes)) return set_error(kEInval, "bp_w8a8_encode_rows: null pointer");
+  TRY(check_device());
+  return launch_w8a8_rows(x, rows, K, exps, codes, (cudaStream_t)stream);
+}
+
 int bp_enable_peer_access(int peer_device) {
   g_err[0] = 0;
   int cur = 0;

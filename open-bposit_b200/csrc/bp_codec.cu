@@ -19,6 +19,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "bp_gemm_common.cuh"
 #include "bp_internal.cuh"
 
@@ -364,24 +366,32 @@ int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *
 namespace bp {
 namespace {
 
-// value(bp32 code) * 2^(re[m] + ce[n]); NaR -> 0.0 like _bp32_to_float
-// (reference/bposit_quantize.py:66-68).
+// 2^e as a double, for e in the normal range [-1022, 1023] (built from its bits).
+__device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
+
+// Exact value of a bp32 code times 2^extra (NaR -> 0.0 like _bp32_to_float,
+// reference/bposit_quantize.py:66-68): one multiply by an exact power of two
+// while that is a normal double, scalbn (which rounds subnormals and
+// overflows as IEEE does) beyond.
+__device__ __forceinline__ double bp32_value_scaled(uint32_t code, int extra) {
+  Dec d = decode_posit<32, 3>(code);
+  if (d.kind != 0) return 0.0;
+  const int e = d.scale - d.fw + extra;
+  const double m = (double)((1u << d.fw) + d.fbits);
+  const double v = (e >= -1022 && e <= 1023) ? m * pow2d(e) : scalbn(m, e);
+  return d.sign ? -v : v;
+}
+
+// value(bp32 code) * 2^(re[m] + ce[n]): rows over blocks, columns over threads.
 __global__ void __launch_bounds__(256) k_bp32_to_f64(const uint32_t *__restrict__ codes, int M, int N,
                                                      const int32_t *__restrict__ re,
                                                      const int32_t *__restrict__ ce,
                                                      double *__restrict__ out) {
-  size_t n = (size_t)M * N;
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = tid; i < n; i += stride) {
-    Dec d = decode_posit<32, 3>(codes[i]);
-    double v = 0.0;
-    if (d.kind == 0) {
-      int ex = d.scale - d.fw + (re ? re[i / N] : 0) + (ce ? ce[i % N] : 0);
-      v = scalbn((double)((1u << d.fw) + d.fbits), ex);
-      if (d.sign) v = -v;
-    }
-    out[i] = v;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    const int rex = re ? re[m] : 0;
+    const size_t rb = (size_t)m * N;
+    for (int n = threadIdx.x; n < N; n += blockDim.x)
+      out[rb + n] = bp32_value_scaled(codes[rb + n], rex + (ce ? ce[n] : 0));
   }
 }
 
@@ -392,19 +402,14 @@ __global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict_
                                                      const int32_t *__restrict__ ce,
                                                      const float *__restrict__ bias,
                                                      float *__restrict__ out) {
-  size_t n = (size_t)M * N;
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = tid; i < n; i += stride) {
-    Dec d = decode_posit<32, 3>(codes[i]);
-    double v = 0.0;
-    if (d.kind == 0) {
-      int ex = d.scale - d.fw + (re ? re[i / N] : 0) + (ce ? ce[i % N] : 0);
-      v = scalbn((double)((1u << d.fw) + d.fbits), ex);
-      if (d.sign) v = -v;
+  for (int m = blockIdx.x; m < M; m += gridDim.x) {
+    const int rex = re ? re[m] : 0;
+    const size_t rb = (size_t)m * N;
+    for (int n = threadIdx.x; n < N; n += blockDim.x) {
+      double v = bp32_value_scaled(codes[rb + n], rex + (ce ? ce[n] : 0));
+      if (bias) v += (double)bias[n];
+      out[rb + n] = __double2float_rn(v);
     }
-    if (bias) v += (double)bias[i % N];
-    out[i] = __double2float_rn(v);
   }
 }
 
@@ -412,19 +417,15 @@ __global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict_
 
 int launch_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
                        const float *bias, float *out, cudaStream_t s) {
-  size_t n = (size_t)M * N;
-  if (n == 0) return kOk;
-  size_t blocks = (n + 255) / 256, cap = (size_t)sm_count() * 8;
-  k_bp32_to_f32<<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(codes, M, N, re, ce, bias, out);
+  if ((size_t)M * N == 0) return kOk;
+  k_bp32_to_f32<<<std::min(M, sm_count() * 8), 256, 0, s>>>(codes, M, N, re, ce, bias, out);
   return check_launch("bp32_to_f32");
 }
 
 int launch_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *re, const int32_t *ce,
                        double *out, cudaStream_t s) {
-  size_t n = (size_t)M * N;
-  if (n == 0) return kOk;
-  size_t blocks = (n + 255) / 256, cap = (size_t)sm_count() * 8;
-  k_bp32_to_f64<<<(int)(blocks < cap ? blocks : cap), 256, 0, s>>>(codes, M, N, re, ce, out);
+  if ((size_t)M * N == 0) return kOk;
+  k_bp32_to_f64<<<std::min(M, sm_count() * 8), 256, 0, s>>>(codes, M, N, re, ce, out);
   return check_launch("bp32_to_f64");
 }
 

@@ -43,6 +43,7 @@ int launch_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *re, c
 int launch_quire_gemm_host(int fmt, const void *A_h, const void *B_h, int M, int N, int K, const int32_t *sa_h,
                            const int32_t *sb_h, int group, uint32_t *out_h, int64_t ldo, int algo,
                            cudaStream_t s);
+int launch_w8a8_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, cudaStream_t s);
 int launch_quire_to_bp16(const uint32_t *limbs, int nlimbs, size_t n, uint16_t *out, cudaStream_t s);
 int launch_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, cudaStream_t s);
 int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *out,

@@ -82,3 +82,28 @@ def test_qwen_shaped_forward_linears_match_oracle(orc):
     h32 = ref_model(ids)
     cos = torch.nn.functional.cosine_similarity(h.flatten(), h32.flatten(), dim=0).item()
     assert cos > 0.97
+
+
+@pytest.mark.parametrize("K", [1, 2, 3, 20, 576, 4864])
+def test_w8a8_encode_rows_matches_reference_rule(orc, K):
+    """ops.w8a8_encode_rows: per-row exponents equal recommended_exponents
+    (reference/bposit_quantize.py:46-63, numpy on the host) and the codes equal
+    the oracle's truncating encode of x / 2^e with the limit_denominator zero cut."""
+    from bposit_b200 import ops
+    from bposit_b200.bposit_quantize import recommended_exponents
+    rng = np.random.default_rng(K)
+    R = 64
+    X = (rng.standard_normal((R, K)) * np.exp2(rng.integers(-20, 20, (R, 1)))).astype(np.float32)
+    X[0] = 0.0                                            # all-zero row
+    X[1, : max(1, K // 20)] *= 1000.0                     # outliers: the p95 branch
+    X[2] = 3.0                                            # all equal (ties at every rank)
+    X[3] = np.where(np.arange(K) % 2 == 0, 1.0, -2.0)     # two values
+    X[4] = (rng.integers(-3, 4, K) * 2.0 ** -30).astype(np.float32)   # tiny: the zero cut after scaling
+    X[5, :] = np.float32(2.0 ** 7)                        # power of two
+    xt = torch.from_numpy(X).cuda()
+    codes, exps = ops.w8a8_encode_rows(xt)
+    ex_ref = recommended_exponents(X.astype(np.float64))
+    assert np.array_equal(exps.cpu().numpy(), ex_ref)
+    s = X.astype(np.float64) / np.exp2(ex_ref.astype(np.float64))[:, None]
+    c_ref = np.where(np.abs(s) <= 4.999999999999999e-09, 0, orc.quantize_bp8_f64(s, nearest=False))
+    assert np.array_equal(codes.cpu().numpy(), c_ref.astype(np.uint8))
