@@ -265,6 +265,28 @@ BP_HD uint32_t bp32_from_mag(bool neg, uint64_t hi, uint64_t lo, int lsb_exp) {
   return (neg ? 0x80000000u : 0u) | field;
 }
 
+// bp32_from_mag for a sum that fits a signed 64-bit integer: value Q * 2^lsb_exp,
+// cut to the bposit32 bit string.  The regime, the three exponent bits and the
+// fraction are laid out left-aligned in one 64-bit word whose top 31 bits are
+// the truncated field; te is clamped to regimes -31 .. 30, where the word
+// already reads maxpos (all ones) or falls below bit 33 (then minpos).
+BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
+  if (Q == 0) return 0u;
+  const bool neg = Q < 0;
+  const uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
+  const int lz = clz64(m);
+  int te = 63 - lz + lsb_exp;
+  te = te < -248 ? -248 : (te > 247 ? 247 : te);
+  const int k = te >> 3, e = te & 7;
+  const int rl = k >= 0 ? k + 2 : 1 - k;
+  const uint64_t R = k >= 0 ? (~0ull << (63 - k)) : (1ull << (63 + k));
+  const uint64_t frac = (m << lz) << 1;
+  const uint64_t w = R | ((uint64_t)e << (61 - rl)) | (frac >> (rl + 3));
+  uint32_t field = (uint32_t)(w >> 33);
+  field = field ? field : 1u;
+  return neg ? 0u - field : field;
+}
+
 // ---- the small rungs: bposit4 (es 1, encode range 2^+-2) and AI-posit5
 // (es 1, 2^+-4) (reference/bposit_ref.py:879-940) --------------------------
 // Fraction(x).limit_denominator(10**8) is 0 exactly when |x| < 1/(2*10**8);

@@ -20,10 +20,11 @@
 //     d = s + t; the S MMAs sharing an A digit plane reuse it from the tensor
 //     core's A collector.  With base-128 digits a diagonal grows by at most
 //     12416 (bp8) / 16512 (bp16) per k, so int32 stays exact for K up to
-//     KCHUNK; longer K is cut into chunks summed by k_tc_reduce.
-//  4. The epilogue reads the 2S-1 diagonals, forms Q = sum_d acc_d * 128^d
-//     (exact, 128-bit), moves it to the output's lsb base la_i + la_j, adds the
-//     tail correction and rounds once to bposit32.
+//     KCHUNK; longer K is cut into chunks summed by k_tc_finish.
+//  4. The epilogue reads the 2S-1 diagonals and stores Q = sum_d acc_d * 128^d
+//     exactly (one int64 word for bp8, two for bp16); k_tc_finish adds the K
+//     chunks, moves Q to the output's lsb base la_i + la_j, adds the tail
+//     correction and rounds once to bposit32.
 //  5. Outputs whose exact window exceeds 128 bits, that need per-term
 //     truncation (products below 2^-96), or whose tail list overflowed are
 //     recomputed by k_tc_fixup with the 512-bit quire of the CUDA-core slow
@@ -38,6 +39,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <climits>
 
 #include <algorithm>
 #include <atomic>
@@ -85,6 +87,11 @@ struct Cfg {
   }
   // K per chunk with every int32 diagonal sum exact, a multiple of BK
   static constexpr int KCHUNK = (int)((0x7FFFFFFFLL / max_diag()) / BK * BK);
+  // int64 words per exact main sum handed to k_tc_finish: bp8 (D = 5) one,
+  // Q = sum_d acc_d 128^d with |Q| < 2^31 * 2^28 * 1.01 < 2^60; bp16 (D = 7)
+  // two, lo = sum_{d<4} acc_d 128^d (< 2^53) and hi = sum_{d>=4} acc_d
+  // 128^(d-4) (< 2^46), Q = lo + hi * 2^28, which may need up to 74 bits.
+  static constexpr int QW = D <= 5 ? 1 : 2;
   static constexpr int A_BYTES = S * BM * BK;
   static constexpr int B_BYTES = S * BNB * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -121,7 +128,7 @@ struct TcParams {
   int64_t ldo;
   uint32_t *quire;
   int nlimbs;
-  ulonglong2 *partial;         // split launch: [tile - tile0][chunk][MM rows][BN cols], 128-bit
+  long long *qbuf;             // [tile - tile0][chunk][MM rows][BN cols]: exact main sums Q (int64)
   uint32_t *extra_out[kMaxExtraOut];   // peer result matrices (row stride ldo)
   int n_extra;
   int64_t extra_col0;
@@ -350,15 +357,6 @@ __device__ __forceinline__ bool finish_code(const TcParams &p, int i, int j, uns
   return true;
 }
 
-// finish_code stored to the output and to every extra output.
-__device__ __forceinline__ void finish_output(const TcParams &p, int i, int j, unsigned __int128 Q, int4 ra,
-                                              int4 rb, int Li, int Lj, int slot_i, int slot_j) {
-  uint32_t code;
-  if (!finish_code(p, i, j, Q, ra, rb, Li, Lj, slot_i, slot_j, code)) return;
-  p.out[(size_t)i * p.ldo + j] = code;
-  for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
-}
-
 // ----------------------------------------------------------------- GEMM ---
 // One CTA per SM.  PAIR: launched in clusters of two; CTA rank 0 (the leader)
 // issues M = 256 MMAs that read A from both CTAs (128 rows each) and B from
@@ -375,8 +373,6 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t *tfull = empty + C::STAGES;
   uint32_t *tmem_slot = (uint32_t *)(tfull + 1);
   volatile int *abort = (volatile int *)(tmem_slot + 1);                  // set by a timed-out wait
-  int4 *sstat = (int4 *)(smem + C::STAGES * C::STAGE_BYTES + 256);          // [BN] B-row stats
-  int2 *sLs = (int2 *)(sstat + C::BN);                                    // [BN] {L, slot}
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;      // 0: issues the pair's MMAs
@@ -398,11 +394,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (PAIR) cluster_sync_all();   // the peer's barriers exist before anything reaches them
-  for (int c = threadIdx.x; c < C::BN; c += THREADS) {
-    int j = n0 + c;
-    sstat[c] = j < p.N ? p.stb[j] : make_int4(0, 0, 0, 0);
-    sLs[c] = j < p.N ? make_int2(p.LB[j], p.slotB[j]) : make_int2(0, -1);
-  }
   if (warp == 0) tmem_alloc_t<PAIR>(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();
@@ -496,76 +487,51 @@ __global__ void __launch_bounds__(THREADS, 1)
   ok = mbar_wait(tfull, 0, 4, abort, true) && ok;
   tc_fence_after();
   const int q4 = warp & 3, half = warp >> 2;
-  const int r = q4 * 32 + lane;
-  const int i = m0 + r;
-  int4 ra = make_int4(0, 0, 0, 0);
-  int Li = 0, slot_i = -1;
-  if (i < p.M) {
-    ra = p.sta[i];
-    Li = p.LA[i];
-    slot_i = p.slotA[i];
-  }
   const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-  // Finished codes are staged per lane quarter in the (now idle) pipeline
-  // buffers -- [32 rows][BN + 1] words, conflict-free both ways -- then stored
-  // row by row with consecutive lanes on consecutive columns, so each warp
-  // store is one 128-byte line (also across NVLink, for the extra outputs).
-  // Outputs left to k_tc_fixup are staged as 0; the fixup, later on the same
-  // stream, overwrites them everywhere.
-  constexpr int CW = C::BN / 2;
+  // The epilogue only moves the exact main sums out (Q = sum_d acc_d 128^d, in
+  // Cfg::QW int64 words) -- staged per lane quarter in the idle pipeline
+  // buffers, [32 rows][BN + 1] int64 per word, conflict-free both ways -- and
+  // stores them row by row (coalesced) into this launch's tile-compact buffer.
+  // Rounding, tail corrections and the stores of the bposit32 outputs run in
+  // k_tc_finish at full occupancy: done here, with one CTA of 8 warps per SM,
+  // they took a third to three quarters of a short-K tile's time.
+  constexpr int CW = C::BN / 2, QW = C::QW, STG = 4 * 32 * (C::BN + 1);
   static_assert(C::BN % 32 == 0 && CW % 16 == 0, "BN must be a multiple of 32");
-  static_assert(4 * 32 * (C::BN + 1) * 4 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
-  uint32_t *stg = (uint32_t *)smem + q4 * 32 * (C::BN + 1);
+  static_assert(QW * STG * 8 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
+  long long *stg = (long long *)smem + q4 * 32 * (C::BN + 1);
 #pragma unroll 1
   for (int c0 = half * CW; c0 < half * CW + CW; c0 += 16) {
     uint32_t v[C::D][16];
 #pragma unroll
     for (int d = 0; d < C::D; ++d) tmem_ld16(trow + d * C::BN + c0, v[d]);
     tmem_ld_wait();
-    if (!ok || i >= p.M) continue;
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) {
-      const int j = n0 + c0 + jj;
-      if (j >= p.N) continue;
-      // |acc_d| < 2^31, so sum_d acc_d 128^d is below 2^60: exact in 64 bits
-      long long Q = 0;
+      long long lo = 0, hi = 0;
 #pragma unroll
-      for (int d = 0; d < C::D; ++d) Q += (long long)(int)v[d][jj] * (1ll << (7 * d));
-      if (p.split > 1) {
-        p.partial[(((size_t)(tile - p.tile0) * p.split + chunk) * C::MM + rank * BM + r) * C::BN + c0 + jj] =
-            make_ulonglong2((unsigned long long)Q, Q < 0 ? ~0ull : 0ull);
-      } else {
-        const int2 ls = sLs[c0 + jj];
-        const int4 rb = sstat[c0 + jj];
-        uint32_t code = 0u;
-        if (!p.quire && slot_i < 0 && ls.y < 0 && ra.z && rb.z) {
-          // no tail correction, no raw quire: round Q * 2^(L_i + L_j) directly
-          if (tc_exact(ra, rb, slot_i, ls.y, p.K)) {
-            const bool neg = Q < 0;
-            code = bp32_from_mag(neg, 0u, neg ? 0ull - (unsigned long long)Q : (unsigned long long)Q, Li + ls.x);
-          }
-        } else if (!finish_code(p, i, j, (unsigned __int128)(__int128)Q, ra, rb, Li, ls.x, slot_i, ls.y, code)) {
-          code = 0u;
-        }
-        stg[lane * (C::BN + 1) + c0 + jj] = code;
+      for (int d = 0; d < C::D; ++d) {
+        if (QW == 1 || d < 4) lo += (long long)(int)v[d][jj] * (1ll << (7 * d));
+        else hi += (long long)(int)v[d][jj] * (1ll << (7 * (d - 4)));
       }
+      stg[lane * (C::BN + 1) + c0 + jj] = lo;
+      if (QW == 2) stg[STG + lane * (C::BN + 1) + c0 + jj] = hi;
     }
   }
-  if (p.split == 1) {
+  {
     // the two warps of a lane quarter meet, then each stores half of its rows
     asm volatile("bar.sync %0, 64;" ::"r"(3 + q4) : "memory");
+    long long *dst = p.qbuf + ((size_t)(tile - p.tile0) * p.split + chunk) * QW * C::MM * C::BN +
+                     (size_t)(rank * BM + q4 * 32) * C::BN;
+    if (ok) {
 #pragma unroll 1
-    for (int rr = half * 16; rr < half * 16 + 16; ++rr) {
-      const int ii = m0 + q4 * 32 + rr;
-      if (ii >= p.M) break;
+      for (int rr = half * 16; rr < half * 16 + 16; ++rr) {
 #pragma unroll
-      for (int qq = 0; qq < C::BN / 32; ++qq) {
-        const int cc = qq * 32 + lane;
-        if (n0 + cc < p.N) {
-          const uint32_t code = stg[rr * (C::BN + 1) + cc];
-          p.out[(size_t)ii * p.ldo + n0 + cc] = code;
-          for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)ii * p.ldo + p.extra_col0 + n0 + cc] = code;
-        }
+        for (int w = 0; w < QW; ++w)
+#pragma unroll
+          for (int qq = 0; qq < C::BN / 32; ++qq) {
+            const int cc = qq * 32 + lane;
+            dst[(size_t)w * C::MM * C::BN + (size_t)rr * C::BN + cc] = stg[w * STG + rr * (C::BN + 1) + cc];
+          }
       }
     }
   }
@@ -577,21 +543,127 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (PAIR) cluster_sync_all();   // neither CTA leaves while the other still deallocates
 }
 
-// ----------------------------------------------------------- split-K sum ---
-// Sums the K chunks of the tiles of a split launch and finishes their outputs.
-template <int MM, int BN>
-__global__ void __launch_bounds__(256) k_tc_reduce(TcParams p, int ntiles) {
-  const size_t per_tile = (size_t)MM * BN;
-  const size_t n = (size_t)ntiles * per_tile;
-  for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < n; o += (size_t)gridDim.x * blockDim.x) {
-    const int tl = (int)(o / per_tile);
-    const int rc = (int)(o % per_tile);
+// --------------------------------------------------------------- finish ---
+// The outputs of a launch's tiles: the exact main sum Q (the K chunks' sums,
+// QW int64 words each, added in 128 bits), moved to the output's lsb base,
+// plus the tail corrections, rounded once to bposit32 and stored (to the
+// output and every extra output).
+//
+// Work unit: RW consecutive rows of one tile, taken by one warp (grid-stride
+// over units).  Lane l owns the columns l, l + 32, ..., whose statistics it
+// loads once per unit; the unit's row statistics are loaded once (lane r holds
+// row r) and broadcast by shuffles.  When every output of the unit is plain
+// (one K chunk, no tail corrections, no raw quire, inside the exact window)
+// the warp runs the short loop -- sum -> bposit32 -> store -- with RU rows x
+// BN / 32 sums per lane in flight.
+template <int MM, int BN, int QW>
+__global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
+  static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
+  constexpr int PL = BN / 32, RW = 8, RU = 4, UPT = MM / RW;
+  constexpr size_t PT = (size_t)MM * BN;   // words of one plane of a tile
+  const int lane = threadIdx.x & 31;
+  const int cl2 = ceil_log2_int(p.K);
+  const int4 z4 = make_int4(0, 0, 0, 0);
+  const bool one_chunk = p.split == 1 && !p.quire;
+  const long long nunits = (long long)ntiles * UPT;
+  for (long long un = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); un < nunits; un += (long long)gridDim.x * 8) {
+    const int tl = (int)(un / UPT), rg = (int)(un % UPT);
     const int tile = p.tile0 + tl;
-    const int i = (tile / p.ntn) * MM + rc / BN, j = (tile % p.ntn) * BN + rc % BN;
-    if (i >= p.M || j >= p.N) continue;
-    unsigned __int128 Q = 0;
-    for (int c = 0; c < p.split; ++c) Q += u128(p.partial[((size_t)tl * p.split + c) * per_tile + rc]);
-    finish_output(p, i, j, Q, p.sta[i], p.stb[j], p.LA[i], p.LB[j], p.slotA[i], p.slotB[j]);
+    const int tm = tile / p.ntn;
+    const int j0 = (tile - tm * p.ntn) * BN;
+    const int rbase = tm * MM + rg * RW;
+    const int nrows = min(RW, p.M - rbase);
+    if (nrows <= 0) continue;
+    const bool rv = lane < nrows;
+    const int4 ral = rv ? p.sta[rbase + lane] : z4;
+    const int Lil = rv ? p.LA[rbase + lane] : 0, sil = rv ? p.slotA[rbase + lane] : -1;
+    // unit bounds for the exact window: min lsb exponent, max width of the rows
+    int ax = rv ? ral.x : INT_MAX, aw = rv ? ral.y - ral.x : INT_MIN;
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      ax = min(ax, __shfl_xor_sync(0xFFFFFFFFu, ax, o));
+      aw = max(aw, __shfl_xor_sync(0xFFFFFFFFu, aw, o));
+    }
+    ax = __shfl_sync(0xFFFFFFFFu, ax, 0);
+    aw = __shfl_sync(0xFFFFFFFFu, aw, 0);
+    const bool rows_plain = __all_sync(0xFFFFFFFFu, !rv || (sil == -1 && ral.z != 0));
+    int4 rb[PL];
+    int Lj[PL], sj[PL];
+    bool jv[PL];
+    bool plain = one_chunk && rows_plain;
+#pragma unroll
+    for (int q = 0; q < PL; ++q) {
+      const int j = j0 + q * 32 + lane;
+      jv[q] = j < p.N;
+      rb[q] = jv[q] ? p.stb[j] : z4;
+      Lj[q] = jv[q] ? p.LB[j] : 0;
+      sj[q] = jv[q] ? p.slotB[j] : -1;
+      plain = plain && (!jv[q] || (sj[q] == -1 && rb[q].z != 0 && ax + rb[q].x + 96 >= 0 &&
+                                   aw + (rb[q].y - rb[q].x) + cl2 + 3 <= 127));
+    }
+    const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + (size_t)rg * RW * BN + lane;
+    // one path per warp: both paths broadcast row statistics by full-warp shuffles
+    if (__all_sync(0xFFFFFFFFu, plain)) {
+      for (int r0 = 0; r0 < nrows; r0 += RU) {
+        long long qv[RU][PL], qh[RU][PL];
+#pragma unroll
+        for (int u = 0; u < RU; ++u)
+#pragma unroll
+          for (int q = 0; q < PL; ++q) {
+            const bool ld = r0 + u < nrows && jv[q];
+            const long long *a = qt + (size_t)(r0 + u) * BN + q * 32;
+            qv[u][q] = ld ? __ldcs(a) : 0ll;
+            qh[u][q] = (QW == 2 && ld) ? __ldcs(a + PT) : 0ll;
+          }
+#pragma unroll
+        for (int u = 0; u < RU; ++u) {
+          const int r = r0 + u;
+          if (r >= nrows) break;
+          const int Li = __shfl_sync(0xFFFFFFFFu, Lil, r);
+          const int i = rbase + r;
+          uint32_t *orow = p.out + (size_t)i * p.ldo;
+#pragma unroll
+          for (int q = 0; q < PL; ++q) {
+            if (!jv[q]) continue;
+            const int j = j0 + q * 32 + lane;
+            uint32_t code;
+            if (QW == 1) {
+              code = bp32_from_i64(qv[u][q], Li + Lj[q]);
+            } else {
+              const __int128 Q = (__int128)qv[u][q] + ((__int128)qh[u][q] << 28);
+              const bool neg = Q < 0;
+              const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
+              code = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + Lj[q]);
+            }
+            orow[j] = code;
+            for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
+          }
+        }
+      }
+      continue;
+    }
+    // general case: K chunks summed in 128 bits, tail corrections, raw quire
+    for (int r = 0; r < nrows; ++r) {
+      const int4 ra = make_int4(__shfl_sync(0xFFFFFFFFu, ral.x, r), __shfl_sync(0xFFFFFFFFu, ral.y, r),
+                                __shfl_sync(0xFFFFFFFFu, ral.z, r), 0);
+      const int Li = __shfl_sync(0xFFFFFFFFu, Lil, r), si = __shfl_sync(0xFFFFFFFFu, sil, r);
+      const int i = rbase + r;
+#pragma unroll
+      for (int q = 0; q < PL; ++q) {
+        if (!jv[q]) continue;
+        const int j = j0 + q * 32 + lane;
+        __int128 Q = 0;
+        for (int ch = 0; ch < p.split; ++ch) {
+          const long long *a = qt + (size_t)ch * QW * PT + (size_t)r * BN + q * 32;
+          Q += (__int128)__ldcs(a);
+          if (QW == 2) Q += (__int128)__ldcs(a + PT) << 28;
+        }
+        uint32_t code;
+        if (!finish_code(p, i, j, (unsigned __int128)Q, ra, rb[q], Li, Lj[q], si, sj[q], code)) continue;
+        p.out[(size_t)i * p.ldo + j] = code;
+        for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
+      }
+    }
   }
   if (p.n_extra) __threadfence_system();
 }
@@ -1061,13 +1133,13 @@ constexpr size_t kCorrBudget = size_t(512) << 20;
 
 // Which tiles run whole and which are split along K.  Tiles are linear (N
 // fastest); tiles [0, whole) run whole, tiles [whole, ntiles) in `split`
-// chunks of kbc K blocks each, their 128-bit partials summed by k_tc_reduce.
+// chunks of kbc K blocks each, their int64 partial sums added by k_tc_finish.
 //  * K longer than one exact int32 chunk: every tile is split (the minimum).
 //  * otherwise the full waves run whole and only the last, partial wave is
 //    split -- as many ways as fit in one wave -- so the machine stays full to
 //    the end instead of idling through a mostly empty last wave.
 struct TcSchedule {
-  int MM, BN, ntn, ntiles, whole, split, kbc;
+  int MM, BN, QW, ntn, ntiles, whole, split, kbc;
 };
 
 int tc_wave_capacity(bool pair);
@@ -1076,6 +1148,7 @@ TcSchedule tc_schedule(int S, int M, int N, int nkb, bool pair) {
   TcSchedule sc{};
   sc.MM = pair ? 2 * BM : BM;
   sc.BN = S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
+  sc.QW = S == 3 ? Cfg<3>::QW : Cfg<4>::QW;
   sc.ntn = (N + sc.BN - 1) / sc.BN;
   sc.ntiles = sc.ntn * ((M + sc.MM - 1) / sc.MM);
   const int exact = (S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
@@ -1097,8 +1170,10 @@ TcSchedule tc_schedule(int S, int M, int N, int nkb, bool pair) {
   return sc;
 }
 
-size_t tc_partial_bytes(const TcSchedule &sc) {
-  return sc.whole < sc.ntiles ? 16 * (size_t)(sc.ntiles - sc.whole) * sc.split * sc.MM * sc.BN : 0;
+// Exact main sums of one GEMM: QW int64 words per output of the whole tiles,
+// then per output and K chunk of the split tiles.
+size_t tc_qbuf_bytes(const TcSchedule &sc) {
+  return 8 * (size_t)sc.QW * ((size_t)sc.whole + (size_t)(sc.ntiles - sc.whole) * sc.split) * sc.MM * sc.BN;
 }
 
 TcLayout tc_layout(int fmt, int M, int N, int K) {
@@ -1123,10 +1198,10 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.ctr = o; o += 256;
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
-  // room for either form's split tiles (the form is chosen at launch)
+  // room for either form's main sums (the form is chosen at launch)
   L.part = o;
-  o += al(std::max(tc_partial_bytes(tc_schedule(L.S, M, N, L.nkb, false)),
-                   tc_partial_bytes(tc_schedule(L.S, M, N, L.nkb, M > BM && BK == 64))));
+  o += al(std::max(tc_qbuf_bytes(tc_schedule(L.S, M, N, L.nkb, false)),
+                   tc_qbuf_bytes(tc_schedule(L.S, M, N, L.nkb, M > BM && BK == 64))));
   L.total = o;
   return L;
 }
@@ -1202,26 +1277,41 @@ int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const Tc
   return check_launch("quire_gemm_tc");
 }
 
+// Blocks of k_tc_finish for `ntiles` tiles: eight 8-row units per block, at
+// most `cap` blocks.
+template <int MM>
+int finish_grid(int ntiles, int cap) {
+  return (int)std::max<long long>(1, std::min<long long>(((long long)ntiles * (MM / 8) + 7) / 8, cap));
+}
+
 template <int S, bool PAIR>
 int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
-                       int grid_reduce, cudaStream_t s) {
+                       int grid_finish, cudaStream_t s) {
+  using C = Cfg<S, PAIR>;
+  long long *qbuf = p.qbuf;
   int rc = kOk;
   p.ntn = sc.ntn;
   if (sc.whole > 0) {
     p.tile0 = 0;
     p.split = 1;
     p.kb_per_chunk = p.nkb;
+    p.qbuf = qbuf;
     rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.whole, s);
+    if (rc) return rc;
+    k_tc_finish<C::MM, C::BN, C::QW><<<finish_grid<C::MM>(sc.whole, grid_finish), 256, 0, s>>>(p, sc.whole);
+    rc = check_launch("tc_finish");
     if (rc) return rc;
   }
   if (sc.whole < sc.ntiles) {
     p.tile0 = sc.whole;
     p.split = sc.split;
     p.kb_per_chunk = sc.kbc;
+    p.qbuf = qbuf + (size_t)sc.whole * C::QW * C::MM * C::BN;
     rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.ntiles - sc.whole, s);
     if (rc) return rc;
-    k_tc_reduce<Cfg<S, PAIR>::MM, Cfg<S, PAIR>::BN><<<grid_reduce, 256, 0, s>>>(p, sc.ntiles - sc.whole);
-    rc = check_launch("tc_reduce");
+    k_tc_finish<C::MM, C::BN, C::QW><<<finish_grid<C::MM>(sc.ntiles - sc.whole, grid_finish), 256, 0, s>>>(
+        p, sc.ntiles - sc.whole);
+    rc = check_launch("tc_finish");
   }
   return rc;
 }
@@ -1255,7 +1345,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   TcCounters *cA = (TcCounters *)(w + L.ctr);
   TcCounters *cB = cA + 1;
   ulonglong2 *CA = (ulonglong2 *)(w + L.CA), *CB = (ulonglong2 *)(w + L.CB);
-  ulonglong2 *part = (ulonglong2 *)(w + L.part);
+  long long *qbuf = (long long *)(w + L.part);
 
   cudaError_t e = reuse_a ? cudaMemsetAsync(cB, 0, sizeof(TcCounters), s)
                           : cudaMemsetAsync(cA, 0, (a_only ? 1 : 2) * sizeof(TcCounters), s);
@@ -1315,11 +1405,11 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   p.M = a.M; p.N = a.N; p.K = a.K; p.Kp = L.Kp; p.nkb = L.nkb;
   p.sta = sta; p.stb = stb; p.LA = LA; p.LB = LB; p.slotA = slotA; p.slotB = slotB;
   p.CA = CA; p.CB = CB;
-  p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.partial = part;
+  p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.qbuf = qbuf;
   p.n_extra = a.n_extra; p.extra_col0 = a.extra_col0;
   for (int e = 0; e < a.n_extra; ++e) p.extra_out[e] = a.extra_out[e];
   const TcSchedule sc = tc_schedule(S, a.M, a.N, L.nkb, pair);
-  if (tc_partial_bytes(sc) > L.total - L.part) return set_error(kEWorkspace, "quire_gemm: split buffer too small");
+  if (tc_qbuf_bytes(sc) > L.total - L.part) return set_error(kEWorkspace, "quire_gemm: sum buffer too small");
   size_t outs = (size_t)a.M * a.N;
   int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);
   if (S == 3)

@@ -3,8 +3,8 @@
 // and compares it with the CPU oracle (oracle/bposit_oracle.c) over every
 // non-negative fp32 bit pattern (bp8 quantize, both modes), a strided sweep
 // of all fp32 patterns (bp16 encode, both modes), every bp8 / bp16 code
-// (decode) and random 128-bit magnitudes (bp32 round, and the bp16 round
-// derived from it).  Test-only.
+// (decode) and random 128-bit magnitudes (bp32 round, its signed 64-bit form,
+// and the bp16 round derived from it).  Test-only.
 //
 // usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32 | small
 #include <math.h>
@@ -153,11 +153,32 @@ int main(int argc, char **argv) {
       uint32_t ref = orc_quire_to_bp32(q, 8);
       uint32_t dev = bp::bp32_from_mag(neg, hi, lo, shift - 96);
       if (ref != dev) { if (bad < 5) fprintf(stderr, "bp32 mismatch bits=%d shift=%d\n", bits, shift); ++bad; }
+      if (bits <= 63) {   // the signed 64-bit form used for sums that fit int64
+        const long long Q = neg ? -(long long)lo : (long long)lo;
+        if (bp::bp32_from_i64(Q, shift - 96) != ref) {
+          if (bad < 5) fprintf(stderr, "bp32 i64 mismatch bits=%d shift=%d\n", bits, shift);
+          ++bad;
+        }
+      }
       // the bp16 round of the same quire, derived from the bp32 code
       uint16_t ref16;
       orc_quire_to_bp16_batch(q, 8, 1, &ref16);
       if (ref16 != bp::bp16_from_bp32(dev)) {
         if (bad < 5) fprintf(stderr, "bp16 mismatch bits=%d shift=%d\n", bits, shift);
+        ++bad;
+      }
+    }
+    // the 64-bit form against the 128-bit one over exponents past both ends
+    // of the bposit32 range (minpos / maxpos saturation)
+    for (int it = 0; it < 400000; ++it) {
+      const int bits = (int)(rnd() % 63) + 1;
+      const uint64_t m = bits == 64 ? rnd() : (rnd() & ((1ull << bits) - 1));
+      if (!m) continue;
+      const int L = (int)(rnd() % 801) - 400;
+      const bool neg = rnd() & 1;
+      const long long Q = neg ? -(long long)m : (long long)m;
+      if (bp::bp32_from_i64(Q, L) != bp::bp32_from_mag(neg, 0u, m, L)) {
+        if (bad < 5) fprintf(stderr, "bp32 i64 vs mag mismatch m=%llx L=%d\n", (unsigned long long)m, L);
         ++bad;
       }
     }

@@ -157,6 +157,31 @@ def test_bp16_normal_range_vs_oracle(ops, orc, algo):
     assert np.array_equal(out, orc.quire_gemm(A, B, 16))
 
 
+@pytest.mark.parametrize("algo", [2, 3])
+@pytest.mark.parametrize("K", [8192, 150000])
+def test_bp16_sums_beyond_64_bits(ops, orc, algo, K):
+    """bp16 rows whose main digits span the full 27 bits (values near 2^10,
+    one tiny element per row sets the base and becomes a listed tail), all of
+    one sign: the exact main sums pass 2^64, so every word of the tensor-core
+    path's sums (and, at K = 150000, its split-K chunks) is exercised."""
+    rng = np.random.default_rng(K + algo)
+    M, N = 200, 192
+    if not tc_ok(ops, 16, M, N, K):
+        pytest.skip("tensor-core path not available for this shape")
+
+    def operand(rows):
+        x = (1024.0 * (1.0 + rng.random((rows, K)))).astype(np.float32)
+        x[:, 0] = np.float32(2.0 ** -16)
+        x[1::7] *= -1.0
+        return orc.encode_bp16(x, True)
+
+    A, B = operand(M), operand(N)
+    out, _ = run(ops, A, B, 16, algo)
+    rows = np.arange(M) if K <= 8192 else np.array([0, 1, 129, 199])
+    assert np.array_equal(out[rows], orc.quire_gemm(A[rows], B, 16))
+    assert _device_error() == 0
+
+
 def test_column_block_output(ops, orc):
     """ldo > N: an output shard written into its column block of a wider matrix."""
     rng = np.random.default_rng(5)
