@@ -265,26 +265,35 @@ BP_HD uint32_t bp32_from_mag(bool neg, uint64_t hi, uint64_t lo, int lsb_exp) {
   return (neg ? 0x80000000u : 0u) | field;
 }
 
+// x >> s for any s >= 0 (0 once s >= 32), one funnel shift on the device.
+BP_HD uint32_t shr_clamp(uint32_t x, int s) {
+#ifdef __CUDA_ARCH__
+  return __funnelshift_rc(x, 0u, (uint32_t)s);
+#else
+  return s >= 32 ? 0u : x >> s;
+#endif
+}
+
 // bp32_from_mag for a sum that fits a signed 64-bit integer: value Q * 2^lsb_exp,
 // cut to the bposit32 bit string.  The regime, the three exponent bits and the
-// fraction are laid out left-aligned in one 64-bit word whose top 31 bits are
-// the truncated field; te is clamped to regimes -31 .. 30, where the word
-// already reads maxpos (all ones) or falls below bit 33 (then minpos).
+// top fraction bits are laid out left-aligned in one 32-bit word W whose top 31
+// bits are the truncated field.  te is clamped to regimes -30 .. 30, where W
+// already reads maxpos (31 ones) or minpos (a single one in bit 1).  Selects
+// only, so unrolled copies stay short.
 BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
-  if (Q == 0) return 0u;
   const bool neg = Q < 0;
   const uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
-  const int lz = clz64(m);
+  const int lz = clz64(m);   // 64 for Q == 0, whose result is selected away below
+  const uint32_t f = (uint32_t)(((m << (lz & 63)) << 1) >> 32);   // top 32 fraction bits
   int te = 63 - lz + lsb_exp;
-  te = te < -248 ? -248 : (te > 247 ? 247 : te);
+  te = te < -240 ? -240 : (te > 247 ? 247 : te);
   const int k = te >> 3, e = te & 7;
-  const int rl = k >= 0 ? k + 2 : 1 - k;
-  const uint64_t R = k >= 0 ? (~0ull << (63 - k)) : (1ull << (63 + k));
-  const uint64_t frac = (m << lz) << 1;
-  const uint64_t w = R | ((uint64_t)e << (61 - rl)) | (frac >> (rl + 3));
-  uint32_t field = (uint32_t)(w >> 33);
-  field = field ? field : 1u;
-  return neg ? 0u - field : field;
+  const int rl = k >= 0 ? k + 2 : 1 - k;   // 2 .. 31
+  const uint32_t R = k >= 0 ? (~0u << (31 - k)) : (1u << (31 + k));
+  const uint32_t W = R | (((uint32_t)e << 29) >> rl) | shr_clamp(f, rl + 3);
+  const uint32_t field = W >> 1;
+  const uint32_t code = neg ? 0u - field : field;
+  return Q ? code : 0u;
 }
 
 // ---- the small rungs: bposit4 (es 1, encode range 2^+-2) and AI-posit5

@@ -545,26 +545,30 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // --------------------------------------------------------------- finish ---
 // The outputs of a launch's tiles: the exact main sum Q (the K chunks' sums,
-// QW int64 words each, added in 128 bits), moved to the output's lsb base,
-// plus the tail corrections, rounded once to bposit32 and stored (to the
-// output and every extra output).
+// QW int64 words each), moved to the output's lsb base, plus the tail
+// corrections, rounded once to bposit32 and stored (to the output and every
+// extra output).
 //
-// Work unit: RW consecutive rows of one tile, taken by one warp (grid-stride
-// over units).  Lane l owns the columns l, l + 32, ..., whose statistics it
-// loads once per unit; the unit's row statistics are loaded once (lane r holds
-// row r) and broadcast by shuffles.  When every output of the unit is plain
-// (one K chunk, no tail corrections, no raw quire, inside the exact window)
-// the warp runs the short loop -- sum -> bposit32 -> store -- with RU rows x
-// BN / 32 sums per lane in flight.
+// Work unit: kFinishRows consecutive rows of one tile, taken by one warp
+// (grid-stride over units).  Lane l owns the columns l, l + 32, ..., whose
+// statistics it loads once per unit; the unit's row statistics are loaded once
+// (lane r holds row r) and broadcast by shuffles.  When every output of the
+// unit is plain (no tail corrections, no raw quire, inside the exact window,
+// chunk sums inside int64) the warp runs the short loop -- load and add the
+// chunks' words, bposit32, store -- with all kFinishRows x BN / 32 sums of a
+// lane in flight.
+constexpr int kFinishRows = 4;
+
 template <int MM, int BN, int QW>
 __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
-  static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
-  constexpr int PL = BN / 32, RW = 8, RU = 4, UPT = MM / RW;
+  static_assert(BN % 32 == 0 && MM % kFinishRows == 0 && (QW == 1 || QW == 2), "tile shape");
+  constexpr int PL = BN / 32, RW = kFinishRows, UPT = MM / RW;
   constexpr size_t PT = (size_t)MM * BN;   // words of one plane of a tile
   const int lane = threadIdx.x & 31;
   const int cl2 = ceil_log2_int(p.K);
   const int4 z4 = make_int4(0, 0, 0, 0);
-  const bool one_chunk = p.split == 1 && !p.quire;
+  // chunk sums stay exact in int64: |word| < 2^60 (bp8) or < 2^53 (bp16 words)
+  const bool sum64 = !p.quire && p.split <= (QW == 1 ? 8 : 1024);
   const long long nunits = (long long)ntiles * UPT;
   for (long long un = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); un < nunits; un += (long long)gridDim.x * 8) {
     const int tl = (int)(un / UPT), rg = (int)(un % UPT);
@@ -580,7 +584,7 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
     // unit bounds for the exact window: min lsb exponent, max width of the rows
     int ax = rv ? ral.x : INT_MAX, aw = rv ? ral.y - ral.x : INT_MIN;
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
+    for (int o = RW / 2; o > 0; o >>= 1) {
       ax = min(ax, __shfl_xor_sync(0xFFFFFFFFu, ax, o));
       aw = max(aw, __shfl_xor_sync(0xFFFFFFFFu, aw, o));
     }
@@ -590,7 +594,7 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
     int4 rb[PL];
     int Lj[PL], sj[PL];
     bool jv[PL];
-    bool plain = one_chunk && rows_plain;
+    bool plain = sum64 && rows_plain;
 #pragma unroll
     for (int q = 0; q < PL; ++q) {
       const int j = j0 + q * 32 + lane;
@@ -604,41 +608,52 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
     const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + (size_t)rg * RW * BN + lane;
     // one path per warp: both paths broadcast row statistics by full-warp shuffles
     if (__all_sync(0xFFFFFFFFu, plain)) {
-      for (int r0 = 0; r0 < nrows; r0 += RU) {
-        long long qv[RU][PL], qh[RU][PL];
+      long long qv[RW][PL], qh[RW][PL];
 #pragma unroll
-        for (int u = 0; u < RU; ++u)
+      for (int u = 0; u < RW; ++u)
 #pragma unroll
-          for (int q = 0; q < PL; ++q) {
-            const bool ld = r0 + u < nrows && jv[q];
-            const long long *a = qt + (size_t)(r0 + u) * BN + q * 32;
-            qv[u][q] = ld ? __ldcs(a) : 0ll;
-            qh[u][q] = (QW == 2 && ld) ? __ldcs(a + PT) : 0ll;
-          }
+        for (int q = 0; q < PL; ++q) qv[u][q] = qh[u][q] = 0ll;
+      for (int ch = 0; ch < p.split; ++ch) {
+        const long long *qc = qt + (size_t)ch * QW * PT;
 #pragma unroll
-        for (int u = 0; u < RU; ++u) {
-          const int r = r0 + u;
-          if (r >= nrows) break;
-          const int Li = __shfl_sync(0xFFFFFFFFu, Lil, r);
-          const int i = rbase + r;
-          uint32_t *orow = p.out + (size_t)i * p.ldo;
+        for (int u = 0; u < RW; ++u)
 #pragma unroll
-          for (int q = 0; q < PL; ++q) {
-            if (!jv[q]) continue;
-            const int j = j0 + q * 32 + lane;
-            uint32_t code;
-            if (QW == 1) {
-              code = bp32_from_i64(qv[u][q], Li + Lj[q]);
-            } else {
-              const __int128 Q = (__int128)qv[u][q] + ((__int128)qh[u][q] << 28);
-              const bool neg = Q < 0;
-              const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
-              code = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + Lj[q]);
+          for (int q = 0; q < PL; ++q)
+            if (u < nrows && jv[q]) {
+              qv[u][q] += __ldcs(qc + (size_t)u * BN + q * 32);
+              if (QW == 2) qh[u][q] += __ldcs(qc + PT + (size_t)u * BN + q * 32);
             }
-            orow[j] = code;
-            for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
+      }
+      // round all RW x PL sums (selects only), then store the valid ones
+      uint32_t cd[RW][PL];
+#pragma unroll
+      for (int u = 0; u < RW; ++u) {
+        const int Li = __shfl_sync(0xFFFFFFFFu, Lil, u);
+#pragma unroll
+        for (int q = 0; q < PL; ++q) {
+          if (QW == 1) {
+            cd[u][q] = bp32_from_i64(qv[u][q], Li + Lj[q]);
+          } else {
+            const __int128 Q = (__int128)qv[u][q] + ((__int128)qh[u][q] << 28);
+            const bool neg = Q < 0;
+            const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
+            cd[u][q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + Lj[q]);
           }
         }
+      }
+      uint32_t *orow = p.out + (size_t)rbase * p.ldo + j0 + lane;
+#pragma unroll
+      for (int u = 0; u < RW; ++u)
+#pragma unroll
+        for (int q = 0; q < PL; ++q)
+          if (u < nrows && jv[q]) orow[(size_t)u * p.ldo + q * 32] = cd[u][q];
+      for (int e = 0; e < p.n_extra; ++e) {
+        uint32_t *erow = p.extra_out[e] + (size_t)rbase * p.ldo + p.extra_col0 + j0 + lane;
+#pragma unroll
+        for (int u = 0; u < RW; ++u)
+#pragma unroll
+          for (int q = 0; q < PL; ++q)
+            if (u < nrows && jv[q]) erow[(size_t)u * p.ldo + q * 32] = cd[u][q];
       }
       continue;
     }
@@ -1277,11 +1292,11 @@ int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const Tc
   return check_launch("quire_gemm_tc");
 }
 
-// Blocks of k_tc_finish for `ntiles` tiles: eight 8-row units per block, at
-// most `cap` blocks.
+// Blocks of k_tc_finish for `ntiles` tiles: eight units (one per warp) per
+// block, at most `cap` blocks.
 template <int MM>
 int finish_grid(int ntiles, int cap) {
-  return (int)std::max<long long>(1, std::min<long long>(((long long)ntiles * (MM / 8) + 7) / 8, cap));
+  return (int)std::max<long long>(1, std::min<long long>(((long long)ntiles * (MM / kFinishRows) + 7) / 8, cap));
 }
 
 template <int S, bool PAIR>
