@@ -410,7 +410,7 @@ def run_ours(args):
         cpu = {"value": v, "unit": "TOPS", "cores": threads, "kind": "port",
                "sample": f"{rows} rows x N={N_} x K={K_} of the same operands ({dt:.1f} s)"}
 
-    traffic = None
+    traffic, traffic_launches = None, None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
         with open(tp) as f:
@@ -418,6 +418,7 @@ def run_ours(args):
         ent = tj.get("quire_gemm_" + ("tc" if args.algo != 1 else "simt"))
         if ent and ent.get("shape") == [m1 - m0, n1 - n0, K_]:
             traffic = ent["dram_bytes_per_call"]
+            traffic_launches = sum(k.get("launches", 1) for k in ent.get("kernels", {}).values())
 
     if rank == 0:
         line = {
@@ -427,7 +428,7 @@ def run_ours(args):
             "data": "synthetic",
             "config": {"workload": WORKLOAD, "M": M_, "N": N_, "K": K_, "fmt": "bp8",
                        "parallelism": (f"{grid[0]}x{grid[1]} (M x N) block grid over {world} ranks + " +
-                                       ("all-gather fused into the GEMM epilogue (NVLink peer stores)" if fused
+                                       ("all-gather fused into the GEMM's finish kernel (NVLink peer stores)" if fused
                                         else "NCCL all-gather")),
                        "l2": "inputs 512 MiB > L2 (no flush needed)", "algo": args.algo},
             "roofline": {"bound": "tensor", "achieved": round(k_tops, 3), "peak": round(int8_peak, 1),
@@ -435,8 +436,9 @@ def run_ours(args):
                          "peak_source": f"int8 dense = 2 x {peak_src} bf16 {peaks['bf16_tflops']} TF/s",
                          "kernel": "quire GEMM (all launches of one bp_quire_gemm call)",
                          "kernel_ms": round(kms, 3),
-                         "traffic_note": ("DRAM bytes read+written by one bp_quire_gemm call (6 launches), one ncu "
-                                          "capture at this shape" if traffic else "no capture at this shape"),
+                         "traffic_note": (f"DRAM bytes read+written by one bp_quire_gemm call ({traffic_launches} "
+                                          "launches), one ncu capture at this shape" if traffic
+                                          else "no capture at this shape"),
                          "issued_int8_TOPS": round(k_tops * slice_pairs, 1) if slice_pairs else None,
                          "issued_frac": round(k_tops * slice_pairs / int8_peak, 4) if slice_pairs else None,
                          "slice_pairs_per_useful_mac": slice_pairs},

@@ -274,25 +274,44 @@ BP_HD uint32_t shr_clamp(uint32_t x, int s) {
 #endif
 }
 
-// bp32_from_mag for a sum that fits a signed 64-bit integer: value Q * 2^lsb_exp,
-// cut to the bposit32 bit string.  The regime, the three exponent bits and the
-// top fraction bits are laid out left-aligned in one 32-bit word W whose top 31
-// bits are the truncated field.  te is clamped to regimes -30 .. 30, where W
-// already reads maxpos (31 ones) or minpos (a single one in bit 1).  Selects
-// only, so unrolled copies stay short.
-BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
+// Q as a double rounded toward zero (|Q| cut to 53 significant bits; exact
+// below 2^53): the device's conversion instruction, emulated on the host.
+BP_HD uint64_t i64_to_f64_rz_bits(long long Q) {
+#ifdef __CUDA_ARCH__
+  return (uint64_t)__double_as_longlong(__ll2double_rz(Q));
+#else
   const bool neg = Q < 0;
-  const uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
-  const int lz = clz64(m);   // 64 for Q == 0, whose result is selected away below
-  const uint32_t f = (uint32_t)(((m << (lz & 63)) << 1) >> 32);   // top 32 fraction bits
-  int te = 63 - lz + lsb_exp;
+  uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
+  const int lz = clz64(m);
+  if (lz < 11) m &= ~((1ull << (11 - lz)) - 1ull);   // keep 53 significant bits
+  double d = (double)m;                              // now exact
+  if (neg) d = -d;
+  uint64_t b;
+  memcpy(&b, &d, 8);
+  return b;
+#endif
+}
+
+// bp32_from_mag for a sum that fits a signed 64-bit integer: value Q * 2^lsb_exp,
+// cut to the bposit32 bit string.  Q goes through one round-toward-zero
+// conversion to double (a cut of |Q| to 53 bits, then the cut below to at most
+// 27 bits: the same as one cut), which hands over the binade and the top
+// fraction bits.  The regime, the three exponent bits and those fraction bits
+// are laid out left-aligned in one 32-bit word W whose top 31 bits are the
+// truncated field; te is clamped to regimes -30 .. 30, where W already reads
+// maxpos (31 ones) or minpos (a single one in bit 1).  Selects only.
+BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
+  const uint64_t bits = i64_to_f64_rz_bits(Q);
+  const uint32_t hi = (uint32_t)(bits >> 32);
+  const uint32_t f = (uint32_t)(bits >> 20);   // top 32 bits of the 52-bit fraction field
+  int te = (int)((hi >> 20) & 0x7FFu) - 1023 + lsb_exp;
   te = te < -240 ? -240 : (te > 247 ? 247 : te);
   const int k = te >> 3, e = te & 7;
   const int rl = k >= 0 ? k + 2 : 1 - k;   // 2 .. 31
   const uint32_t R = k >= 0 ? (~0u << (31 - k)) : (1u << (31 + k));
   const uint32_t W = R | (((uint32_t)e << 29) >> rl) | shr_clamp(f, rl + 3);
   const uint32_t field = W >> 1;
-  const uint32_t code = neg ? 0u - field : field;
+  const uint32_t code = (hi >> 31) ? 0u - field : field;
   return Q ? code : 0u;
 }
 

@@ -549,65 +549,86 @@ __global__ void __launch_bounds__(THREADS, 1)
 // corrections, rounded once to bposit32 and stored (to the output and every
 // extra output).
 //
-// Work unit: kFinishRows consecutive rows of one tile, taken by one warp
-// (grid-stride over units).  Lane l owns the columns l, l + 32, ..., whose
-// statistics it loads once per unit; the unit's row statistics are loaded once
-// (lane r holds row r) and broadcast by shuffles.  When every output of the
-// unit is plain (no tail corrections, no raw quire, inside the exact window,
-// chunk sums inside int64) the warp runs the short loop -- load and add the
-// chunks' words, bposit32, store -- with all kFinishRows x BN / 32 sums of a
-// lane in flight.
-constexpr int kFinishRows = 4;
+// A block takes items -- 1/parts of a tile's rows, all its columns -- in a
+// grid-stride loop; lane l owns the columns l, l + 32, ..., whose statistics
+// it loads once per item; warp w takes the item's units of kFinishRows rows
+// w, w + 8, ..., whose row statistics are loaded once (lane r holds row r)
+// and broadcast by shuffles.  While the chunk sums stay inside int64 (always,
+// but for a raw quire output or more than 8 bp8 K chunks) a lane loads and
+// adds its sums and rounds the plain ones (no tail correction, nonzero row and
+// column, inside the exact window) with the short builder; per row, the others
+// load all their tail corrections at once and take finish_code's 128-bit
+// rule.  Otherwise every output goes through finish_general one by one.
+constexpr int kFinishRows = 1;
+
+// The general rule for output (i, j) of a unit: the chunks' sums added in 128
+// bits, finish_code (tail corrections, zero rows, raw quire), stores.
+template <int QW>
+__device__ __forceinline__ void finish_general(const TcParams &p, const long long *a, size_t plane, int i, int j) {
+  __int128 Q = 0;
+  for (int ch = 0; ch < p.split; ++ch) {
+    const long long *ac = a + (size_t)ch * QW * plane;
+    Q += (__int128)__ldcs(ac);
+    if (QW == 2) Q += (__int128)__ldcs(ac + plane) << 28;
+  }
+  uint32_t code;
+  if (!finish_code(p, i, j, (unsigned __int128)Q, p.sta[i], p.stb[j], p.LA[i], p.LB[j], p.slotA[i], p.slotB[j],
+                   code))
+    return;
+  p.out[(size_t)i * p.ldo + j] = code;
+  for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
+}
 
 template <int MM, int BN, int QW>
-__global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
-  static_assert(BN % 32 == 0 && MM % kFinishRows == 0 && (QW == 1 || QW == 2), "tile shape");
-  constexpr int PL = BN / 32, RW = kFinishRows, UPT = MM / RW;
+__global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, int parts) {
+  static_assert(BN % 32 == 0 && MM % (8 * kFinishRows) == 0 && (QW == 1 || QW == 2), "tile shape");
+  constexpr int PL = BN / 32, RW = kFinishRows;
+  static_assert(RW * PL <= 32, "one bit per output of a lane");
   constexpr size_t PT = (size_t)MM * BN;   // words of one plane of a tile
-  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cl2 = ceil_log2_int(p.K);
   const int4 z4 = make_int4(0, 0, 0, 0);
   // chunk sums stay exact in int64: |word| < 2^60 (bp8) or < 2^53 (bp16 words)
   const bool sum64 = !p.quire && p.split <= (QW == 1 ? 8 : 1024);
-  const long long nunits = (long long)ntiles * UPT;
-  for (long long un = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); un < nunits; un += (long long)gridDim.x * 8) {
-    const int tl = (int)(un / UPT), rg = (int)(un % UPT);
+  const int rpp = MM / parts;   // rows per item, a multiple of 8 * RW
+  const long long nitems = (long long)ntiles * parts;
+  for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
+    const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
     const int tile = p.tile0 + tl;
     const int tm = tile / p.ntn;
     const int j0 = (tile - tm * p.ntn) * BN;
-    const int rbase = tm * MM + rg * RW;
-    const int nrows = min(RW, p.M - rbase);
-    if (nrows <= 0) continue;
-    const bool rv = lane < nrows;
-    const int4 ral = rv ? p.sta[rbase + lane] : z4;
-    const int Lil = rv ? p.LA[rbase + lane] : 0, sil = rv ? p.slotA[rbase + lane] : -1;
-    // unit bounds for the exact window: min lsb exponent, max width of the rows
-    int ax = rv ? ral.x : INT_MAX, aw = rv ? ral.y - ral.x : INT_MIN;
-#pragma unroll
-    for (int o = RW / 2; o > 0; o >>= 1) {
-      ax = min(ax, __shfl_xor_sync(0xFFFFFFFFu, ax, o));
-      aw = max(aw, __shfl_xor_sync(0xFFFFFFFFu, aw, o));
-    }
-    ax = __shfl_sync(0xFFFFFFFFu, ax, 0);
-    aw = __shfl_sync(0xFFFFFFFFu, aw, 0);
-    const bool rows_plain = __all_sync(0xFFFFFFFFu, !rv || (sil == -1 && ral.z != 0));
-    int4 rb[PL];
-    int Lj[PL], sj[PL];
-    bool jv[PL];
-    bool plain = sum64 && rows_plain;
+    // per column: lsb base, tail slot, min lsb exponent, exact-window width
+    // share (max binade - min lsb + ceil log2 K + 3), valid and nonzero flags
+    int Lj[PL], sj[PL], bx[PL], bw[PL];
+    bool jv[PL], bz[PL];
 #pragma unroll
     for (int q = 0; q < PL; ++q) {
       const int j = j0 + q * 32 + lane;
       jv[q] = j < p.N;
-      rb[q] = jv[q] ? p.stb[j] : z4;
+      const int4 rb = jv[q] ? p.stb[j] : z4;
       Lj[q] = jv[q] ? p.LB[j] : 0;
       sj[q] = jv[q] ? p.slotB[j] : -1;
-      plain = plain && (!jv[q] || (sj[q] == -1 && rb[q].z != 0 && ax + rb[q].x + 96 >= 0 &&
-                                   aw + (rb[q].y - rb[q].x) + cl2 + 3 <= 127));
+      bx[q] = rb.x;
+      bw[q] = (rb.y - rb.x) + cl2 + 3;
+      bz[q] = rb.z != 0;
     }
-    const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + (size_t)rg * RW * BN + lane;
-    // one path per warp: both paths broadcast row statistics by full-warp shuffles
-    if (__all_sync(0xFFFFFFFFu, plain)) {
+    for (int r0 = part * rpp + warp * RW; r0 < (part + 1) * rpp; r0 += 8 * RW) {
+      const int rbase = tm * MM + r0;
+      const int nrows = min(RW, p.M - rbase);
+      if (nrows <= 0) break;
+      const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + (size_t)r0 * BN + lane;
+      if (!sum64) {
+        for (int u = 0; u < nrows; ++u)
+#pragma unroll 1
+          for (int q = 0; q < PL; ++q) {
+            const int j = j0 + q * 32 + lane;
+            if (j < p.N) finish_general<QW>(p, qt + (size_t)u * BN + q * 32, PT, rbase + u, j);
+          }
+        continue;
+      }
+      const bool rv = lane < nrows;
+      const int4 ral = rv ? p.sta[rbase + lane] : z4;
+      const int Lil = rv ? p.LA[rbase + lane] : 0, sil = rv ? p.slotA[rbase + lane] : -1;
       long long qv[RW][PL], qh[RW][PL];
 #pragma unroll
       for (int u = 0; u < RW; ++u)
@@ -624,11 +645,15 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
               if (QW == 2) qh[u][q] += __ldcs(qc + PT + (size_t)u * BN + q * 32);
             }
       }
-      // round all RW x PL sums (selects only), then store the valid ones
       uint32_t cd[RW][PL];
+      uint32_t keep = 0u;   // outputs to store (the others are left to k_tc_fixup)
 #pragma unroll
       for (int u = 0; u < RW; ++u) {
-        const int Li = __shfl_sync(0xFFFFFFFFu, Lil, u);
+        const int rax = __shfl_sync(0xFFFFFFFFu, ral.x, u), ray = __shfl_sync(0xFFFFFFFFu, ral.y, u);
+        const int raz = __shfl_sync(0xFFFFFFFFu, ral.z, u);
+        const int Li = __shfl_sync(0xFFFFFFFFu, Lil, u), si = __shfl_sync(0xFFFFFFFFu, sil, u);
+        // plain outputs: short builder on the main sum (selects only)
+        uint32_t slow = 0u;
 #pragma unroll
         for (int q = 0; q < PL; ++q) {
           if (QW == 1) {
@@ -639,6 +664,42 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
             const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
             cd[u][q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + Lj[q]);
           }
+          const bool valid = u < nrows && jv[q];
+          const bool plain = si == -1 && sj[q] == -1 && raz != 0 && bz[q] && rax + bx[q] + 96 >= 0 &&
+                             (ray - rax) + bw[q] <= 127;
+          if (valid) {
+            if (plain) keep |= 1u << (u * PL + q);
+            else slow |= 1u << q;
+          }
+        }
+        // the others (a tail row or column, a zero row or column, outside the
+        // exact window): all their tail corrections are loaded at once, then
+        // combined in 128 bits (finish_code's rule)
+        if (__any_sync(0xFFFFFFFFu, slow != 0u)) {
+          ulonglong2 ca[PL], cb[PL];
+#pragma unroll
+          for (int q = 0; q < PL; ++q) {
+            const bool sb = (slow >> q) & 1u;
+            const ulonglong2 z2 = make_ulonglong2(0ull, 0ull);
+            ca[q] = (sb && si >= 0) ? p.CA[(size_t)si * p.N + j0 + q * 32 + lane] : z2;
+            cb[q] = (sb && sj[q] >= 0) ? p.CB[(size_t)sj[q] * p.M + rbase + u] : z2;
+          }
+#pragma unroll
+          for (int q = 0; q < PL; ++q) {
+            if (!((slow >> q) & 1u)) continue;
+            if (!(raz && bz[q])) {
+              cd[u][q] = 0u;
+            } else {
+              // tc_exact: inside the 128-bit window, no overflowed tail list
+              if (rax + bx[q] + 96 < 0 || (ray - rax) + bw[q] > 127 || si == -2 || sj[q] == -2)
+                continue;   // left to k_tc_fixup
+              const __int128 Q = (__int128)qv[u][q] + (QW == 2 ? ((__int128)qh[u][q] << 28) : (__int128)0);
+              const int sh = (Li - rax) + (Lj[q] - bx[q]);
+              const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
+              cd[u][q] = write_fast_output(tot, rax + bx[q] + 96, nullptr, nullptr, 0);
+            }
+            keep |= 1u << (u * PL + q);
+          }
         }
       }
       uint32_t *orow = p.out + (size_t)rbase * p.ldo + j0 + lane;
@@ -646,37 +707,14 @@ __global__ void __launch_bounds__(256) k_tc_finish(TcParams p, int ntiles) {
       for (int u = 0; u < RW; ++u)
 #pragma unroll
         for (int q = 0; q < PL; ++q)
-          if (u < nrows && jv[q]) orow[(size_t)u * p.ldo + q * 32] = cd[u][q];
+          if ((keep >> (u * PL + q)) & 1u) orow[(size_t)u * p.ldo + q * 32] = cd[u][q];
       for (int e = 0; e < p.n_extra; ++e) {
         uint32_t *erow = p.extra_out[e] + (size_t)rbase * p.ldo + p.extra_col0 + j0 + lane;
 #pragma unroll
         for (int u = 0; u < RW; ++u)
 #pragma unroll
           for (int q = 0; q < PL; ++q)
-            if (u < nrows && jv[q]) erow[(size_t)u * p.ldo + q * 32] = cd[u][q];
-      }
-      continue;
-    }
-    // general case: K chunks summed in 128 bits, tail corrections, raw quire
-    for (int r = 0; r < nrows; ++r) {
-      const int4 ra = make_int4(__shfl_sync(0xFFFFFFFFu, ral.x, r), __shfl_sync(0xFFFFFFFFu, ral.y, r),
-                                __shfl_sync(0xFFFFFFFFu, ral.z, r), 0);
-      const int Li = __shfl_sync(0xFFFFFFFFu, Lil, r), si = __shfl_sync(0xFFFFFFFFu, sil, r);
-      const int i = rbase + r;
-#pragma unroll
-      for (int q = 0; q < PL; ++q) {
-        if (!jv[q]) continue;
-        const int j = j0 + q * 32 + lane;
-        __int128 Q = 0;
-        for (int ch = 0; ch < p.split; ++ch) {
-          const long long *a = qt + (size_t)ch * QW * PT + (size_t)r * BN + q * 32;
-          Q += (__int128)__ldcs(a);
-          if (QW == 2) Q += (__int128)__ldcs(a + PT) << 28;
-        }
-        uint32_t code;
-        if (!finish_code(p, i, j, (unsigned __int128)Q, ra, rb[q], Li, Lj[q], si, sj[q], code)) continue;
-        p.out[(size_t)i * p.ldo + j] = code;
-        for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
+            if ((keep >> (u * PL + q)) & 1u) erow[(size_t)u * p.ldo + q * 32] = cd[u][q];
       }
     }
   }
@@ -913,7 +951,9 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
         uint32_t v[16];
         uint32_t any = 0u;
         if (k0 < K) {
-          uint4 cw = *(const uint4 *)((const uint8_t *)codes + rb + k0);
+          // last read of these codes; the plane stores below stream past L2
+          // (evict-first) so that this second pass finds its row still there
+          uint4 cw = __ldcs((const uint4 *)((const uint8_t *)codes + rb + k0));
           uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
@@ -947,7 +987,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
           }
 #pragma unroll
           for (int sd = 0; sd < 3; ++sd)
-            *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[sd][0], wd[sd][1], wd[sd][2], wd[sd][3]);
+            __stcs((uint4 *)(row + sd * plane + k0), make_uint4(wd[sd][0], wd[sd][1], wd[sd][2], wd[sd][3]));
         } else {
 #pragma unroll
           for (int sd = 0; sd < S; ++sd) {
@@ -959,7 +999,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
               uint32_t hi2 = __byte_perm(v[4 * g + 2], v[4 * g + 3], sel);
               wd[g] = __byte_perm(lo2, hi2, 0x5410);
             }
-            *(uint4 *)(row + sd * plane + k0) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            __stcs((uint4 *)(row + sd * plane + k0), make_uint4(wd[0], wd[1], wd[2], wd[3]));
           }
         }
       }
@@ -1292,41 +1332,111 @@ int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const Tc
   return check_launch("quire_gemm_tc");
 }
 
-// Blocks of k_tc_finish for `ntiles` tiles: eight units (one per warp) per
-// block, at most `cap` blocks.
+// Launch shape of k_tc_finish for `ntiles` tiles and at most `cap` blocks:
+// each tile cut into `parts` items (a power of two up to MM / (8 rows x
+// kFinishRows)) until there are at least eight items per block.
 template <int MM>
-int finish_grid(int ntiles, int cap) {
-  return (int)std::max<long long>(1, std::min<long long>(((long long)ntiles * (MM / kFinishRows) + 7) / 8, cap));
+void finish_shape(int ntiles, int cap, int &grid, int &parts) {
+  parts = 1;
+  while (parts < MM / (8 * kFinishRows) && (long long)ntiles * parts < 8LL * cap) parts *= 2;
+  grid = (int)std::max<long long>(1, std::min<long long>((long long)ntiles * parts, cap));
 }
 
+// A per-thread, per-device side stream (lowest priority) and events for the
+// finish kernels that overlap the next GEMM launch.  Per thread, so a stream
+// captured into a CUDA graph by one thread never shares it with another.
+// Never destroyed: they live as long as the thread's CUDA context.
+struct SideStream {
+  cudaStream_t st = nullptr;
+  cudaEvent_t ev[3] = {};
+};
+
+SideStream *side_stream() {
+  constexpr int kDev = 64;
+  thread_local SideStream ss[kDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDev) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  SideStream &x = ss[dev];
+  if (!x.st) {
+    int lo = 0, hi = 0;
+    cudaDeviceGetStreamPriorityRange(&lo, &hi);
+    cudaStream_t st = nullptr;
+    if (cudaStreamCreateWithPriority(&st, cudaStreamNonBlocking, lo) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    for (cudaEvent_t &e : x.ev)
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+      }
+    x.st = st;
+  }
+  return &x;
+}
+
+// The GEMM in segments of tiles: all whole tiles but the last full wave, the
+// last full wave, then the K-split remainder.  A segment's finish kernel runs
+// on the side stream while the next segment's GEMM runs (its grid capped at
+// two blocks per SM, so the GEMM's CTA still fits beside them) when that GEMM
+// hides it: measured on B200, a tile's finish at two blocks per SM costs
+// about half of one 64-deep K block of a full wave of tiles, so the rule is
+// tiles <= 2 x the next segment's K blocks per tile (long K only: the
+// 4096 x 4096 x 65536 GEMM overlaps, K <= 4864 does not).  Otherwise, and for
+// the last segment, the finish runs on the caller's stream, which finally
+// waits for the side stream.
 template <int S, bool PAIR>
 int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
                        int grid_finish, cudaStream_t s) {
   using C = Cfg<S, PAIR>;
-  long long *qbuf = p.qbuf;
-  int rc = kOk;
-  p.ntn = sc.ntn;
+  struct Seg {
+    int tile0, n, split, kbc;
+  } seg[3];
+  int nseg = 0;
+  const int P = std::max(1, tc_wave_capacity(PAIR));
+  SideStream *side = side_stream();
   if (sc.whole > 0) {
-    p.tile0 = 0;
-    p.split = 1;
-    p.kb_per_chunk = p.nkb;
-    p.qbuf = qbuf;
-    rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.whole, s);
-    if (rc) return rc;
-    k_tc_finish<C::MM, C::BN, C::QW><<<finish_grid<C::MM>(sc.whole, grid_finish), 256, 0, s>>>(p, sc.whole);
-    rc = check_launch("tc_finish");
-    if (rc) return rc;
+    if (side && sc.whole >= 2 * P && sc.whole - P <= 2 * p.nkb) {
+      seg[nseg++] = {0, sc.whole - P, 1, p.nkb};
+      seg[nseg++] = {sc.whole - P, P, 1, p.nkb};
+    } else {
+      seg[nseg++] = {0, sc.whole, 1, p.nkb};
+    }
   }
-  if (sc.whole < sc.ntiles) {
-    p.tile0 = sc.whole;
-    p.split = sc.split;
-    p.kb_per_chunk = sc.kbc;
-    p.qbuf = qbuf + (size_t)sc.whole * C::QW * C::MM * C::BN;
-    rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, sc.ntiles - sc.whole, s);
-    if (rc) return rc;
-    k_tc_finish<C::MM, C::BN, C::QW><<<finish_grid<C::MM>(sc.ntiles - sc.whole, grid_finish), 256, 0, s>>>(
-        p, sc.ntiles - sc.whole);
+  if (sc.whole < sc.ntiles) seg[nseg++] = {sc.whole, sc.ntiles - sc.whole, sc.split, sc.kbc};
+  long long *qbuf = p.qbuf;
+  p.ntn = sc.ntn;
+  bool forked = false;
+  int rc = kOk;
+  for (int k = 0; k < nseg && rc == kOk; ++k) {
+    p.tile0 = seg[k].tile0;
+    p.split = seg[k].split;
+    p.kb_per_chunk = seg[k].kbc;
+    // every tile before this segment ran whole
+    p.qbuf = qbuf + (size_t)seg[k].tile0 * C::QW * C::MM * C::BN;
+    rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, seg[k].n, s);
+    if (rc) break;
+    const bool on_s = k == nseg - 1 || !side || seg[k].n > 2 * seg[k + 1].kbc;
+    cudaStream_t fs = on_s ? s : side->st;
+    if (!on_s) {
+      if (cudaEventRecord(side->ev[k], s) != cudaSuccess || cudaStreamWaitEvent(side->st, side->ev[k], 0) != cudaSuccess) {
+        rc = set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
+        break;
+      }
+      forked = true;
+    }
+    int g = 1, parts = 1;
+    finish_shape<C::MM>(seg[k].n, on_s ? grid_finish : std::min(grid_finish, 2 * sm_count()), g, parts);
+    k_tc_finish<C::MM, C::BN, C::QW><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
     rc = check_launch("tc_finish");
+  }
+  if (forked) {
+    // join, also on the error path: the caller's stream never runs ahead of the side stream
+    if (cudaEventRecord(side->ev[2], side->st) != cudaSuccess || cudaStreamWaitEvent(s, side->ev[2], 0) != cudaSuccess)
+      if (rc == kOk) rc = set_error(kECuda, "quire_gemm: side stream join: %s", cudaGetErrorString(cudaGetLastError()));
   }
   return rc;
 }
@@ -1427,10 +1537,11 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   if (tc_qbuf_bytes(sc) > L.total - L.part) return set_error(kEWorkspace, "quire_gemm: sum buffer too small");
   size_t outs = (size_t)a.M * a.N;
   int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);
+  const int gf = sms * 4;   // k_tc_finish: four blocks per SM are resident
   if (S == 3)
-    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, g, s) : launch_tc_schedule<3, false>(ma, mb, p, sc, g, s);
+    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s) : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s);
   else
-    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, g, s) : launch_tc_schedule<4, false>(ma, mb, p, sc, g, s);
+    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, gf, s) : launch_tc_schedule<4, false>(ma, mb, p, sc, gf, s);
   if (rc) return rc;
   if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
