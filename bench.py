@@ -397,6 +397,14 @@ def run_ours(args):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ems = float(tt.item())
     e2e_tops = 2.0 * M_ * N_ * K_ / (ems * 1e-3) / 1e12
+    # the box's host link, for reading the e2e figure: one plain pinned copy of A
+    # (the e2e step is bound by its host-to-device bytes on a healthy link)
+    hs, ht = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hs.record(stream)
+    dA.copy_(hA, non_blocking=True)
+    ht.record(stream)
+    torch.cuda.synchronize()
+    h2d_gbs = A.numel() * A.element_size() / (hs.elapsed_time(ht) * 1e-3) / 1e9
     del hA, hB, dA, dB
 
     codec = codec_sweep(ops, torch, device, world, 10, peaks)
@@ -444,7 +452,8 @@ def run_ours(args):
                          "slice_pairs_per_useful_mac": slice_pairs},
             "e2e": {"value": round(e2e_tops, 3), "unit": "TOPS", "ms_per_step": round(ems, 3),
                     "h2d_bytes_per_step": int((m1 - m0) * K_ + (n1 - n0) * K_),
-                    "d2h_bytes_per_step": int(M_ * N_ * 4)},
+                    "d2h_bytes_per_step": int(M_ * N_ * 4),
+                    "h2d_link_gbs": round(h2d_gbs, 1)},
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
             "clocks": clk,

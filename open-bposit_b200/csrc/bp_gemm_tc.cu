@@ -551,15 +551,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 //
 // A block takes items -- 1/parts of a tile's rows, all its columns -- in a
 // grid-stride loop; lane l owns the columns l, l + 32, ..., whose statistics
-// it loads once per item; warp w takes the item's units of kFinishRows rows
-// w, w + 8, ..., whose row statistics are loaded once (lane r holds row r)
-// and broadcast by shuffles.  While the chunk sums stay inside int64 (always,
-// but for a raw quire output or more than 8 bp8 K chunks) a lane loads and
-// adds its sums and rounds the plain ones (no tail correction, nonzero row and
-// column, inside the exact window) with the short builder; per row, the others
-// load all their tail corrections at once and take finish_code's 128-bit
-// rule.  Otherwise every output goes through finish_general one by one.
-constexpr int kFinishRows = 1;
+// it loads once per item; warp w takes the item's rows w, w + 8, ...  While
+// the chunk sums stay inside int64 (always, but for a raw quire output or
+// more than 8 bp8 K chunks) a lane adds its sums in int64 and rounds the plain
+// ones (no tail correction, nonzero row and column, inside the exact window)
+// with the short builder; the others of the row load all their tail
+// corrections at once and take finish_code's 128-bit rule.  With one K chunk
+// the loads of the warp's next row are issued before the current row is
+// rounded (software pipelining: the loads' latency was the kernel's main
+// stall).  Otherwise every output goes through finish_general one by one.
 
 // The general rule for output (i, j) of a unit: the chunks' sums added in 128
 // bits, finish_code (tail corrections, zero rows, raw quire), stores.
@@ -579,143 +579,173 @@ __device__ __forceinline__ void finish_general(const TcParams &p, const long lon
   for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
 }
 
+// Per-column state of a finish item, one entry per column a lane owns: lsb
+// base, tail slot, min lsb exponent, exact-window width share (max binade - min
+// lsb + ceil log2 K + 3), valid and nonzero flags.
+template <int PL>
+struct FinishCols {
+  int Lj[PL], sj[PL], bx[PL], bw[PL];
+  bool jv[PL], bz[PL];
+};
+
+// Rounds and stores row i of an item from its int64 sums (words qv, qh) and
+// row statistics (ra, Li, si).  Whole warp: the tail corrections' loads are
+// taken only when some lane of the warp needs them.
+template <int PL, int QW>
+__device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<PL> &c, int i, int j0, int lane,
+                                           const long long (&qv)[PL], const long long (&qh)[PL], int4 ra, int Li,
+                                           int si) {
+  uint32_t cd[PL];
+  uint32_t slow = 0u, keep = 0u;
+#pragma unroll
+  for (int q = 0; q < PL; ++q) {
+    if (QW == 1) {
+      cd[q] = bp32_from_i64(qv[q], Li + c.Lj[q]);
+    } else {
+      const __int128 Q = (__int128)qv[q] + ((__int128)qh[q] << 28);
+      const bool neg = Q < 0;
+      const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
+      cd[q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + c.Lj[q]);
+    }
+    const bool plain = si == -1 && c.sj[q] == -1 && ra.z != 0 && c.bz[q] && ra.x + c.bx[q] + 96 >= 0 &&
+                       (ra.y - ra.x) + c.bw[q] <= 127;
+    if (c.jv[q]) {
+      if (plain) keep |= 1u << q;
+      else slow |= 1u << q;
+    }
+  }
+  // the others (a tail row or column, a zero row or column, outside the exact
+  // window): all their tail corrections are loaded at once, then combined in
+  // 128 bits (finish_code's rule)
+  if (__any_sync(0xFFFFFFFFu, slow != 0u)) {
+    ulonglong2 ca[PL], cb[PL];
+#pragma unroll
+    for (int q = 0; q < PL; ++q) {
+      const bool sb = (slow >> q) & 1u;
+      const ulonglong2 z2 = make_ulonglong2(0ull, 0ull);
+      ca[q] = (sb && si >= 0) ? p.CA[(size_t)si * p.N + j0 + q * 32 + lane] : z2;
+      cb[q] = (sb && c.sj[q] >= 0) ? p.CB[(size_t)c.sj[q] * p.M + i] : z2;
+    }
+#pragma unroll
+    for (int q = 0; q < PL; ++q) {
+      if (!((slow >> q) & 1u)) continue;
+      if (!(ra.z && c.bz[q])) {
+        cd[q] = 0u;
+      } else {
+        // tc_exact: inside the 128-bit window, no overflowed tail list
+        if (ra.x + c.bx[q] + 96 < 0 || (ra.y - ra.x) + c.bw[q] > 127 || si == -2 || c.sj[q] == -2)
+          continue;   // left to k_tc_fixup
+        const __int128 Q = (__int128)qv[q] + (QW == 2 ? ((__int128)qh[q] << 28) : (__int128)0);
+        const int sh = (Li - ra.x) + (c.Lj[q] - c.bx[q]);
+        const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
+        cd[q] = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
+      }
+      keep |= 1u << q;
+    }
+  }
+  uint32_t *orow = p.out + (size_t)i * p.ldo + j0 + lane;
+#pragma unroll
+  for (int q = 0; q < PL; ++q)
+    if ((keep >> q) & 1u) orow[q * 32] = cd[q];
+  for (int e = 0; e < p.n_extra; ++e) {
+    uint32_t *erow = p.extra_out[e] + (size_t)i * p.ldo + p.extra_col0 + j0 + lane;
+#pragma unroll
+    for (int q = 0; q < PL; ++q)
+      if ((keep >> q) & 1u) erow[q * 32] = cd[q];
+  }
+}
+
 template <int MM, int BN, int QW>
 __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, int parts) {
-  static_assert(BN % 32 == 0 && MM % (8 * kFinishRows) == 0 && (QW == 1 || QW == 2), "tile shape");
-  constexpr int PL = BN / 32, RW = kFinishRows;
-  static_assert(RW * PL <= 32, "one bit per output of a lane");
+  static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
+  constexpr int PL = BN / 32;
   constexpr size_t PT = (size_t)MM * BN;   // words of one plane of a tile
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cl2 = ceil_log2_int(p.K);
   const int4 z4 = make_int4(0, 0, 0, 0);
   // chunk sums stay exact in int64: |word| < 2^60 (bp8) or < 2^53 (bp16 words)
   const bool sum64 = !p.quire && p.split <= (QW == 1 ? 8 : 1024);
-  const int rpp = MM / parts;   // rows per item, a multiple of 8 * RW
+  const int rpp = MM / parts;   // rows per item, a multiple of 8
   const long long nitems = (long long)ntiles * parts;
   for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
     const int tile = p.tile0 + tl;
     const int tm = tile / p.ntn;
     const int j0 = (tile - tm * p.ntn) * BN;
-    // per column: lsb base, tail slot, min lsb exponent, exact-window width
-    // share (max binade - min lsb + ceil log2 K + 3), valid and nonzero flags
-    int Lj[PL], sj[PL], bx[PL], bw[PL];
-    bool jv[PL], bz[PL];
+    FinishCols<PL> c;
 #pragma unroll
     for (int q = 0; q < PL; ++q) {
       const int j = j0 + q * 32 + lane;
-      jv[q] = j < p.N;
-      const int4 rb = jv[q] ? p.stb[j] : z4;
-      Lj[q] = jv[q] ? p.LB[j] : 0;
-      sj[q] = jv[q] ? p.slotB[j] : -1;
-      bx[q] = rb.x;
-      bw[q] = (rb.y - rb.x) + cl2 + 3;
-      bz[q] = rb.z != 0;
+      c.jv[q] = j < p.N;
+      const int4 rb = c.jv[q] ? p.stb[j] : z4;
+      c.Lj[q] = c.jv[q] ? p.LB[j] : 0;
+      c.sj[q] = c.jv[q] ? p.slotB[j] : -1;
+      c.bx[q] = rb.x;
+      c.bw[q] = (rb.y - rb.x) + cl2 + 3;
+      c.bz[q] = rb.z != 0;
     }
-    for (int r0 = part * rpp + warp * RW; r0 < (part + 1) * rpp; r0 += 8 * RW) {
-      const int rbase = tm * MM + r0;
-      const int nrows = min(RW, p.M - rbase);
-      if (nrows <= 0) break;
-      const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + (size_t)r0 * BN + lane;
-      if (!sum64) {
-        for (int u = 0; u < nrows; ++u)
+    // rows of this item that exist, relative to the tile; a warp's rows are
+    // r0 + 8k
+    const int rend = min((part + 1) * rpp, p.M - tm * MM);
+    const int r0 = part * rpp + warp;
+    const long long *qt = p.qbuf + (size_t)tl * p.split * QW * PT + lane;
+    if (!sum64) {
+      for (int r = r0; r < rend; r += 8)
 #pragma unroll 1
-          for (int q = 0; q < PL; ++q) {
-            const int j = j0 + q * 32 + lane;
-            if (j < p.N) finish_general<QW>(p, qt + (size_t)u * BN + q * 32, PT, rbase + u, j);
-          }
-        continue;
-      }
-      const bool rv = lane < nrows;
-      const int4 ral = rv ? p.sta[rbase + lane] : z4;
-      const int Lil = rv ? p.LA[rbase + lane] : 0, sil = rv ? p.slotA[rbase + lane] : -1;
-      long long qv[RW][PL], qh[RW][PL];
-#pragma unroll
-      for (int u = 0; u < RW; ++u)
-#pragma unroll
-        for (int q = 0; q < PL; ++q) qv[u][q] = qh[u][q] = 0ll;
-      for (int ch = 0; ch < p.split; ++ch) {
-        const long long *qc = qt + (size_t)ch * QW * PT;
-#pragma unroll
-        for (int u = 0; u < RW; ++u)
-#pragma unroll
-          for (int q = 0; q < PL; ++q)
-            if (u < nrows && jv[q]) {
-              qv[u][q] += __ldcs(qc + (size_t)u * BN + q * 32);
-              if (QW == 2) qh[u][q] += __ldcs(qc + PT + (size_t)u * BN + q * 32);
-            }
-      }
-      uint32_t cd[RW][PL];
-      uint32_t keep = 0u;   // outputs to store (the others are left to k_tc_fixup)
-#pragma unroll
-      for (int u = 0; u < RW; ++u) {
-        const int rax = __shfl_sync(0xFFFFFFFFu, ral.x, u), ray = __shfl_sync(0xFFFFFFFFu, ral.y, u);
-        const int raz = __shfl_sync(0xFFFFFFFFu, ral.z, u);
-        const int Li = __shfl_sync(0xFFFFFFFFu, Lil, u), si = __shfl_sync(0xFFFFFFFFu, sil, u);
-        // plain outputs: short builder on the main sum (selects only)
-        uint32_t slow = 0u;
+        for (int q = 0; q < PL; ++q) {
+          const int j = j0 + q * 32 + lane;
+          if (j < p.N) finish_general<QW>(p, qt + (size_t)r * BN + q * 32, PT, tm * MM + r, j);
+        }
+      continue;
+    }
+    if (p.split == 1) {
+      // software pipeline over the warp's rows: row r + 8's sums and row
+      // statistics are in flight while row r is rounded and stored
+      long long nq[PL], nh[PL];
+      int4 nra = z4;
+      int nL = 0, ns = -1;
+      auto fetch = [&](int r) {
 #pragma unroll
         for (int q = 0; q < PL; ++q) {
-          if (QW == 1) {
-            cd[u][q] = bp32_from_i64(qv[u][q], Li + Lj[q]);
-          } else {
-            const __int128 Q = (__int128)qv[u][q] + ((__int128)qh[u][q] << 28);
-            const bool neg = Q < 0;
-            const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
-            cd[u][q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + Lj[q]);
-          }
-          const bool valid = u < nrows && jv[q];
-          const bool plain = si == -1 && sj[q] == -1 && raz != 0 && bz[q] && rax + bx[q] + 96 >= 0 &&
-                             (ray - rax) + bw[q] <= 127;
-          if (valid) {
-            if (plain) keep |= 1u << (u * PL + q);
-            else slow |= 1u << q;
-          }
+          const long long *a = qt + (size_t)r * BN + q * 32;
+          nq[q] = c.jv[q] ? __ldcs(a) : 0ll;
+          nh[q] = (QW == 2 && c.jv[q]) ? __ldcs(a + PT) : 0ll;
         }
-        // the others (a tail row or column, a zero row or column, outside the
-        // exact window): all their tail corrections are loaded at once, then
-        // combined in 128 bits (finish_code's rule)
-        if (__any_sync(0xFFFFFFFFu, slow != 0u)) {
-          ulonglong2 ca[PL], cb[PL];
+        const int i = tm * MM + r;
+        nra = p.sta[i];
+        nL = p.LA[i];
+        ns = p.slotA[i];
+      };
+      if (r0 < rend) fetch(r0);
+      for (int r = r0; r < rend; r += 8) {
+        long long cq[PL], chh[PL];
 #pragma unroll
-          for (int q = 0; q < PL; ++q) {
-            const bool sb = (slow >> q) & 1u;
-            const ulonglong2 z2 = make_ulonglong2(0ull, 0ull);
-            ca[q] = (sb && si >= 0) ? p.CA[(size_t)si * p.N + j0 + q * 32 + lane] : z2;
-            cb[q] = (sb && sj[q] >= 0) ? p.CB[(size_t)sj[q] * p.M + rbase + u] : z2;
-          }
-#pragma unroll
-          for (int q = 0; q < PL; ++q) {
-            if (!((slow >> q) & 1u)) continue;
-            if (!(raz && bz[q])) {
-              cd[u][q] = 0u;
-            } else {
-              // tc_exact: inside the 128-bit window, no overflowed tail list
-              if (rax + bx[q] + 96 < 0 || (ray - rax) + bw[q] > 127 || si == -2 || sj[q] == -2)
-                continue;   // left to k_tc_fixup
-              const __int128 Q = (__int128)qv[u][q] + (QW == 2 ? ((__int128)qh[u][q] << 28) : (__int128)0);
-              const int sh = (Li - rax) + (Lj[q] - bx[q]);
-              const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
-              cd[u][q] = write_fast_output(tot, rax + bx[q] + 96, nullptr, nullptr, 0);
-            }
-            keep |= 1u << (u * PL + q);
-          }
+        for (int q = 0; q < PL; ++q) {
+          cq[q] = nq[q];
+          chh[q] = nh[q];
         }
+        const int4 ra = nra;
+        const int Li = nL, si = ns;
+        if (r + 8 < rend) fetch(r + 8);
+        finish_row<PL, QW>(p, c, tm * MM + r, j0, lane, cq, chh, ra, Li, si);
       }
-      uint32_t *orow = p.out + (size_t)rbase * p.ldo + j0 + lane;
+      continue;
+    }
+    for (int r = r0; r < rend; r += 8) {
+      long long cq[PL], chh[PL];
 #pragma unroll
-      for (int u = 0; u < RW; ++u)
+      for (int q = 0; q < PL; ++q) cq[q] = chh[q] = 0ll;
+      for (int ch = 0; ch < p.split; ++ch) {
 #pragma unroll
         for (int q = 0; q < PL; ++q)
-          if ((keep >> (u * PL + q)) & 1u) orow[(size_t)u * p.ldo + q * 32] = cd[u][q];
-      for (int e = 0; e < p.n_extra; ++e) {
-        uint32_t *erow = p.extra_out[e] + (size_t)rbase * p.ldo + p.extra_col0 + j0 + lane;
-#pragma unroll
-        for (int u = 0; u < RW; ++u)
-#pragma unroll
-          for (int q = 0; q < PL; ++q)
-            if ((keep >> (u * PL + q)) & 1u) erow[(size_t)u * p.ldo + q * 32] = cd[u][q];
+          if (c.jv[q]) {
+            const long long *a = qt + (size_t)ch * QW * PT + (size_t)r * BN + q * 32;
+            cq[q] += __ldcs(a);
+            if (QW == 2) chh[q] += __ldcs(a + PT);
+          }
       }
+      const int i = tm * MM + r;
+      finish_row<PL, QW>(p, c, i, j0, lane, cq, chh, p.sta[i], p.LA[i], p.slotA[i]);
     }
   }
   if (p.n_extra) __threadfence_system();
@@ -1333,12 +1363,12 @@ int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const Tc
 }
 
 // Launch shape of k_tc_finish for `ntiles` tiles and at most `cap` blocks:
-// each tile cut into `parts` items (a power of two up to MM / (8 rows x
-// kFinishRows)) until there are at least eight items per block.
+// each tile cut into `parts` items (a power of two up to MM / 8 rows) until
+// there are at least eight items per block.
 template <int MM>
 void finish_shape(int ntiles, int cap, int &grid, int &parts) {
   parts = 1;
-  while (parts < MM / (8 * kFinishRows) && (long long)ntiles * parts < 8LL * cap) parts *= 2;
+  while (parts < MM / 8 && (long long)ntiles * parts < 8LL * cap) parts *= 2;
   grid = (int)std::max<long long>(1, std::min<long long>((long long)ntiles * parts, cap));
 }
 
