@@ -374,7 +374,7 @@ def run_ours(args):
 
     def e2e_step():
         if world == 1:
-            # the host-buffer C ABI: B streamed in chunks, copies overlapped with the GEMM
+            # the host-buffer C ABI: A streamed in row chunks (M >= N), copies overlapped with the GEMM
             ops.quire_gemm_host(hA, hB, 8, out=hOut, algo=args.algo)
             return
         dA.copy_(hA, non_blocking=True)

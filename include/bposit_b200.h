@@ -158,9 +158,15 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
 
 /* bp_quire_gemm on HOST buffers: A, B, sa, sb and out_bp32 are host pointers
  * (page-locked memory gives full PCIe bandwidth; pageable memory works,
- * slower).  B is streamed to the device in row chunks while earlier chunks
- * are multiplied and their bposit32 blocks copied back, so the copies in,
- * the tensor-core work and the copies out overlap; A is prepared once.  The
+ * slower).  One operand goes to the device whole and is prepared once; the
+ * other is streamed in row chunks (A when M >= N, whose chunks' results are
+ * whole rows and leave in one contiguous copy each; else B) while earlier
+ * chunks are multiplied and their bposit32 blocks copied back, so the copies
+ * in, the tensor-core work and the copies out overlap.  Its device buffers
+ * are kept per host thread and device for later calls (they grow to the
+ * largest call's sizes, about 1.6 GB for 4096 x 4096 x 65536 bp8, and are
+ * held until the process exits); a call waits for the previous call of the
+ * same thread on that device, whatever its stream.  The
  * call is asynchronous on `stream` like every other entry point: out_bp32 is
  * complete when the stream is.  Same results as bp_quire_gemm.  Replaces
  * matmul_quire + quire256_to_bposit32 on numpy arrays
@@ -168,8 +174,8 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
 int bp_quire_gemm_host(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
                        const int32_t *sb, int group, uint32_t *out_bp32, int64_t ldo, int algo, void *stream);
 
-/* bp_quire_gemm whose bposit32 results are also stored, by the GEMM epilogue
- * itself, into n_peer further [M, ldo] matrices at column peer_col0 -- on a
+/* bp_quire_gemm whose bposit32 results are also stored, by the GEMM's finish
+ * kernel itself, into n_peer further [M, ldo] matrices at column peer_col0 -- on a
  * multi-GPU node, the full result matrices of the other ranks, reached over
  * NVLink (mapped with bp_ipc_open; peer access from bp_enable_peer_access).  One call both
  * computes this rank's N-shard and all-gathers it: after every rank's call has

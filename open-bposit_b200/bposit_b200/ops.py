@@ -194,10 +194,12 @@ def quire_gemm(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, gro
 
 def quire_gemm_host(A, B, fmt=None, sa=None, sb=None, group: int = 128, out=None, algo: int = 0):
     """Exact quire GEMM on host arrays (CPU tensors or numpy; page-locked CPU
-    tensors copy fastest): the library streams B to the device in chunks and
-    overlaps the copies with the tensor-core work.  Returns the [M, N] uint32
-    bposit32 codes as a CPU tensor (`out`, if given), complete once the
-    current CUDA stream is synchronized."""
+    tensors copy fastest): the library sends one operand whole and streams the
+    other in row chunks (A when M >= N, so that each chunk's results leave in
+    one contiguous copy; else B), overlapping the copies with the tensor-core
+    work.  Returns the [M, N] uint32 bposit32 codes as a CPU tensor (`out`, if
+    given; its rows may be strided), complete once the current CUDA stream is
+    synchronized."""
     def host(x, dtype):
         t = torch.as_tensor(x)
         if t.is_cuda:
@@ -227,7 +229,7 @@ def quire_gemm_multi(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, peer_p
                      fmt=None, sa=None, sb=None, group: int = 128, algo: int = 0, workspace=None):
     """quire_gemm whose bp32 results are also stored into every matrix in
     `peer_ptrs` (device addresses of [M, ldo] uint32 matrices, normally other
-    GPUs' result buffers) at column `peer_col0`, by the GEMM epilogue itself.
+    GPUs' result buffers) at column `peer_col0`, by the GEMM's finish kernel itself.
     `out` is this rank's [M, N] column block (row stride ldo)."""
     f = fmt_bits(fmt) if fmt is not None else (8 if A.dtype == torch.uint8 else 16)
     a = _dev(A, "A", _CODE_DTYPE[f])

@@ -93,7 +93,7 @@ int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cu
     if (ws_bytes < need_stats + need) return set_error(kEWorkspace, "quire_gemm: workspace too small");
     return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo == 3, a_mode, s);
   }
-  if (a_mode == 2) return kOk;   // the CUDA-core path prepares nothing ahead
+  if (a_mode == 2 || a_mode == 3) return kOk;   // the CUDA-core path prepares nothing ahead
   int rc = launch_row_stats(a.fmt, a.A, a.M, a.K, a.sa, a.group, sta, s);
   if (rc) return rc;
   rc = launch_row_stats(a.fmt, a.B, a.N, a.K, a.sb, a.group, stb, s);

@@ -39,7 +39,6 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
-#include <climits>
 
 #include <algorithm>
 #include <atomic>
@@ -1481,14 +1480,15 @@ bool gemm_tc_supported(int fmt, int M, int N, int K) {
 size_t gemm_tc_workspace(int fmt, int M, int N, int K) { return tc_layout(fmt, M, N, K).total; }
 
 // sta / stb are outputs here: the prep kernels write the row statistics.
-// A's preparation (statistics in sta, digit planes, bases, tail lists,
-// counters) can be done alone (a_mode 2) and reused by later calls with the
-// same A, M, K and workspace layout (the same N) that prepare only B (a_mode 1).
+// One operand's preparation (statistics, digit planes, bases, tail lists,
+// counters) can be done alone (a_mode 2 for A, 3 for B) and reused by later
+// calls with the same operand, M, N, K and workspace that prepare only the
+// other one (a_mode 1 reuses A, 4 reuses B).
 int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
                    int a_mode, cudaStream_t s) {
   // a_mode 0: prepare A and B and multiply; 1: A already prepared (reuse);
-  // 2: prepare A only
-  const bool reuse_a = a_mode == 1, a_only = a_mode == 2;
+  // 2: prepare A only; 3: prepare B only; 4: B already prepared (reuse)
+  const bool reuse_a = a_mode == 1, a_only = a_mode == 2, b_only = a_mode == 3, reuse_b = a_mode == 4;
   TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K);
   if (ws_bytes < L.total) return set_error(kEWorkspace, "quire_gemm: tensor-core workspace too small");
   char *w = (char *)ws;
@@ -1502,8 +1502,9 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   ulonglong2 *CA = (ulonglong2 *)(w + L.CA), *CB = (ulonglong2 *)(w + L.CB);
   long long *qbuf = (long long *)(w + L.part);
 
-  cudaError_t e = reuse_a ? cudaMemsetAsync(cB, 0, sizeof(TcCounters), s)
-                          : cudaMemsetAsync(cA, 0, (a_only ? 1 : 2) * sizeof(TcCounters), s);
+  // zero the counters of the operands prepared by this call
+  cudaError_t e = (reuse_a || b_only) ? cudaMemsetAsync(cB, 0, sizeof(TcCounters), s)
+                  : cudaMemsetAsync(cA, 0, ((a_only || reuse_b) ? 1 : 2) * sizeof(TcCounters), s);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(e));
   const int sms = sm_count();
   auto prep = [&](const void *codes, int rows, const int32_t *sc, int4 *st, int8_t *planes, int *Lr, int *slot,
@@ -1518,12 +1519,14 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     return check_launch("tc_prep");
   };
   int rc = kOk;
-  if (!reuse_a) {
+  if (!reuse_a && !b_only) {
     rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA);
     if (rc || a_only) return rc;
   }
-  rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB);
-  if (rc) return rc;
+  if (!reuse_b) {
+    rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB);
+    if (rc || b_only) return rc;
+  }
 
   // tail corrections (the kernels read the tail-row counts on the device)
   dim3 ga((unsigned)std::min(L.capA, sms * 2), (unsigned)std::min((a.N + 255) / 256, 64));

@@ -72,7 +72,8 @@ struct GemmArgs {
 size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo);
 bool gemm_uses_tc(const GemmArgs &a, int algo);
 // a_mode (tensor-core path): 0 prepare A and B, then multiply; 1 reuse A's
-// preparation from an earlier call on the same workspace; 2 prepare A only.
+// preparation from an earlier call on the same workspace; 2 prepare A only;
+// 3 prepare B only; 4 reuse B's preparation.
 int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s,
                       int a_mode = 0);
 

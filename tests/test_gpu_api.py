@@ -157,19 +157,23 @@ def test_small_rungs_against_reference_vectors():
                for i in range(5) for j in range(4))
 
 
-@pytest.mark.parametrize("case", ["chunked", "chunked_groups", "bp16_small", "pageable"])
+@pytest.mark.parametrize("case", ["chunked", "chunked_groups", "bp16_small", "pageable", "rows", "rows_groups",
+                                  "rows_strided_out"])
 def test_quire_gemm_host_buffers(case):
-    """bp_quire_gemm_host (host buffers, B streamed in chunks, A prepared once)
-    gives exactly the device GEMM's codes."""
+    """bp_quire_gemm_host (host buffers; one operand prepared once, the other
+    streamed in row chunks: B when M < N, A when M >= N) gives exactly the
+    device GEMM's codes."""
     from bposit_b200 import ops
     rng = np.random.default_rng(7)
     group = 128
     if case in ("chunked", "chunked_groups", "pageable"):
-        M, N, K, fmt = 2048, 3000, 16384, 8      # 82 MB of codes: 4 chunks of 768 rows, the last padded
+        M, N, K, fmt = 2048, 3000, 16384, 8      # 82 MB of codes: B in 4 chunks of 768 rows, the last padded
+    elif case.startswith("rows"):
+        M, N, K, fmt = 3000, 2048, 16384, 8      # A in 4 chunks of 768 rows, the last padded
     else:
         M, N, K, fmt = 200, 300, 1000, 16
     dt = np.uint8 if fmt == 8 else np.uint16
-    if case == "chunked_groups":
+    if case in ("chunked_groups", "rows_groups"):
         X = torch.randn(M, K, device="cuda")
         W = torch.randn(N, K, device="cuda") * 0.02
         A, sa = ops.quantize_bp8_grouped(X, group=group)
@@ -186,6 +190,13 @@ def test_quire_gemm_host_buffers(case):
         hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
         hsa = None if sa is None else sa.cpu().pin_memory()
         hsb = None if sb is None else sb.cpu().pin_memory()
-        out = ops.quire_gemm_host(hA, hB, fmt, sa=hsa, sb=hsb, group=group)
+        wide = None
+        if case == "rows_strided_out":          # the result lands in a column block of a wider matrix
+            wide = torch.zeros((M, N + 40), dtype=torch.uint32).pin_memory()
+        out = ops.quire_gemm_host(hA, hB, fmt, sa=hsa, sb=hsb, group=group,
+                                  out=None if wide is None else wide[:, 16:16 + N])
+        if wide is not None:
+            torch.cuda.current_stream().synchronize()
+            assert not wide[:, :16].view(torch.int32).any() and not wide[:, 16 + N:].view(torch.int32).any()
     torch.cuda.current_stream().synchronize()
     assert torch.equal(out.view(torch.int32), ref.cpu().view(torch.int32))
