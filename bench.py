@@ -5,7 +5,7 @@ Headline (one JSON line on rank 0): bit-exact bp8 quire-GEMM throughput in
 TOPS (2*M*N*K / time) on the large bp8 GEMM M=4096, N=4096, K=65536 with
 operands N(0,1) * 2^U{-8..8} per row (seeded, synthetic), the output split into
 blocks over a pm x pn grid of ranks (chosen by dist.choose_grid) and the
-bposit32 result all-gathered by the GEMM epilogue itself (NVLink peer stores;
+bposit32 result all-gathered by the GEMM's finish kernel itself (NVLink peer stores;
 --gather nccl for N shards and an NCCL all-gather).
 The same line carries the encode/decode sweep (2^28 fp32 per rank) in GB/s.
 
@@ -477,7 +477,7 @@ def main():
     ap.add_argument("--algo", type=int, default=0, help="0 auto, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--gather", choices=["fused", "nccl"], default="fused",
-                    help="all-gather of the output blocks: in the GEMM epilogue (peer stores, M x N rank grid) "
+                    help="all-gather of the output blocks: in the GEMM's finish kernel (peer stores, M x N rank grid) "
                          "or NCCL (N shards)")
     args = ap.parse_args()
     if args.warmup < 3:

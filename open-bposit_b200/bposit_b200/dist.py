@@ -9,7 +9,7 @@ Two ways to all-gather the blocks:
   ShardedQuireGemm       -- one NCCL all_gather_into_tensor of the [M, N/p]
                             uint32 shards into [p, M, N/p], then a local
                             transpose into [M, N];
-  FusedShardedQuireGemm  -- the GEMM epilogue stores every finished bposit32
+  FusedShardedQuireGemm  -- the GEMM's finish kernel stores every bposit32
                             straight into all ranks' [M, N] result buffers over
                             NVLink (peer stores into CUDA-IPC-shared memory);
                             two one-word NCCL all-reduces order the call
@@ -143,7 +143,7 @@ def choose_grid(world: int, M: int, N: int, K: int, fmt: int = 8, wave: int = 74
 
 
 class FusedShardedQuireGemm:
-    """N-sharded quire GEMM with the all-gather fused into the GEMM epilogue.
+    """N-sharded quire GEMM with the all-gather fused into the GEMM's finish kernel.
 
     Every rank allocates one [M, N] uint32 result in CUDA-IPC-shareable memory
     and maps every peer's result into its own device context; each rank's
