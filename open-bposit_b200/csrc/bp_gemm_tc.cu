@@ -1377,7 +1377,7 @@ void finish_shape(int ntiles, int cap, int &grid, int &parts) {
 // Never destroyed: they live as long as the thread's CUDA context.
 struct SideStream {
   cudaStream_t st = nullptr;
-  cudaEvent_t ev[3] = {};
+  cudaEvent_t ev[5] = {};   // 0, 1: finish forks; 2: join; 3: tail-correction fork; 4: corrections done
 };
 
 SideStream *side_stream() {
@@ -1419,7 +1419,7 @@ SideStream *side_stream() {
 // waits for the side stream.
 template <int S, bool PAIR>
 int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
-                       int grid_finish, cudaStream_t s) {
+                       int grid_finish, cudaStream_t s, cudaEvent_t corr_done) {
   using C = Cfg<S, PAIR>;
   struct Seg {
     int tile0, n, split, kbc;
@@ -1438,7 +1438,9 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
   if (sc.whole < sc.ntiles) seg[nseg++] = {sc.whole, sc.ntiles - sc.whole, sc.split, sc.kbc};
   long long *qbuf = p.qbuf;
   p.ntn = sc.ntn;
-  bool forked = false;
+  // corrections computed on the side stream: finishes there follow them in
+  // stream order, the caller's stream waits for them before its first finish
+  bool forked = corr_done != nullptr, corr_waited = false;
   int rc = kOk;
   for (int k = 0; k < nseg && rc == kOk; ++k) {
     p.tile0 = seg[k].tile0;
@@ -1456,6 +1458,13 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
         break;
       }
       forked = true;
+    }
+    if (on_s && corr_done && !corr_waited) {
+      if (cudaStreamWaitEvent(s, corr_done, 0) != cudaSuccess) {
+        rc = set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
+        break;
+      }
+      corr_waited = true;
     }
     int g = 1, parts = 1;
     finish_shape<C::MM>(seg[k].n, on_s ? grid_finish : std::min(grid_finish, 2 * sm_count()), g, parts);
@@ -1528,27 +1537,6 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     if (rc || b_only) return rc;
   }
 
-  // tail corrections (the kernels read the tail-row counts on the device)
-  dim3 ga((unsigned)std::min(L.capA, sms * 2), (unsigned)std::min((a.N + 255) / 256, 64));
-  dim3 gb((unsigned)std::min(L.capB, sms * 2), (unsigned)std::min((a.M + 255) / 256, 64));
-  if (a.fmt == 8) {
-    k_tc_corr<8><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA, cA,
-                                    L.capA, CA);
-    rc = check_launch("tc_corr");
-    if (rc) return rc;
-    k_tc_corr<8><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB, cB,
-                                    L.capB, CB);
-  } else {
-    k_tc_corr<16><<<ga, 256, 0, s>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
-                                     cA, L.capA, CA);
-    rc = check_launch("tc_corr");
-    if (rc) return rc;
-    k_tc_corr<16><<<gb, 256, 0, s>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB, cB,
-                                     L.capB, CB);
-  }
-  rc = check_launch("tc_corr");
-  if (rc) return rc;
-
   int S = L.S;
   // Paired SMs whenever the tile has a second 128-row half to work on.
   const bool pair = !single_sm && BK == 64 && a.M > BM;
@@ -1571,10 +1559,58 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   size_t outs = (size_t)a.M * a.N;
   int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);
   const int gf = sms * 4;   // k_tc_finish: four blocks per SM are resident
+
+  // tail corrections (the kernels read the tail-row counts on the device).
+  // Only the finish kernels read them: with long K (64-deep K blocks >= 256)
+  // they run on the side stream, at most two blocks per SM beside the GEMM's
+  // first segment, instead of ahead of it.
+  SideStream *side = L.nkb >= 256 ? side_stream() : nullptr;
+  if (side && (cudaEventRecord(side->ev[3], s) != cudaSuccess ||
+               cudaStreamWaitEvent(side->st, side->ev[3], 0) != cudaSuccess)) {
+    cudaGetLastError();
+    side = nullptr;   // corrections on the caller's stream instead
+  }
+  const cudaStream_t cs = side ? side->st : s;
+  const int cy = side ? 2 : 64;
+  dim3 ga((unsigned)std::min(L.capA, side ? sms : sms * 2), (unsigned)std::min((a.N + 255) / 256, cy));
+  dim3 gb((unsigned)std::min(L.capB, side ? sms : sms * 2), (unsigned)std::min((a.M + 255) / 256, cy));
+  if (a.fmt == 8) {
+    k_tc_corr<8><<<ga, 256, 0, cs>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
+                                     cA, L.capA, CA);
+    rc = check_launch("tc_corr");
+    if (rc == kOk) {
+      k_tc_corr<8><<<gb, 256, 0, cs>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB,
+                                       cB, L.capB, CB);
+      rc = check_launch("tc_corr");
+    }
+  } else {
+    k_tc_corr<16><<<ga, 256, 0, cs>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
+                                      cA, L.capA, CA);
+    rc = check_launch("tc_corr");
+    if (rc == kOk) {
+      k_tc_corr<16><<<gb, 256, 0, cs>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB,
+                                        cB, L.capB, CB);
+      rc = check_launch("tc_corr");
+    }
+  }
+  cudaEvent_t corr_done = nullptr;
+  if (side) {
+    // the caller's stream always joins the side stream, on the error path too
+    if (cudaEventRecord(side->ev[4], side->st) == cudaSuccess) corr_done = side->ev[4];
+    else cudaGetLastError();
+    if (rc || !corr_done) {
+      if (corr_done) cudaStreamWaitEvent(s, corr_done, 0);
+      else cudaStreamSynchronize(side->st);
+      return rc ? rc : set_error(kECuda, "quire_gemm: side stream event failed");
+    }
+  }
+  if (rc) return rc;
   if (S == 3)
-    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s) : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s);
+    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s, corr_done)
+              : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s, corr_done);
   else
-    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, gf, s) : launch_tc_schedule<4, false>(ma, mb, p, sc, gf, s);
+    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, gf, s, corr_done)
+              : launch_tc_schedule<4, false>(ma, mb, p, sc, gf, s, corr_done);
   if (rc) return rc;
   if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
