@@ -23,6 +23,13 @@ Two scale recipes:
   group's largest value to bp8's maxpos, where the format has no fraction bits,
   so it is the benchmark's definition rather than an accurate recipe.
 
+With ``act="bp16"`` (``scales="w8a8"`` only) the activations are not scaled
+but encoded as bp16, round-to-nearest-even (``encode_bposit16(·, "rtne")``,
+reference/bposit_ref.py:382-507), and the bp8 weight codes are widened exactly
+to bp16 (every bp8 value is a bp16 value): the same exact quire GEMM then runs
+in bp16, one bposit32 round, value * 2^e_w (+ bias) rounded once to fp32 --
+the bp16 activation path of the mixed-rung quire.
+
 The weight is encoded once, on first use or by ``quantize_weight()``.  The
 reference itself has no module API; this wraps its recipe for torch models.
 """
@@ -66,11 +73,15 @@ def _encode_scaled(x: torch.Tensor, ex: torch.Tensor) -> torch.Tensor:
 
 class BpositLinear(torch.nn.Module):
     def __init__(self, in_features: int, out_features: int, bias: bool = True, group: int = 128,
-                 scales: str = "w8a8", device=None, dtype=torch.float32):
+                 scales: str = "w8a8", device=None, dtype=torch.float32, act: str = "bp8"):
         super().__init__()
         if scales not in ("w8a8", "group128"):
             raise ValueError(f"unknown scale recipe {scales!r}")
+        if act not in ("bp8", "bp16") or (act == "bp16" and scales != "w8a8"):
+            raise ValueError(f"unsupported activation format {act!r} with scales {scales!r}")
         self.in_features, self.out_features, self.group, self.scales = in_features, out_features, group, scales
+        self.act = act
+        self._wq16 = None        # bp8 weight codes widened to bp16 (act="bp16")
         self.weight = torch.nn.Parameter(torch.empty((out_features, in_features), device=device, dtype=dtype),
                                          requires_grad=False)
         self.bias = (torch.nn.Parameter(torch.zeros(out_features, device=device, dtype=dtype), requires_grad=False)
@@ -80,9 +91,10 @@ class BpositLinear(torch.nn.Module):
         self._ws_key = None
 
     @classmethod
-    def from_linear(cls, lin: torch.nn.Linear, group: int = 128, scales: str = "w8a8") -> "BpositLinear":
+    def from_linear(cls, lin: torch.nn.Linear, group: int = 128, scales: str = "w8a8",
+                    act: str = "bp8") -> "BpositLinear":
         m = cls(lin.in_features, lin.out_features, bias=lin.bias is not None, group=group, scales=scales,
-                device=lin.weight.device, dtype=torch.float32)
+                device=lin.weight.device, dtype=torch.float32, act=act)
         with torch.no_grad():
             m.weight.copy_(lin.weight.float())
             if lin.bias is not None:
@@ -100,12 +112,14 @@ class BpositLinear(torch.nn.Module):
             Wn = W.double().cpu().numpy()
             ew = recommended_exponents(Wn)
             self._wq = (_encode_rows(Wn, ew, W.device), torch.from_numpy(ew.astype(np.int32)).to(W.device))
+        self._wq16 = ops.transcode(self._wq[0], 8, 16) if self.act == "bp16" else None
         return self._wq
 
     def _workspace(self, M: int, device):
-        key = (M, self.out_features, self.in_features)
+        fmt = 16 if self.act == "bp16" else 8
+        key = (M, self.out_features, self.in_features, fmt)
         if self._ws_key != key:
-            need = ops.gemm_workspace_size(8, M, self.out_features, self.in_features)
+            need = ops.gemm_workspace_size(fmt, M, self.out_features, self.in_features)
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
             self._ws_key = key
@@ -127,6 +141,10 @@ class BpositLinear(torch.nn.Module):
             codes, _ = ops.quire_gemm(xc, wc, 8, sa=xs, sb=ws, group=self.group,
                                       workspace=self._workspace(M, x2.device))
             y = ops.bp32_to_f32(codes, bias=bias)
+        elif self.act == "bp16":
+            xc = ops.encode_bp16(x2, rtne=True)
+            codes, _ = ops.quire_gemm(xc, self._wq16, 16, workspace=self._workspace(M, x2.device))
+            y = ops.bp32_to_f32(codes, col_exp=ws, bias=bias)
         else:
             xc, ex = ops.w8a8_encode_rows(x2)
             codes, _ = ops.quire_gemm(xc, wc, 8, workspace=self._workspace(M, x2.device))
@@ -134,15 +152,16 @@ class BpositLinear(torch.nn.Module):
         return y.reshape(*lead, self.out_features)
 
     def extra_repr(self) -> str:
+        arith = "bp8 W8A8" if self.act == "bp8" else "bp8 weights, bp16 activations"
         return (f"in_features={self.in_features}, out_features={self.out_features}, "
-                f"bias={self.bias is not None}, scales={self.scales}, arithmetic=bp8 W8A8 exact quire")
+                f"bias={self.bias is not None}, scales={self.scales}, arithmetic={arith} exact quire")
 
 
-def bpositify(module: torch.nn.Module, group: int = 128, scales: str = "w8a8") -> torch.nn.Module:
+def bpositify(module: torch.nn.Module, group: int = 128, scales: str = "w8a8", act: str = "bp8") -> torch.nn.Module:
     """Replace every torch.nn.Linear inside `module` by a BpositLinear (in place)."""
     for name, child in list(module.named_children()):
         if isinstance(child, torch.nn.Linear):
-            setattr(module, name, BpositLinear.from_linear(child, group=group, scales=scales))
+            setattr(module, name, BpositLinear.from_linear(child, group=group, scales=scales, act=act))
         else:
-            bpositify(child, group=group, scales=scales)
+            bpositify(child, group=group, scales=scales, act=act)
     return module

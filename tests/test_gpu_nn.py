@@ -11,9 +11,19 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def oracle_linear(orc, X: np.ndarray, W: np.ndarray, bias, scales: str = "w8a8", group: int = 128) -> np.ndarray:
+def oracle_linear(orc, X: np.ndarray, W: np.ndarray, bias, scales: str = "w8a8", group: int = 128,
+                  act: str = "bp8") -> np.ndarray:
     """The oracle's output of BpositLinear for rows X[M, K] (fp32 values)."""
-    if scales == "group128":
+    if act == "bp16":
+        from bposit_b200.bposit_quantize import recommended_exponents
+        W64 = W.astype(np.float64)
+        ew = recommended_exponents(W64)
+        s = W64 / np.exp2(ew.astype(np.float64))[:, None]
+        wc = np.where(np.abs(s) <= 4.999999999999999e-09, 0, orc.quantize_bp8_f64(s, nearest=False)).astype(np.uint8)
+        xc = orc.encode_bp16(X.astype(np.float32), True)
+        v = orc.bp32_to_double(orc.quire_gemm(xc, orc.transcode(wc, 8, 16), 16))
+        v = v * np.exp2(ew[None, :].astype(np.float64))
+    elif scales == "group128":
         xs = orc.group_scales(X, group)
         ws = orc.group_scales(W, group)
         xc = orc.quantize_bp8_grouped(X, xs, group, True)
@@ -107,3 +117,18 @@ def test_w8a8_encode_rows_matches_reference_rule(orc, K):
     s = X.astype(np.float64) / np.exp2(ex_ref.astype(np.float64))[:, None]
     c_ref = np.where(np.abs(s) <= 4.999999999999999e-09, 0, orc.quantize_bp8_f64(s, nearest=False))
     assert np.array_equal(codes.cpu().numpy(), c_ref.astype(np.uint8))
+
+
+@pytest.mark.parametrize("M,K,N,bias", [(37, 576, 200, True), (130, 896, 1152, False)])
+def test_bposit_linear_bp16_activations_match_oracle(orc, M, K, N, bias):
+    """act="bp16": RTNE bp16 activations, bp8 weights widened to bp16, one exact
+    bp16 quire GEMM -- equal to the oracle's composition of the same steps."""
+    from bposit_b200.nn import BpositLinear
+    torch.manual_seed(M + 1)
+    lin = torch.nn.Linear(K, N, bias=bias).cuda()
+    x = torch.randn(M, K, device="cuda")
+    x[torch.rand(M, K, device="cuda") < 0.01] *= 300.0
+    y = BpositLinear.from_linear(lin, act="bp16")(x)
+    ref = oracle_linear(orc, x.cpu().numpy(), lin.weight.detach().cpu().numpy(),
+                        None if not bias else lin.bias.detach().cpu().numpy(), act="bp16")
+    assert np.array_equal(y.cpu().numpy(), ref)
