@@ -1,7 +1,7 @@
 /*
  * bposit_oracle.c -- CPU restatement of the open-bposit W8A8 hot path.
  *
- * TEST INFRASTRUCTURE ONLY.  This file is the checker that the CUDA library
+ * TEST INFRASTRUCTURE ONLY.  This file is the oracle that the CUDA library
  * (open-bposit_b200/csrc) is compared against.  Only tests/, the smoke check in
  * __graft_entry__.py and the cpu_baseline / reference arm of bench.py may load
  * it; no product code path calls it, and the product fails loudly when its own
