@@ -356,6 +356,24 @@ __device__ __forceinline__ bool finish_code(const TcParams &p, int i, int j, uns
   return true;
 }
 
+// Tile order: groups of kTileGroup tile rows, M fastest inside a group, so
+// that the tiles of one wave (consecutive indices) cover a compact block of
+// the output -- 8 tile rows x ~10 tile columns for a 74-pair wave -- and the
+// digit-plane slices they read at the same K position are shared in L2 by
+// more CTAs (an N-fastest order made every wave read all of B's planes).
+// A bijection of [0, ntm * ntn) onto the tile grid.
+constexpr int kTileGroup = 8;
+
+__device__ __forceinline__ void tile_coords(int tile, int ntm, int ntn, int &tm, int &tn) {
+  const int per_group = kTileGroup * ntn;
+  const int g = tile / per_group;
+  const int first = g * kTileGroup;
+  const int gs = min(ntm - first, kTileGroup);
+  const int r = tile - g * per_group;
+  tm = first + r % gs;
+  tn = r / gs;
+}
+
 // ----------------------------------------------------------------- GEMM ---
 // One CTA per SM.  PAIR: launched in clusters of two; CTA rank 0 (the leader)
 // issues M = 256 MMAs that read A from both CTAs (128 rows each) and B from
@@ -375,10 +393,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;      // 0: issues the pair's MMAs
-  // linear tiles, N fastest (consecutive CTAs share an A row block); y = K chunk
+  // tiles in tile_coords order; y = K chunk
   const int tile = p.tile0 + (PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x);
-  const int n0 = (tile % p.ntn) * C::BN;
-  const int m0 = (tile / p.ntn) * C::MM + (int)rank * BM, chunk = blockIdx.y;
+  int tm, tn;
+  tile_coords(tile, (p.M + C::MM - 1) / C::MM, p.ntn, tm, tn);
+  const int n0 = tn * C::BN;
+  const int m0 = tm * C::MM + (int)rank * BM, chunk = blockIdx.y;
   const int kb0 = chunk * p.kb_per_chunk;
   const int kb1 = min(p.nkb, kb0 + p.kb_per_chunk);
   const int nkb = kb1 - kb0;
@@ -669,8 +689,9 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
   for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
     const int tile = p.tile0 + tl;
-    const int tm = tile / p.ntn;
-    const int j0 = (tile - tm * p.ntn) * BN;
+    int tm, tn;
+    tile_coords(tile, (p.M + MM - 1) / MM, p.ntn, tm, tn);
+    const int j0 = tn * BN;
     FinishCols<PL> c;
 #pragma unroll
     for (int q = 0; q < PL; ++q) {
@@ -1215,8 +1236,8 @@ struct TcLayout {
 // the cap are finished by the fixup kernel instead.
 constexpr size_t kCorrBudget = size_t(512) << 20;
 
-// Which tiles run whole and which are split along K.  Tiles are linear (N
-// fastest); tiles [0, whole) run whole, tiles [whole, ntiles) in `split`
+// Which tiles run whole and which are split along K.  Tiles are indexed in
+// tile_coords order; tiles [0, whole) run whole, tiles [whole, ntiles) in `split`
 // chunks of kbc K blocks each, their int64 partial sums added by k_tc_finish.
 //  * K longer than one exact int32 chunk: every tile is split (the minimum).
 //  * otherwise the full waves run whole and only the last, partial wave is
