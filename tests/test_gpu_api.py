@@ -158,7 +158,7 @@ def test_small_rungs_against_reference_vectors():
 
 
 @pytest.mark.parametrize("case", ["chunked", "chunked_groups", "bp16_small", "pageable", "rows", "rows_groups",
-                                  "rows_strided_out"])
+                                  "rows_strided_out", "rows_bp16_small"])
 def test_quire_gemm_host_buffers(case):
     """bp_quire_gemm_host (host buffers; one operand prepared once, the other
     streamed in row chunks: B when M < N, A when M >= N) gives exactly the
@@ -168,6 +168,8 @@ def test_quire_gemm_host_buffers(case):
     group = 128
     if case in ("chunked", "chunked_groups", "pageable"):
         M, N, K, fmt = 2048, 3000, 16384, 8      # 82 MB of codes: B in 4 chunks of 768 rows, the last padded
+    elif case == "rows_bp16_small":
+        M, N, K, fmt = 300, 200, 1000, 16        # one chunk, CUDA-core GEMM (B's preparation step is a no-op)
     elif case.startswith("rows"):
         M, N, K, fmt = 3000, 2048, 16384, 8      # A in 4 chunks of 768 rows, the last padded
     else:
