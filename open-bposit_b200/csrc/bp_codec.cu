@@ -12,10 +12,12 @@
 //    2^ceil(log2(absmax / 2^24)) folded into the exponent, then quantize_bp8.
 //  * quire_to_bp32: quire256_to_bposit32 (reference/bposit_ref.py:703-722).
 //
-// Layout: flat arrays; the fast paths move 16 elements per thread per step with
-// 128-bit loads and stores and fall back to scalar code for unaligned heads,
-// tails and pointers.  Grids are grid-stride loops sized to a multiple of the
-// SM count.
+// Layout: flat arrays.  The streaming kernels move units of four elements (a
+// float4 of fp32 on one side, 4 or 8 bytes of codes on the other) in tiles
+// whose every warp instruction touches one contiguous span, several loads in
+// flight per thread; misaligned pointers and the last few elements take a
+// scalar loop.  Grids are one block per tile (decode) or a multiple of the SM
+// count (the encoders, grid-stride).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -38,52 +40,67 @@ inline int grid_for(size_t work_items, int per_sm = 8) {
 }
 
 // ---------------------------------------------------------------- decode ---
+// Tiles of kThreads * U vector units per block step: unit t + j * kThreads of
+// a tile goes to thread t, so every load and every store instruction of a warp
+// covers one contiguous span (a word of 4 bp8 codes or 4 bp16 codes in, a
+// float4 out).  The U loads of a step are issued before any store.  The grid
+// is one block per tile (no grid-stride for the vector part); elements past
+// the last whole unit, and every element of a misaligned call, take the
+// scalar loop.
+template <int U>
 __global__ void __launch_bounds__(kThreads) k_decode_bp8(const uint8_t *__restrict__ codes, size_t n,
                                                          float *__restrict__ out, bool vec) {
   __shared__ uint32_t lut[256];
   lut[threadIdx.x] = posit_to_f32_bits<8, 2>(threadIdx.x);
   __syncthreads();
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  size_t nv = vec ? n / 16 : 0;
-  const uint4 *c4 = reinterpret_cast<const uint4 *>(codes);
+  const size_t nw = vec ? n / 4 : 0;
+  const uint32_t *w = reinterpret_cast<const uint32_t *>(codes);
   uint4 *o4 = reinterpret_cast<uint4 *>(out);
-  for (size_t i = tid; i < nv; i += stride) {
-    uint4 c = __ldcs(c4 + i);
-    uint32_t w[4] = {c.x, c.y, c.z, c.w};
+  const size_t tile = (size_t)kThreads * U;
+  for (size_t base = blockIdx.x * tile; base < nw; base += (size_t)gridDim.x * tile) {
+    uint32_t v[U];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 r;
-      r.x = lut[w[q] & 0xFFu];
-      r.y = lut[(w[q] >> 8) & 0xFFu];
-      r.z = lut[(w[q] >> 16) & 0xFFu];
-      r.w = lut[w[q] >> 24];
-      __stcs(o4 + 4 * i + q, r);
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      v[j] = i < nw ? __ldcs(w + i) : 0u;
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      if (i < nw)
+        __stcs(o4 + i, make_uint4(lut[v[j] & 0xFFu], lut[(v[j] >> 8) & 0xFFu], lut[(v[j] >> 16) & 0xFFu],
+                                  lut[v[j] >> 24]));
     }
   }
-  for (size_t i = nv * 16 + tid; i < n; i += stride) out[i] = __uint_as_float(lut[codes[i]]);
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = nw * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(lut[codes[i]]);
 }
 
+// bp16: closed-form decode (bp16_to_f32_bits), four codes (8 bytes) per unit.
+template <int U>
 __global__ void __launch_bounds__(kThreads) k_decode_bp16(const uint16_t *__restrict__ codes, size_t n,
                                                           float *__restrict__ out, bool vec) {
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  size_t nv = vec ? n / 8 : 0;
-  const uint4 *c4 = reinterpret_cast<const uint4 *>(codes);
+  const size_t nq = vec ? n / 4 : 0;
+  const uint2 *c2 = reinterpret_cast<const uint2 *>(codes);
   uint4 *o4 = reinterpret_cast<uint4 *>(out);
-  for (size_t i = tid; i < nv; i += stride) {
-    uint4 c = __ldcs(c4 + i);
-    uint32_t w[4] = {c.x, c.y, c.z, c.w};
-    uint32_t r[8];
+  const size_t tile = (size_t)kThreads * U;
+  for (size_t base = blockIdx.x * tile; base < nq; base += (size_t)gridDim.x * tile) {
+    uint2 v[U];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      r[2 * q] = posit_to_f32_bits<16, 3>(w[q] & 0xFFFFu);
-      r[2 * q + 1] = posit_to_f32_bits<16, 3>(w[q] >> 16);
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      v[j] = i < nq ? __ldcs(c2 + i) : make_uint2(0u, 0u);
     }
-    __stcs(o4 + 2 * i, make_uint4(r[0], r[1], r[2], r[3]));
-    __stcs(o4 + 2 * i + 1, make_uint4(r[4], r[5], r[6], r[7]));
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      if (i < nq)
+        __stcs(o4 + i, make_uint4(bp16_to_f32_bits(v[j].x & 0xFFFFu), bp16_to_f32_bits(v[j].x >> 16),
+                                  bp16_to_f32_bits(v[j].y & 0xFFFFu), bp16_to_f32_bits(v[j].y >> 16)));
+    }
   }
-  for (size_t i = nv * 8 + tid; i < n; i += stride) out[i] = __uint_as_float(posit_to_f32_bits<16, 3>(codes[i]));
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = nq * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(bp16_to_f32_bits(codes[i]));
 }
 
 // ------------------------------------------------------------ quantize bp8 ---
@@ -143,24 +160,44 @@ __global__ void __launch_bounds__(kThreads) k_quantize_bp8(const float *__restri
 }
 
 // ------------------------------------------------------------ encode bp16 ---
-template <bool RTNE>
+// Per-binade table (bp16_qentry, 2 KB of shared memory): a code costs one
+// table load and a handful of integer operations (bp16_encode_tbl).  Units of
+// four elements (a float4 in, 8 bytes of codes out) in the tile order of the
+// decode kernels; grid-stride over tiles, 8 blocks per SM.
+template <bool RTNE, int U>
 __global__ void __launch_bounds__(kThreads) k_encode_bp16(const float *__restrict__ x, size_t n,
                                                           uint16_t *__restrict__ codes, bool vec) {
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  size_t nv = vec ? n / 8 : 0;
-  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
-  uint4 *c4 = reinterpret_cast<uint4 *>(codes);
-  for (size_t i = tid; i < nv; i += stride) {
-    uint4 a = __ldcs(x4 + 2 * i), b = __ldcs(x4 + 2 * i + 1);
-    uint4 r;
-    r.x = bp16_encode_bits(a.x, RTNE) | (bp16_encode_bits(a.y, RTNE) << 16);
-    r.y = bp16_encode_bits(a.z, RTNE) | (bp16_encode_bits(a.w, RTNE) << 16);
-    r.z = bp16_encode_bits(b.x, RTNE) | (bp16_encode_bits(b.y, RTNE) << 16);
-    r.w = bp16_encode_bits(b.z, RTNE) | (bp16_encode_bits(b.w, RTNE) << 16);
-    __stcs(c4 + i, r);
+  __shared__ uint2 tbl[256];
+  {
+    uint32_t lo, hm;
+    bp16_qentry(threadIdx.x, RTNE, lo, hm);
+    tbl[threadIdx.x] = make_uint2(lo, hm);
   }
-  for (size_t i = nv * 8 + tid; i < n; i += stride) codes[i] = (uint16_t)bp16_encode_bits(__float_as_uint(x[i]), RTNE);
+  __syncthreads();
+  const size_t nq = vec ? n / 4 : 0;
+  const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
+  uint2 *c2 = reinterpret_cast<uint2 *>(codes);
+  const size_t tile = (size_t)kThreads * U;
+  auto enc = [&](uint32_t u) {
+    const uint2 t = tbl[(u >> 23) & 0xFFu];
+    return bp16_encode_tbl(u, t.x, t.y, RTNE);
+  };
+  for (size_t base = blockIdx.x * tile; base < nq; base += (size_t)gridDim.x * tile) {
+    uint4 v[U];
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      v[j] = i < nq ? __ldcs(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      if (i < nq)
+        __stcs(c2 + i, make_uint2(enc(v[j].x) | (enc(v[j].y) << 16), enc(v[j].z) | (enc(v[j].w) << 16)));
+    }
+  }
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = nq * 4 + tid; i < n; i += stride) codes[i] = (uint16_t)enc(__float_as_uint(x[i]));
 }
 
 // ------------------------------------------------- grouped quantize (bp8) ---
@@ -280,14 +317,24 @@ __global__ void __launch_bounds__(kThreads) k_bp32_to_bp16(const uint32_t *__res
 }  // namespace
 
 // --------------------------------------------------------------- launchers ---
+// One block per tile of kThreads * U units of `per` elements (at least one block).
+inline int tile_grid(size_t n, int per, int U) {
+  const size_t tile = (size_t)kThreads * U * per;
+  const size_t b = (n + tile - 1) / tile;
+  return (int)std::min<size_t>(std::max<size_t>(b, 1), (size_t)1 << 30);
+}
+
+constexpr int kDecU8 = 4, kDecU16 = 8, kEncU16 = 8;
+
 int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t s) {
   if (n == 0) return kOk;
+  const bool oal = aligned16(out);
   if (fmt == 8) {
-    bool vec = aligned16(codes) && aligned16(out);
-    k_decode_bp8<<<grid_for(vec ? n / 16 + 1 : n), kThreads, 0, s>>>((const uint8_t *)codes, n, out, vec);
+    const bool vec = oal && ((uintptr_t)codes & 3u) == 0u;
+    k_decode_bp8<kDecU8><<<tile_grid(n, 4, kDecU8), kThreads, 0, s>>>((const uint8_t *)codes, n, out, vec);
   } else {
-    bool vec = aligned16(codes) && aligned16(out);
-    k_decode_bp16<<<grid_for(vec ? n / 8 + 1 : n), kThreads, 0, s>>>((const uint16_t *)codes, n, out, vec);
+    const bool vec = oal && ((uintptr_t)codes & 7u) == 0u;
+    k_decode_bp16<kDecU16><<<tile_grid(n, 4, kDecU16), kThreads, 0, s>>>((const uint16_t *)codes, n, out, vec);
   }
   return check_launch("decode");
 }
@@ -309,10 +356,10 @@ int launch_quantize_bp8(const float *x, size_t n, bool nearest, uint8_t *codes, 
 
 int launch_encode_bp16(const float *x, size_t n, bool rtne, uint16_t *codes, cudaStream_t s) {
   if (n == 0) return kOk;
-  bool vec = aligned16(x) && aligned16(codes);
-  int g = grid_for(vec ? n / 8 + 1 : n);
-  if (rtne) k_encode_bp16<true><<<g, kThreads, 0, s>>>(x, n, codes, vec);
-  else k_encode_bp16<false><<<g, kThreads, 0, s>>>(x, n, codes, vec);
+  const bool vec = aligned16(x) && ((uintptr_t)codes & 7u) == 0u;
+  const int g = std::min(tile_grid(n, 4, kEncU16), sm_count() * 8);
+  if (rtne) k_encode_bp16<true, kEncU16><<<g, kThreads, 0, s>>>(x, n, codes, vec);
+  else k_encode_bp16<false, kEncU16><<<g, kThreads, 0, s>>>(x, n, codes, vec);
   return check_launch("encode_bp16");
 }
 

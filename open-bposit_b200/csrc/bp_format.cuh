@@ -224,6 +224,74 @@ BP_HD uint32_t bp16_encode_bits(uint32_t u, bool rtne) {
   return (sign << 15) | field;
 }
 
+// The same encoder as a per-binade table, for the streaming kernels.  Inside
+// one fp32 binade b (biased exponent) the regime and exponent bits are fixed,
+// so the 15-bit field is base(b) + (M >> sh(b)) with M the 23-bit mantissa,
+// sh = 23 - (fraction bits kept); binades whose field is a constant (zero and
+// subnormal inputs -> minpos, beyond +-2^112 or a regime of 15 bits -> the
+// saturated field) use sh = 24, which keeps no mantissa bit and never rounds.
+// Round to nearest even on the field: with half = 2^(sh-1) the rounded field
+// is base + ((M + half - 1 + lsb) >> sh), lsb = the truncated field's lowest
+// bit -- the rbit && (sticky || odd) rule of bp16_encode_bits, including its
+// quirk that with fewer than three exponent bits kept (sh = 23) the round bit
+// is the first fraction bit.  In the normal binades the field stays below
+// 0x7FFE before rounding, so the reference's saturation check never fires.
+// Entry: lo = base | sh << 16, hm1 = half - 1 (0 for truncation).
+BP_HD void bp16_qentry(int b, bool rtne, uint32_t &lo, uint32_t &hm1) {
+  uint32_t base, sh = 24u;
+  const int E = b - 127;
+  if (b == 0 || E < -112) base = 0x0001u;
+  else if (b == 255 || E > 112) base = 0x7FFFu;
+  else {
+    const int k = E >> 3, e = E & 7;
+    const int rl = k >= 0 ? k + 2 : 1 - k;
+    if (rl >= 15) {
+      base = k >= 0 ? (k >= 14 ? 0x7FFFu : 0x7FFEu) : 0x0001u;
+    } else {
+      const int avail = 15 - rl;
+      const int eb = avail < 3 ? avail : 3;
+      const int fb = avail - eb;
+      const uint32_t R = k >= 0 ? (((1u << (k + 1)) - 1u) << 1) : 1u;
+      base = (R << avail) | ((uint32_t)(e >> (3 - eb)) << fb);
+      sh = 23u - (uint32_t)fb;
+    }
+  }
+  lo = base | (sh << 16);
+  hm1 = rtne ? (1u << (sh - 1u)) - 1u : 0u;
+}
+
+// Code of fp32 bits u from its binade's entry (bp16_qentry of (u >> 23) & 0xFF):
+// identical to bp16_encode_bits(u, rtne).
+BP_HD uint32_t bp16_encode_tbl(uint32_t u, uint32_t lo, uint32_t hm1, bool rtne) {
+  const uint32_t a = u & 0x7FFFFFFFu;
+  const uint32_t M = a & 0x7FFFFFu;
+  const uint32_t base = lo & 0xFFFFu, sh = lo >> 16;
+  uint32_t field = base + (M >> sh);
+  if (rtne) field = base + ((M + hm1 + (field & 1u)) >> sh);
+  uint32_t code = (u >> 31) ? (0x8000u | ((0u - field) & 0x7FFFu)) : field;
+  code = a == 0u ? 0u : code;
+  return a > 0x7F800000u ? 0x8000u : code;
+}
+
+// fp32 bit pattern of a bp16 code (posit_to_f32_bits<16, 3> in closed form):
+// the 15-bit field is left-aligned at bit 31, the regime run r is counted with
+// one clz, and shifting the field past the regime and its terminator leaves
+// the three exponent bits and then the fraction at the top of the word (the
+// bits the regime leaves no room for shift in as zeros).  Zero and NaR -> +0.0.
+BP_HD uint32_t bp16_to_f32_bits(uint32_t c) {
+  const uint32_t neg = (c >> 15) & 1u;
+  const uint32_t f = (neg ? (0u - c) : c) & 0x7FFFu;
+  const uint32_t al = f << 17;
+  const uint32_t inv = al ^ (uint32_t)((int32_t)al >> 31);
+  int r = clz32(inv);
+  r = r > 15 ? 15 : r;
+  const int k = (al >> 31) ? r - 1 : -r;
+  const uint32_t x = al << (r + 1);                  // r <= 15
+  const int scale = 8 * k + (int)(x >> 29);
+  const uint32_t bits = (neg << 31) | ((uint32_t)(scale + 127) << 23) | ((x << 3) >> 9);
+  return f ? bits : 0u;
+}
+
 // ---------------------------------------------------------------------------
 // bp32 from an exact magnitude: value = mag * 2^lsb_exp, mag = (hi:lo) 128-bit.
 // The truncating bit-string encoder of reference/bposit_ref.py:97-150 as used

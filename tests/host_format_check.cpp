@@ -4,9 +4,11 @@
 // non-negative fp32 bit pattern (bp8 quantize, both modes), a strided sweep
 // of all fp32 patterns (bp16 encode, both modes), every bp8 / bp16 code
 // (decode) and random 128-bit magnitudes (bp32 round, its signed 64-bit form,
-// and the bp16 round derived from it).  Test-only.
+// and the bp16 round derived from it).  The streaming kernels' table-driven
+// bp16 encoder and closed-form bp16 decoder are compared with the bit-string
+// forms above over every fp32 pattern and every bp16 code.  Test-only.
 //
-// usage: host_format_check <what> <threads>   what in q8 | e16 | dec | bp32 | small
+// usage: host_format_check <what> <threads>   what in q8 | e16 | e16t | dec | bp32 | small
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -75,6 +77,24 @@ static void e16_range(uint64_t lo, uint64_t hi, uint64_t step, bool rtne) {
   g_bad += bad;
 }
 
+// the per-binade table encoder against bp16_encode_bits on [lo, hi)
+static void e16t_range(uint64_t lo, uint64_t hi, bool rtne) {
+  uint32_t tlo[256], thm[256];
+  for (int b = 0; b < 256; ++b) bp::bp16_qentry(b, rtne, tlo[b], thm[b]);
+  long long bad = 0;
+  for (uint64_t v = lo; v < hi; ++v) {
+    const uint32_t u = (uint32_t)v;
+    const uint32_t b = (u >> 23) & 0xFFu;
+    const uint32_t t = bp::bp16_encode_tbl(u, tlo[b], thm[b], rtne);
+    const uint32_t ref = bp::bp16_encode_bits(u, rtne);
+    if (t != ref) {
+      if (bad < 5) fprintf(stderr, "e16t mismatch rtne=%d x=%08x tbl=%04x bits=%04x\n", rtne, u, t, ref);
+      ++bad;
+    }
+  }
+  g_bad += bad;
+}
+
 static uint64_t rng_state = 0x9E3779B97F4A7C15ull;
 static uint64_t rnd() {
   rng_state ^= rng_state << 13; rng_state ^= rng_state >> 7; rng_state ^= rng_state << 17;
@@ -114,6 +134,16 @@ int main(int argc, char **argv) {
           e16_range(base + 0x7FFFFF - 0x2000, base + 0x800000, 1, mode == 1);
         }
     }
+  } else if (!strcmp(what, "e16t")) {
+    // every fp32 pattern, both modes
+    for (int mode = 0; mode < 2; ++mode) {
+      for (int t = 0; t < nt; ++t) {
+        uint64_t lo = (0x100000000ull * t) / nt, hi = (0x100000000ull * (t + 1)) / nt;
+        th.emplace_back(e16t_range, lo, hi, mode == 1);
+      }
+      for (auto &x : th) x.join();
+      th.clear();
+    }
   } else if (!strcmp(what, "dec")) {
     long long bad = 0;
     for (uint32_t c = 0; c < 256; ++c) {
@@ -127,6 +157,11 @@ int main(int argc, char **argv) {
       orc_decode_me(16, c, &m, &e);
       bp::posit_to_me<16, 3>(c, dm, de);
       if (m != dm || (m && e != de)) { if (bad < 5) fprintf(stderr, "bp16 decode %04x\n", c); ++bad; }
+      // the closed-form fp32 decode of the streaming kernel
+      if (bp::bp16_to_f32_bits(c) != bp::posit_to_f32_bits<16, 3>(c)) {
+        if (bad < 5) fprintf(stderr, "bp16 f32 decode %04x\n", c);
+        ++bad;
+      }
     }
     g_bad += bad;
   } else if (!strcmp(what, "bp32")) {

@@ -44,6 +44,30 @@ def test_decode_unaligned_and_ragged(ops, orc):
             assert np.array_equal(got.view(np.uint32), orc.decode_f32(base[off:off + n], 8).view(np.uint32))
 
 
+@pytest.mark.parametrize("off", [0, 1, 2, 3, 4, 5, 8])
+def test_codec_ragged_offsets_all_kernels(ops, orc, off):
+    """Every codec kernel on views starting `off` elements into an aligned
+    buffer (vector path when the view stays 4/8/16-byte aligned, scalar path
+    otherwise) and on lengths around the tile sizes (partial tiles, the
+    elements after the last whole four-element unit)."""
+    from bposit_b200 import workloads
+    big = workloads.codec_sweep(3 * 32768 + 64, "bp16", seed=off)
+    xt = dev(big)
+    c8 = np.random.default_rng(off).integers(0, 256, big.size, dtype=np.uint8)
+    c16 = np.random.default_rng(off + 1).integers(0, 65536, big.size).astype(np.uint16)
+    c8t, c16t = dev(c8), dev(c16)
+    for n in (0, 1, 3, 4, 5, 4095, 4096, 4097, 8193, 3 * 32768 + 7):
+        sl = slice(off, off + n)
+        assert np.array_equal(ops.decode(c8t[sl]).cpu().numpy().view(np.uint32),
+                              orc.decode_f32(c8[sl], 8).view(np.uint32))
+        assert np.array_equal(ops.decode(c16t[sl]).cpu().numpy().view(np.uint32),
+                              orc.decode_f32(c16[sl], 16).view(np.uint32))
+        for rtne in (True, False):
+            assert np.array_equal(ops.encode_bp16(xt[sl], rtne=rtne).cpu().numpy(), orc.encode_bp16(big[sl], rtne))
+        got = ops.quantize_bp8(xt[sl], nearest=True).cpu().numpy()
+        assert np.array_equal(got, orc.quantize_bp8(big[sl], nearest=True)[0])
+
+
 def test_quantize_bp8_golden(ops):
     """bposit_fast.quantize_bp8 codes on every midpoint / grid point +-1 ulp,
     the specials and a seeded sample (both modes)."""
