@@ -6,8 +6,15 @@
  * to memory of the current CUDA device.  Every call is asynchronous on
  * `stream` and returns a status: BP_OK (0) or a negative BP_E* code, with a
  * message in bp_last_error() (thread-local).  No C++ exception crosses the ABI.
- * Library-owned state is limited to immutable tables each kernel builds in
- * shared memory; calls on different streams are independent.
+ *
+ * Library-owned state: the tables each kernel builds in its shared memory;
+ * per device, one kernel error word (bp_device_error) and the fixed 1 MiB
+ * scratch array of bp_quire_gemm_noalloc; per host thread and device, the
+ * device and pinned host buffers that bp_quire_gemm_host keeps for later
+ * calls (grown to the largest call, held until exit); the CUDA-IPC mappings
+ * made by bp_ipc_open until bp_ipc_close.  Apart from the no-alloc scratch
+ * (shared by its calls on a device) and the error word, calls on different
+ * streams are independent.
  *
  * Formats: fmt = 8 (bp8: 8-bit posit, eS=2, codes uint8) or 16 (bp16: 16-bit
  * posit, eS=3, codes uint16).  bp32 results are uint32 codes (eS=3).  Quires
@@ -47,9 +54,14 @@ const char *bp_last_error(void);
 unsigned long long bp_launch_count(void);
 
 /* Reads and clears the current device's kernel error word: nonzero when a
- * bounded wait inside a tensor-core GEMM kernel gave up (the kernel then left
- * its outputs unwritten and returned).  Synchronizes with the device.
- * Diagnostic; no reference counterpart. */
+ * bounded wait inside a tensor-core GEMM kernel gave up.  That kernel then
+ * drained its own copies in flight (bounded), released its tensor memory and
+ * returned; from then until this call clears the word, every bposit32 output
+ * of the tensor-core path (bp_quire_gemm, _multi, _host) is NaR (0x80000000),
+ * a code no quire round produces.  The GEMM entry points return before their
+ * kernels run, so C callers poll this after synchronizing the stream (the
+ * Python API does so wherever it copies results to the host).  Synchronizes
+ * with the device.  Diagnostic; no reference counterpart. */
 int bp_device_error(int *out);
 
 /* Decode n codes to their exact fp32 values; zero and NaR give +0.0.
@@ -240,8 +252,9 @@ int bp_bp32_to_f64(const uint32_t *codes, int M, int N, const int32_t *row_exp,
 
 /* The same values plus an optional fp32 column bias [N], each rounded once to
  * the nearest-even fp32: the hand-off from an exact W8A8 GEMM to the next
- * fp32 op of a model (the nn.Linear drop-in).  No reference counterpart (the
- * reference stops at float64). */
+ * fp32 op of a model (the nn.Linear drop-in).  NaR -> NaN (no quire round
+ * produces NaR; a GEMM that gave up on a bounded wait writes it).  No reference
+ * counterpart (the reference stops at float64). */
 int bp_bp32_to_f32(const uint32_t *codes, int M, int N, const int32_t *row_exp, const int32_t *col_exp,
                    const float *bias, float *out, void *stream);
 

@@ -110,7 +110,7 @@ def dot_quire(a_codes, b_codes, fmt: str) -> int:
     b = _codes_to_dev(b_codes, nb).reshape(1, -1)
     a, b = _broadcast(a, b)
     _, q = ops.quire_gemm(a, b, _gemm_bits(nb), quire_limbs=16)
-    return int(_limbs_to_ints(q.cpu().numpy())[0, 0])
+    return int(_limbs_to_ints(ops.to_host(q))[0, 0])
 
 
 _OUT_FMTS = ("bp16", "bp32")   # reference/bposit_ref.py:989-992
@@ -128,7 +128,7 @@ def dot(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
     out, _ = ops.quire_gemm(a, b, _gemm_bits(nb))
     if out_fmt == "bp16":
         out = ops.bp32_to_bp16(out)
-    return int(out.cpu().numpy()[0, 0])
+    return int(ops.to_host(out)[0, 0])
 
 
 def matmul_quire(A_codes, B_codes, fmt: str):
@@ -140,7 +140,7 @@ def matmul_quire(A_codes, B_codes, fmt: str):
     A = _codes_to_dev(A_codes, nb)
     B = _codes_to_dev(B_codes, nb)
     _, q = ops.quire_gemm(A, B, _gemm_bits(nb), quire_limbs=16)
-    return _limbs_to_ints(q.cpu().numpy())
+    return _limbs_to_ints(ops.to_host(q))
 
 
 def matmul_bp16(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,
@@ -150,7 +150,7 @@ def matmul_bp16(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None,
     out = matmul_bp32(A_codes, B_codes, fmt, a_exps=a_exps, b_exps=b_exps, group=group, algo=algo)
     on_dev = isinstance(out, torch.Tensor)
     r = ops.bp32_to_bp16(out if on_dev else torch.from_numpy(out).to(_device()))
-    return r if on_dev else r.cpu().numpy()
+    return r if on_dev else ops.to_host(r)
 
 
 def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None, group: int = 128,
@@ -166,4 +166,4 @@ def matmul_bp32(A_codes, B_codes, fmt: str = "bp8", *, a_exps=None, b_exps=None,
     sa = None if a_exps is None else torch.as_tensor(a_exps, dtype=torch.int32).to(A.device).contiguous()
     sb = None if b_exps is None else torch.as_tensor(b_exps, dtype=torch.int32).to(A.device).contiguous()
     out, _ = ops.quire_gemm(A, B, _gemm_bits(nb), sa=sa, sb=sb, group=group, algo=algo)
-    return out if on_dev else out.cpu().numpy()
+    return out if on_dev else ops.to_host(out)

@@ -28,7 +28,7 @@ def recommended_exponents(M: np.ndarray) -> np.ndarray:
     for r in range(M.shape[0]):
         v = M[r]
         rms = float(np.sqrt(np.mean(v ** 2)))
-        if not rms > 0:
+        if rms <= 0:          # a NaN row falls through and raises in int() below, as in the reference
             continue
         p95 = float(np.percentile(np.abs(v), 95))
         ref = p95 if (p95 > 0 and p95 > 2 * rms) else rms
@@ -64,4 +64,4 @@ def quantize_w8a8(W: np.ndarray, X: np.ndarray) -> np.ndarray:
     bp32, _ = ops.quire_gemm(xc, wc, 8)
     y = ops.bp32_to_f64(bp32, torch.from_numpy(x_exp.astype(np.int32)).to(dev),
                         torch.from_numpy(w_exp.astype(np.int32)).to(dev))
-    return y.cpu().numpy()
+    return ops.to_host(y)

@@ -71,7 +71,7 @@ def dot_at_precision(a_codes, b_codes, fmt: str, out_fmt: str = "bp32") -> int:
     b = _codes_dev(list(b_codes), nb).reshape(1, -1)
     n = min(a.shape[1], b.shape[1])                     # zip() semantics
     out, _ = ops.quire_gemm(a[:, :n].contiguous(), b[:, :n].contiguous(), 8)
-    return int(_round_out(out, out_fmt).cpu().numpy()[0, 0])
+    return int(ops.to_host(_round_out(out, out_fmt))[0, 0])
 
 
 def mixed_precision_sum(items, out_fmt: str) -> int:
@@ -98,7 +98,7 @@ def mixed_precision_sum(items, out_fmt: str) -> int:
             row[idx] = ops.transcode(t, nb, 16).cpu().numpy()
     ones = torch.full((1, len(items)), 0x4000, dtype=torch.uint16, device=dev)   # bp16 1.0
     out, _ = ops.quire_gemm(torch.from_numpy(row).to(dev).reshape(1, -1), ones, 16)
-    return int(_round_out(out, out_fmt).cpu().numpy()[0, 0])
+    return int(ops.to_host(_round_out(out, out_fmt))[0, 0])
 
 
 def encode_bposit16(value, mode: str = "truncate"):
@@ -112,10 +112,19 @@ def encode_bposit16(value, mode: str = "truncate"):
     return int(c) if c.ndim == 0 else c
 
 
+# |q| >= 2^(96 + 241) rounds to +-maxpos in both bposit32 and bposit16 (total
+# exponent above 240, resp. 112: reference/bposit_ref.py:104-105, 416-419), so
+# larger Python ints are clamped there before they are cut into 16 limbs.
+_QUIRE_SAT = 1 << (96 + 241)
+
+
 def _ints_to_limbs(qs, nl: int = 16) -> np.ndarray:
     out = np.empty((len(qs), nl), dtype=np.uint32)
     for i, q in enumerate(qs):
-        out[i] = np.frombuffer((int(q) & ((1 << (32 * nl)) - 1)).to_bytes(4 * nl, "little"), dtype=np.uint32)
+        q = int(q)
+        if abs(q) >= _QUIRE_SAT:
+            q = _QUIRE_SAT if q > 0 else -_QUIRE_SAT
+        out[i] = np.frombuffer((q & ((1 << (32 * nl)) - 1)).to_bytes(4 * nl, "little"), dtype=np.uint32)
     return out
 
 

@@ -17,6 +17,33 @@ _FMT = {"bp8": 8, "bp16": 16, 8: 8, 16: 16}
 _CODE_DTYPE = {8: torch.uint8, 16: torch.uint16}
 
 
+def device_error() -> int:
+    """Read and clear the current device's kernel error word (synchronizes with
+    the device): nonzero when a bounded wait inside a tensor-core GEMM gave up.
+    While the word is set, every bposit32 output of the tensor-core path is NaR
+    (0x80000000), a code no quire round produces."""
+    v = ctypes.c_int(0)
+    _lib.check(_lib.lib().bp_device_error(ctypes.byref(v)))
+    return int(v.value)
+
+
+def check_device_error() -> None:
+    """Raise BpositError if a tensor-core GEMM gave up on a bounded wait since
+    the last check (the word is cleared by the check)."""
+    v = device_error()
+    if v:
+        raise _lib.BpositError(_lib.BP_ECUDA, f"a tensor-core GEMM gave up on a bounded wait (error word {v:#x}); "
+                                              "its bposit32 outputs were set to NaR")
+
+
+def to_host(t: torch.Tensor):
+    """t as a numpy array, once the device work behind it is done and no GEMM
+    reported a timed-out wait (check_device_error)."""
+    a = t.cpu().numpy()
+    check_device_error()
+    return a
+
+
 def fmt_bits(fmt) -> int:
     try:
         return _FMT[fmt]

@@ -443,7 +443,9 @@ __global__ void __launch_bounds__(256) k_bp32_to_f64(const uint32_t *__restrict_
 }
 
 // The same exact value (plus an optional fp32 column bias), rounded once to
-// the nearest-even fp32 -- the hand-off to the next fp32 op of a model.
+// the nearest-even fp32 -- the hand-off to the next fp32 op of a model.  NaR,
+// which no quire round produces but a GEMM that gave up on a bounded wait
+// writes, becomes NaN here, so the failure shows in the model's output.
 __global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict__ codes, int M, int N,
                                                      const int32_t *__restrict__ re,
                                                      const int32_t *__restrict__ ce,
@@ -453,9 +455,10 @@ __global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict_
     const int rex = re ? re[m] : 0;
     const size_t rb = (size_t)m * N;
     for (int n = threadIdx.x; n < N; n += blockDim.x) {
-      double v = bp32_value_scaled(codes[rb + n], rex + (ce ? ce[n] : 0));
+      const uint32_t c = codes[rb + n];
+      double v = bp32_value_scaled(c, rex + (ce ? ce[n] : 0));
       if (bias) v += (double)bias[n];
-      out[rb + n] = __double2float_rn(v);
+      out[rb + n] = c == 0x80000000u ? __uint_as_float(0x7FC00000u) : __double2float_rn(v);
     }
   }
 }

@@ -58,6 +58,7 @@ namespace {
 #endif
 constexpr int BM = 128, BK = BP_TC_BK, THREADS = 256;
 constexpr long long WAIT_LIMIT = 4000000000LL;   // cycles (~2 s) before a wait gives up
+constexpr long long DRAIN_LIMIT = 200000000LL;   // cycles (~0.1 s) per stage drained after a timeout
 constexpr int TAILCAP = 1024;                    // listed tail elements per row (more -> fixup)
 constexpr int BIG = 1 << 20;                     // offset that makes max-reductions find a minimum
 
@@ -315,6 +316,24 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, i
   }
 }
 
+// Abort path of the TMA producer: wait, bounded and without the abort
+// shortcut, for the completion of the last round issued on each stage, so
+// that no bulk copy still writes this CTA's shared memory once it exits.
+// `remote` (the paired form's second CTA, whose copies complete on the
+// leader's barriers): sleep a settle time instead.
+template <int STAGES>
+__device__ __noinline__ void drain_loads(uint64_t *full, int issued, bool remote) {
+  if (remote) {
+    for (int i = 0; i < 400; ++i) __nanosleep(1000);   // ~0.4 ms
+    return;
+  }
+  for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; ++it) {
+    const long long t0 = clock64();
+    const uint32_t par = (uint32_t)(it / STAGES) & 1u;
+    while (!mbar_try_wait(&full[it % STAGES], par) && clock64() - t0 < DRAIN_LIMIT) __nanosleep(256);
+  }
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -422,11 +441,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      int issued = 0;   // K blocks whose loads were issued
       for (int it = 0; it < nkb && ok; ++it) {
         int st = it % C::STAGES;
         uint32_t round = (uint32_t)(it / C::STAGES);
         ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1, abort);
         if (!ok) break;
+        issued = it + 1;
         uint8_t *sa = smem + st * C::STAGE_BYTES;
         if (PAIR) {
           // both CTAs' loads complete on the leader's barrier, which expects both
@@ -440,6 +461,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           tma_load_3d(sa + C::A_BYTES, &tmB, &full[st], (kb0 + it) * BK, n0, 0);
         }
       }
+      // After a timeout, the loads still in flight land before this CTA
+      // releases its shared memory: wait (bounded, regardless of the abort
+      // word) for the last issued round of every stage.  In the paired form
+      // the leader's barriers count both CTAs' bytes; the other CTA, whose
+      // loads complete on the leader's barriers, waits a settle time instead.
+      if (!ok || *abort) drain_loads<C::STAGES>(full, issued, PAIR && rank != 0);
     }
     __syncwarp();
   } else if ((warp == 1 || warp == 2) && rank == 0) {
@@ -503,7 +530,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   // ---------------------------------------------------------------- epilogue
   // Eight warps: warp w reads TMEM lane quarter w & 3 (tile rows 32q..32q+31,
   // the only lanes its tcgen05.ld may touch) and column half w >> 2.
-  ok = mbar_wait(tfull, 0, 4, abort, true) && ok;
+  // The issuing warps commit to tfull whether or not they aborted, so this wait
+  // (bounded, but not cut short by the abort word) also drains every MMA in
+  // flight before TMEM is read or released.
+  ok = mbar_wait(tfull, 0, 4, nullptr, true) && ok && !*abort;
   tc_fence_after();
   const int q4 = warp & 3, half = warp >> 2;
   const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
@@ -686,12 +716,25 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
   const bool sum64 = !p.quire && p.split <= (QW == 1 ? 8 : 1024);
   const int rpp = MM / parts;   // rows per item, a multiple of 8
   const long long nitems = (long long)ntiles * parts;
+  // After a timed-out wait in any tensor-core GEMM on this device (the error
+  // word stays set until bp_device_error reads it), every output is NaR.
+  const bool poisoned = *(volatile int *)&g_tc_error != 0;
   for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
     const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
     const int tile = p.tile0 + tl;
     int tm, tn;
     tile_coords(tile, (p.M + MM - 1) / MM, p.ntn, tm, tn);
     const int j0 = tn * BN;
+    if (poisoned) {
+      const int rend = min((part + 1) * rpp, p.M - tm * MM);
+      for (int r = part * rpp + warp; r < rend; r += 8)
+        for (int j = j0 + lane; j < min(j0 + BN, p.N); j += 32) {
+          const size_t i = (size_t)(tm * MM + r);
+          p.out[i * p.ldo + j] = 0x80000000u;
+          for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][i * p.ldo + p.extra_col0 + j] = 0x80000000u;
+        }
+      continue;
+    }
     FinishCols<PL> c;
 #pragma unroll
     for (int q = 0; q < PL; ++q) {
@@ -1181,6 +1224,7 @@ __global__ void __launch_bounds__(256) k_tc_fixup(GemmArgs a, const int4 *__rest
   // Every output is 0 when an operand has no nonzero row; and when the
   // global bounds already make every pair exact there is nothing to redo.
   if (!cA->v[5] || !cB->v[5]) return;
+  if (*(volatile int *)&g_tc_error != 0) return;   // k_tc_finish wrote NaR everywhere
   const int min_la = (BIG - cA->v[2]) + (BIG - cB->v[2]);
   const int max_w = cA->v[3] + cB->v[3] + 2 + ceil_log2_int(a.K) + 1;
   if (min_la + 96 >= 0 && max_w <= 127 && !cA->v[4] && !cB->v[4]) return;

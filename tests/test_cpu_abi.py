@@ -103,3 +103,25 @@ def test_format_logic_matches_oracle_exhaustively(host_check, what):
     r = subprocess.run([host_check, what, str(nt)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "mismatches: 0" in r.stdout
+
+
+def test_recommended_exponents_nan_row_raises_like_reference():
+    """A NaN row passes the reference's `rms <= 0` guard and fails in
+    int(np.round(np.log2(nan))) (reference/bposit_quantize.py:56-62)."""
+    import numpy as np
+    from bposit_b200.bposit_quantize import recommended_exponents
+    with pytest.raises(ValueError):
+        recommended_exponents(np.array([[np.nan, 1.0, 2.0]]))
+    assert list(recommended_exponents(np.array([[0.0, 0.0], [4.0, 4.0]]))) == [0, 2]
+
+
+def test_huge_quires_clamp_to_saturation():
+    """Python-int quires beyond 16 limbs are clamped to 2^(96+241), which both
+    the bposit32 and bposit16 rounds saturate at, instead of wrapping."""
+    from bposit_b200.bposit_ref import _QUIRE_SAT, _ints_to_limbs
+    from oracle import oracle as orc
+    limbs = _ints_to_limbs([1 << 700, -(1 << 700), 5])
+    assert orc.limbs_to_int(limbs[0]) == _QUIRE_SAT and orc.limbs_to_int(limbs[1]) == -_QUIRE_SAT
+    assert orc.limbs_to_int(limbs[2]) == 5
+    b32 = orc.quire_to_bp32(limbs)
+    assert list(b32) == [0x7FFFFFFF, 0x80000001, orc.quire_to_bp32(limbs[2:3])[0]]

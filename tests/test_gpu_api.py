@@ -36,6 +36,36 @@ def test_quantize_bp8_values_match_reference(api, orc):
     assert np.array_equal(bf.quantize_bp8_codes(x, nearest=True), q["codes_nearest"])
 
 
+def test_device_error_word_clear_and_nar_handoff():
+    """After ordinary tensor-core GEMMs the device error word reads 0 (a
+    nonzero word makes the Python API raise and marks every tensor-core output
+    NaR); NaR, which no quire round produces, reaches a model as NaN through the
+    fp32 hand-off, while the reference's float64 rescale keeps NaR -> 0.0."""
+    from bposit_b200 import ops
+    rng = np.random.default_rng(5)
+    A = torch.from_numpy(rng.integers(0, 256, (256, 256), dtype=np.uint8)).cuda()
+    out, _ = ops.quire_gemm(A, A, 8, algo=2)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    assert not bool((out == 0x80000000).any())
+    codes = torch.tensor([[0x80000000, 0x40000000, 0]], dtype=torch.int64).to(torch.uint32).cuda()
+    f32 = ops.bp32_to_f32(codes).cpu().numpy()
+    assert np.isnan(f32[0, 0]) and f32[0, 1] == 1.0 and f32[0, 2] == 0.0
+    f64 = ops.bp32_to_f64(codes).cpu().numpy()
+    assert f64[0, 0] == 0.0 and f64[0, 1] == 1.0
+
+
+def test_quire256_clamps_huge_python_ints(api):
+    """quires far beyond 512 bits round to +-maxpos exactly as the reference's
+    unbounded Python ints do (bposit32 saturates above total exponent 240,
+    bposit16 above 112), instead of wrapping in the 16-limb buffer."""
+    _, _, br = api
+    for q in (1 << 600, -(1 << 600), (1 << 511) + 12345, (1 << (96 + 241)) - 1):
+        s = -1 if q < 0 else 1
+        assert br.quire256_to_bposit32(q) == (0x7FFFFFFF if s > 0 else 0x80000001)
+        assert br.quire256_to_bposit16(q) == (0x7FFF if s > 0 else 0x8001)
+
+
 def test_dot_and_dot_quire_selftest(api):
     bf, _, _ = api
     g = golden("fast_selftest")
