@@ -49,7 +49,9 @@ int sm_count() {
 // 1 when the current device is compute capability 10.x (B200 / sm_100).
 static std::atomic<int> g_ok[128];
 
-static int check_device() {
+void clear_error() { g_err[0] = 0; }
+
+int check_device() {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(kENoDev, "no CUDA device: %s", cudaGetErrorString(e));

@@ -21,6 +21,8 @@ enum {
 };
 
 int set_error(int code, const char *fmt, ...);
+void clear_error();    // empties this host thread's bp_last_error() message
+int check_device();    // kENoDev unless the current device is an sm_100 GPU
 int check_launch(const char *what);
 int sm_count();   // SMs of the current device
 
