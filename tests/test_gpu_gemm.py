@@ -245,6 +245,35 @@ def test_large_bp8_k65536_row_subsample(ops, orc):
     torch.cuda.empty_cache()
 
 
+def test_large_bp16_8192_row_subsample(ops, orc):
+    """bp16 8192 x 8192 x 8192 (operands N(0,1) * 2^U{-8..8} per row,
+    encode_bposit16 RTNE): every output on the device; four full rows and a
+    64 x 64 block checked against the oracle.  With 256 x 64 tile pairs the
+    8192^3 grid is 4096 pairs, 55 full waves of 74 and a last partial wave that
+    runs split along K; in the grouped tile order those last tiles are tile
+    rows 24..31 x tile columns 124..127, so rows 6200 and 8191 cross them
+    (columns 7936..8191) and row 0 / the block cross whole-K tiles."""
+    M = N = K = 8192
+    gen = torch.Generator(device="cuda").manual_seed(2)
+
+    def operand(rows):
+        x = torch.randn((rows, K), device="cuda", generator=gen)
+        e = torch.randint(-8, 9, (rows, 1), device="cuda", generator=gen).float()
+        return ops.encode_bp16(x * torch.exp2(e), rtne=True)
+
+    A, B = operand(M), operand(N)
+    out, _ = ops.quire_gemm(A, B, 16)
+    o = out.cpu().numpy()
+    An, Bn = A.cpu().numpy(), B.cpu().numpy()
+    rows = np.array([0, 4321, 6200, 8191])
+    assert np.array_equal(o[rows], orc.quire_gemm(An[rows], Bn, 16))
+    blk_r, blk_c = np.arange(1000, 1064), np.arange(3000, 3064)
+    assert np.array_equal(o[np.ix_(blk_r, blk_c)], orc.quire_gemm(An[blk_r], Bn[blk_c], 16))
+    assert _device_error() == 0
+    del A, B, out
+    torch.cuda.empty_cache()
+
+
 @pytest.mark.parametrize("algo", [2, 3])
 def test_balanced_last_wave(ops, orc, algo):
     """96 paired (192 single) tiles: one full wave runs whole, the remaining tiles

@@ -94,6 +94,45 @@ def test_qwen_shaped_forward_linears_match_oracle(orc):
     assert cos > 0.97
 
 
+def test_qwen_full_size_forward_row_subsample(orc):
+    """The whole Qwen2.5-0.5B-shaped forward of the benchmark (24 layers, batch
+    8 x 1024 tokens): at 8192 tokens every linear takes the tensor-core path
+    (qkv 8192x1152x896, o 8192x896x896, gate/up 8192x9728x896, down
+    8192x896x4864, with K-split last waves and side-stream finishes).  For the
+    first, a middle and the last layer, eight rows of every linear's captured
+    input and output are checked against the oracle."""
+    from bposit_b200.forward import qwen05, synthetic_ids
+    from bposit_b200.nn import BpositLinear
+    model = qwen05(layers=24)
+    ids = synthetic_ids(8, 1024, seed=0)
+    rng = np.random.default_rng(24)
+    rows = np.sort(np.concatenate([[0, 8191], rng.choice(np.arange(1, 8191), 6, replace=False)]))
+    rows_t = torch.from_numpy(rows).cuda()
+    check = {0, 12, 23}
+    captured = []
+
+    def hook(mod, inp, out):
+        x = inp[0].detach().reshape(-1, mod.in_features)
+        y = out.detach().reshape(-1, mod.out_features)
+        captured.append((mod, x.index_select(0, rows_t).cpu(), y.index_select(0, rows_t).cpu()))
+
+    hs = []
+    for li, layer in enumerate(model.layers):
+        if li in check:
+            hs += [m.register_forward_hook(hook) for m in layer.modules() if isinstance(m, BpositLinear)]
+    h = model(ids)
+    for x in hs:
+        x.remove()
+    assert torch.isfinite(h).all()
+    assert len(captured) == 4 * len(check)
+    for mod, x, y in captured:
+        ref = oracle_linear(orc, x.numpy(), mod.weight.cpu().numpy(),
+                            None if mod.bias is None else mod.bias.cpu().numpy(), mod.scales)
+        assert np.array_equal(y.numpy(), ref), (mod.in_features, mod.out_features)
+    from bposit_b200 import ops
+    assert ops.device_error() == 0
+
+
 @pytest.mark.parametrize("K", [1, 2, 3, 20, 576, 4864])
 def test_w8a8_encode_rows_matches_reference_rule(orc, K):
     """ops.w8a8_encode_rows: per-row exponents equal recommended_exponents
