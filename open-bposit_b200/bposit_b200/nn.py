@@ -32,6 +32,16 @@ the bp16 activation path of the mixed-rung quire.
 
 The weight is encoded once, on first use or by ``quantize_weight()``.  The
 reference itself has no module API; this wraps its recipe for torch models.
+
+Multi-GPU (one process per GPU, ``torch.distributed`` initialised):
+``shard_linears(model)`` makes every BpositLinear split its GEMM's output block
+over the process group -- a pm x pn grid of (tokens, output features) blocks,
+``dist.choose_grid`` -- each rank computing its block from its rows of the
+activation codes and of the (replicated) weight codes, the GEMM's finish
+kernel storing the bposit32 words into every rank's copy of the full output
+over NVLink (``dist.FusedShardedQuireGemm``).  Outputs are column- and
+row-independent and no partial sum crosses a rank, so the result is the same
+words as on one GPU; everything outside the linears runs replicated.
 """
 from __future__ import annotations
 
@@ -89,6 +99,7 @@ class BpositLinear(torch.nn.Module):
         self._wq = None          # (codes [N, K] uint8, exponents [N, G] int32)
         self._ws = None          # GEMM workspace, grown on demand
         self._ws_key = None
+        self.sharded = False     # split the GEMM over the process group (shard_linears)
 
     @classmethod
     def from_linear(cls, lin: torch.nn.Linear, group: int = 128, scales: str = "w8a8",
@@ -138,18 +149,29 @@ class BpositLinear(torch.nn.Module):
         bias = None if self.bias is None else self.bias.float().contiguous()
         if self.scales == "group128":
             xc, xs = ops.quantize_bp8_grouped(x2, group=self.group)
-            codes, _ = ops.quire_gemm(xc, wc, 8, sa=xs, sb=ws, group=self.group,
-                                      workspace=self._workspace(M, x2.device))
+            codes = self._gemm(xc, wc, 8, xs, ws, M)
             y = ops.bp32_to_f32(codes, bias=bias)
         elif self.act == "bp16":
             xc = ops.encode_bp16(x2, rtne=True)
-            codes, _ = ops.quire_gemm(xc, self._wq16, 16, workspace=self._workspace(M, x2.device))
+            codes = self._gemm(xc, self._wq16, 16, None, None, M)
             y = ops.bp32_to_f32(codes, col_exp=ws, bias=bias)
         else:
             xc, ex = ops.w8a8_encode_rows(x2)
-            codes, _ = ops.quire_gemm(xc, wc, 8, workspace=self._workspace(M, x2.device))
+            codes = self._gemm(xc, wc, 8, None, None, M)
             y = ops.bp32_to_f32(codes, row_exp=ex, col_exp=ws, bias=bias)
         return y.reshape(*lead, self.out_features)
+
+    def _gemm(self, xc, wc, fmt, sa, sb, M):
+        """bposit32 codes [M, N] of xc @ wc^T: on this GPU, or -- sharded --
+        this rank's output block, all-gathered into the full matrix."""
+        if self.sharded and _world() > 1:
+            g = _shared_gemm(M, self.out_features, self.in_features, fmt, xc.device)
+            m0, m1, n0, n1 = g.block
+            return g(xc[m0:m1], wc[n0:n1], sa=None if sa is None else sa[m0:m1],
+                     sb=None if sb is None else sb[n0:n1])
+        codes, _ = ops.quire_gemm(xc, wc, fmt, sa=sa, sb=sb, group=self.group,
+                                  workspace=self._workspace(M, xc.device))
+        return codes
 
     def extra_repr(self) -> str:
         arith = "bp8 W8A8" if self.act == "bp8" else "bp8 weights, bp16 activations"
@@ -165,3 +187,43 @@ def bpositify(module: torch.nn.Module, group: int = 128, scales: str = "w8a8", a
         else:
             bpositify(child, group=group, scales=scales, act=act)
     return module
+
+
+# ---- multi-GPU: N-sharded linears -------------------------------------------
+_SHARED_GEMMS: dict = {}
+
+
+def _world() -> int:
+    import torch.distributed as dist
+    return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+
+
+def _shared_gemm(M: int, N: int, K: int, fmt: int, device):
+    """The fused sharded GEMM of one (M, N, K, fmt) shape, shared by every
+    linear of that shape (its result buffer is consumed by the caller's
+    bp32 -> fp32 hand-off before the next call's opening barrier).  Creating
+    one is collective: every rank runs the same linears in the same order."""
+    from .dist import FusedShardedQuireGemm
+    key = (M, N, K, fmt, str(device))
+    g = _SHARED_GEMMS.get(key)
+    if g is None:
+        g = FusedShardedQuireGemm(M, N, device, fmt=fmt, K=K)
+        _SHARED_GEMMS[key] = g
+    return g
+
+
+def shard_linears(module: torch.nn.Module) -> torch.nn.Module:
+    """Make every BpositLinear inside `module` split its GEMM over the default
+    process group (see the module docstring).  In place; no-op on one rank."""
+    for m in module.modules():
+        if isinstance(m, BpositLinear):
+            m.sharded = True
+    return module
+
+
+def close_sharded() -> None:
+    """Release the shared sharded GEMMs' buffers.  Collective: call on every
+    rank before destroying the process group."""
+    for g in list(_SHARED_GEMMS.values()):
+        g.close()
+    _SHARED_GEMMS.clear()

@@ -3,7 +3,8 @@ through torch.distributed.run, one process per GPU, NCCL).  Every rank computes
 its N-shard on the tensor cores, the shards are all-gathered (NCCL, and the
 fused epilogue peer stores), and every rank compares its whole bposit32 matrix
 with an unsharded single-GPU GEMM: the quire result must be bit-identical for
-any rank count."""
+any rank count.  Then the Qwen-shaped forward with every linear sharded
+(nn.shard_linears) against the same forward on one GPU."""
 from __future__ import annotations
 
 import datetime
@@ -80,6 +81,25 @@ def main():
         if rank == 0:
             results.append({"shape": [M, N, K], "group": group, "gather": ok[0], "fused": ok[1:],
                             "equal": bool(flags.item())})
+    # The N-sharded Qwen-shaped forward (every linear's output block over the
+    # ranks, all-gathered by the finish kernel) against the same model on this
+    # GPU alone: identical bposit32 words give an identical forward.
+    from bposit_b200.forward import qwen05, synthetic_ids
+    from bposit_b200.nn import close_sharded, shard_linears
+    ids = synthetic_ids(2, 256, seed=5, device=dev)
+    one = qwen05(layers=2, device=dev, seed=3)
+    h1 = one(ids)
+    sh = shard_linears(qwen05(layers=2, device=dev, seed=3))
+    h2 = sh(ids)
+    h3 = sh(ids.flip(1))
+    h4 = one(ids.flip(1))
+    torch.cuda.synchronize()
+    close_sharded()
+    ok_f = bool(torch.equal(h1, h2)) and bool(torch.equal(h3, h4))
+    flags = torch.tensor([int(ok_f)], device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    if rank == 0:
+        results.append({"shape": "qwen05 2 layers x 512 tokens, sharded linears", "equal": bool(flags.item())})
     dist.barrier()
     if rank == 0:
         print(json.dumps({"world": world, "results": results}), flush=True)

@@ -80,11 +80,13 @@ def test_shard_bounds():
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 6, 8])
 def test_block_grid_covers_output_once(world):
-    """Every pm x pn grid (and the chosen one) tiles [M, N] exactly once."""
+    """Every pm x pn grid (and the chosen one) tiles [M, N] exactly once: the
+    large GEMM and the Qwen-shaped linears that nn.shard_linears splits."""
     from bposit_b200.dist import block_bounds, choose_grid
-    for M, N in ((4096, 4096), (300, 777), (5, 3), (1, 64)):
+    for M, N, K in ((4096, 4096, 65536), (300, 777, 65536), (5, 3, 65536), (1, 64, 65536),
+                    (8192, 1152, 896), (8192, 896, 896), (8192, 9728, 896), (8192, 896, 4864)):
         grids = [(pm, world // pm) for pm in range(1, world + 1) if world % pm == 0]
-        chosen = choose_grid(world, M, N, 65536)
+        chosen = choose_grid(world, M, N, K)
         assert chosen in grids
         for grid in grids:
             cover = np.zeros((M, N), np.int32)
