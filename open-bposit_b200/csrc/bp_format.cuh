@@ -293,6 +293,87 @@ BP_HD uint32_t bp16_to_f32_bits(uint32_t c) {
 }
 
 // ---------------------------------------------------------------------------
+// Signed streaming tables.  Indexed by u >> 23 (the sign and the biased
+// exponent of the fp32 bits u), each entry gives a signed base code bs and a
+// shift sh so that, with M the 23-bit mantissa, c the entry's rounding addend
+// and q = (M + c) >> sh, the code is bs + q for positive x and bs - q for
+// negative x (low 8 / 16 bits).  Negative entries hold 2^NB - base, so bs - q
+// is the two's complement of the magnitude code base + q.  Zero, subnormal,
+// inf and NaN inputs need no special case: their entries use sh = 23 and
+// c = 2^23 - 1 (minus the RTNE parity bit for bp16), which makes q = 1 exactly
+// when M != 0 -- zero -> code 0 (the -0 entry's 2^NB wraps to 0), subnormal ->
+// +-minpos, inf -> +-maxpos and NaN -> maxpos + 1 = NaR.
+// ---------------------------------------------------------------------------
+
+// bp8 (bp8_qentry semantics).  x = bs | sh << 16; c = 2^sh - 1 - thr, the
+// addend that carries into the code exactly when M's dropped bits exceed thr
+// (0 for the truncating mode's "never").
+BP_HD void bp8_qentry_signed(int idx, bool nearest, uint32_t &x, uint32_t &c) {
+  const int b = idx & 0xFF;
+  const bool neg = (idx >> 8) & 1;
+  const QEntry q = bp8_qentry(b, nearest);
+  const uint32_t base = q.lo_sh & 0xFFu, sh = q.lo_sh >> 8;
+  c = q.thr >= 0x7FFFFFu ? 0u : (1u << sh) - 1u - q.thr;
+  if (b == 255) c = 0x7FFFFFu;   // sh = 23: inf -> maxpos (127), NaN -> 128 = NaR
+  x = (neg ? 0x100u - base : base) | (sh << 16);
+}
+
+BP_HD uint32_t bp8_encode_signed(uint32_t u, uint32_t x, uint32_t c) {
+  const uint32_t q = ((u & 0x7FFFFFu) + c) >> (x >> 16);
+  const uint32_t m = (uint32_t)((int32_t)u >> 31);
+  return ((x & 0xFFFFu) + ((q ^ m) - m)) & 0xFFu;
+}
+
+// bp16 (bp16_qentry semantics, RTNE or truncating).  x = bs | sh << 17 (the
+// -0 entry's bs is 0x10000, 17 bits); c = half - 1 for RTNE, 0 for
+// truncation; with RTNE the parity of the truncated field, (bs ^ (M >> sh)) & 1,
+// is added as well.
+BP_HD void bp16_qentry_signed(int idx, bool rtne, uint32_t &x, uint32_t &c) {
+  const int b = idx & 0xFF;
+  const bool neg = (idx >> 8) & 1;
+  uint32_t lo, hm1;
+  bp16_qentry(b, rtne, lo, hm1);
+  uint32_t base = lo & 0xFFFFu, sh = lo >> 16;
+  c = hm1;
+  if (b == 0) { base = 0u; sh = 23u; c = 0x7FFFFFu; }                          // 0 -> 0, subnormal -> minpos
+  if (b == 255) { base = 0x7FFFu; sh = 23u; c = rtne ? 0x7FFFFEu : 0x7FFFFFu; }  // odd base: parity adds 1
+  x = (neg ? 0x10000u - base : base) | (sh << 17);
+}
+
+template <bool RTNE>
+BP_HD uint32_t bp16_encode_signed(uint32_t u, uint32_t x, uint32_t c) {
+  const uint32_t M = u & 0x7FFFFFu, sh = x >> 17, bs = x & 0x1FFFFu;
+  const uint32_t lsb = RTNE ? ((bs ^ (M >> sh)) & 1u) : 0u;
+  const uint32_t q = (M + c + lsb) >> sh;
+  const uint32_t m = (uint32_t)((int32_t)u >> 31);
+  return (bs + ((q ^ m) - m)) & 0xFFFFu;
+}
+
+// bp16 decode table over the top 8 bits t of a positive 15-bit field: when
+// the regime, its terminator and the three exponent bits all lie in those 8
+// bits (fraction width fw >= 7), the low 7 field bits are the lowest fraction
+// bits and the fp32 pattern is base + (low7 << (23 - fw)); the entry is
+// base | (23 - fw) (base has no bit below 2^14).  0 marks the other fields
+// (regime runs of 5 or more: |value| >= 2^32 or < 2^-32, and zero), decoded in
+// closed form instead.
+BP_HD uint32_t bp16_dec_entry(uint32_t t) {
+  const uint32_t f = (t & 0xFFu) << 7;
+  if (f == 0u) return 0u;
+  const Dec d = decode_posit<16, 3>(f);
+  if (d.fw < 7) return 0u;
+  return (((uint32_t)(d.scale + 127) << 23) | (d.fbits << (23 - d.fw))) | (uint32_t)(23 - d.fw);
+}
+
+BP_HD uint32_t bp16_decode_lut(uint32_t c, uint32_t e) {
+  // e = table[f >> 7] for f the code's positive 15-bit field
+  const uint32_t neg = (c >> 15) & 1u;
+  const uint32_t f = (neg ? 0u - c : c) & 0x7FFFu;
+  return e ? (((e & ~31u) + ((f & 0x7Fu) << (e & 31u))) | (neg << 31)) : bp16_to_f32_bits(c);
+}
+
+BP_HD uint32_t bp16_field(uint32_t c) { return (((c >> 15) & 1u) ? 0u - c : c) & 0x7FFFu; }
+
+// ---------------------------------------------------------------------------
 // bp32 from an exact magnitude: value = mag * 2^lsb_exp, mag = (hi:lo) 128-bit.
 // The truncating bit-string encoder of reference/bposit_ref.py:97-150 as used
 // by quire256_to_bposit32 (:703-722): total_e = floor(log2 value), regime,

@@ -5,10 +5,11 @@
 // of all fp32 patterns (bp16 encode, both modes), every bp8 / bp16 code
 // (decode) and random 128-bit magnitudes (bp32 round, its signed 64-bit form,
 // and the bp16 round derived from it).  The streaming kernels' table-driven
-// bp16 encoder and closed-form bp16 decoder are compared with the bit-string
-// forms above over every fp32 pattern and every bp16 code.  Test-only.
+// bp16 encoder and closed-form bp16 decoder, and the signed bp8 / bp16 tables
+// and bp16 decode table, are compared with the bit-string forms above over
+// every fp32 pattern and every bp16 code.  Test-only.
 //
-// usage: host_format_check <what> <threads>   what in q8 | e16 | e16t | dec | bp32 | small
+// usage: host_format_check <what> <threads>   what in q8 | e16 | e16t | signed | dec | bp32 | small
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -95,6 +96,37 @@ static void e16t_range(uint64_t lo, uint64_t hi, bool rtne) {
   g_bad += bad;
 }
 
+// the signed streaming tables against the per-binade forms on [lo, hi)
+static void signed_range(uint64_t lo, uint64_t hi, int mode) {
+  uint32_t x8[512], c8[512], x16[512], c16[512];
+  for (int i = 0; i < 512; ++i) {
+    bp::bp8_qentry_signed(i, mode == 1, x8[i], c8[i]);
+    bp::bp16_qentry_signed(i, mode == 1, x16[i], c16[i]);
+  }
+  bp::QEntry t8[256];
+  for (int b = 0; b < 256; ++b) t8[b] = bp::bp8_qentry(b, mode == 1);
+  long long bad = 0;
+  for (uint64_t v = lo; v < hi; ++v) {
+    const uint32_t u = (uint32_t)v, a = u & 0x7FFFFFFFu, i = u >> 23;
+    uint32_t r8;
+    if (a > 0x7F800000u) r8 = 0x80u;
+    else {
+      const uint32_t mag = bp::bp8_apply(t8[a >> 23], a & 0x7FFFFFu);
+      r8 = (u >> 31) ? ((0u - mag) & 0xFFu) : mag;
+    }
+    const uint32_t s8 = bp::bp8_encode_signed(u, x8[i], c8[i]);
+    const uint32_t r16 = bp::bp16_encode_bits(u, mode == 1);
+    const uint32_t s16 = mode == 1 ? bp::bp16_encode_signed<true>(u, x16[i], c16[i])
+                                   : bp::bp16_encode_signed<false>(u, x16[i], c16[i]);
+    if (s8 != r8 || s16 != r16) {
+      if (bad < 5)
+        fprintf(stderr, "signed mismatch mode=%d x=%08x bp8 %02x/%02x bp16 %04x/%04x\n", mode, u, s8, r8, s16, r16);
+      ++bad;
+    }
+  }
+  g_bad += bad;
+}
+
 static uint64_t rng_state = 0x9E3779B97F4A7C15ull;
 static uint64_t rnd() {
   rng_state ^= rng_state << 13; rng_state ^= rng_state >> 7; rng_state ^= rng_state << 17;
@@ -144,8 +176,25 @@ int main(int argc, char **argv) {
       for (auto &x : th) x.join();
       th.clear();
     }
+  } else if (!strcmp(what, "signed")) {
+    // every fp32 pattern, both modes: signed bp8 / bp16 tables vs the table / bit-string forms
+    for (int mode = 0; mode < 2; ++mode) {
+      for (int t = 0; t < nt; ++t) {
+        uint64_t lo = (0x100000000ull * t) / nt, hi = (0x100000000ull * (t + 1)) / nt;
+        th.emplace_back(signed_range, lo, hi, mode);
+      }
+      for (auto &x : th) x.join();
+      th.clear();
+    }
   } else if (!strcmp(what, "dec")) {
     long long bad = 0;
+    uint32_t lut16[256];
+    for (uint32_t t = 0; t < 256; ++t) lut16[t] = bp::bp16_dec_entry(t);
+    for (uint32_t c = 0; c < 65536; ++c)
+      if (bp::bp16_decode_lut(c, lut16[bp::bp16_field(c) >> 7]) != bp::posit_to_f32_bits<16, 3>(c)) {
+        if (bad < 5) fprintf(stderr, "bp16 lut decode %04x\n", c);
+        ++bad;
+      }
     for (uint32_t c = 0; c < 256; ++c) {
       int64_t m; int e; int dm, de;
       orc_decode_me(8, c, &m, &e);

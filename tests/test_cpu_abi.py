@@ -90,7 +90,7 @@ def host_check():
     return exe
 
 
-@pytest.mark.parametrize("what", ["dec", "bp32", "q8", "e16", "e16t", "small"])
+@pytest.mark.parametrize("what", ["dec", "bp32", "q8", "e16", "e16t", "signed", "small"])
 def test_format_logic_matches_oracle_exhaustively(host_check, what):
     """The kernels' format logic (bp_format.cuh) compiled for the host vs the
     oracle: all bp8/bp16 codes; 2M random quires; every non-negative fp32
@@ -98,7 +98,8 @@ def test_format_logic_matches_oracle_exhaustively(host_check, what):
     fp32 patterns plus every binade edge for the bp16 encoder (both modes); a
     strided fp32 sweep and 2M random doubles for the bposit4 / AI-posit5 encoders;
     the streaming kernels' table bp16 encoder on every fp32 pattern (both modes)
-    and their closed-form bp16 decode on every code."""
+    and their closed-form bp16 decode on every code; the signed bp8 / bp16 tables
+    on every fp32 pattern (both modes) and the bp16 decode table on every code."""
     nt = max(1, min(8, len(os.sched_getaffinity(0))))
     r = subprocess.run([host_check, what, str(nt)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
