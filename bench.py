@@ -375,11 +375,10 @@ def run_headline(ctx, fmt=8, M=M_, N=N_, K=K_):
     else:
         g = ShardedQuireGemm(M, N, ctx.device, algo=args.algo, fmt=fmt)
         (n0, n1), (m0, m1), grid = g.plan.bounds, (0, M), (1, ctx.world)
-    A_full = A
+    A_full, B_full = A, B
     A = A_full[m0:m1].contiguous()
     Bs = B[n0:n1].contiguous()
     del B
-    torch.cuda.empty_cache()
     ws = torch.empty(max(256, ops.gemm_workspace_size(fmt, m1 - m0, n1 - n0, K, args.algo)), dtype=torch.uint8,
                      device=ctx.device)
     peers = [p + 4 * m0 * N for p in g.peer_ptrs] if fused else []
@@ -418,6 +417,20 @@ def run_headline(ctx, fmt=8, M=M_, N=N_, K=K_):
         else None
     breakdown = kernel_breakdown(ctx, lambda: shard_step(A, Bs))
     per_rank = gather_obj(ctx, breakdown)
+    nccl_variant = None
+    if ctx.world > 1 and fused:
+        # the same workload with N shards and one NCCL all-gather (+ local transpose)
+        g2 = ShardedQuireGemm(M, N, ctx.device, algo=args.algo, fmt=fmt)
+        a0, a1 = g2.plan.bounds
+        Bn = B_full[a0:a1].contiguous()
+        ws2 = torch.empty(max(256, ops.gemm_workspace_size(fmt, M, a1 - a0, K, args.algo)), dtype=torch.uint8,
+                          device=ctx.device)
+        ms2, _, _ = ctx.timed(lambda: g2(A_full, Bn), max(3, steps // 2), args.warmup)
+        nccl_variant = {"value": round(2.0 * M * N * K / (ms2 * 1e-3) / 1e12, 3), "unit": "TOPS",
+                        "ms_per_step": round(ms2, 3), "layout": f"1x{ctx.world} N shards + NCCL all_gather_into_tensor"}
+        del g2, Bn, ws2
+    del B_full
+    torch.cuda.empty_cache()
 
     # end to end with host buffers (pinned): one GPU through bp_quire_gemm_host;
     # several through H2D of each rank's blocks, the sharded step and a D2H of the result
@@ -484,6 +497,7 @@ def run_headline(ctx, fmt=8, M=M_, N=N_, K=K_):
                 "d2h_bytes_per_step": int(M * N * 4), "h2d_link_gbs": round(h2d_gbs, 1),
                 "matches_device_result": e2e_ok},
         "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clk,
+        "nccl_gather_variant": nccl_variant,
         "breakdown_ms_per_step": {"rank0": per_rank[0], "per_rank": per_rank if ctx.world > 1 else None,
                                   "how": "CUDA activity trace (torch.profiler) of 2 extra untimed steps"},
     })
