@@ -76,10 +76,17 @@ __global__ void __launch_bounds__(kThreads) k_decode_bp8(const uint8_t *__restri
   for (size_t i = nw * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(lut[codes[i]]);
 }
 
-// bp16: closed-form decode (bp16_to_f32_bits), four codes (8 bytes) per unit.
+// bp16: a 256-entry table over the top 8 bits of the code's 15-bit field
+// (bp16_dec_entry) gives the fp32 pattern of every value with a regime run of
+// at most 4 (2^-32 <= |v| < 2^32) as base + (low 7 field bits << shift); the
+// rest decode in closed form (bp16_to_f32_bits).  Four codes (8 bytes) per unit.
 template <int U>
 __global__ void __launch_bounds__(kThreads) k_decode_bp16(const uint16_t *__restrict__ codes, size_t n,
                                                           float *__restrict__ out, bool vec) {
+  __shared__ uint32_t lut[256];
+  lut[threadIdx.x] = bp16_dec_entry(threadIdx.x);
+  __syncthreads();
+  auto dec = [&](uint32_t c) { return bp16_decode_lut(c, lut[bp16_field(c) >> 7]); };
   const size_t nq = vec ? n / 4 : 0;
   const uint2 *c2 = reinterpret_cast<const uint2 *>(codes);
   uint4 *o4 = reinterpret_cast<uint4 *>(out);
@@ -95,93 +102,90 @@ __global__ void __launch_bounds__(kThreads) k_decode_bp16(const uint16_t *__rest
     for (int j = 0; j < U; ++j) {
       const size_t i = base + threadIdx.x + j * kThreads;
       if (i < nq)
-        __stcs(o4 + i, make_uint4(bp16_to_f32_bits(v[j].x & 0xFFFFu), bp16_to_f32_bits(v[j].x >> 16),
-                                  bp16_to_f32_bits(v[j].y & 0xFFFFu), bp16_to_f32_bits(v[j].y >> 16)));
+        __stcs(o4 + i, make_uint4(dec(v[j].x & 0xFFFFu), dec(v[j].x >> 16), dec(v[j].y & 0xFFFFu), dec(v[j].y >> 16)));
     }
   }
   const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = nq * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(bp16_to_f32_bits(codes[i]));
+  for (size_t i = nq * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(dec(codes[i]));
 }
 
 // ------------------------------------------------------------ quantize bp8 ---
-__device__ __forceinline__ uint32_t q8_one(const uint2 *tbl, uint32_t u) {
-  uint32_t a = u & 0x7FFFFFFFu;
-  uint2 t = tbl[a >> 23];
-  QEntry q{t.x, t.y};
-  uint32_t mag = bp8_apply(q, a & 0x7FFFFFu);
-  uint32_t code = (u >> 31) ? ((0u - mag) & 0xFFu) : mag;
-  return a > 0x7F800000u ? 0x80u : code;   // NaN -> NaR
-}
-
-template <bool NEAREST, bool VALUES>
+// Signed per-binade table (bp8_qentry_signed, 512 entries indexed by the sign
+// and biased exponent): a code is one table load, a shift-add and a
+// conditional negate (bp8_encode_signed), with zero, subnormals, inf and NaN
+// folded into their entries.  Units of four elements (a float4 in, a word of
+// codes out, and with `vals` a float4 of exact values) in the decode kernels'
+// tile order; grid-stride over tiles, 8 blocks per SM.
+template <bool NEAREST, bool VALUES, int U>
 __global__ void __launch_bounds__(kThreads) k_quantize_bp8(const float *__restrict__ x, size_t n,
                                                            uint8_t *__restrict__ codes,
                                                            float *__restrict__ vals, bool vec) {
-  __shared__ uint2 tbl[256];
-  __shared__ uint32_t lut[256];
-  {
-    QEntry q = bp8_qentry(threadIdx.x, NEAREST);
-    tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
-    if (VALUES) lut[threadIdx.x] = posit_to_f32_bits<8, 2>(threadIdx.x);
+  __shared__ uint2 tbl[512];
+  __shared__ uint32_t lut[VALUES ? 256 : 1];
+  for (int i = threadIdx.x; i < 512; i += kThreads) {
+    uint32_t e, c;
+    bp8_qentry_signed(i, NEAREST, e, c);
+    tbl[i] = make_uint2(e, c);
   }
+  if (VALUES) lut[threadIdx.x] = threadIdx.x == 0x80 ? 0x7FC00000u : posit_to_f32_bits<8, 2>(threadIdx.x);
   __syncthreads();
-  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  size_t stride = (size_t)gridDim.x * blockDim.x;
-  size_t nv = vec ? n / 16 : 0;
+  auto enc = [&](uint32_t u) {
+    const uint2 t = tbl[u >> 23];
+    return bp8_encode_signed(u, t.x, t.y);
+  };
+  const size_t nq = vec ? n / 4 : 0;
   const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
-  uint4 *c4 = reinterpret_cast<uint4 *>(codes);
+  uint32_t *cw = reinterpret_cast<uint32_t *>(codes);
   uint4 *v4 = reinterpret_cast<uint4 *>(vals);
-  for (size_t i = tid; i < nv; i += stride) {
-    uint4 in[4];
+  const size_t tile = (size_t)kThreads * U;
+  for (size_t base = blockIdx.x * tile; base < nq; base += (size_t)gridDim.x * tile) {
+    uint4 v[U];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) in[q] = __ldcs(x4 + 4 * i + q);
-    uint32_t cw[4];
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      v[j] = i < nq ? __ldcs(x4 + i) : make_uint4(0u, 0u, 0u, 0u);
+    }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint32_t c0 = q8_one(tbl, in[q].x), c1 = q8_one(tbl, in[q].y);
-      uint32_t c2 = q8_one(tbl, in[q].z), c3 = q8_one(tbl, in[q].w);
-      cw[q] = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
-      if (VALUES) {
-        uint4 v;
-        v.x = (c0 == 0x80u) ? 0x7FC00000u : lut[c0];
-        v.y = (c1 == 0x80u) ? 0x7FC00000u : lut[c1];
-        v.z = (c2 == 0x80u) ? 0x7FC00000u : lut[c2];
-        v.w = (c3 == 0x80u) ? 0x7FC00000u : lut[c3];
-        __stcs(v4 + 4 * i + q, v);
+    for (int j = 0; j < U; ++j) {
+      const size_t i = base + threadIdx.x + j * kThreads;
+      if (i < nq) {
+        const uint32_t c0 = enc(v[j].x), c1 = enc(v[j].y), c2 = enc(v[j].z), c3 = enc(v[j].w);
+        __stcs(cw + i, c0 | (c1 << 8) | (c2 << 16) | (c3 << 24));
+        if (VALUES) __stcs(v4 + i, make_uint4(lut[c0], lut[c1], lut[c2], lut[c3]));
       }
     }
-    __stcs(c4 + i, make_uint4(cw[0], cw[1], cw[2], cw[3]));
   }
-  for (size_t i = nv * 16 + tid; i < n; i += stride) {
-    uint32_t c = q8_one(tbl, __float_as_uint(x[i]));
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = nq * 4 + tid; i < n; i += stride) {
+    const uint32_t c = enc(__float_as_uint(x[i]));
     codes[i] = (uint8_t)c;
-    if (VALUES) vals[i] = __uint_as_float(c == 0x80u ? 0x7FC00000u : lut[c]);
+    if (VALUES) vals[i] = __uint_as_float(lut[c]);
   }
 }
 
 // ------------------------------------------------------------ encode bp16 ---
-// Per-binade table (bp16_qentry, 2 KB of shared memory): a code costs one
-// table load and a handful of integer operations (bp16_encode_tbl).  Units of
-// four elements (a float4 in, 8 bytes of codes out) in the tile order of the
-// decode kernels; grid-stride over tiles, 8 blocks per SM.
+// Signed per-binade table (bp16_qentry_signed, 512 entries): a code is one
+// table load, the RTNE parity bit, a shift-add and a conditional negate
+// (bp16_encode_signed).  Units of four elements (a float4 in, 8 bytes of codes
+// out) in the decode kernels' tile order; grid-stride over tiles, 8 blocks per SM.
 template <bool RTNE, int U>
 __global__ void __launch_bounds__(kThreads) k_encode_bp16(const float *__restrict__ x, size_t n,
                                                           uint16_t *__restrict__ codes, bool vec) {
-  __shared__ uint2 tbl[256];
-  {
-    uint32_t lo, hm;
-    bp16_qentry(threadIdx.x, RTNE, lo, hm);
-    tbl[threadIdx.x] = make_uint2(lo, hm);
+  __shared__ uint2 tbl[512];
+  for (int i = threadIdx.x; i < 512; i += kThreads) {
+    uint32_t e, c;
+    bp16_qentry_signed(i, RTNE, e, c);
+    tbl[i] = make_uint2(e, c);
   }
   __syncthreads();
+  auto enc = [&](uint32_t u) {
+    const uint2 t = tbl[u >> 23];
+    return bp16_encode_signed<RTNE>(u, t.x, t.y);
+  };
   const size_t nq = vec ? n / 4 : 0;
   const uint4 *x4 = reinterpret_cast<const uint4 *>(x);
   uint2 *c2 = reinterpret_cast<uint2 *>(codes);
   const size_t tile = (size_t)kThreads * U;
-  auto enc = [&](uint32_t u) {
-    const uint2 t = tbl[(u >> 23) & 0xFFu];
-    return bp16_encode_tbl(u, t.x, t.y, RTNE);
-  };
   for (size_t base = blockIdx.x * tile; base < nq; base += (size_t)gridDim.x * tile) {
     uint4 v[U];
 #pragma unroll
@@ -324,7 +328,7 @@ inline int tile_grid(size_t n, int per, int U) {
   return (int)std::min<size_t>(std::max<size_t>(b, 1), (size_t)1 << 30);
 }
 
-constexpr int kDecU8 = 4, kDecU16 = 8, kEncU16 = 8;
+constexpr int kDecU8 = 4, kDecU16 = 8, kEncU16 = 8, kEncU8 = 8;
 
 int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t s) {
   if (n == 0) return kOk;
@@ -342,14 +346,14 @@ int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t
 int launch_quantize_bp8(const float *x, size_t n, bool nearest, uint8_t *codes, float *values,
                         cudaStream_t s) {
   if (n == 0) return kOk;
-  bool vec = aligned16(x) && aligned16(codes) && (values == nullptr || aligned16(values));
-  int g = grid_for(vec ? n / 16 + 1 : n);
+  const bool vec = aligned16(x) && ((uintptr_t)codes & 3u) == 0u && (values == nullptr || aligned16(values));
+  const int g = std::min(tile_grid(n, 4, kEncU8), sm_count() * 8);
   if (nearest) {
-    if (values) k_quantize_bp8<true, true><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
-    else k_quantize_bp8<true, false><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    if (values) k_quantize_bp8<true, true, kEncU8><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    else k_quantize_bp8<true, false, kEncU8><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
   } else {
-    if (values) k_quantize_bp8<false, true><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
-    else k_quantize_bp8<false, false><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    if (values) k_quantize_bp8<false, true, kEncU8><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
+    else k_quantize_bp8<false, false, kEncU8><<<g, kThreads, 0, s>>>(x, n, codes, values, vec);
   }
   return check_launch("quantize_bp8");
 }
