@@ -168,6 +168,24 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K,
                   uint32_t *out_bp32, int64_t ldo, uint32_t *out_quire, int quire_limbs,
                   int algo, void *workspace, size_t workspace_bytes, void *stream);
 
+/* bp_quire_gemm with the hand-off to the next fp32 op of a model written by
+ * the GEMM's own output stage:
+ *   out_f32[m * ldf + n] = fp32( value(bp32[m,n]) * 2^(row_exp[m] + col_exp[n]) + bias[n] )
+ * -- the bposit32 round of the exact quire, its exact value scaled by the
+ * power-of-two exponents (each optional, NULL = 0) plus the optional fp32 bias,
+ * added in float64 and rounded once to the nearest-even fp32; NaR -> NaN.
+ * The same numbers as bp_quire_gemm followed by bp_bp32_to_f32, without the
+ * second pass over the [M, N] codes.  out_bp32 is optional (NULL: the codes
+ * are not stored).  No raw-quire output; single GPU.  Replaces matmul_quire +
+ * quire256_to_bposit32 (reference/bposit_fast.py:136-176,
+ * reference/bposit_ref.py:703-722) followed by the rescale of quantize_w8a8
+ * (reference/bposit_quantize.py:66-68, 88), in fp32 for a torch model. */
+int bp_quire_gemm_f32(int fmt, const void *A, const void *B, int M, int N, int K,
+                      const int32_t *sa, const int32_t *sb, int group,
+                      const int32_t *row_exp, const int32_t *col_exp, const float *bias,
+                      float *out_f32, int64_t ldf, uint32_t *out_bp32, int64_t ldo,
+                      int algo, void *workspace, size_t workspace_bytes, void *stream);
+
 /* bp_quire_gemm on HOST buffers: A, B, sa, sb and out_bp32 are host pointers
  * (page-locked memory gives full PCIe bandwidth; pageable memory works,
  * slower).  One operand goes to the device whole and is prepared once; the

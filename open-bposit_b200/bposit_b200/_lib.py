@@ -70,6 +70,8 @@ def lib() -> ctypes.CDLL:
             "bp_quire_gemm": ([i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, i64, vp, i32, i32,
                                vp, sz, vp], i32),
             "bp_quire_gemm_workspace_size": ([i32, i32, i32, i32, i32], sz),
+            "bp_quire_gemm_f32": ([i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, vp, vp, vp, i64, vp, i64, i32,
+                                   vp, sz, vp], i32),
             "bp_quire_gemm_multi": ([i32, vp, vp, i32, i32, i32, vp, vp, i32, vp, i64, vp, i32, i64, i32,
                                      vp, sz, vp], i32),
             "bp_enable_peer_access": ([i32], i32),
@@ -100,7 +102,7 @@ EXPORTED = (
     "bp_quantize_bp8_grouped", "bp_encode_bp16", "bp_quire_to_bp32", "bp_quire_to_bp16", "bp_bp32_to_bp16",
     "bp_quantize_small", "bp_transcode", "bp_bp32_to_f32", "bp_quire_gemm_host",
     "bp_w8a8_encode_rows",
-    "bp_quire_gemm",
+    "bp_quire_gemm", "bp_quire_gemm_f32",
     "bp_quire_gemm_workspace_size", "bp_quire_gemm_multi", "bp_enable_peer_access",
     "bp_ipc_alloc", "bp_ipc_free", "bp_ipc_open", "bp_ipc_close", "bp_quire_gemm_noalloc",
     "bp_bp32_to_f64",

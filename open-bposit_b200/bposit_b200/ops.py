@@ -219,6 +219,44 @@ def quire_gemm(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, gro
     return out, q
 
 
+def quire_gemm_f32(A: torch.Tensor, B: torch.Tensor, fmt=None, sa=None, sb=None, group: int = 128,
+                   row_exp=None, col_exp=None, bias=None, out=None, out_bp32=None, algo: int = 0,
+                   workspace=None) -> torch.Tensor:
+    """Exact quire GEMM A[M,K] @ B[N,K]^T whose output stage writes the fp32
+    hand-off directly: value(bposit32) * 2^(row_exp[m] + col_exp[n]) + bias[n],
+    rounded once to fp32 -- the numbers of quire_gemm followed by bp32_to_f32.
+    `out` (optional) is a [M, N] float32 view with unit column stride;
+    `out_bp32` (optional) also receives the bposit32 codes."""
+    f = fmt_bits(fmt) if fmt is not None else (8 if A.dtype == torch.uint8 else 16)
+    a = _dev(A, "A", _CODE_DTYPE[f])
+    b = _dev(B, "B", _CODE_DTYPE[f])
+    if a.dim() != 2 or b.dim() != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError("quire_gemm_f32 expects A[M,K] and B[N,K]")
+    M, K = a.shape
+    N = b.shape[0]
+    sa_ = None if sa is None else _dev(sa, "sa", torch.int32)
+    sb_ = None if sb is None else _dev(sb, "sb", torch.int32)
+    re = None if row_exp is None else _dev(row_exp, "row_exp", torch.int32)
+    ce = None if col_exp is None else _dev(col_exp, "col_exp", torch.int32)
+    bs = None if bias is None else _dev(bias, "bias", torch.float32)
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    elif out.dtype != torch.float32 or out.shape != (M, N) or out.stride(1) != 1:
+        raise ValueError("out must be a [M, N] float32 view with unit column stride")
+    ldo = 0
+    if out_bp32 is not None:
+        if out_bp32.dtype != torch.uint32 or out_bp32.shape != (M, N) or out_bp32.stride(1) != 1:
+            raise ValueError("out_bp32 must be a [M, N] uint32 view with unit column stride")
+        ldo = out_bp32.stride(0)
+    need = gemm_workspace_size(f, M, N, K, algo)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=a.device)
+    _lib.check(_lib.lib().bp_quire_gemm_f32(f, _p(a), _p(b), M, N, K, _p(sa_), _p(sb_), group, _p(re), _p(ce),
+                                            _p(bs), _p(out), out.stride(0), _p(out_bp32), ldo, algo,
+                                            _p(workspace), workspace.numel(), _stream()))
+    return out
+
+
 def quire_gemm_host(A, B, fmt=None, sa=None, sb=None, group: int = 128, out=None, algo: int = 0):
     """Exact quire GEMM on host arrays (CPU tensors or numpy; page-locked CPU
     tensors copy fastest): the library sends one operand whole and streams the

@@ -222,6 +222,45 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K, co
   return rc;
 }
 
+int bp_quire_gemm_f32(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
+                      const int32_t *sb, int group, const int32_t *row_exp, const int32_t *col_exp,
+                      const float *bias, float *out_f32, int64_t ldf, uint32_t *out_bp32, int64_t ldo, int algo,
+                      void *workspace, size_t workspace_bytes, void *stream) {
+  g_err[0] = 0;
+  if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_f32: fmt must be 8 or 16 (got %d)", fmt);
+  if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_f32: negative size");
+  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_f32: algo must be 0, 1, 2 or 3");
+  if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_f32: group must be > 0 with scales");
+  if (ldf < N) return set_error(kEInval, "bp_quire_gemm_f32: ldf (%lld) < N (%d)", (long long)ldf, N);
+  if (out_bp32 && ldo < N) return set_error(kEInval, "bp_quire_gemm_f32: ldo (%lld) < N (%d)", (long long)ldo, N);
+  if (M == 0 || N == 0) return kOk;
+  if (!out_f32 || (K > 0 && (!A || !B))) return set_error(kEInval, "bp_quire_gemm_f32: null pointer");
+  if (workspace && ((uintptr_t)workspace & 255u))
+    return set_error(kEAlign, "bp_quire_gemm_f32: workspace not 256-byte aligned");
+  TRY(check_device());
+  GemmArgs a{};
+  a.fmt = fmt; a.A = A; a.B = B; a.M = M; a.N = N; a.K = K;
+  a.sa = sa; a.sb = sb; a.group = group > 0 ? group : 1;
+  a.G = group > 0 ? (K + group - 1) / group : 1;
+  a.out = out_bp32; a.ldo = out_bp32 ? ldo : 0;
+  a.out_f32 = out_f32; a.ldf = ldf; a.re = row_exp; a.ce = col_exp; a.bias = bias;
+  cudaStream_t s = (cudaStream_t)stream;
+  size_t need = gemm_workspace_size(fmt, M, N, K, algo);
+  if (workspace) {
+    if (workspace_bytes < need)
+      return set_error(kEWorkspace, "bp_quire_gemm_f32: workspace %zu bytes < %zu needed", workspace_bytes, need);
+    return launch_quire_gemm(a, algo, workspace, workspace_bytes, s);
+  }
+  void *ws = nullptr;
+  cudaError_t e = cudaMallocAsync(&ws, need, s);
+  if (e != cudaSuccess)
+    return set_error(kECuda, "bp_quire_gemm_f32: workspace allocation: %s", cudaGetErrorString(e));
+  int rc = launch_quire_gemm(a, algo, ws, need, s);
+  cudaError_t f = cudaFreeAsync(ws, s);
+  if (rc == kOk && f != cudaSuccess) rc = set_error(kECuda, "bp_quire_gemm_f32: workspace free: %s", cudaGetErrorString(f));
+  return rc;
+}
+
 int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int K, const int32_t *sa,
                         const int32_t *sb, int group, uint32_t *out_bp32, int64_t ldo,
                         uint32_t *const *peer_outs, int n_peer, int64_t peer_col0, int algo, void *workspace,

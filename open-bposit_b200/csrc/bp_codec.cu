@@ -417,22 +417,6 @@ int launch_quire_to_bp32(const uint32_t *limbs, int nlimbs, size_t n, uint32_t *
 namespace bp {
 namespace {
 
-// 2^e as a double, for e in the normal range [-1022, 1023] (built from its bits).
-__device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
-
-// Exact value of a bp32 code times 2^extra (NaR -> 0.0 like _bp32_to_float,
-// reference/bposit_quantize.py:66-68): one multiply by an exact power of two
-// while that is a normal double, scalbn (which rounds subnormals and
-// overflows as IEEE does) beyond.
-__device__ __forceinline__ double bp32_value_scaled(uint32_t code, int extra) {
-  Dec d = decode_posit<32, 3>(code);
-  if (d.kind != 0) return 0.0;
-  const int e = d.scale - d.fw + extra;
-  const double m = (double)((1u << d.fw) + d.fbits);
-  const double v = (e >= -1022 && e <= 1023) ? m * pow2d(e) : scalbn(m, e);
-  return d.sign ? -v : v;
-}
-
 // value(bp32 code) * 2^(re[m] + ce[n]): rows over blocks, columns over threads.
 __global__ void __launch_bounds__(256) k_bp32_to_f64(const uint32_t *__restrict__ codes, int M, int N,
                                                      const int32_t *__restrict__ re,
@@ -459,10 +443,7 @@ __global__ void __launch_bounds__(256) k_bp32_to_f32(const uint32_t *__restrict_
     const int rex = re ? re[m] : 0;
     const size_t rb = (size_t)m * N;
     for (int n = threadIdx.x; n < N; n += blockDim.x) {
-      const uint32_t c = codes[rb + n];
-      double v = bp32_value_scaled(c, rex + (ce ? ce[n] : 0));
-      if (bias) v += (double)bias[n];
-      out[rb + n] = c == 0x80000000u ? __uint_as_float(0x7FC00000u) : __double2float_rn(v);
+      out[rb + n] = bp32_f32_out(codes[rb + n], rex + (ce ? ce[n] : 0), bias ? bias[n] : 0.0f);
     }
   }
 }

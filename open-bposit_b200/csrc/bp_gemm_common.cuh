@@ -81,6 +81,39 @@ __device__ __forceinline__ uint32_t write_fast_output(unsigned __int128 acc, int
   return code;
 }
 
+// 2^e as a double, for e in the normal range [-1022, 1023] (built from its bits).
+__device__ __forceinline__ double pow2d(int e) { return __longlong_as_double((long long)(e + 1023) << 52); }
+
+// Exact value of a bp32 code times 2^extra (NaR -> 0.0 like _bp32_to_float,
+// reference/bposit_quantize.py:66-68): one multiply by an exact power of two
+// while that is a normal double, scalbn (which rounds subnormals and
+// overflows as IEEE does) beyond.
+__device__ __forceinline__ double bp32_value_scaled(uint32_t code, int extra) {
+  Dec d = decode_posit<32, 3>(code);
+  if (d.kind != 0) return 0.0;
+  const int e = d.scale - d.fw + extra;
+  const double m = (double)((1u << d.fw) + d.fbits);
+  const double v = (e >= -1022 && e <= 1023) ? m * pow2d(e) : scalbn(m, e);
+  return d.sign ? -v : v;
+}
+
+// The fp32 hand-off of one output: value(code) * 2^extra (exact in float64)
+// plus bias, added in float64 and rounded to the nearest-even fp32 -- the same
+// two steps as the oracle's float64 rescale followed by astype(float32).
+// NaR -> NaN.
+__device__ __forceinline__ float bp32_f32_out(uint32_t code, int extra, float bias) {
+  const double v = bp32_value_scaled(code, extra) + (double)bias;
+  return code == 0x80000000u ? __uint_as_float(0x7FC00000u) : __double2float_rn(v);
+}
+
+// Stores output (i, j)'s bposit32 code and, when requested, its fp32 hand-off.
+__device__ __forceinline__ void store_output(const GemmArgs &a, int i, int j, uint32_t code) {
+  if (a.out) a.out[(size_t)i * a.ldo + j] = code;
+  if (a.out_f32)
+    a.out_f32[(size_t)i * a.ldf + j] =
+        bp32_f32_out(code, (a.re ? a.re[i] : 0) + (a.ce ? a.ce[j] : 0), a.bias ? a.bias[j] : 0.0f);
+}
+
 // ---- exact per-element form and the slow (512-bit, per-term truncating) path ----
 struct ElemME {
   int m;   // signed mantissa (0 for zero / NaR)

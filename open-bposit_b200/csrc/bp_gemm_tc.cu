@@ -124,8 +124,12 @@ struct TcParams {
   const int4 *sta, *stb;
   const int *LA, *LB, *slotA, *slotB;
   const ulonglong2 *CA, *CB;   // tail corrections [slot][other dim], 128-bit
-  uint32_t *out;
+  uint32_t *out;               // may be null when out_f32 is set
   int64_t ldo;
+  float *out_f32;              // optional fp32 hand-off (GemmArgs::out_f32), row stride ldf
+  int64_t ldf;
+  const int32_t *re, *ce;
+  const float *bias;
   uint32_t *quire;
   int nlimbs;
   long long *qbuf;             // [tile - tile0][chunk][MM rows][BN cols]: exact main sums Q (int64)
@@ -624,7 +628,10 @@ __device__ __forceinline__ void finish_general(const TcParams &p, const long lon
   if (!finish_code(p, i, j, (unsigned __int128)Q, p.sta[i], p.stb[j], p.LA[i], p.LB[j], p.slotA[i], p.slotB[j],
                    code))
     return;
-  p.out[(size_t)i * p.ldo + j] = code;
+  if (p.out) p.out[(size_t)i * p.ldo + j] = code;
+  if (p.out_f32)
+    p.out_f32[(size_t)i * p.ldf + j] =
+        bp32_f32_out(code, (p.re ? p.re[i] : 0) + (p.ce ? p.ce[j] : 0), p.bias ? p.bias[j] : 0.0f);
   for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
 }
 
@@ -634,6 +641,8 @@ __device__ __forceinline__ void finish_general(const TcParams &p, const long lon
 template <int PL>
 struct FinishCols {
   int Lj[PL], sj[PL], bx[PL], bw[PL];
+  int fe[PL];     // column exponent of the fp32 hand-off (0 without)
+  float fb[PL];   // column bias of the fp32 hand-off (0 without)
   bool jv[PL], bz[PL];
 };
 
@@ -692,10 +701,19 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
       keep |= 1u << q;
     }
   }
-  uint32_t *orow = p.out + (size_t)i * p.ldo + j0 + lane;
+  if (p.out) {
+    uint32_t *orow = p.out + (size_t)i * p.ldo + j0 + lane;
 #pragma unroll
-  for (int q = 0; q < PL; ++q)
-    if ((keep >> q) & 1u) orow[q * 32] = cd[q];
+    for (int q = 0; q < PL; ++q)
+      if ((keep >> q) & 1u) orow[q * 32] = cd[q];
+  }
+  if (p.out_f32) {
+    float *frow = p.out_f32 + (size_t)i * p.ldf + j0 + lane;
+    const int rex = p.re ? p.re[i] : 0;
+#pragma unroll
+    for (int q = 0; q < PL; ++q)
+      if ((keep >> q) & 1u) frow[q * 32] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
+  }
   for (int e = 0; e < p.n_extra; ++e) {
     uint32_t *erow = p.extra_out[e] + (size_t)i * p.ldo + p.extra_col0 + j0 + lane;
 #pragma unroll
@@ -730,7 +748,8 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
       for (int r = part * rpp + warp; r < rend; r += 8)
         for (int j = j0 + lane; j < min(j0 + BN, p.N); j += 32) {
           const size_t i = (size_t)(tm * MM + r);
-          p.out[i * p.ldo + j] = 0x80000000u;
+          if (p.out) p.out[i * p.ldo + j] = 0x80000000u;
+          if (p.out_f32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
           for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][i * p.ldo + p.extra_col0 + j] = 0x80000000u;
         }
       continue;
@@ -746,6 +765,8 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
       c.bx[q] = rb.x;
       c.bw[q] = (rb.y - rb.x) + cl2 + 3;
       c.bz[q] = rb.z != 0;
+      c.fe[q] = (c.jv[q] && p.ce) ? p.ce[j] : 0;
+      c.fb[q] = (c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
     }
     // rows of this item that exist, relative to the tile; a warp's rows are
     // r0 + 8k
@@ -1234,9 +1255,10 @@ __global__ void __launch_bounds__(256) k_tc_fixup(GemmArgs a, const int4 *__rest
     int4 ra = sta[i], rb = stb[j];
     if (!(ra.z && rb.z)) continue;
     if (tc_exact(ra, rb, slotA[i], slotB[j], a.K)) continue;
-    uint32_t *ob = a.out + (size_t)i * a.ldo + j;
-    slow_output<FMT>(a, i, j, ob, a.quire ? a.quire + ((size_t)i * a.N + j) * a.nlimbs : nullptr);
-    for (int e = 0; e < a.n_extra; ++e) a.extra_out[e][(size_t)i * a.ldo + a.extra_col0 + j] = *ob;
+    uint32_t code;
+    slow_output<FMT>(a, i, j, &code, a.quire ? a.quire + ((size_t)i * a.N + j) * a.nlimbs : nullptr);
+    store_output(a, i, j, code);
+    for (int e = 0; e < a.n_extra; ++e) a.extra_out[e][(size_t)i * a.ldo + a.extra_col0 + j] = code;
   }
   if (a.n_extra) __threadfence_system();
 }
@@ -1617,6 +1639,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   p.sta = sta; p.stb = stb; p.LA = LA; p.LB = LB; p.slotA = slotA; p.slotB = slotB;
   p.CA = CA; p.CB = CB;
   p.out = a.out; p.ldo = a.ldo; p.quire = a.quire; p.nlimbs = a.nlimbs; p.qbuf = qbuf;
+  p.out_f32 = a.out_f32; p.ldf = a.ldf; p.re = a.re; p.ce = a.ce; p.bias = a.bias;
   p.n_extra = a.n_extra; p.extra_col0 = a.extra_col0;
   for (int e = 0; e < a.n_extra; ++e) p.extra_out[e] = a.extra_out[e];
   const TcSchedule sc = tc_schedule(S, a.M, a.N, L.nkb, pair);

@@ -59,8 +59,15 @@ struct GemmArgs {
   int M, N, K;
   const int32_t *sa, *sb;  // per-(row, group) exponents or null
   int group, G;
-  uint32_t *out;           // bp32 codes, row stride ldo
+  uint32_t *out;           // bp32 codes, row stride ldo (may be null when out_f32 is set)
   int64_t ldo;
+  // Optional fp32 hand-off written by the GEMM's own output stage:
+  // out_f32[i * ldf + j] = fp32(value(bp32) * 2^(re[i] + ce[j]) + bias[j])
+  // (re, ce, bias optional); single-GPU calls only (no extra outputs).
+  float *out_f32;
+  int64_t ldf;
+  const int32_t *re, *ce;
+  const float *bias;
   // Extra destinations (tensor-core path): every bp32 word is also stored at
   // extra_out[r][i * ldo + extra_col0 + j] -- e.g. the full result matrices of
   // peer GPUs, written over NVLink by the GEMM epilogue.

@@ -3,14 +3,15 @@
 // and the truncating bp8 encode of the row scaled by 2^-e
 // (encode_bposit8 on floats, reference/bposit_ref.py:258-270).
 //
-// One block per row (grid-stride over rows):
-//   rms  = sqrt(sum(x^2) / K)                       float64, block reduction
+// One warp per row (rows of up to kStageK elements staged in the warp's slice
+// of shared memory, longer ones re-read through L2), no block-wide barrier:
+//   rms  = sqrt(sum(x^2) / K)                       float64, warp reduction
 //   p95  = numpy's 'linear' percentile of |x| at 95: the order statistics at
 //          ranks lo = floor(0.95 (K - 1)) and lo + 1 by a 4-pass radix select
-//          on the fp32 bit patterns of |x| (their order is the values'),
-//          then lerp exactly as numpy does (b - (b - a)(1 - t) when t >= 0.5);
-//          skipped when a count of |x| > 2 rms shows a[lo + 1] <= 2 rms
-//          (then ref = rms whatever p95 is)
+//          on the fp32 bit patterns of |x| (their order is the values'), with
+//          a 256-bin histogram per warp, then lerp exactly as numpy does
+//          (b - (b - a)(1 - t) when t >= 0.5); skipped when a count of
+//          |x| > 2 rms shows a[lo + 1] <= 2 rms (then ref = rms whatever p95 is)
 //   ref  = p95 if p95 > 0 and p95 > 2 rms, else rms;  e = rint(log2(ref)),
 //          0 for an all-zero row
 //   code = truncating bp8 of x * 2^-e (exact in float64), 0 when
@@ -29,32 +30,29 @@
 namespace bp {
 namespace {
 
-constexpr int kT = 256;
+constexpr int kT = 256, kWarps = kT / 32;
+constexpr int kStageK = 1024;   // rows up to this length are staged in shared memory
 
-__device__ __forceinline__ double block_sum_d(double v, double *red) {
+__device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  double r = 0.0;
-  for (int w = 0; w < kT / 32; ++w) r += red[w];
-  return r;
+  return v;
 }
 
-__device__ __forceinline__ uint32_t block_min_u(uint32_t v, uint32_t *red) {
+__device__ __forceinline__ uint32_t warp_sum_u(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ uint32_t warp_min_u(uint32_t v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  uint32_t r = red[0];
-  for (int w = 1; w < kT / 32; ++w) r = min(r, red[w]);
-  return r;
+  return v;
 }
 
-// Histogram add with warp aggregation: lanes that hit the same bin add once
-// (the exponent byte of |x| is shared by most of a row).
+// Histogram add with lane aggregation: lanes that hit the same bin add once
+// (the exponent byte of |x| is shared by most of a row).  Whole warp.
 __device__ __forceinline__ void hist_add(uint32_t *hist, uint32_t bin, bool active) {
   const uint32_t act = __ballot_sync(0xFFFFFFFFu, active);
   if (!active) return;
@@ -62,104 +60,100 @@ __device__ __forceinline__ void hist_add(uint32_t *hist, uint32_t bin, bool acti
   if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
 }
 
-// Rows of up to SMEM_K elements are staged in shared memory once; longer rows
-// are re-read from global memory (L2) by every pass.
-constexpr int SMEM_K = 10240;
-
+template <bool STAGED>
 __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, int rows, int K,
                                                   int32_t *__restrict__ exps, uint8_t *__restrict__ codes) {
   __shared__ uint2 tbl[256];          // truncating bp8 quantize table (bp8_qentry)
-  __shared__ uint32_t hist[256];
-  __shared__ double redd[kT / 32];
-  __shared__ uint32_t redu[kT / 32];
-  __shared__ uint32_t s_prefix, s_rank, s_eq;
-  extern __shared__ float s_row[];
+  __shared__ uint32_t hists[kWarps][256];
+  extern __shared__ float s_rows[];   // [kWarps][K] when STAGED
   {
     QEntry q = bp8_qentry(threadIdx.x, false);
     tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
   }
   __syncthreads();
-  const bool staged = K <= SMEM_K;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t *hist = hists[warp];
+  float *srow = STAGED ? s_rows + (size_t)warp * K : nullptr;
   const double pos = 0.95 * (double)(K - 1);
   const int lo = (int)floor(pos);
   const double t = pos - (double)lo;
-  const int kpad = (K + kT - 1) / kT * kT;   // every lane runs every loop trip (warp collectives)
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  const int kpad = (K + 31) / 32 * 32;   // every lane runs every trip of the histogram loop
+  for (int r = blockIdx.x * kWarps + warp; r < rows; r += gridDim.x * kWarps) {
     const float *xg = x + (size_t)r * K;
     double ss = 0.0;
-    for (int k = threadIdx.x; k < K; k += kT) {
+    for (int k = lane; k < K; k += 32) {
       const float f = xg[k];
-      if (staged) s_row[k] = f;
+      if (STAGED) srow[k] = f;
       ss += (double)f * (double)f;
     }
-    const double rms = sqrt(block_sum_d(ss, redd) / (double)K);   // (its syncs also publish s_row)
-    const float *xr = staged ? s_row : xg;
+    const double rms = sqrt(warp_sum_d(ss) / (double)K);
+    __syncwarp();
+    const float *xr = STAGED ? srow : xg;
     // The percentile only matters when it exceeds 2 rms.  With c = #{|x| > 2 rms}:
     // c <= K - lo - 2 means a[lo + 1] <= 2 rms, so p95 (between a[lo] and
     // a[lo + 1]) does not exceed it and ref = rms without the selection.
     uint32_t cnt = 0u;
     const double two_rms = 2.0 * rms;
-    for (int k = threadIdx.x; k < K; k += kT) cnt += fabs((double)xr[k]) > two_rms ? 1u : 0u;
-    cnt = (uint32_t)block_sum_d((double)cnt, redd);
+    for (int k = lane; k < K; k += 32) cnt += fabs((double)xr[k]) > two_rms ? 1u : 0u;
+    cnt = warp_sum_u(cnt);
     const bool need_p95 = rms > 0.0 && (long long)cnt > (long long)K - lo - 2;
     // radix select of rank lo among the keys |x| (fp32 bits, sign cleared)
-    uint32_t prefix = 0u, mask = 0u, rank = (uint32_t)lo;
+    uint32_t prefix = 0u, mask = 0u, rank = (uint32_t)lo, eq = 0u;
     for (int shift = 24; shift >= 0 && need_p95; shift -= 8) {
-      hist[threadIdx.x] = 0u;
-      __syncthreads();
-      for (int k = threadIdx.x; k < kpad; k += kT) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
+      __syncwarp();
+      for (int k = lane; k < kpad; k += 32) {
         const uint32_t key = k < K ? (__float_as_uint(xr[k]) & 0x7FFFFFFFu) : 0u;
         hist_add(hist, (key >> shift) & 255u, k < K && (key & mask) == prefix);
       }
-      __syncthreads();
-      if (threadIdx.x < 32) {
-        // lane l owns bins 8l .. 8l+7: inclusive prefix over lanes, then the
-        // first bin whose running count passes `rank`
-        uint32_t c[8], tot = 0u;
+      __syncwarp();
+      // lane l owns bins 8l .. 8l+7: inclusive prefix over lanes, then the
+      // first bin whose running count passes `rank`
+      uint32_t c[8], tot = 0u;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          c[q] = hist[8 * threadIdx.x + q];
-          tot += c[q];
-        }
-        uint32_t incl = tot;
+      for (int q = 0; q < 8; ++q) {
+        c[q] = hist[8 * lane + q];
+        tot += c[q];
+      }
+      uint32_t incl = tot;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-          if ((int)threadIdx.x >= o) incl += y;
-        }
-        const uint32_t excl = incl - tot;
-        const bool mine = excl <= rank && rank < incl;
-        if (mine) {
-          uint32_t below = excl, b = 8u * threadIdx.x;
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const uint32_t excl = incl - tot;
+      const bool mine = excl <= rank && rank < incl;
+      uint32_t below = excl, b = 8u * lane, cb = c[0];
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (below + c[q] <= rank && q < 7) {
-              below += c[q];
-              ++b;
-            } else {
-              break;
-            }
-          s_prefix = prefix | (b << shift);
-          s_rank = rank - below;
-          s_eq = hist[b];
+      for (int q = 0; q < 8; ++q) {
+        cb = c[q];
+        if (below + c[q] <= rank && q < 7) {
+          below += c[q];
+          ++b;
+        } else {
+          break;
         }
       }
-      __syncthreads();
-      prefix = s_prefix;
-      rank = s_rank;
+      const int owner = __ffs(__ballot_sync(0xFFFFFFFFu, mine)) - 1;
+      b = __shfl_sync(0xFFFFFFFFu, b, owner);
+      below = __shfl_sync(0xFFFFFFFFu, below, owner);
+      eq = __shfl_sync(0xFFFFFFFFu, cb, owner);
+      prefix |= b << shift;
+      rank -= below;
       mask |= 255u << shift;
+      __syncwarp();
     }
     const double a_lo = (double)__uint_as_float(prefix);
     // rank lo + 1: the same key while it repeats, else the next larger key
     double a_hi = a_lo;
-    if (need_p95 && lo + 1 < K && rank + 1 >= s_eq) {
+    if (need_p95 && lo + 1 < K && rank + 1 >= eq) {
       uint32_t nxt = 0xFFFFFFFFu;
-      for (int k = threadIdx.x; k < K; k += kT) {
+      for (int k = lane; k < K; k += 32) {
         const uint32_t key = __float_as_uint(xr[k]) & 0x7FFFFFFFu;
         if (key > prefix) nxt = min(nxt, key);
       }
-      nxt = block_min_u(nxt, redu);
-      a_hi = (double)__uint_as_float(nxt);
+      a_hi = (double)__uint_as_float(warp_min_u(nxt));
     }
     const double d = a_hi - a_lo;
     const double p95 = t >= 0.5 ? a_hi - d * (1.0 - t) : a_lo + d * t;
@@ -168,11 +162,11 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
       const double ref = (need_p95 && p95 > 0.0 && p95 > 2.0 * rms) ? p95 : rms;
       e = (int)rint(log2(ref));
     }
-    if (threadIdx.x == 0) exps[r] = e;
+    if (lane == 0) exps[r] = e;
     // truncating encode of x * 2^-e (float64 bit logic of the bp8 f64 quantizer)
     const double sc = scalbn(1.0, -e);
     uint8_t *cr = codes + (size_t)r * K;
-    for (int k = threadIdx.x; k < K; k += kT) {
+    for (int k = lane; k < K; k += 32) {
       const double v = (double)xr[k] * sc;
       const unsigned long long u = (unsigned long long)__double_as_longlong(v);
       const unsigned long long a = u & 0x7FFFFFFFFFFFFFFFull;
@@ -195,7 +189,7 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
       }
       cr[k] = (uint8_t)code;
     }
-    __syncthreads();
+    __syncwarp();   // the next row reuses this warp's staging and histogram
   }
 }
 
@@ -203,8 +197,16 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
 
 int launch_w8a8_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, cudaStream_t s) {
   if (rows == 0 || K == 0) return kOk;
-  const size_t smem = K <= SMEM_K ? (size_t)K * sizeof(float) : 0;
-  k_w8a8_rows<<<std::min(rows, sm_count() * 4), kT, smem, s>>>(x, rows, K, exps, codes);
+  const int blocks = (rows + kWarps - 1) / kWarps;
+  if (K <= kStageK) {
+    // 32 KB of staging at most: several blocks per SM stay resident
+    const size_t smem = (size_t)kWarps * K * sizeof(float);
+    k_w8a8_rows<true><<<std::min(blocks, sm_count() * 6), kT, smem, s>>>(x, rows, K, exps, codes);
+  } else {
+    // long rows through L2: 4 blocks (32 rows) per SM in flight keep the
+    // re-read rows of a 4864-wide activation (~90 MB) inside L2
+    k_w8a8_rows<false><<<std::min(blocks, sm_count() * 4), kT, 0, s>>>(x, rows, K, exps, codes);
+  }
   return check_launch("w8a8_rows");
 }
 
