@@ -149,29 +149,28 @@ class BpositLinear(torch.nn.Module):
         bias = None if self.bias is None else self.bias.float().contiguous()
         if self.scales == "group128":
             xc, xs = ops.quantize_bp8_grouped(x2, group=self.group)
-            codes = self._gemm(xc, wc, 8, xs, ws, M)
-            y = ops.bp32_to_f32(codes, bias=bias)
+            y = self._linear(xc, wc, 8, xs, ws, None, None, bias, M)
         elif self.act == "bp16":
             xc = ops.encode_bp16(x2, rtne=True)
-            codes = self._gemm(xc, self._wq16, 16, None, None, M)
-            y = ops.bp32_to_f32(codes, col_exp=ws, bias=bias)
+            y = self._linear(xc, self._wq16, 16, None, None, None, ws, bias, M)
         else:
             xc, ex = ops.w8a8_encode_rows(x2)
-            codes = self._gemm(xc, wc, 8, None, None, M)
-            y = ops.bp32_to_f32(codes, row_exp=ex, col_exp=ws, bias=bias)
+            y = self._linear(xc, wc, 8, None, None, ex, ws, bias, M)
         return y.reshape(*lead, self.out_features)
 
-    def _gemm(self, xc, wc, fmt, sa, sb, M):
-        """bposit32 codes [M, N] of xc @ wc^T: on this GPU, or -- sharded --
-        this rank's output block, all-gathered into the full matrix."""
+    def _linear(self, xc, wc, fmt, sa, sb, row_exp, col_exp, bias, M):
+        """fp32 [M, N] of xc @ wc^T: on this GPU one GEMM whose output stage
+        writes the fp32 hand-off (value * 2^(row_exp + col_exp) + bias); sharded,
+        this rank's block of bposit32 codes all-gathered into the full matrix,
+        then the same hand-off."""
         if self.sharded and _world() > 1:
             g = _shared_gemm(M, self.out_features, self.in_features, fmt, xc.device)
             m0, m1, n0, n1 = g.block
-            return g(xc[m0:m1], wc[n0:n1], sa=None if sa is None else sa[m0:m1],
-                     sb=None if sb is None else sb[n0:n1])
-        codes, _ = ops.quire_gemm(xc, wc, fmt, sa=sa, sb=sb, group=self.group,
-                                  workspace=self._workspace(M, xc.device))
-        return codes
+            codes = g(xc[m0:m1], wc[n0:n1], sa=None if sa is None else sa[m0:m1],
+                      sb=None if sb is None else sb[n0:n1])
+            return ops.bp32_to_f32(codes, row_exp=row_exp, col_exp=col_exp, bias=bias)
+        return ops.quire_gemm_f32(xc, wc, fmt, sa=sa, sb=sb, group=self.group, row_exp=row_exp, col_exp=col_exp,
+                                  bias=bias, workspace=self._workspace(M, xc.device))
 
     def extra_repr(self) -> str:
         arith = "bp8 W8A8" if self.act == "bp8" else "bp8 weights, bp16 activations"

@@ -55,6 +55,41 @@ def test_device_error_word_clear_and_nar_handoff():
     assert f64[0, 0] == 0.0 and f64[0, 1] == 1.0
 
 
+@pytest.mark.parametrize("algo,M,N,K,fmt,opts", [
+    (1, 37, 50, 300, 8, "exps+bias"), (0, 512, 1152, 896, 8, "exps+bias"), (2, 256, 300, 2000, 8, "none"),
+    (0, 300, 1024, 1000, 16, "col+bias"), (0, 64, 96, 640, 8, "groups"), (2, 1024, 768, 4096, 8, "groups")])
+def test_quire_gemm_f32_equals_gemm_then_handoff(algo, M, N, K, fmt, opts):
+    """bp_quire_gemm_f32 (the fp32 hand-off written by the GEMM's output stage)
+    gives the same fp32 words as bp_quire_gemm followed by bp_bp32_to_f32, on
+    the CUDA-core and tensor-core paths, and the same bposit32 codes when asked."""
+    from bposit_b200 import ops
+    rng = np.random.default_rng(M + N + K)
+    dt = np.uint8 if fmt == 8 else np.uint16
+    A = torch.from_numpy(rng.integers(0, 1 << fmt, (M, K)).astype(dt)).cuda()
+    B = torch.from_numpy(rng.integers(0, 1 << fmt, (N, K)).astype(dt)).cuda()
+    sa = sb = re = ce = bias = None
+    if opts == "groups":
+        G = (K + 127) // 128
+        sa = torch.from_numpy(rng.integers(-10, 5, (M, G)).astype(np.int32)).cuda()
+        sb = torch.from_numpy(rng.integers(-10, 5, (N, G)).astype(np.int32)).cuda()
+    if opts in ("exps+bias",):
+        re = torch.from_numpy(rng.integers(-6, 6, M).astype(np.int32)).cuda()
+    if opts in ("exps+bias", "col+bias"):
+        ce = torch.from_numpy(rng.integers(-6, 6, N).astype(np.int32)).cuda()
+        bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).cuda()
+    codes, _ = ops.quire_gemm(A, B, fmt, sa=sa, sb=sb, algo=algo)
+    ref = ops.bp32_to_f32(codes, row_exp=re, col_exp=ce, bias=bias)
+    out_bp32 = torch.empty((M, N), dtype=torch.uint32, device="cuda")
+    got = ops.quire_gemm_f32(A, B, fmt, sa=sa, sb=sb, row_exp=re, col_exp=ce, bias=bias, out_bp32=out_bp32,
+                             algo=algo)
+    got2 = ops.quire_gemm_f32(A, B, fmt, sa=sa, sb=sb, row_exp=re, col_exp=ce, bias=bias, algo=algo)
+    torch.cuda.synchronize()
+    assert torch.equal(got.view(torch.int32), ref.view(torch.int32))
+    assert torch.equal(got2.view(torch.int32), ref.view(torch.int32))
+    assert torch.equal(out_bp32.view(torch.int32), codes.view(torch.int32))
+    assert ops.device_error() == 0
+
+
 def test_quire256_clamps_huge_python_ints(api):
     """quires far beyond 512 bits round to +-maxpos exactly as the reference's
     unbounded Python ints do (bposit32 saturates above total exponent 240,
