@@ -835,6 +835,145 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
   if (p.n_extra) __threadfence_system();
 }
 
+// Staged form of the finish for whole-tile launches that have the SMs to
+// themselves (the caller's stream, one K chunk, int64 sums, no raw quires):
+// thread 0 streams a block's items in chunks of 8 tile rows -- one row per
+// warp, QW planes of 8 x BN int64 sums, contiguous in the tile-compact buffer
+// -- with bulk copies into a ring of kFinStages shared-memory buffers, each
+// with its own mbarrier, so several chunks per block are in flight while the
+// warps round the previous ones from shared memory (the per-thread loads of
+// k_tc_finish left the kernel stalled on their latency at a third of HBM
+// bandwidth).  A chunk's buffer is refilled after a block barrier that ends
+// its use.  Waits are bounded: a timeout records code 16 in g_tc_error, and
+// the block stops after the barrier at which it learns of it.
+constexpr int kFinStages = 4;
+
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int MM, int BN, int QW>
+size_t finish_staged_smem() {
+  return (size_t)kFinStages * QW * 8 * BN * sizeof(long long) + kFinStages * sizeof(uint64_t);
+}
+
+template <int MM, int BN, int QW>
+__global__ void __launch_bounds__(256, 4) k_tc_finish_staged(TcParams p, int ntiles, int parts) {
+  static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
+  constexpr int PL = BN / 32;
+  constexpr size_t PT = (size_t)MM * BN;              // words of one plane of a tile
+  constexpr uint32_t CHUNK = 8u * BN * 8u;            // bytes of one plane of a chunk (16-byte multiple)
+  extern __shared__ __align__(16) uint8_t fsm[];
+  long long *buf = (long long *)fsm;                  // [kFinStages][QW][8][BN]
+  uint64_t *bar = (uint64_t *)(fsm + (size_t)kFinStages * QW * CHUNK);
+  __shared__ int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cl2 = ceil_log2_int(p.K);
+  const int4 z4 = make_int4(0, 0, 0, 0);
+  const int rpp = MM / parts, cpi = rpp / 8;          // rows and chunks per item
+  const long long nitems = (long long)ntiles * parts;
+  const long long mine = (long long)blockIdx.x < nitems ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const long long total = mine * cpi;
+  if (*(volatile int *)&g_tc_error != 0) {
+    // a tensor-core GEMM on this device gave up on a bounded wait: NaR everywhere
+    for (long long it = blockIdx.x; it < nitems; it += gridDim.x) {
+      const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
+      int tm, tn;
+      tile_coords(p.tile0 + tl, (p.M + MM - 1) / MM, p.ntn, tm, tn);
+      const int rend = min((part + 1) * rpp, p.M - tm * MM);
+      for (int r = part * rpp + warp; r < rend; r += 8)
+        for (int j = tn * BN + lane; j < min(tn * BN + BN, p.N); j += 32) {
+          const size_t i = (size_t)(tm * MM + r);
+          if (p.out) p.out[i * p.ldo + j] = 0x80000000u;
+          if (p.out_f32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
+          for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][i * p.ldo + p.extra_col0 + j] = 0x80000000u;
+        }
+    }
+    return;
+  }
+  auto issue = [&](long long g) {   // thread 0: bulk copies of chunk g into buffer g % kFinStages
+    const long long it = blockIdx.x + (g / cpi) * gridDim.x;
+    const int c = (int)(g % cpi);
+    const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
+    const long long *src = p.qbuf + (size_t)tl * QW * PT + (size_t)(part * rpp + 8 * c) * BN;
+    const int st = (int)(g % kFinStages);
+    mbar_expect_tx(&bar[st], QW * CHUNK);
+#pragma unroll
+    for (int w = 0; w < QW; ++w) bulk_g2s(buf + ((size_t)st * QW + w) * 8 * BN, src + w * PT, CHUNK, &bar[st]);
+  };
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kFinStages; ++st) mbar_init(&bar[st], 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (long long g = 0; g < total && g < kFinStages; ++g) issue(g);
+  }
+  __syncthreads();
+  FinishCols<PL> c;
+  long long cur = -1;
+  int tm = 0, tn = 0, j0 = 0, part = 0, rend = 0;
+  for (long long g = 0; g < total; ++g) {
+    const long long item = g / cpi;
+    const int ci = (int)(g % cpi);
+    if (item != cur) {   // columns of the new item, loaded once
+      cur = item;
+      const long long it = blockIdx.x + item * gridDim.x;
+      const int tl = (int)(it / parts);
+      part = (int)(it - (long long)tl * parts);
+      tile_coords(p.tile0 + tl, (p.M + MM - 1) / MM, p.ntn, tm, tn);
+      j0 = tn * BN;
+      rend = min((part + 1) * rpp, p.M - tm * MM);
+#pragma unroll
+      for (int q = 0; q < PL; ++q) {
+        const int j = j0 + q * 32 + lane;
+        c.jv[q] = j < p.N;
+        const int4 rb = c.jv[q] ? p.stb[j] : z4;
+        c.Lj[q] = c.jv[q] ? p.LB[j] : 0;
+        c.sj[q] = c.jv[q] ? p.slotB[j] : -1;
+        c.bx[q] = rb.x;
+        c.bw[q] = (rb.y - rb.x) + cl2 + 3;
+        c.bz[q] = rb.z != 0;
+        c.fe[q] = (c.jv[q] && p.ce) ? p.ce[j] : 0;
+        c.fb[q] = (c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
+      }
+    }
+    const int st = (int)(g % kFinStages);
+    const uint32_t par = (uint32_t)(g / kFinStages) & 1u;
+    bool ok = true;
+    {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&bar[st], par)) {
+        if (clock64() - t0 > WAIT_LIMIT) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) {
+      atomicOr(&g_tc_error, 16);
+      s_abort = 1;
+    }
+    const int r = part * rpp + 8 * ci + warp;
+    if (ok && r < rend) {
+      const long long *row = buf + (size_t)st * QW * 8 * BN + (size_t)warp * BN + lane;
+      long long qv[PL], qh[PL];
+#pragma unroll
+      for (int q = 0; q < PL; ++q) {
+        qv[q] = c.jv[q] ? row[q * 32] : 0ll;
+        qh[q] = (QW == 2 && c.jv[q]) ? row[8 * BN + q * 32] : 0ll;
+      }
+      const int i = tm * MM + r;
+      finish_row<PL, QW>(p, c, i, j0, lane, qv, qh, p.sta[i], p.LA[i], p.slotA[i]);
+    }
+    __syncthreads();   // every warp is done with buffer st
+    if (s_abort) break;
+    if (threadIdx.x == 0 && g + kFinStages < total) issue(g + kFinStages);
+  }
+  if (p.n_extra) __threadfence_system();
+}
+
 // ----------------------------------------------------------- digit planes ---
 template <int FMT>
 __device__ __forceinline__ ElemME decode_scaled(uint32_t c, const int32_t *s, int row, int k, int G, int group) {
@@ -1555,7 +1694,13 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
     }
     int g = 1, parts = 1;
     finish_shape<C::MM>(seg[k].n, on_s ? grid_finish : std::min(grid_finish, 2 * sm_count()), g, parts);
-    k_tc_finish<C::MM, C::BN, C::QW><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
+    if (on_s && p.split == 1 && !p.quire) {
+      // the SMs are free: stream the sums through shared memory
+      k_tc_finish_staged<C::MM, C::BN, C::QW>
+          <<<g, 256, finish_staged_smem<C::MM, C::BN, C::QW>(), fs>>>(p, seg[k].n, parts);
+    } else {
+      k_tc_finish<C::MM, C::BN, C::QW><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
+    }
     rc = check_launch("tc_finish");
   }
   if (forked) {
