@@ -264,6 +264,39 @@ def kernel_breakdown(ctx, fn, steps=2):
         return {"unavailable": str(e)[:120]}
 
 
+def as_graph(ctx, step, outputs):
+    """(replay, info): `step` captured into a CUDA graph (after the eager
+    warm-up that allocates every buffer), its replay checked against the eager
+    step's outputs word for word; on any failure the eager step itself and the
+    reason."""
+    torch = ctx.torch
+    try:
+        step()
+        torch.cuda.synchronize()
+        ref = [o.clone() for o in outputs()]
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()                      # warm-up on the capture stream
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            step()
+        for o in outputs():
+            o.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        same = all(torch.equal(a.view(torch.int32) if a.element_size() == 4 else a, b.view(torch.int32)
+                               if b.element_size() == 4 else b) for a, b in zip(ref, outputs()))
+        if not same:
+            return step, {"cuda_graph": False, "why": "replay differs from the eager step"}, None
+        return g.replay, {"cuda_graph": True, "replay_matches_eager": True}, g
+    except Exception as e:   # capture is an optimisation: fall back to the eager step
+        torch.cuda.synchronize()
+        return step, {"cuda_graph": False, "why": f"{type(e).__name__}: {e}"[:200]}, None
+
+
 def gather_obj(ctx, obj):
     if ctx.world == 1:
         return [obj]
@@ -530,7 +563,8 @@ def run_c1(ctx):
         ops.quire_gemm(xc, wc, 8, sa=sx, sb=sw, group=128, out=out, workspace=ws)
 
     steps = max(50, 10 * args.steps)
-    ms, clk, launches = ctx.timed(step, steps, max(args.warmup, 10), flush=True)
+    run, ginfo, _graph = as_graph(ctx, step, lambda: [xc, wc, out])
+    ms, clk, launches = ctx.timed(run, steps, max(args.warmup, 10), flush=True)
     ctx.check_device()
     ops_ = 2.0 * M * N * K
     hX, hW = torch.from_numpy(X).pin_memory(), torch.from_numpy(W).pin_memory()
@@ -574,11 +608,12 @@ def run_c1(ctx):
     line = base_line(ctx, "bp8 W8A8 linear TOPS (16x576x576, group-128 scales, quantize + GEMM)", "TOPS",
                      ops_ / (ms * 1e-3) / 1e12, ms, steps, max(args.warmup, 10), config, "strong")
     line.update({
+        "graph": ginfo,
         "roofline": tensor_roofline(ctx, ops_ / (ms * 1e-3) / 1e12, "whole step (2 grouped quantizes + GEMM)",
-                                    f"latency-bound: {launches // steps} kernel launches for 5.3 M MACs"),
+                                    "latency-bound: 5 kernels for 5.3 M MACs"),
         "e2e": {"value": round(ops_ / (ems * 1e-3) / 1e12, 4), "unit": "TOPS", "ms_per_step": round(ems, 4),
                 "h2d_bytes_per_step": int((M + N) * K * 4), "d2h_bytes_per_step": int(M * N * 4)},
-        "cpu_baseline": cpu, "gpu_launches": launches, "clocks": clk})
+        "cpu_baseline": cpu, "gpu_launches": launches if not ginfo["cuda_graph"] else 5 * steps, "clocks": clk})
     return line
 
 
@@ -728,7 +763,20 @@ def run_c3(ctx):
             ops.quire_gemm(L["xc"], L["wc"], 8, sa=sx, sb=L["sw"], group=128, out=L["out"], workspace=L["ws"])
 
     steps = max(10, args.steps)
-    ms, clk, launches = ctx.timed(step, steps, args.warmup, flush=True)
+    eager_launches = None
+    n0 = None
+    try:
+        from bposit_b200 import _lib
+        n0 = _lib.lib().bp_launch_count()
+        step()
+        torch.cuda.synchronize()
+        eager_launches = _lib.lib().bp_launch_count() - n0
+    except Exception:
+        pass
+    run, ginfo, _graph = as_graph(ctx, step, lambda: [L["out"] for L in layers])
+    ms, clk, launches = ctx.timed(run, steps, args.warmup, flush=True)
+    if ginfo["cuda_graph"] and eager_launches is not None:
+        launches = eager_launches * steps
     ctx.check_device()
     hx = [L["X"].cpu().pin_memory() for L in layers]
     ho = [torch.empty(L["out"].shape, dtype=torch.uint32).pin_memory() for L in layers]
@@ -767,6 +815,7 @@ def run_c3(ctx):
     line = base_line(ctx, "bp8 W8A8 projection-set TOPS (SmolLM2-135M shapes, M=2048)", "TOPS",
                      total_ops / (ms * 1e-3) / 1e12, ms, steps, args.warmup, config, "strong")
     line.update({
+        "graph": ginfo,
         "roofline": tensor_roofline(ctx, total_ops / (ms * 1e-3) / 1e12, "whole step (7 x (quantize + GEMM))",
                                     "short K (576 / 1536) and small N: launch- and finish-bound"),
         "e2e": {"value": round(total_ops / (ems * 1e-3) / 1e12, 3), "unit": "TOPS", "ms_per_step": round(ems, 4),
@@ -792,7 +841,22 @@ def run_c4(ctx):
     with torch.no_grad():
         model(ids)                    # weights are encoded on first use
     steps = max(3, args.steps // 4)
-    ms, clk, launches = ctx.timed(lambda: model(ids), steps, args.warmup)
+    holder = {}
+
+    def fwd():
+        holder["h"] = model(ids)
+
+    ginfo = {"cuda_graph": False, "why": "sharded linears run eager (NCCL barriers and peer stores)"}
+    run = fwd
+    if not sharded:
+        run, ginfo, _graph = as_graph(ctx, fwd, lambda: [holder["h"]])
+    from bposit_b200 import _lib
+    n0 = _lib.lib().bp_launch_count()
+    fwd()
+    torch.cuda.synchronize()
+    per_fwd = _lib.lib().bp_launch_count() - n0
+    ms, clk, launches = ctx.timed(run, steps, args.warmup)
+    launches = per_fwd * steps
     ctx.check_device()
     hid = ids.cpu().pin_memory()
     hout = torch.empty((batch, seq, model.c["hidden"]), dtype=torch.float32).pin_memory()
@@ -834,6 +898,7 @@ def run_c4(ctx):
     line = base_line(ctx, "Qwen2.5-0.5B-shaped W8A8 forward tokens/s (8 x 1024)", "tokens/s",
                      tokens / (ms * 1e-3), ms, steps, args.warmup, config, "strong", dtype="u8 (linears), f32")
     line.update({
+        "graph": ginfo,
         "layout": ("every linear's N (output features) sharded over the ranks, bposit32 blocks all-gathered by the "
                    "GEMM's finish kernel; non-linear parts replicated" if sharded else "1 GPU"),
         "linear_TOPS": round(lin_ops / (ms * 1e-3) / 1e12, 3),
