@@ -107,9 +107,6 @@ __global__ void __launch_bounds__(TM *TN *KS) k_quire_gemm_simt(GemmArgs a, cons
 
 }  // namespace
 
-int launch_row_stats(int fmt, const void *codes, int rows, int K, const int32_t *s, int group,
-                     int4 *stats, cudaStream_t st);
-
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s) {
   dim3 grid((a.N + TN - 1) / TN, (a.M + TM - 1) / TM);
   if (grid.y > 65535u) return set_error(kERange, "quire_gemm: M too large for the CUDA-core path");

@@ -85,5 +85,8 @@ bool gemm_uses_tc(const GemmArgs &a, int algo);
 // 3 prepare B only; 4 reuse B's preparation.
 int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cudaStream_t s,
                       int a_mode = 0);
+// Row statistics {min lsb exponent, max binade, nonzero} of both operands in one launch.
+int launch_row_stats2(int fmt, const void *codes, int rows, const int32_t *s, int4 *stats, const void *codes2,
+                      int rows2, const int32_t *s2, int4 *stats2, int K, int group, cudaStream_t st);
 
 }  // namespace bp

@@ -31,8 +31,6 @@
 #include "bp_internal.cuh"
 
 namespace bp {
-int launch_row_stats(int fmt, const void *codes, int rows, int K, const int32_t *s, int group,
-                     int4 *stats, cudaStream_t st);
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
 }  // namespace bp
 
@@ -119,9 +117,7 @@ extern "C" int bp_quire_gemm_noalloc(int fmt, const void *A, const void *B, int 
   cudaStream_t s = (cudaStream_t)stream;
   int4 *sta = (int4 *)scratch;
   int4 *stb = sta + M;
-  rc = launch_row_stats(fmt, A, M, K, sa, a.group, sta, s);
-  if (rc != kOk) return rc;
-  rc = launch_row_stats(fmt, B, N, K, sb, a.group, stb, s);
+  rc = launch_row_stats2(fmt, A, M, sa, sta, B, N, sb, stb, K, a.group, s);
   if (rc != kOk) return rc;
   return launch_gemm_simt(a, sta, stb, s);
 }
