@@ -579,7 +579,7 @@ def run_c1(ctx):
 
     ems, _, _ = ctx.timed(e2e, steps, 10, flush=True)
     cpu = None
-    if ctx.rank == 0 and not args.no_cpu:
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         from oracle import oracle as orc
 
         def oracle_step(threads):
@@ -687,7 +687,7 @@ def run_c2(ctx):
     ems, _, _ = ctx.timed(e2e, 3, 1)
     del hx, hc, dx
     cpu = None
-    if ctx.rank == 0 and not args.no_cpu:
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         cpu = codec_cpu_baseline(x[: 1 << 22].cpu().numpy())
     del x, c8, c16, y
     torch.cuda.empty_cache()
@@ -791,7 +791,7 @@ def run_c3(ctx):
 
     ems, _, _ = ctx.timed(e2e, steps, args.warmup, flush=True)
     cpu = None
-    if ctx.rank == 0 and not args.no_cpu:
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         from oracle import oracle as orc
         th = host_threads()
         res = {}
@@ -868,7 +868,7 @@ def run_c4(ctx):
 
     ems, _, _ = ctx.timed(e2e, steps, 1)
     cpu = None
-    if ctx.rank == 0 and not args.no_cpu:
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         import numpy as np
         from oracle import oracle as orc
         rng = np.random.default_rng(4)
