@@ -1043,13 +1043,23 @@ __device__ __forceinline__ ElemME prep_decode(uint32_t c, const uint32_t *s_dec)
 // correction slot.  Pass 2 re-reads the row, which is still in L2.  bp8 codes
 // are decoded through a 256-entry table; for unscaled bp8 rows pass 2 also
 // uses a per-row table of each code's packed digits (bit 31 marks a tail).
+// One operand of a prep launch.
+struct PrepOp {
+  const void *codes;
+  int rows;
+  const int32_t *sc;
+  int4 *stats;
+  int8_t *planes;
+  int *Lr, *slot;
+  int4 *seg;
+  int *tails;
+  int cap;
+  TcCounters *ctr;
+};
+
 template <int FMT, int S>
-__global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes, int rows, int K, int Kp,
-                                                 const int32_t *__restrict__ sc, int G, int group,
-                                                 int4 *__restrict__ stats, int8_t *__restrict__ planes,
-                                                 int *__restrict__ Lr, int *__restrict__ slot,
-                                                 int4 *__restrict__ seg, int *__restrict__ tails, int pool_cap,
-                                                 int cap, TcCounters *__restrict__ ctr) {
+__global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp opB, int K, int Kp, int G,
+                                                 int group, int pool_cap) {
   constexpr int SPAN = Cfg<S>::SPAN;
   constexpr int EPT = FMT == 8 ? 16 : 8;   // elements per 16-byte load
   constexpr bool LUT_DIGITS = FMT == 8 && S <= 4;
@@ -1067,9 +1077,23 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
     }
     __syncthreads();
   }
-  const size_t plane = (size_t)rows * Kp;
-  const bool vec = (K % EPT) == 0 && (((uintptr_t)codes) & 15u) == 0;
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  // rows of A, then rows of B: both operands in one launch (block-uniform choice)
+  for (int rr = blockIdx.x; rr < opA.rows + opB.rows; rr += gridDim.x) {
+    const bool second = rr >= opA.rows;
+    const int r = second ? rr - opA.rows : rr;
+    const void *__restrict__ codes = second ? opB.codes : opA.codes;
+    const int rows = second ? opB.rows : opA.rows;
+    const int32_t *__restrict__ sc = second ? opB.sc : opA.sc;
+    int4 *__restrict__ stats = second ? opB.stats : opA.stats;
+    int8_t *__restrict__ planes = second ? opB.planes : opA.planes;
+    int *__restrict__ Lr = second ? opB.Lr : opA.Lr;
+    int *__restrict__ slot = second ? opB.slot : opA.slot;
+    int4 *__restrict__ seg = second ? opB.seg : opA.seg;
+    int *__restrict__ tails = second ? opB.tails : opA.tails;
+    const int cap = second ? opB.cap : opA.cap;
+    TcCounters *__restrict__ ctr = second ? opB.ctr : opA.ctr;
+    const size_t plane = (size_t)rows * Kp;
+    const bool vec = (K % EPT) == 0 && (((uintptr_t)codes) & 15u) == 0;
     const size_t rb = (size_t)r * K;
     // pass 1: statistics.  A posit's lsb exponent and binade are both
     // non-decreasing in its magnitude, so the row's min lsb and max binade are
@@ -1341,20 +1365,46 @@ __global__ void __launch_bounds__(256) k_tc_prep(const void *__restrict__ codes,
 //   C[s][y] = sum over its tail elements (x, k):  v(X[x,k]) * v(Y[y,k])
 // exactly, in units of 2^(la_x + la_y).  When YL is given, Y's own tail
 // elements (lsb below YL[y]) are skipped (they are counted from Y's side).
+// One side of the correction launch.  blockIdx.z selects the side; each side
+// runs on its own gx x gy corner of the launch's grid (the rest of that
+// side's blocks exit), so both sides are one launch.
+struct CorrSide {
+  const void *X, *Y;
+  int Yrows;
+  const int32_t *xs, *ys;
+  const int4 *xst, *yst;
+  const int *YL;
+  const int4 *seg;
+  const int *tails;
+  const TcCounters *ctr;
+  int cap;
+  ulonglong2 *Cout;
+  int gx, gy;
+};
+
 template <int FMT>
-__global__ void __launch_bounds__(256) k_tc_corr(const void *__restrict__ X, const void *__restrict__ Y, int Yrows,
-                                                 int K, const int32_t *__restrict__ xs, const int32_t *__restrict__ ys,
-                                                 int G, int group, const int4 *__restrict__ xst,
-                                                 const int4 *__restrict__ yst, const int *__restrict__ YL,
-                                                 const int4 *__restrict__ seg, const int *__restrict__ tails,
-                                                 const TcCounters *__restrict__ ctr, int cap,
-                                                 ulonglong2 *__restrict__ Cout) {
-  const int nslots = min(ctr->v[0], cap);
-  for (int sl = blockIdx.x; sl < nslots; sl += gridDim.x) {
+__global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSide s1, int K, int G, int group) {
+  const bool second = blockIdx.z != 0;
+  const int gx = second ? s1.gx : s0.gx, gy = second ? s1.gy : s0.gy;
+  if ((int)blockIdx.x >= gx || (int)blockIdx.y >= gy) return;
+  const void *__restrict__ X = second ? s1.X : s0.X;
+  const void *__restrict__ Y = second ? s1.Y : s0.Y;
+  const int Yrows = second ? s1.Yrows : s0.Yrows;
+  const int32_t *__restrict__ xs = second ? s1.xs : s0.xs;
+  const int32_t *__restrict__ ys = second ? s1.ys : s0.ys;
+  const int4 *__restrict__ xst = second ? s1.xst : s0.xst;
+  const int4 *__restrict__ yst = second ? s1.yst : s0.yst;
+  const int *__restrict__ YL = second ? s1.YL : s0.YL;
+  const int4 *__restrict__ seg = second ? s1.seg : s0.seg;
+  const int *__restrict__ tails = second ? s1.tails : s0.tails;
+  const TcCounters *__restrict__ ctr = second ? s1.ctr : s0.ctr;
+  ulonglong2 *__restrict__ Cout = second ? s1.Cout : s0.Cout;
+  const int nslots = min(ctr->v[0], second ? s1.cap : s0.cap);
+  for (int sl = blockIdx.x; sl < nslots; sl += gx) {
     const int4 sg = seg[sl];
     const int x = sg.z;
     const int la_x = xst[x].x;
-    for (int y0 = blockIdx.y * 256; y0 < Yrows; y0 += gridDim.y * 256) {
+    for (int y0 = blockIdx.y * 256; y0 < Yrows; y0 += gy * 256) {
       const int y = y0 + threadIdx.x;
       if (y >= Yrows) continue;
       const int la_y = yst[y].x;
@@ -1748,26 +1798,21 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
                   : cudaMemsetAsync(cA, 0, ((a_only || reuse_b) ? 1 : 2) * sizeof(TcCounters), s);
   if (e != cudaSuccess) return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(e));
   const int sms = sm_count();
-  auto prep = [&](const void *codes, int rows, const int32_t *sc, int4 *st, int8_t *planes, int *Lr, int *slot,
-                  int4 *seg, int *tails, int cap, TcCounters *c) {
-    int g = std::min(rows, sms * 8);
-    if (a.fmt == 8)
-      k_tc_prep<8, 3><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, seg, tails,
-                                        L.pool, cap, c);
-    else
-      k_tc_prep<16, 4><<<g, 256, 0, s>>>(codes, rows, a.K, L.Kp, sc, a.G, a.group, st, planes, Lr, slot, seg,
-                                         tails, L.pool, cap, c);
-    return check_launch("tc_prep");
-  };
+  // the operands this call prepares, in one launch (an operand with rows = 0 is skipped)
+  PrepOp pa{a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA};
+  PrepOp pb{a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB};
+  if (reuse_a || b_only) pa.rows = 0;
+  if (reuse_b || a_only) pb.rows = 0;
   int rc = kOk;
-  if (!reuse_a && !b_only) {
-    rc = prep(a.A, a.M, a.sa, sta, planesA, LA, slotA, segA, tailA, L.capA, cA);
-    if (rc || a_only) return rc;
+  if (pa.rows + pb.rows > 0) {
+    const int g = std::min(pa.rows + pb.rows, sms * 8);
+    if (a.fmt == 8)
+      k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+    else
+      k_tc_prep<16, 4><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+    rc = check_launch("tc_prep");
   }
-  if (!reuse_b) {
-    rc = prep(a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB);
-    if (rc || b_only) return rc;
-  }
+  if (rc || a_only || b_only) return rc;
 
   int S = L.S;
   // Paired SMs whenever the tile has a second 128-row half to work on.
@@ -1790,7 +1835,10 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   const TcSchedule sc = tc_schedule(S, a.M, a.N, L.nkb, pair);
   if (tc_qbuf_bytes(sc) > L.total - L.part) return set_error(kEWorkspace, "quire_gemm: sum buffer too small");
   size_t outs = (size_t)a.M * a.N;
-  int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 8);
+  // k_tc_fixup almost always exits at once (the global row bounds show nothing
+  // to redo): a small grid keeps that exit cheap; when there is work, its
+  // blocks stride over all outputs
+  int g = (int)std::min<size_t>((outs + 255) / 256, (size_t)sms * 2);
   const int gf = sms * 4;   // k_tc_finish: four blocks per SM are resident
 
   // tail corrections (the kernels read the tail-row counts on the device).
@@ -1805,27 +1853,14 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   }
   const cudaStream_t cs = side ? side->st : s;
   const int cy = side ? 2 : 64;
-  dim3 ga((unsigned)std::min(L.capA, side ? sms : sms * 2), (unsigned)std::min((a.N + 255) / 256, cy));
-  dim3 gb((unsigned)std::min(L.capB, side ? sms : sms * 2), (unsigned)std::min((a.M + 255) / 256, cy));
-  if (a.fmt == 8) {
-    k_tc_corr<8><<<ga, 256, 0, cs>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
-                                     cA, L.capA, CA);
-    rc = check_launch("tc_corr");
-    if (rc == kOk) {
-      k_tc_corr<8><<<gb, 256, 0, cs>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB,
-                                       cB, L.capB, CB);
-      rc = check_launch("tc_corr");
-    }
-  } else {
-    k_tc_corr<16><<<ga, 256, 0, cs>>>(a.A, a.B, a.N, a.K, a.sa, a.sb, a.G, a.group, sta, stb, nullptr, segA, tailA,
-                                      cA, L.capA, CA);
-    rc = check_launch("tc_corr");
-    if (rc == kOk) {
-      k_tc_corr<16><<<gb, 256, 0, cs>>>(a.B, a.A, a.M, a.K, a.sb, a.sa, a.G, a.group, stb, sta, LA, segB, tailB,
-                                        cB, L.capB, CB);
-      rc = check_launch("tc_corr");
-    }
-  }
+  const CorrSide ca{a.A, a.B, a.N, a.sa, a.sb, sta, stb, nullptr, segA, tailA, cA, L.capA, CA,
+                    std::min(L.capA, side ? sms : sms * 2), std::min((a.N + 255) / 256, cy)};
+  const CorrSide cb{a.B, a.A, a.M, a.sb, a.sa, stb, sta, LA, segB, tailB, cB, L.capB, CB,
+                    std::min(L.capB, side ? sms : sms * 2), std::min((a.M + 255) / 256, cy)};
+  const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
+  if (a.fmt == 8) k_tc_corr<8><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+  else k_tc_corr<16><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+  rc = check_launch("tc_corr");
   cudaEvent_t corr_done = nullptr;
   if (side) {
     // the caller's stream always joins the side stream, on the error path too
