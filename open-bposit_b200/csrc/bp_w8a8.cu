@@ -3,15 +3,18 @@
 // and the truncating bp8 encode of the row scaled by 2^-e
 // (encode_bposit8 on floats, reference/bposit_ref.py:258-270).
 //
-// One warp per row (rows of up to kStageK elements staged in the warp's slice
-// of shared memory, longer ones re-read through L2), no block-wide barrier:
+// One warp per row (rows staged in the warp's slice of shared memory, as many
+// warps per block as 48 KB of rows allow; only rows beyond 12288 elements are
+// re-read through L2), no block-wide barrier, float4 loads several at a time:
 //   rms  = sqrt(sum(x^2) / K)                       float64, warp reduction
 //   p95  = numpy's 'linear' percentile of |x| at 95: the order statistics at
 //          ranks lo = floor(0.95 (K - 1)) and lo + 1 by a 4-pass radix select
 //          on the fp32 bit patterns of |x| (their order is the values'), with
-//          a 256-bin histogram per warp, then lerp exactly as numpy does
-//          (b - (b - a)(1 - t) when t >= 0.5); skipped when a count of
-//          |x| > 2 rms shows a[lo + 1] <= 2 rms (then ref = rms whatever p95 is)
+//          a 256-bin histogram per warp, over the candidates |x| > 2 rms only
+//          (when the percentile can matter, its ranks are among them or just
+//          below), then lerp exactly as numpy does (b - (b - a)(1 - t) when
+//          t >= 0.5); skipped when a count of |x| > 2 rms shows
+//          a[lo + 1] <= 2 rms (then ref = rms whatever p95 is)
 //   ref  = p95 if p95 > 0 and p95 > 2 rms, else rms;  e = rint(log2(ref)),
 //          0 for an all-zero row
 //   code = truncating bp8 of x * 2^-e (exact in float64), 0 when
@@ -31,7 +34,7 @@ namespace bp {
 namespace {
 
 constexpr int kT = 256, kWarps = kT / 32;
-constexpr int kStageK = 1024;   // rows up to this length are staged in shared memory
+constexpr int kStageFloats = 12288;   // 48 KB of staged rows per block
 
 __device__ __forceinline__ double warp_sum_d(double v) {
 #pragma unroll
@@ -60,100 +63,163 @@ __device__ __forceinline__ void hist_add(uint32_t *hist, uint32_t bin, bool acti
   if ((threadIdx.x & 31) == (uint32_t)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
 }
 
-template <bool STAGED>
+__device__ __forceinline__ double warp_max_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmax(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Truncating bp8 code of x * 2^-e (float64 bit logic of the bp8 f64
+// quantizer), 0 when |x * 2^-e| <= the float entry's zero cut.
+__device__ __forceinline__ uint32_t w8a8_code(const uint2 *tbl, float xf, double sc) {
+  const double v = (double)xf * sc;
+  const unsigned long long u = (unsigned long long)__double_as_longlong(v);
+  const unsigned long long a = u & 0x7FFFFFFFFFFFFFFFull;
+  if (a > 0x7FF0000000000000ull) return 0x80u;
+  if (__longlong_as_double((long long)a) <= BP_LIMIT_ZERO) return 0u;
+  const int b64 = (int)(a >> 52);
+  const unsigned long long Mm = a & 0xFFFFFFFFFFFFFull;
+  int b32 = b64 - 1023 + 127;
+  b32 = b32 < 1 ? 1 : (b32 > 255 ? 255 : b32);
+  const uint2 q = tbl[b32];
+  const uint32_t sh = (q.x >> 8) + 29u;
+  const unsigned long long thr = q.y == 0x7FFFFFu ? 0xFFFFFFFFFFFFFull : ((unsigned long long)q.y << 29);
+  const unsigned long long msk = (1ull << sh) - 1ull;
+  const uint32_t mag = (q.x & 0xFFu) + (uint32_t)(Mm >> sh) + ((Mm & msk) > thr ? 1u : 0u);
+  return (u >> 63) ? ((0u - mag) & 0xFFu) : mag;
+}
+
+// One warp per row; blockDim.x / 32 warps per block, each with a K-float
+// slice of the dynamic shared memory (STAGED) and a 256-bin histogram.  VEC:
+// K % 4 == 0 and 16-byte aligned rows -- float4 loads, eight at a time in
+// flight per lane, and four codes per 32-bit store.
+template <bool STAGED, bool VEC>
 __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, int rows, int K,
                                                   int32_t *__restrict__ exps, uint8_t *__restrict__ codes) {
   __shared__ uint2 tbl[256];          // truncating bp8 quantize table (bp8_qentry)
   __shared__ uint32_t hists[kWarps][256];
-  extern __shared__ float s_rows[];   // [kWarps][K] when STAGED
-  {
-    QEntry q = bp8_qentry(threadIdx.x, false);
-    tbl[threadIdx.x] = make_uint2(q.lo_sh, q.thr);
+  extern __shared__ float s_rows[];   // [warps][K] when STAGED
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    QEntry q = bp8_qentry(i, false);
+    tbl[i] = make_uint2(q.lo_sh, q.thr);
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   uint32_t *hist = hists[warp];
   float *srow = STAGED ? s_rows + (size_t)warp * K : nullptr;
   const double pos = 0.95 * (double)(K - 1);
   const int lo = (int)floor(pos);
   const double t = pos - (double)lo;
   const int kpad = (K + 31) / 32 * 32;   // every lane runs every trip of the histogram loop
-  for (int r = blockIdx.x * kWarps + warp; r < rows; r += gridDim.x * kWarps) {
+  const int K4 = K / 4;
+  for (int r = blockIdx.x * nwarps + warp; r < rows; r += gridDim.x * nwarps) {
     const float *xg = x + (size_t)r * K;
     double ss = 0.0;
-    for (int k = lane; k < K; k += 32) {
-      const float f = xg[k];
-      if (STAGED) srow[k] = f;
-      ss += (double)f * (double)f;
+    if (VEC) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(xg);
+      float4 *s4 = reinterpret_cast<float4 *>(srow);
+      for (int u0 = lane; u0 < K4; u0 += 256) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = u0 + 32 * j < K4 ? __ldcs(x4 + u0 + 32 * j) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (STAGED && u0 + 32 * j < K4) s4[u0 + 32 * j] = v[j];
+          ss += (double)v[j].x * v[j].x + (double)v[j].y * v[j].y + (double)v[j].z * v[j].z + (double)v[j].w * v[j].w;
+        }
+      }
+    } else {
+      for (int k = lane; k < K; k += 32) {
+        const float f = xg[k];
+        if (STAGED) srow[k] = f;
+        ss += (double)f * (double)f;
+      }
     }
     const double rms = sqrt(warp_sum_d(ss) / (double)K);
     __syncwarp();
     const float *xr = STAGED ? srow : xg;
-    // The percentile only matters when it exceeds 2 rms.  With c = #{|x| > 2 rms}:
-    // c <= K - lo - 2 means a[lo + 1] <= 2 rms, so p95 (between a[lo] and
-    // a[lo + 1]) does not exceed it and ref = rms without the selection.
-    uint32_t cnt = 0u;
+    // The percentile only matters when it exceeds 2 rms.  With c = #{|x| > 2 rms}
+    // (the top c of the row, the "candidates"): c <= K - lo - 2 means
+    // a[lo + 1] <= 2 rms, so p95 (between a[lo] and a[lo + 1]) does not exceed
+    // it and ref = rms without the selection.
     const double two_rms = 2.0 * rms;
+    uint32_t cnt = 0u;
     for (int k = lane; k < K; k += 32) cnt += fabs((double)xr[k]) > two_rms ? 1u : 0u;
     cnt = warp_sum_u(cnt);
     const bool need_p95 = rms > 0.0 && (long long)cnt > (long long)K - lo - 2;
-    // radix select of rank lo among the keys |x| (fp32 bits, sign cleared)
-    uint32_t prefix = 0u, mask = 0u, rank = (uint32_t)lo, eq = 0u;
-    for (int shift = 24; shift >= 0 && need_p95; shift -= 8) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
-      __syncwarp();
-      for (int k = lane; k < kpad; k += 32) {
-        const uint32_t key = k < K ? (__float_as_uint(xr[k]) & 0x7FFFFFFFu) : 0u;
-        hist_add(hist, (key >> shift) & 255u, k < K && (key & mask) == prefix);
-      }
-      __syncwarp();
-      // lane l owns bins 8l .. 8l+7: inclusive prefix over lanes, then the
-      // first bin whose running count passes `rank`
-      uint32_t c[8], tot = 0u;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        c[q] = hist[8 * lane + q];
-        tot += c[q];
-      }
-      uint32_t incl = tot;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const uint32_t excl = incl - tot;
-      const bool mine = excl <= rank && rank < incl;
-      uint32_t below = excl, b = 8u * lane, cb = c[0];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        cb = c[q];
-        if (below + c[q] <= rank && q < 7) {
-          below += c[q];
-          ++b;
-        } else {
-          break;
-        }
-      }
-      const int owner = __ffs(__ballot_sync(0xFFFFFFFFu, mine)) - 1;
-      b = __shfl_sync(0xFFFFFFFFu, b, owner);
-      below = __shfl_sync(0xFFFFFFFFu, below, owner);
-      eq = __shfl_sync(0xFFFFFFFFu, cb, owner);
-      prefix |= b << shift;
-      rank -= below;
-      mask |= 255u << shift;
-      __syncwarp();
-    }
-    const double a_lo = (double)__uint_as_float(prefix);
-    // rank lo + 1: the same key while it repeats, else the next larger key
-    double a_hi = a_lo;
-    if (need_p95 && lo + 1 < K && rank + 1 >= eq) {
-      uint32_t nxt = 0xFFFFFFFFu;
+    double a_lo = 0.0, a_hi = 0.0;
+    if (need_p95 && lo < K - (int)cnt) {
+      // lo = K - c - 1: a[lo] is the largest non-candidate, a[lo + 1] the smallest candidate
+      double mx = 0.0, mn = INFINITY;
       for (int k = lane; k < K; k += 32) {
-        const uint32_t key = __float_as_uint(xr[k]) & 0x7FFFFFFFu;
-        if (key > prefix) nxt = min(nxt, key);
+        const double v = fabs((double)xr[k]);
+        if (v > two_rms) mn = fmin(mn, v);
+        else mx = fmax(mx, v);
       }
-      a_hi = (double)__uint_as_float(warp_min_u(nxt));
+      a_lo = warp_max_d(mx);
+      a_hi = lo + 1 < K ? -warp_max_d(-mn) : a_lo;   // no candidate at all only when lo = K - 1
+    } else if (need_p95) {
+      // radix select of rank lo - (K - c) among the candidates only (keys: fp32
+      // bits of |x|, sign cleared; their order is the values')
+      uint32_t prefix = 0u, mask = 0u, rank = (uint32_t)(lo - (K - (int)cnt)), eq = 0u;
+      for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) hist[lane * 8 + q] = 0u;
+        __syncwarp();
+        for (int k = lane; k < kpad; k += 32) {
+          const float f = k < K ? xr[k] : 0.0f;
+          const uint32_t key = __float_as_uint(f) & 0x7FFFFFFFu;
+          const bool cand = k < K && fabs((double)f) > two_rms && (key & mask) == prefix;
+          hist_add(hist, (key >> shift) & 255u, cand);
+        }
+        __syncwarp();
+        // lane l owns bins 8l .. 8l+7: inclusive prefix over lanes, then the
+        // first bin whose running count passes `rank`
+        uint32_t c[8], tot = 0u;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          c[q] = hist[8 * lane + q];
+          tot += c[q];
+        }
+        uint32_t incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const uint32_t excl = incl - tot;
+        const bool mine = excl <= rank && rank < incl;
+        uint32_t below = excl, b = 8u * lane, cb = c[0];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          cb = c[q];
+          if (below + c[q] <= rank && q < 7) {
+            below += c[q];
+            ++b;
+          } else {
+            break;
+          }
+        }
+        const int owner = __ffs(__ballot_sync(0xFFFFFFFFu, mine)) - 1;
+        b = __shfl_sync(0xFFFFFFFFu, b, owner);
+        below = __shfl_sync(0xFFFFFFFFu, below, owner);
+        eq = __shfl_sync(0xFFFFFFFFu, cb, owner);
+        prefix |= b << shift;
+        rank -= below;
+        mask |= 255u << shift;
+        __syncwarp();
+      }
+      a_lo = (double)__uint_as_float(prefix);
+      // rank lo + 1: the same key while it repeats, else the next larger key
+      a_hi = a_lo;
+      if (lo + 1 < K && rank + 1 >= eq) {
+        uint32_t nxt = 0xFFFFFFFFu;
+        for (int k = lane; k < K; k += 32) {
+          const uint32_t key = __float_as_uint(xr[k]) & 0x7FFFFFFFu;
+          if (key > prefix) nxt = min(nxt, key);
+        }
+        a_hi = (double)__uint_as_float(warp_min_u(nxt));
+      }
     }
     const double d = a_hi - a_lo;
     const double p95 = t >= 0.5 ? a_hi - d * (1.0 - t) : a_lo + d * t;
@@ -163,31 +229,19 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
       e = (int)rint(log2(ref));
     }
     if (lane == 0) exps[r] = e;
-    // truncating encode of x * 2^-e (float64 bit logic of the bp8 f64 quantizer)
+    // truncating encode of x * 2^-e
     const double sc = scalbn(1.0, -e);
     uint8_t *cr = codes + (size_t)r * K;
-    for (int k = lane; k < K; k += 32) {
-      const double v = (double)xr[k] * sc;
-      const unsigned long long u = (unsigned long long)__double_as_longlong(v);
-      const unsigned long long a = u & 0x7FFFFFFFFFFFFFFFull;
-      uint32_t code;
-      if (a > 0x7FF0000000000000ull) {
-        code = 0x80u;
-      } else if (__longlong_as_double((long long)a) <= BP_LIMIT_ZERO) {
-        code = 0u;
-      } else {
-        const int b64 = (int)(a >> 52);
-        const unsigned long long Mm = a & 0xFFFFFFFFFFFFFull;
-        int b32 = b64 - 1023 + 127;
-        b32 = b32 < 1 ? 1 : (b32 > 255 ? 255 : b32);
-        const uint2 q = tbl[b32];
-        const uint32_t sh = (q.x >> 8) + 29u;
-        const unsigned long long thr = q.y == 0x7FFFFFu ? 0xFFFFFFFFFFFFFull : ((unsigned long long)q.y << 29);
-        const unsigned long long msk = (1ull << sh) - 1ull;
-        const uint32_t mag = (q.x & 0xFFu) + (uint32_t)(Mm >> sh) + ((Mm & msk) > thr ? 1u : 0u);
-        code = (u >> 63) ? ((0u - mag) & 0xFFu) : mag;
+    if (VEC) {
+      const float4 *r4 = reinterpret_cast<const float4 *>(xr);
+      uint32_t *cw = reinterpret_cast<uint32_t *>(cr);
+      for (int u = lane; u < K4; u += 32) {
+        const float4 v = r4[u];
+        cw[u] = w8a8_code(tbl, v.x, sc) | (w8a8_code(tbl, v.y, sc) << 8) | (w8a8_code(tbl, v.z, sc) << 16) |
+                (w8a8_code(tbl, v.w, sc) << 24);
       }
-      cr[k] = (uint8_t)code;
+    } else {
+      for (int k = lane; k < K; k += 32) cr[k] = (uint8_t)w8a8_code(tbl, xr[k], sc);
     }
     __syncwarp();   // the next row reuses this warp's staging and histogram
   }
@@ -197,15 +251,19 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
 
 int launch_w8a8_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, cudaStream_t s) {
   if (rows == 0 || K == 0) return kOk;
-  const int blocks = (rows + kWarps - 1) / kWarps;
-  if (K <= kStageK) {
-    // 32 KB of staging at most: several blocks per SM stay resident
-    const size_t smem = (size_t)kWarps * K * sizeof(float);
-    k_w8a8_rows<true><<<std::min(blocks, sm_count() * 6), kT, smem, s>>>(x, rows, K, exps, codes);
+  const bool vec = (K % 4) == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)codes & 3u) == 0;
+  if (K <= kStageFloats) {
+    // rows staged in shared memory: as many warps per block as 48 KB of rows allow
+    const int w = std::max(1, std::min(kWarps, kStageFloats / K));
+    const size_t smem = (size_t)w * K * sizeof(float);
+    const int blocks = std::min((rows + w - 1) / w, sm_count() * 16);
+    if (vec) k_w8a8_rows<true, true><<<blocks, 32 * w, smem, s>>>(x, rows, K, exps, codes);
+    else k_w8a8_rows<true, false><<<blocks, 32 * w, smem, s>>>(x, rows, K, exps, codes);
   } else {
-    // long rows through L2: 4 blocks (32 rows) per SM in flight keep the
-    // re-read rows of a 4864-wide activation (~90 MB) inside L2
-    k_w8a8_rows<false><<<std::min(blocks, sm_count() * 4), kT, 0, s>>>(x, rows, K, exps, codes);
+    // very long rows re-read through L2
+    const int blocks = std::min((rows + kWarps - 1) / kWarps, sm_count() * 4);
+    if (vec) k_w8a8_rows<false, true><<<blocks, kT, 0, s>>>(x, rows, K, exps, codes);
+    else k_w8a8_rows<false, false><<<blocks, kT, 0, s>>>(x, rows, K, exps, codes);
   }
   return check_launch("w8a8_rows");
 }

@@ -133,7 +133,7 @@ def test_qwen_full_size_forward_row_subsample(orc):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("K", [1, 2, 3, 20, 576, 4864])
+@pytest.mark.parametrize("K", [1, 2, 3, 20, 21, 576, 896, 4864, 12289, 12292])
 def test_w8a8_encode_rows_matches_reference_rule(orc, K):
     """ops.w8a8_encode_rows: per-row exponents equal recommended_exponents
     (reference/bposit_quantize.py:46-63, numpy on the host) and the codes equal
@@ -149,6 +149,9 @@ def test_w8a8_encode_rows_matches_reference_rule(orc, K):
     X[3] = np.where(np.arange(K) % 2 == 0, 1.0, -2.0)     # two values
     X[4] = (rng.integers(-3, 4, K) * 2.0 ** -30).astype(np.float32)   # tiny: the zero cut after scaling
     X[5, :] = np.float32(2.0 ** 7)                        # power of two
+    X[6, :] = 1.0                                         # exactly one element above 2 rms (when K allows):
+    X[6, K // 2] = 10.0                                   # the 95th percentile's rank at the candidates' edge
+    X[7] = (rng.standard_normal(K) * np.where(rng.random(K) < 0.08, 30.0, 1.0)).astype(np.float32)  # heavy tail
     xt = torch.from_numpy(X).cuda()
     codes, exps = ops.w8a8_encode_rows(xt)
     ex_ref = recommended_exponents(X.astype(np.float64))
