@@ -464,6 +464,35 @@ BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
   return Q ? code : 0u;
 }
 
+// The exact value of bp32_from_i64(Q, lsb_exp) as a double times 2^extra, for
+// the sums whose bposit32 keeps all three exponent bits (regime of at most 28
+// bits: total exponent in [-216, 215]), where that value is |Q| cut to its top
+// 29 - rl bits: returns false for the others (and for Q = 0) so the caller can
+// take the field route.  The double is exact (at most 27 significant bits);
+// the scaling is an exponent add while the result stays a normal double.
+BP_HD bool bp32_value_i64(long long Q, int lsb_exp, int extra, double &v) {
+  if (Q == 0) return false;
+  const bool neg = Q < 0;
+  uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
+  const int msb = 63 - clz64(m);
+  const int te = msb + lsb_exp;
+  const int k = te >> 3;
+  const int rl = k >= 0 ? k + 2 : 1 - k;
+  if (rl > 28) return false;
+  const int drop = msb + 1 - (29 - rl);
+  if (drop > 0) m &= ~((1ull << drop) - 1ull);
+  const int e = lsb_exp + extra;
+  // double(m) has exponent msb; the product stays normal for msb + e in [-1022, 1023]
+  if (msb + e < -1022 || msb + e > 1023) return false;
+  double d = (double)m;   // exact: at most 27 significant bits
+  uint64_t b;
+  memcpy(&b, &d, 8);
+  b += (uint64_t)(int64_t)e << 52;
+  memcpy(&d, &b, 8);
+  v = neg ? -d : d;
+  return true;
+}
+
 // ---- the small rungs: bposit4 (es 1, encode range 2^+-2) and AI-posit5
 // (es 1, 2^+-4) (reference/bposit_ref.py:879-940) --------------------------
 // Fraction(x).limit_denominator(10**8) is 0 exactly when |x| < 1/(2*10**8);

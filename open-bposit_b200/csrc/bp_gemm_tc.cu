@@ -654,16 +654,26 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
                                            const long long (&qv)[PL], const long long (&qh)[PL], int4 ra, int Li,
                                            int si) {
   uint32_t cd[PL];
+  float fv[PL];
   uint32_t slow = 0u, keep = 0u;
+  const int rex = (p.out_f32 && p.re) ? p.re[i] : 0;
 #pragma unroll
   for (int q = 0; q < PL; ++q) {
+    fv[q] = 0.0f;
     if (QW == 1) {
-      cd[q] = bp32_from_i64(qv[q], Li + c.Lj[q]);
+      // the fp32 hand-off straight from the exact sum (bp32_value_i64); the
+      // code itself only when it is stored or the value needs the field route
+      double v = 0.0;
+      const bool direct = p.out_f32 && bp32_value_i64(qv[q], Li + c.Lj[q], rex + c.fe[q], v);
+      if (p.out || !direct) cd[q] = bp32_from_i64(qv[q], Li + c.Lj[q]);
+      if (p.out_f32)
+        fv[q] = direct ? __double2float_rn(v + (double)c.fb[q]) : bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
     } else {
       const __int128 Q = (__int128)qv[q] + ((__int128)qh[q] << 28);
       const bool neg = Q < 0;
       const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
       cd[q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + c.Lj[q]);
+      if (p.out_f32) fv[q] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
     }
     const bool plain = si == -1 && c.sj[q] == -1 && ra.z != 0 && c.bz[q] && ra.x + c.bx[q] + 96 >= 0 &&
                        (ra.y - ra.x) + c.bw[q] <= 127;
@@ -698,6 +708,7 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
         const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
         cd[q] = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
       }
+      if (p.out_f32) fv[q] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
       keep |= 1u << q;
     }
   }
@@ -709,10 +720,9 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
   }
   if (p.out_f32) {
     float *frow = p.out_f32 + (size_t)i * p.ldf + j0 + lane;
-    const int rex = p.re ? p.re[i] : 0;
 #pragma unroll
     for (int q = 0; q < PL; ++q)
-      if ((keep >> q) & 1u) frow[q * 32] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
+      if ((keep >> q) & 1u) frow[q * 32] = fv[q];
   }
   for (int e = 0; e < p.n_extra; ++e) {
     uint32_t *erow = p.extra_out[e] + (size_t)i * p.ldo + p.extra_col0 + j0 + lane;

@@ -252,6 +252,24 @@ int main(int argc, char **argv) {
         ++bad;
       }
     }
+    // the direct value of a 64-bit sum (the finish kernel's fp32 hand-off)
+    // against the value of its bposit32 code
+    for (int it = 0; it < 2000000; ++it) {
+      const int bits = (int)(rnd() % 63) + 1;
+      const uint64_t mm = rnd() & ((1ull << bits) - 1);
+      if (!mm) continue;
+      const int L = (int)(rnd() % 601) - 300, extra = (int)(rnd() % 81) - 40;
+      const long long Q = (rnd() & 1) ? -(long long)mm : (long long)mm;
+      double v;
+      if (!bp::bp32_value_i64(Q, L, extra, v)) continue;
+      const uint32_t code = bp::bp32_from_i64(Q, L);
+      bp::Dec d = bp::decode_posit<32, 3>(code);
+      const double ref = (d.sign ? -1.0 : 1.0) * ldexp((double)((1u << d.fw) + d.fbits), d.scale - d.fw + extra);
+      if (d.kind != 0 || v != ref) {
+        if (bad < 5) fprintf(stderr, "bp32 value mismatch Q=%lld L=%d extra=%d\n", Q, L, extra);
+        ++bad;
+      }
+    }
     // the 64-bit form against the 128-bit one over exponents past both ends
     // of the bposit32 range (minpos / maxpos saturation)
     for (int it = 0; it < 400000; ++it) {
