@@ -618,14 +618,23 @@ def run_c1(ctx):
 
 
 # -------------------------------------------------- config 2: codec sweep ---
-def codec_input(ctx, n):
+def codec_input(ctx, n, lim):
+    """The sweep's values for a format whose range is 2^+-lim: half N(0,1), half
+    log-uniform magnitudes over 2^+-(lim + 2) with random signs, and, at the
+    start, +-0, the saturation edges (+-maxpos, twice it, +-minpos, a quarter of
+    it), exact midpoints of the bp8 grid (ties) and powers of two."""
     torch = ctx.torch
-    gen = torch.Generator(device=ctx.device).manual_seed(1234 + ctx.rank)
+    gen = torch.Generator(device=ctx.device).manual_seed(1234 + ctx.rank + lim)
     x = torch.empty(n, dtype=torch.float32, device=ctx.device)
     half = n // 2
     x[:half].normal_(generator=gen)
-    e = torch.empty(n - half, dtype=torch.float32, device=ctx.device).uniform_(-26, 26, generator=gen)
+    e = torch.empty(n - half, dtype=torch.float32, device=ctx.device).uniform_(-lim - 2, lim + 2, generator=gen)
     x[half:] = torch.exp2(e) * torch.where(torch.rand(n - half, device=ctx.device, generator=gen) < 0.5, -1.0, 1.0)
+    del e
+    m = 2.0 ** lim
+    edges = [0.0, -0.0, m, -m, 2 * m, -2 * m, 1 / m, -1 / m, 0.25 / m, -0.25 / m, 1.0, -1.0, 1.5, 1.0625, 1.03125,
+             1.09375, 3 / m, 12.0, -12.0, 0.75]
+    x[:len(edges)] = torch.tensor(edges, dtype=torch.float32, device=ctx.device)
     return x
 
 
@@ -638,7 +647,8 @@ def run_c2(ctx):
 
     from bposit_b200 import _lib, ops
     n = 1 << 28
-    x = codec_input(ctx, n)
+    x = codec_input(ctx, n, 24)       # bp8's range 2^+-24
+    x16 = codec_input(ctx, n, 112)    # bp16's range 2^+-112
     c8 = torch.empty(n, dtype=torch.uint8, device=ctx.device)
     c16 = torch.empty(n, dtype=torch.uint16, device=ctx.device)
     y = torch.empty(n, dtype=torch.float32, device=ctx.device)
@@ -652,7 +662,7 @@ def run_c2(ctx):
     kernels = {
         "bp8_encode_rtn": (lambda: ops.quantize_bp8(x, nearest=True, out=c8), 5),
         "bp8_decode": (lambda: dec(c8), 5),
-        "bp16_encode_rtne": (lambda: ops.encode_bp16(x, rtne=True, out=c16), 6),
+        "bp16_encode_rtne": (lambda: ops.encode_bp16(x16, rtne=True, out=c16), 6),
         "bp16_decode": (lambda: dec(c16), 6),
     }
     markers = {
@@ -688,11 +698,12 @@ def run_c2(ctx):
     del hx, hc, dx
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
-        cpu = codec_cpu_baseline(x[: 1 << 22].cpu().numpy())
-    del x, c8, c16, y
+        cpu = codec_cpu_baseline(x[: 1 << 22].cpu().numpy(), x16[: 1 << 22].cpu().numpy())
+    del x, x16, c8, c16, y
     torch.cuda.empty_cache()
-    config = {"workload": "2^28 fp32 per rank: half N(0,1), half +-2^U(-26,26); bp8 RTN encode, bp8 decode, "
-                          "bp16 RTNE encode, bp16 decode",
+    config = {"workload": "2^28 fp32 per rank and format: half N(0,1), half log-uniform magnitudes over the format's "
+                          "range (bp8 2^+-26, bp16 2^+-114) with +-0, saturation edges and exact ties; bp8 RTN "
+                          "encode, bp8 decode, bp16 RTNE encode, bp16 decode (of the codes just encoded)",
               "elements_per_rank": n, "fmt": "bp8+bp16", "l2": "1 GiB input > L2", "ranks": ctx.world}
     line = base_line(ctx, "bp8/bp16 encode+decode GB/s (algorithmic bytes, 4 kernels)", "GB/s", value,
                      tot_ms, steps, args.warmup, config, "weak", dtype="f32/u8/u16")
@@ -710,16 +721,16 @@ def run_c2(ctx):
     return line
 
 
-def codec_cpu_baseline(xs):
-    """The oracle port's quantize_bp8(nearest=True) and bp16 RTNE encode on a
-    seeded 2^22-element sample of the sweep, all host threads and one."""
+def codec_cpu_baseline(xs, xs16):
+    """The oracle port's quantize_bp8(nearest=True) and bp16 RTNE encode on
+    seeded 2^22-element samples of the sweep, all host threads and one."""
     import numpy as np
     from oracle import oracle as orc
     th = host_threads()
-    chunks = np.array_split(xs, max(1, th * 4))
     out = {}
-    for name, fn, bpe in (("bp8_encode_rtn", lambda c: orc.quantize_bp8(c, True), 5),
-                          ("bp16_encode_rtne", lambda c: orc.encode_bp16(c, True), 6)):
+    for name, fn, bpe, src in (("bp8_encode_rtn", lambda c: orc.quantize_bp8(c, True), 5, xs),
+                               ("bp16_encode_rtne", lambda c: orc.encode_bp16(c, True), 6, xs16)):
+        chunks = np.array_split(src, max(1, th * 4))
         for t in (th, 1):
             t0 = time.perf_counter()
             reps = 0

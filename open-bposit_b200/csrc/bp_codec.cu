@@ -76,31 +76,38 @@ __global__ void __launch_bounds__(kThreads) k_decode_bp8(const uint8_t *__restri
   for (size_t i = nw * 4 + tid; i < n; i += stride) out[i] = __uint_as_float(lut[codes[i]]);
 }
 
-// bp16: a 256-entry table over the top 8 bits of the code's 15-bit field
-// (bp16_dec_entry) gives the fp32 pattern of every value with a regime run of
-// at most 4 (2^-32 <= |v| < 2^32) as base + (low 7 field bits << shift); the
-// rest decode in closed form (bp16_to_f32_bits).  Four codes (8 bytes) per unit.
+// bp16: the fp32 pattern of every positive 15-bit field in a 32,768-entry
+// table (128 KB of shared memory, built once per block from the closed form);
+// a code costs one table load and a sign fix-up, whatever its regime length.
+// One 1024-thread block per SM, grid-stride over tiles; four codes (8 bytes)
+// per unit.
+constexpr int kDec16Threads = 1024;
+constexpr size_t kDec16Smem = (size_t)32768 * sizeof(uint32_t);
+
 template <int U>
-__global__ void __launch_bounds__(kThreads) k_decode_bp16(const uint16_t *__restrict__ codes, size_t n,
-                                                          float *__restrict__ out, bool vec) {
-  __shared__ uint32_t lut[256];
-  lut[threadIdx.x] = bp16_dec_entry(threadIdx.x);
+__global__ void __launch_bounds__(kDec16Threads, 1) k_decode_bp16(const uint16_t *__restrict__ codes, size_t n,
+                                                                  float *__restrict__ out, bool vec) {
+  extern __shared__ uint32_t lut16[];
+  for (int f = threadIdx.x; f < 32768; f += kDec16Threads) lut16[f] = bp16_to_f32_bits((uint32_t)f);
   __syncthreads();
-  auto dec = [&](uint32_t c) { return bp16_decode_lut(c, lut[bp16_field(c) >> 7]); };
+  auto dec = [&](uint32_t c) {
+    const uint32_t f = bp16_field(c);
+    return f ? (lut16[f] | ((c & 0x8000u) << 16)) : 0u;
+  };
   const size_t nq = vec ? n / 4 : 0;
   const uint2 *c2 = reinterpret_cast<const uint2 *>(codes);
   uint4 *o4 = reinterpret_cast<uint4 *>(out);
-  const size_t tile = (size_t)kThreads * U;
+  const size_t tile = (size_t)kDec16Threads * U;
   for (size_t base = blockIdx.x * tile; base < nq; base += (size_t)gridDim.x * tile) {
     uint2 v[U];
 #pragma unroll
     for (int j = 0; j < U; ++j) {
-      const size_t i = base + threadIdx.x + j * kThreads;
+      const size_t i = base + threadIdx.x + j * kDec16Threads;
       v[j] = i < nq ? __ldcs(c2 + i) : make_uint2(0u, 0u);
     }
 #pragma unroll
     for (int j = 0; j < U; ++j) {
-      const size_t i = base + threadIdx.x + j * kThreads;
+      const size_t i = base + threadIdx.x + j * kDec16Threads;
       if (i < nq)
         __stcs(o4 + i, make_uint4(dec(v[j].x & 0xFFFFu), dec(v[j].x >> 16), dec(v[j].y & 0xFFFFu), dec(v[j].y >> 16)));
     }
@@ -338,7 +345,18 @@ int launch_decode(int fmt, const void *codes, size_t n, float *out, cudaStream_t
     k_decode_bp8<kDecU8><<<tile_grid(n, 4, kDecU8), kThreads, 0, s>>>((const uint8_t *)codes, n, out, vec);
   } else {
     const bool vec = oal && ((uintptr_t)codes & 7u) == 0u;
-    k_decode_bp16<kDecU16><<<tile_grid(n, 4, kDecU16), kThreads, 0, s>>>((const uint16_t *)codes, n, out, vec);
+    static bool attr_set[128] = {};   // per device: the 128 KB table needs the opt-in
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 128 && !attr_set[dev]) {
+      if (cudaFuncSetAttribute(k_decode_bp16<kDecU16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)kDec16Smem) != cudaSuccess)
+        return set_error(kECuda, "decode: shared-memory opt-in: %s", cudaGetErrorString(cudaGetLastError()));
+      attr_set[dev] = true;
+    }
+    const size_t tile = (size_t)kDec16Threads * kDecU16 * 4;
+    const int g = (int)std::min<size_t>(std::max<size_t>((n + tile - 1) / tile, 1), (size_t)sm_count());
+    k_decode_bp16<kDecU16><<<g, kDec16Threads, kDec16Smem, s>>>((const uint16_t *)codes, n, out, vec);
   }
   return check_launch("decode");
 }

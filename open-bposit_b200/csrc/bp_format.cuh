@@ -349,28 +349,7 @@ BP_HD uint32_t bp16_encode_signed(uint32_t u, uint32_t x, uint32_t c) {
   return (bs + ((q ^ m) - m)) & 0xFFFFu;
 }
 
-// bp16 decode table over the top 8 bits t of a positive 15-bit field: when
-// the regime, its terminator and the three exponent bits all lie in those 8
-// bits (fraction width fw >= 7), the low 7 field bits are the lowest fraction
-// bits and the fp32 pattern is base + (low7 << (23 - fw)); the entry is
-// base | (23 - fw) (base has no bit below 2^14).  0 marks the other fields
-// (regime runs of 5 or more: |value| >= 2^32 or < 2^-32, and zero), decoded in
-// closed form instead.
-BP_HD uint32_t bp16_dec_entry(uint32_t t) {
-  const uint32_t f = (t & 0xFFu) << 7;
-  if (f == 0u) return 0u;
-  const Dec d = decode_posit<16, 3>(f);
-  if (d.fw < 7) return 0u;
-  return (((uint32_t)(d.scale + 127) << 23) | (d.fbits << (23 - d.fw))) | (uint32_t)(23 - d.fw);
-}
-
-BP_HD uint32_t bp16_decode_lut(uint32_t c, uint32_t e) {
-  // e = table[f >> 7] for f the code's positive 15-bit field
-  const uint32_t neg = (c >> 15) & 1u;
-  const uint32_t f = (neg ? 0u - c : c) & 0x7FFFu;
-  return e ? (((e & ~31u) + ((f & 0x7Fu) << (e & 31u))) | (neg << 31)) : bp16_to_f32_bits(c);
-}
-
+// The positive 15-bit field of a bp16 code (two's complement for negatives).
 BP_HD uint32_t bp16_field(uint32_t c) { return (((c >> 15) & 1u) ? 0u - c : c) & 0x7FFFu; }
 
 // ---------------------------------------------------------------------------

@@ -99,7 +99,7 @@ def test_format_logic_matches_oracle_exhaustively(host_check, what):
     strided fp32 sweep and 2M random doubles for the bposit4 / AI-posit5 encoders;
     the streaming kernels' table bp16 encoder on every fp32 pattern (both modes)
     and their closed-form bp16 decode on every code; the signed bp8 / bp16 tables
-    on every fp32 pattern (both modes) and the bp16 decode table on every code."""
+    on every fp32 pattern (both modes)."""
     nt = max(1, min(8, len(os.sched_getaffinity(0))))
     r = subprocess.run([host_check, what, str(nt)], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
