@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // The general rule for output (i, j) of a unit: the chunks' sums added in 128
 // bits, finish_code (tail corrections, zero rows, raw quire), stores.
-template <int QW>
+template <int QW, bool F32>
 __device__ __forceinline__ void finish_general(const TcParams &p, const long long *a, size_t plane, int i, int j) {
   __int128 Q = 0;
   for (int ch = 0; ch < p.split; ++ch) {
@@ -629,7 +629,7 @@ __device__ __forceinline__ void finish_general(const TcParams &p, const long lon
                    code))
     return;
   if (p.out) p.out[(size_t)i * p.ldo + j] = code;
-  if (p.out_f32)
+  if (F32)
     p.out_f32[(size_t)i * p.ldf + j] =
         bp32_f32_out(code, (p.re ? p.re[i] : 0) + (p.ce ? p.ce[j] : 0), p.bias ? p.bias[j] : 0.0f);
   for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
@@ -650,30 +650,20 @@ struct FinishCols {
 // row statistics (ra, Li, si).  Whole warp: the tail corrections' loads are
 // taken only when some lane of the warp needs them.
 template <int PL, int QW>
-__device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<PL> &c, int i, int j0, int lane,
+__device__ __forceinline__ void finish_row_codes(const TcParams &p, const FinishCols<PL> &c, int i, int j0, int lane,
                                            const long long (&qv)[PL], const long long (&qh)[PL], int4 ra, int Li,
                                            int si) {
   uint32_t cd[PL];
-  float fv[PL];
   uint32_t slow = 0u, keep = 0u;
-  const int rex = (p.out_f32 && p.re) ? p.re[i] : 0;
 #pragma unroll
   for (int q = 0; q < PL; ++q) {
-    fv[q] = 0.0f;
     if (QW == 1) {
-      // the fp32 hand-off straight from the exact sum (bp32_value_i64); the
-      // code itself only when it is stored or the value needs the field route
-      double v = 0.0;
-      const bool direct = p.out_f32 && bp32_value_i64(qv[q], Li + c.Lj[q], rex + c.fe[q], v);
-      if (p.out || !direct) cd[q] = bp32_from_i64(qv[q], Li + c.Lj[q]);
-      if (p.out_f32)
-        fv[q] = direct ? __double2float_rn(v + (double)c.fb[q]) : bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
+      cd[q] = bp32_from_i64(qv[q], Li + c.Lj[q]);
     } else {
       const __int128 Q = (__int128)qv[q] + ((__int128)qh[q] << 28);
       const bool neg = Q < 0;
       const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
       cd[q] = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, Li + c.Lj[q]);
-      if (p.out_f32) fv[q] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
     }
     const bool plain = si == -1 && c.sj[q] == -1 && ra.z != 0 && c.bz[q] && ra.x + c.bx[q] + 96 >= 0 &&
                        (ra.y - ra.x) + c.bw[q] <= 127;
@@ -708,7 +698,6 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
         const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
         cd[q] = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
       }
-      if (p.out_f32) fv[q] = bp32_f32_out(cd[q], rex + c.fe[q], c.fb[q]);
       keep |= 1u << q;
     }
   }
@@ -718,12 +707,6 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
     for (int q = 0; q < PL; ++q)
       if ((keep >> q) & 1u) orow[q * 32] = cd[q];
   }
-  if (p.out_f32) {
-    float *frow = p.out_f32 + (size_t)i * p.ldf + j0 + lane;
-#pragma unroll
-    for (int q = 0; q < PL; ++q)
-      if ((keep >> q) & 1u) frow[q * 32] = fv[q];
-  }
   for (int e = 0; e < p.n_extra; ++e) {
     uint32_t *erow = p.extra_out[e] + (size_t)i * p.ldo + p.extra_col0 + j0 + lane;
 #pragma unroll
@@ -732,7 +715,94 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
   }
 }
 
-template <int MM, int BN, int QW>
+template <int PL, int QW>
+__device__ __forceinline__ void finish_row_f32(const TcParams &p, const FinishCols<PL> &c, int i, int j0, int lane,
+                                           const long long (&qv)[PL], const long long (&qh)[PL], int4 ra, int Li,
+                                           int si) {
+  uint32_t slow = 0u;
+  const int rex = (p.out_f32 && p.re) ? p.re[i] : 0;
+  uint32_t *orow = p.out ? p.out + (size_t)i * p.ldo + j0 + lane : nullptr;
+  float *frow = p.out_f32 ? p.out_f32 + (size_t)i * p.ldf + j0 + lane : nullptr;
+  // one output's stores: its code (output and extra outputs) and fp32 hand-off
+  auto put = [&](int q, uint32_t code, float f) {
+    if (orow) orow[q * 32] = code;
+    if (frow) frow[q * 32] = f;
+    for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j0 + lane + q * 32] = code;
+  };
+  // plain outputs (no tail correction, nonzero row and column, inside the
+  // exact window) are rounded and stored at once; the others are marked
+#pragma unroll
+  for (int q = 0; q < PL; ++q) {
+    if (!c.jv[q]) continue;
+    const bool plain = si == -1 && c.sj[q] == -1 && ra.z != 0 && c.bz[q] && ra.x + c.bx[q] + 96 >= 0 &&
+                       (ra.y - ra.x) + c.bw[q] <= 127;
+    if (!plain) {
+      slow |= 1u << q;
+      continue;
+    }
+    const int L = Li + c.Lj[q];
+    uint32_t code = 0u;
+    float f = 0.0f;
+    if (QW == 1) {
+      // the fp32 hand-off straight from the exact sum (bp32_value_i64) when the
+      // code is not stored; otherwise from the code
+      double v;
+      if (frow && !orow && p.n_extra == 0 && bp32_value_i64(qv[q], L, rex + c.fe[q], v)) {
+        f = __double2float_rn(v + (double)c.fb[q]);
+      } else {
+        code = bp32_from_i64(qv[q], L);
+        if (frow) f = bp32_f32_out(code, rex + c.fe[q], c.fb[q]);
+      }
+    } else {
+      const __int128 Q = (__int128)qv[q] + ((__int128)qh[q] << 28);
+      const bool neg = Q < 0;
+      const unsigned __int128 m = neg ? (unsigned __int128)0 - (unsigned __int128)Q : (unsigned __int128)Q;
+      code = bp32_from_mag(neg, (uint64_t)(m >> 64), (uint64_t)m, L);
+      if (frow) f = bp32_f32_out(code, rex + c.fe[q], c.fb[q]);
+    }
+    put(q, code, f);
+  }
+  // the others (a tail row or column, a zero row or column, outside the exact
+  // window): all their tail corrections are loaded at once, then combined in
+  // 128 bits (finish_code's rule)
+  if (__any_sync(0xFFFFFFFFu, slow != 0u)) {
+    ulonglong2 ca[PL], cb[PL];
+#pragma unroll
+    for (int q = 0; q < PL; ++q) {
+      const bool sb = (slow >> q) & 1u;
+      const ulonglong2 z2 = make_ulonglong2(0ull, 0ull);
+      ca[q] = (sb && si >= 0) ? p.CA[(size_t)si * p.N + j0 + q * 32 + lane] : z2;
+      cb[q] = (sb && c.sj[q] >= 0) ? p.CB[(size_t)c.sj[q] * p.M + i] : z2;
+    }
+#pragma unroll
+    for (int q = 0; q < PL; ++q) {
+      if (!((slow >> q) & 1u)) continue;
+      uint32_t code = 0u;
+      if (ra.z && c.bz[q]) {
+        // tc_exact: inside the 128-bit window, no overflowed tail list
+        if (ra.x + c.bx[q] + 96 < 0 || (ra.y - ra.x) + c.bw[q] > 127 || si == -2 || c.sj[q] == -2)
+          continue;   // left to k_tc_fixup
+        const __int128 Q = (__int128)qv[q] + (QW == 2 ? ((__int128)qh[q] << 28) : (__int128)0);
+        const int sh = (Li - ra.x) + (c.Lj[q] - c.bx[q]);
+        const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
+        code = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
+      }
+      put(q, code, frow ? bp32_f32_out(code, rex + c.fe[q], c.fb[q]) : 0.0f);
+    }
+  }
+}
+
+// Codes only (the kernels without an fp32 output keep this lean form: they
+// run beside a GEMM segment at 64 registers) or with the fp32 hand-off.
+template <int PL, int QW, bool F32>
+__device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<PL> &c, int i, int j0, int lane,
+                                           const long long (&qv)[PL], const long long (&qh)[PL], int4 ra, int Li,
+                                           int si) {
+  if (F32) finish_row_f32<PL, QW>(p, c, i, j0, lane, qv, qh, ra, Li, si);
+  else finish_row_codes<PL, QW>(p, c, i, j0, lane, qv, qh, ra, Li, si);
+}
+
+template <int MM, int BN, int QW, bool F32>
 __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, int parts) {
   static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
   constexpr int PL = BN / 32;
@@ -759,7 +829,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
         for (int j = j0 + lane; j < min(j0 + BN, p.N); j += 32) {
           const size_t i = (size_t)(tm * MM + r);
           if (p.out) p.out[i * p.ldo + j] = 0x80000000u;
-          if (p.out_f32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
+          if (F32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
           for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][i * p.ldo + p.extra_col0 + j] = 0x80000000u;
         }
       continue;
@@ -775,8 +845,8 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
       c.bx[q] = rb.x;
       c.bw[q] = (rb.y - rb.x) + cl2 + 3;
       c.bz[q] = rb.z != 0;
-      c.fe[q] = (c.jv[q] && p.ce) ? p.ce[j] : 0;
-      c.fb[q] = (c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
+      c.fe[q] = (F32 && c.jv[q] && p.ce) ? p.ce[j] : 0;
+      c.fb[q] = (F32 && c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
     }
     // rows of this item that exist, relative to the tile; a warp's rows are
     // r0 + 8k
@@ -788,7 +858,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
 #pragma unroll 1
         for (int q = 0; q < PL; ++q) {
           const int j = j0 + q * 32 + lane;
-          if (j < p.N) finish_general<QW>(p, qt + (size_t)r * BN + q * 32, PT, tm * MM + r, j);
+          if (j < p.N) finish_general<QW, F32>(p, qt + (size_t)r * BN + q * 32, PT, tm * MM + r, j);
         }
       continue;
     }
@@ -821,7 +891,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
         const int4 ra = nra;
         const int Li = nL, si = ns;
         if (r + 8 < rend) fetch(r + 8);
-        finish_row<PL, QW>(p, c, tm * MM + r, j0, lane, cq, chh, ra, Li, si);
+        finish_row<PL, QW, F32>(p, c, tm * MM + r, j0, lane, cq, chh, ra, Li, si);
       }
       continue;
     }
@@ -839,7 +909,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, in
           }
       }
       const int i = tm * MM + r;
-      finish_row<PL, QW>(p, c, i, j0, lane, cq, chh, p.sta[i], p.LA[i], p.slotA[i]);
+      finish_row<PL, QW, F32>(p, c, i, j0, lane, cq, chh, p.sta[i], p.LA[i], p.slotA[i]);
     }
   }
   if (p.n_extra) __threadfence_system();
@@ -870,8 +940,8 @@ size_t finish_staged_smem() {
   return (size_t)kFinStages * QW * 8 * BN * sizeof(long long) + kFinStages * sizeof(uint64_t);
 }
 
-template <int MM, int BN, int QW>
-__global__ void __launch_bounds__(256, 4) k_tc_finish_staged(TcParams p, int ntiles, int parts) {
+template <int MM, int BN, int QW, bool F32>
+__global__ void __launch_bounds__(256, F32 ? 3 : 4) k_tc_finish_staged(TcParams p, int ntiles, int parts) {
   static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
   constexpr int PL = BN / 32;
   constexpr size_t PT = (size_t)MM * BN;              // words of one plane of a tile
@@ -898,7 +968,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish_staged(TcParams p, int nti
         for (int j = tn * BN + lane; j < min(tn * BN + BN, p.N); j += 32) {
           const size_t i = (size_t)(tm * MM + r);
           if (p.out) p.out[i * p.ldo + j] = 0x80000000u;
-          if (p.out_f32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
+          if (F32) p.out_f32[i * p.ldf + j] = __uint_as_float(0x7FC00000u);
           for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][i * p.ldo + p.extra_col0 + j] = 0x80000000u;
         }
     }
@@ -945,8 +1015,8 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish_staged(TcParams p, int nti
         c.bx[q] = rb.x;
         c.bw[q] = (rb.y - rb.x) + cl2 + 3;
         c.bz[q] = rb.z != 0;
-        c.fe[q] = (c.jv[q] && p.ce) ? p.ce[j] : 0;
-        c.fb[q] = (c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
+        c.fe[q] = (F32 && c.jv[q] && p.ce) ? p.ce[j] : 0;
+        c.fb[q] = (F32 && c.jv[q] && p.bias) ? p.bias[j] : 0.0f;
       }
     }
     const int st = (int)(g % kFinStages);
@@ -975,7 +1045,7 @@ __global__ void __launch_bounds__(256, 4) k_tc_finish_staged(TcParams p, int nti
         qh[q] = (QW == 2 && c.jv[q]) ? row[8 * BN + q * 32] : 0ll;
       }
       const int i = tm * MM + r;
-      finish_row<PL, QW>(p, c, i, j0, lane, qv, qh, p.sta[i], p.LA[i], p.slotA[i]);
+      finish_row<PL, QW, F32>(p, c, i, j0, lane, qv, qh, p.sta[i], p.LA[i], p.slotA[i]);
     }
     __syncthreads();   // every warp is done with buffer st
     if (s_abort) break;
@@ -1754,12 +1824,14 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
     }
     int g = 1, parts = 1;
     finish_shape<C::MM>(seg[k].n, on_s ? grid_finish : std::min(grid_finish, 2 * sm_count()), g, parts);
+    const size_t ssm = finish_staged_smem<C::MM, C::BN, C::QW>();
     if (on_s && p.split == 1 && !p.quire) {
       // the SMs are free: stream the sums through shared memory
-      k_tc_finish_staged<C::MM, C::BN, C::QW>
-          <<<g, 256, finish_staged_smem<C::MM, C::BN, C::QW>(), fs>>>(p, seg[k].n, parts);
+      if (p.out_f32) k_tc_finish_staged<C::MM, C::BN, C::QW, true><<<g, 256, ssm, fs>>>(p, seg[k].n, parts);
+      else k_tc_finish_staged<C::MM, C::BN, C::QW, false><<<g, 256, ssm, fs>>>(p, seg[k].n, parts);
     } else {
-      k_tc_finish<C::MM, C::BN, C::QW><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
+      if (p.out_f32) k_tc_finish<C::MM, C::BN, C::QW, true><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
+      else k_tc_finish<C::MM, C::BN, C::QW, false><<<g, 256, 0, fs>>>(p, seg[k].n, parts);
     }
     rc = check_launch("tc_finish");
   }

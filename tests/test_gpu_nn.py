@@ -133,7 +133,7 @@ def test_qwen_full_size_forward_row_subsample(orc):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("K", [1, 2, 3, 20, 21, 576, 896, 4864, 12289, 12292])
+@pytest.mark.parametrize("K", [1, 2, 3, 20, 21, 576, 896, 1536, 4864, 9216, 9217, 12292])
 def test_w8a8_encode_rows_matches_reference_rule(orc, K):
     """ops.w8a8_encode_rows: per-row exponents equal recommended_exponents
     (reference/bposit_quantize.py:46-63, numpy on the host) and the codes equal
