@@ -69,6 +69,11 @@ __device__ __forceinline__ void hist_add(uint32_t *hist, uint32_t bin, bool acti
 }
 
 
+// Shared-memory slice of one warp, in 4-byte words, rounded to 16-byte units:
+// the staged row (K floats) and the candidate list (K / 4 + 1 keys).
+__host__ __device__ __forceinline__ int w8a8_row_floats(int K) { return (K + 3) & ~3; }
+__host__ __device__ __forceinline__ int w8a8_list_words(int K) { return (K / 4 + 1 + 3) & ~3; }
+
 // Truncating bp8 code of x * 2^-e from the fp32 bits of x, with integer
 // exponent arithmetic: the scaled value's biased exponent E - e + 127
 // (clamped to the table's [1, 255], which saturates or flushes exactly as the
@@ -111,7 +116,7 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
                                                   int32_t *__restrict__ exps, uint8_t *__restrict__ codes) {
   __shared__ uint2 tbl[256];          // truncating bp8 quantize table (bp8_qentry)
   __shared__ uint32_t hists[kWarps][256];
-  extern __shared__ float s_rows[];   // per warp: [K] row (STAGED), [K / 4 + 1] candidate keys
+  extern __shared__ __align__(16) float s_rows[];   // per warp: [K] row (STAGED), [K / 4 + 1] candidate keys
   for (int i = threadIdx.x; i < 256; i += blockDim.x) {
     QEntry q = bp8_qentry(i, false);
     tbl[i] = make_uint2(q.lo_sh, q.thr);
@@ -120,9 +125,11 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const uint32_t lt_mask = (1u << lane) - 1u;
   uint32_t *hist = hists[warp];
-  const size_t per_warp = (STAGED ? (size_t)K : 0) + (size_t)(K / 4 + 1);
+  // per warp: the row, then the candidate list, each a whole number of
+  // 16-byte units so that every warp's row is float4-aligned
+  const size_t rowf = STAGED ? (size_t)w8a8_row_floats(K) : 0, per_warp = rowf + (size_t)w8a8_list_words(K);
   float *srow = STAGED ? s_rows + (size_t)warp * per_warp : nullptr;
-  uint32_t *cand = reinterpret_cast<uint32_t *>(s_rows + (size_t)warp * per_warp + (STAGED ? K : 0));
+  uint32_t *cand = reinterpret_cast<uint32_t *>(s_rows + (size_t)warp * per_warp + rowf);
   const double pos = 0.95 * (double)(K - 1);
   const int lo = (int)floor(pos);
   const double t = pos - (double)lo;
@@ -276,8 +283,8 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
 int launch_w8a8_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *codes, cudaStream_t s) {
   if (rows == 0 || K == 0) return kOk;
   const bool vec = (K % 4) == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)codes & 3u) == 0;
-  const size_t list = (size_t)(K / 4 + 1) * sizeof(uint32_t);   // candidate list per warp
-  const size_t staged = (size_t)K * sizeof(float) + list;
+  const size_t list = (size_t)w8a8_list_words(K) * sizeof(uint32_t);   // candidate list per warp
+  const size_t staged = (size_t)w8a8_row_floats(K) * sizeof(float) + list;
   if (staged <= kStageBytes) {
     // rows staged in shared memory: as many warps per block as the budget allows
     const int w = std::max(1, std::min(kWarps, (int)(kStageBytes / staged)));
