@@ -155,7 +155,12 @@ int bp_bp32_to_bp16(const uint32_t *codes, size_t n, uint16_t *out, void *stream
  * [rows, ceil(K/group)].  If out_quire is non-NULL, the raw quires are also
  * written as [M, N, quire_limbs] (quire_limbs 8, 12 or 16; truncated two's
  * complement).  algo: 0 = auto, 1 = CUDA cores, 2 = tensor cores (tcgen05; paired SMs,
- * cta_group::2, when M > 128), 3 = tensor cores with one SM per output tile.
+ * cta_group::2, when M > 128), 3 = tensor cores with one SM per output tile,
+ * 4 / 5 = tensor cores (paired) with the narrow / wide bp8 digit-plane form
+ * (2 base-256 planes over a 15-bit window, or 3 base-128 planes over 20 bits;
+ * elements below a row's window are corrected on CUDA cores).  Algos 0, 2 and
+ * 3 take the narrow form for unscaled bp8 with K >= 16384, else the wide one;
+ * bp16 always uses 4 base-128 planes.  Every algo gives the same result.
  * workspace: device memory of at least bp_quire_gemm_workspace_size() bytes,
  * 256-byte aligned; NULL lets the library take it stream-ordered from the
  * device's default memory pool for the duration of the call.

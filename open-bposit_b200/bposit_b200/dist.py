@@ -20,6 +20,9 @@ Two ways to all-gather the blocks:
 """
 from __future__ import annotations
 
+import contextlib
+import threading
+import time
 from dataclasses import dataclass
 from typing import Callable, Optional
 
@@ -142,6 +145,89 @@ def choose_grid(world: int, M: int, N: int, K: int, fmt: int = 8, wave: int = 74
     return best
 
 
+class CallWatchdog:
+    """Host deadline for multi-GPU calls.
+
+    `with wd.guard("gemm"): ...` runs the block under a deadline of
+    `deadline_s` seconds.  A monitor thread that sees a guarded block outlive
+    it calls `on_timeout(what)` -- by default it aborts the process group
+    (`ProcessGroup.abort()`, which ends a collective still waiting on a rank
+    that died or never joined with an error on this rank) -- and trips the
+    watchdog: the block, and every later guarded block, raises BpositError.
+    With `sync=True` the guard also waits for the current CUDA stream, so the
+    deadline covers the call's device work (kernels, peer stores, NCCL).
+    Kernel waits have their own bounds; this covers a peer process that is
+    gone.
+    """
+
+    def __init__(self, deadline_s: float, on_timeout: Optional[Callable[[str], None]] = None, group=None,
+                 sync: bool = False):
+        if deadline_s <= 0:
+            raise ValueError("deadline_s must be positive")
+        self.deadline_s = float(deadline_s)
+        self.group = group
+        self.sync = sync
+        self.on_timeout = on_timeout if on_timeout is not None else self._abort_group
+        self.tripped: Optional[str] = None
+        self._cv = threading.Condition()
+        self._armed: Optional[tuple[str, float]] = None   # (what, deadline on time.monotonic)
+        self._closed = False
+        self._thread = threading.Thread(target=self._run, name="bposit-watchdog", daemon=True)
+        self._thread.start()
+
+    def _abort_group(self, what: str) -> None:
+        pg = self.group if self.group is not None else dist.distributed_c10d._get_default_group()
+        pg.abort()
+
+    def _run(self) -> None:
+        with self._cv:
+            while not self._closed:
+                if self._armed is None:
+                    self._cv.wait()
+                    continue
+                what, due = self._armed
+                left = due - time.monotonic()
+                if left > 0:
+                    self._cv.wait(timeout=left)
+                    continue
+                self._armed = None
+                self.tripped = f"{what} exceeded its {self.deadline_s:g} s deadline"
+                try:
+                    self.on_timeout(what)
+                except Exception as exc:   # the trip stands even if the abort fails
+                    self.tripped += f" (abort failed: {exc})"
+
+    @contextlib.contextmanager
+    def guard(self, what: str = "call"):
+        from ._lib import BP_ECUDA, BpositError
+        if self.tripped:
+            raise BpositError(BP_ECUDA, f"watchdog tripped earlier: {self.tripped}")
+        with self._cv:
+            self._armed = (what, time.monotonic() + self.deadline_s)
+            self._cv.notify()
+        err: Optional[BaseException] = None
+        try:
+            yield self
+            if self.sync and torch.cuda.is_available():
+                torch.cuda.current_stream().synchronize()
+        except BaseException as exc:   # a collective that the abort ended
+            err = exc
+        finally:
+            with self._cv:
+                self._armed = None
+                self._cv.notify()
+        if self.tripped:
+            raise BpositError(BP_ECUDA, f"watchdog: {self.tripped}") from err
+        if err is not None:
+            raise err
+
+    def close(self) -> None:
+        with self._cv:
+            self._closed = True
+            self._cv.notify()
+        self._thread.join(timeout=5)
+
+
 class FusedShardedQuireGemm:
     """N-sharded quire GEMM with the all-gather fused into the GEMM's finish kernel.
 
@@ -158,9 +244,12 @@ class FusedShardedQuireGemm:
     """
 
     def __init__(self, M: int, N: int, device, group=None, fmt: int = 8, algo: int = 0,
-                 group_size: int = 128, grid: Optional[tuple[int, int]] = None, K: Optional[int] = None):
+                 group_size: int = 128, grid: Optional[tuple[int, int]] = None, K: Optional[int] = None,
+                 deadline_s: Optional[float] = None):
         from . import ops
         self.group = group
+        # optional host deadline per call (CallWatchdog, synchronizing)
+        self.watchdog = CallWatchdog(deadline_s, group=group, sync=True) if deadline_s else None
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if self.world - 1 > 8:
@@ -200,6 +289,14 @@ class FusedShardedQuireGemm:
         if A_block.shape[0] != m1 - m0 or B_block.shape[0] != n1 - n0:
             raise ValueError(f"rank {self.rank} owns rows [{m0}, {m1}) of A and [{n0}, {n1}) of B, got "
                              f"{A_block.shape[0]} and {B_block.shape[0]}")
+        if self.watchdog is not None:
+            with self.watchdog.guard("FusedShardedQuireGemm"):
+                return self._call(A_block, B_block, sa, sb)
+        return self._call(A_block, B_block, sa, sb)
+
+    def _call(self, A_block, B_block, sa, sb) -> torch.Tensor:
+        from . import ops
+        m0, m1, n0, n1 = self.block
         if self.world > 1:
             dist.all_reduce(self.flag, group=self.group)
         if m1 > m0 and n1 > n0:
@@ -219,6 +316,8 @@ class FusedShardedQuireGemm:
         from . import ops
         if self.result is None:
             return
+        if self.watchdog is not None:
+            self.watchdog.close()
         torch.cuda.synchronize(self.device)
         if self.world > 1:
             dist.barrier(group=self.group)

@@ -192,7 +192,7 @@ int bp_quire_gemm(int fmt, const void *A, const void *B, int M, int N, int K, co
   g_err[0] = 0;
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm: negative size");
-  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm: algo must be 0, 1, 2 or 3");
+  if (algo < 0 || algo > 5) return set_error(kEInval, "bp_quire_gemm: algo must be 0 to 5");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm: group must be > 0 with scales");
   if (ldo < N) return set_error(kEInval, "bp_quire_gemm: ldo (%lld) < N (%d)", (long long)ldo, N);
   if (out_quire && quire_limbs != 8 && quire_limbs != 12 && quire_limbs != 16)
@@ -229,7 +229,7 @@ int bp_quire_gemm_f32(int fmt, const void *A, const void *B, int M, int N, int K
   g_err[0] = 0;
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_f32: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_f32: negative size");
-  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_f32: algo must be 0, 1, 2 or 3");
+  if (algo < 0 || algo > 5) return set_error(kEInval, "bp_quire_gemm_f32: algo must be 0 to 5");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_f32: group must be > 0 with scales");
   if (ldf < N) return set_error(kEInval, "bp_quire_gemm_f32: ldf (%lld) < N (%d)", (long long)ldf, N);
   if (out_bp32 && ldo < N) return set_error(kEInval, "bp_quire_gemm_f32: ldo (%lld) < N (%d)", (long long)ldo, N);
@@ -274,7 +274,7 @@ int bp_quire_gemm_multi(int fmt, const void *A, const void *B, int M, int N, int
     if (!peer_outs[e]) return set_error(kEInval, "bp_quire_gemm_multi: null peer output %d", e);
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_multi: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_multi: negative size");
-  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_multi: algo must be 0, 1, 2 or 3");
+  if (algo < 0 || algo > 5) return set_error(kEInval, "bp_quire_gemm_multi: algo must be 0 to 5");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_multi: group must be > 0 with scales");
   if (ldo < N) return set_error(kEInval, "bp_quire_gemm_multi: ldo (%lld) < N (%d)", (long long)ldo, N);
   if (M == 0 || N == 0) return kOk;
@@ -317,7 +317,7 @@ int bp_quire_gemm_host(int fmt, const void *A, const void *B, int M, int N, int 
   g_err[0] = 0;
   if (fmt != 8 && fmt != 16) return set_error(kEFmt, "bp_quire_gemm_host: fmt must be 8 or 16 (got %d)", fmt);
   if (M < 0 || N < 0 || K < 0) return set_error(kEInval, "bp_quire_gemm_host: negative size");
-  if (algo < 0 || algo > 3) return set_error(kEInval, "bp_quire_gemm_host: algo must be 0, 1, 2 or 3");
+  if (algo < 0 || algo > 5) return set_error(kEInval, "bp_quire_gemm_host: algo must be 0 to 5");
   if ((sa || sb) && group <= 0) return set_error(kEInval, "bp_quire_gemm_host: group must be > 0 with scales");
   if (ldo < N) return set_error(kEInval, "bp_quire_gemm_host: ldo (%lld) < N (%d)", (long long)ldo, N);
   if (M == 0 || N == 0) return kOk;

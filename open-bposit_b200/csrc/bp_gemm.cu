@@ -9,9 +9,9 @@
 namespace bp {
 
 int launch_gemm_simt(const GemmArgs &a, int4 *sta, int4 *stb, cudaStream_t s);
-int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, int algo,
                    int a_mode, cudaStream_t s);
-size_t gemm_tc_workspace(int fmt, int M, int N, int K);
+size_t gemm_tc_workspace(int fmt, int M, int N, int K, int algo);
 bool gemm_tc_supported(int fmt, int M, int N, int K);
 
 namespace {
@@ -83,7 +83,7 @@ static size_t stats_bytes(int M, int N) { return align_up((size_t)(M + N) * size
 static bool use_tc(const GemmArgs &a, int algo) {
   if (algo == 1) return false;
   if (!gemm_tc_supported(a.fmt, a.M, a.N, a.K)) return false;
-  if (algo == 2 || algo == 3) return true;
+  if (algo >= 2) return true;
   // auto: tensor cores once there is enough work to fill the machine
   return (long long)a.M * a.N >= 128LL * 128 * 8 && a.K >= 64;
 }
@@ -92,7 +92,7 @@ bool gemm_uses_tc(const GemmArgs &a, int algo) { return use_tc(a, algo); }
 
 size_t gemm_workspace_size(int fmt, int M, int N, int K, int algo) {
   size_t ws = stats_bytes(M, N);
-  if (algo != 1 && gemm_tc_supported(fmt, M, N, K)) ws += gemm_tc_workspace(fmt, M, N, K);
+  if (algo != 1 && gemm_tc_supported(fmt, M, N, K)) ws += gemm_tc_workspace(fmt, M, N, K, algo);
   return ws;
 }
 
@@ -102,9 +102,9 @@ int launch_quire_gemm(const GemmArgs &a, int algo, void *ws, size_t ws_bytes, cu
   int4 *sta = (int4 *)ws;
   int4 *stb = sta + a.M;
   if (use_tc(a, algo)) {   // the tensor-core prep computes the row statistics itself
-    size_t need = gemm_tc_workspace(a.fmt, a.M, a.N, a.K);
+    size_t need = gemm_tc_workspace(a.fmt, a.M, a.N, a.K, algo);
     if (ws_bytes < need_stats + need) return set_error(kEWorkspace, "quire_gemm: workspace too small");
-    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo == 3, a_mode, s);
+    return launch_gemm_tc(a, sta, stb, (char *)ws + need_stats, ws_bytes - need_stats, algo, a_mode, s);
   }
   if (a_mode == 2 || a_mode == 3) return kOk;   // the CUDA-core path prepares nothing ahead
   int rc = launch_row_stats2(a.fmt, a.A, a.M, a.sa, sta, a.B, a.N, a.sb, stb, a.K, a.group, s);

@@ -43,6 +43,7 @@
 #include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "bp_gemm_common.cuh"
 #include "bp_internal.cuh"
@@ -65,15 +66,22 @@ constexpr int BIG = 1 << 20;                     // offset that makes max-reduct
 // Tile configuration.  PAIR: the 2-SM form -- a cluster of two CTAs issues
 // M = 256 MMAs (tcgen05 cta_group::2); each CTA holds its own 128 rows of A and
 // half of the tile's B rows, and owns 128 rows of the output tile.
+// S = 2 is the narrow bp8 form: two base-256 digits (low digit in [-128, 127])
+// over a 15-bit main window; a bp8 significand has at most 4 bits, so |X| <=
+// 2^15 - 2^11 and the top digit stays within [-120, 120].  S = 3 (bp8) and
+// S = 4 (bp16) are the wide forms, base-128 digits (low digits in [-64, 63]).
 template <int S, bool PAIR = false>
 struct Cfg {
-  static constexpr int BN = S == 3 ? 96 : 64;
+  static constexpr int DB = S == 2 ? 8 : 7;        // bits per digit
+  static constexpr int BN = S == 2 ? 128 : (S == 3 ? 96 : 64);
   static constexpr int BNB = PAIR ? BN / 2 : BN;   // B rows (tile columns) staged by one CTA
   static constexpr int MM = PAIR ? 2 * BM : BM;    // rows of one MMA
   static constexpr int D = 2 * S - 1;
-  static constexpr int SPAN = 7 * S - 1;
-  static constexpr int TOP = (1 << (SPAN - 7 * (S - 1))) + 1;   // bound of |top digit|
-  static constexpr long long digit_max(int s) { return s == S - 1 ? TOP : 64; }
+  static constexpr int SPAN = S == 2 ? 15 : 7 * S - 1;
+  static constexpr int HALF = 1 << (DB - 1);       // low digits lie in [-HALF, HALF)
+  static constexpr int TOP = S == 2 ? ((1 << 15) - (1 << 11) + HALF) >> 8
+                                    : (1 << (SPAN - 7 * (S - 1))) + 1;   // bound of |top digit|
+  static constexpr long long digit_max(int s) { return s == S - 1 ? TOP : HALF; }
   static constexpr long long diag_bound(int d) {
     long long b = 0;
     for (int s = 0; s < S; ++s)
@@ -91,11 +99,13 @@ struct Cfg {
   // Q = sum_d acc_d 128^d with |Q| < 2^31 * 2^28 * 1.01 < 2^60; bp16 (D = 7)
   // two, lo = sum_{d<4} acc_d 128^d (< 2^53) and hi = sum_{d>=4} acc_d
   // 128^(d-4) (< 2^46), Q = lo + hi * 2^28, which may need up to 74 bits.
+  // S = 2: Q = acc_0 + acc_1 2^8 + acc_2 2^16, |Q| < 2^48, one word.
   static constexpr int QW = D <= 5 ? 1 : 2;
   static constexpr int A_BYTES = S * BM * BK;
   static constexpr int B_BYTES = S * BNB * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR ? (S == 3 ? 6 : 5) : (BK == 128 ? 2 : (S == 3 ? 5 : 4));
+  static constexpr int STAGES = PAIR ? (S == 2 ? 8 : (S == 3 ? 6 : 5))
+                                     : (BK == 128 ? 2 : (S == 2 ? 6 : (S == 3 ? 5 : 4)));
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + BN * 32;
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                                     ((uint32_t)(MM >> 4) << 24);
@@ -563,8 +573,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       long long lo = 0, hi = 0;
 #pragma unroll
       for (int d = 0; d < C::D; ++d) {
-        if (QW == 1 || d < 4) lo += (long long)(int)v[d][jj] * (1ll << (7 * d));
-        else hi += (long long)(int)v[d][jj] * (1ll << (7 * (d - 4)));
+        if (QW == 1 || d < 4) lo += (long long)(int)v[d][jj] * (1ll << (C::DB * d));
+        else hi += (long long)(int)v[d][jj] * (1ll << (C::DB * (d - 4)));
       }
       stg[lane * (C::BN + 1) + c0 + jj] = lo;
       if (QW == 2) stg[STG + lane * (C::BN + 1) + c0 + jj] = hi;
@@ -635,6 +645,23 @@ __device__ __forceinline__ void finish_general(const TcParams &p, const long lon
   for (int e = 0; e < p.n_extra; ++e) p.extra_out[e][(size_t)i * p.ldo + p.extra_col0 + j] = code;
 }
 
+// The bposit32 of Q * 2^sh + ca + cb (units of 2^lsb_exp; ca, cb 128-bit tail
+// corrections): int64 when every part lies in [-2^61, 2^61) (the narrow form's
+// usual case: sums of a few tail elements), else the 128-bit rule.
+template <int QW>
+__device__ __forceinline__ uint32_t finish_with_tails(long long qv, long long qh, int sh, ulonglong2 ca,
+                                                      ulonglong2 cb, int lsb_exp) {
+  if (QW == 1 && sh <= 61) {
+    const long long a = (long long)ca.x, b = (long long)cb.x;
+    if ((long long)ca.y == (a >> 63) && (long long)cb.y == (b >> 63) && (a >> 61) == (a >> 63) &&
+        (b >> 61) == (b >> 63) && (qv >> (61 - sh)) == (qv >> 63))
+      return bp32_from_i64((long long)((unsigned long long)qv << sh) + a + b, lsb_exp);
+  }
+  const __int128 Q = (__int128)qv + (QW == 2 ? ((__int128)qh << 28) : (__int128)0);
+  const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca) + u128(cb);
+  return write_fast_output(tot, lsb_exp + 96, nullptr, nullptr, 0);
+}
+
 // Per-column state of a finish item, one entry per column a lane owns: lsb
 // base, tail slot, min lsb exponent, exact-window width share (max binade - min
 // lsb + ceil log2 K + 3), valid and nonzero flags.
@@ -693,10 +720,8 @@ __device__ __forceinline__ void finish_row_codes(const TcParams &p, const Finish
         // tc_exact: inside the 128-bit window, no overflowed tail list
         if (ra.x + c.bx[q] + 96 < 0 || (ra.y - ra.x) + c.bw[q] > 127 || si == -2 || c.sj[q] == -2)
           continue;   // left to k_tc_fixup
-        const __int128 Q = (__int128)qv[q] + (QW == 2 ? ((__int128)qh[q] << 28) : (__int128)0);
-        const int sh = (Li - ra.x) + (c.Lj[q] - c.bx[q]);
-        const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
-        cd[q] = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
+        cd[q] = finish_with_tails<QW>(qv[q], qh[q], (Li - ra.x) + (c.Lj[q] - c.bx[q]), ca[q], cb[q],
+                                      ra.x + c.bx[q]);
       }
       keep |= 1u << q;
     }
@@ -782,10 +807,8 @@ __device__ __forceinline__ void finish_row_f32(const TcParams &p, const FinishCo
         // tc_exact: inside the 128-bit window, no overflowed tail list
         if (ra.x + c.bx[q] + 96 < 0 || (ra.y - ra.x) + c.bw[q] > 127 || si == -2 || c.sj[q] == -2)
           continue;   // left to k_tc_fixup
-        const __int128 Q = (__int128)qv[q] + (QW == 2 ? ((__int128)qh[q] << 28) : (__int128)0);
-        const int sh = (Li - ra.x) + (c.Lj[q] - c.bx[q]);
-        const unsigned __int128 tot = ((unsigned __int128)Q << sh) + u128(ca[q]) + u128(cb[q]);
-        code = write_fast_output(tot, ra.x + c.bx[q] + 96, nullptr, nullptr, 0);
+        code = finish_with_tails<QW>(qv[q], qh[q], (Li - ra.x) + (c.Lj[q] - c.bx[q]), ca[q], cb[q],
+                                     ra.x + c.bx[q]);
       }
       put(q, code, frow ? bp32_f32_out(code, rex + c.fe[q], c.fb[q]) : 0.0f);
     }
@@ -1141,6 +1164,7 @@ template <int FMT, int S>
 __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp opB, int K, int Kp, int G,
                                                  int group, int pool_cap) {
   constexpr int SPAN = Cfg<S>::SPAN;
+  constexpr int DB = Cfg<S>::DB, HALF = Cfg<S>::HALF, DMASK = (1 << DB) - 1;   // digit base 2^DB
   constexpr int EPT = FMT == 8 ? 16 : 8;   // elements per 16-byte load
   constexpr bool LUT_DIGITS = FMT == 8 && S <= 4;
   __shared__ int s_tail[TAILCAP];
@@ -1288,9 +1312,9 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
             int x = dec_m(t) * (1 << (dec_lsb(t) - L));
 #pragma unroll
             for (int s = 0; s < S - 1; ++s) {
-              int dg = ((x + 64) & 127) - 64;
+              int dg = ((x + HALF) & DMASK) - HALF;
               v |= ((uint32_t)(uint8_t)dg) << (8 * s);
-              x = (x - dg) >> 7;
+              x = (x - dg) >> DB;
             }
             v |= ((uint32_t)(uint8_t)x) << (8 * (S - 1));
           }
@@ -1399,9 +1423,9 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
           int t = x.m * (1 << (x.e - L));
 #pragma unroll
           for (int sd = 0; sd < S - 1; ++sd) {
-            int dg = ((t + 64) & 127) - 64;
+            int dg = ((t + HALF) & DMASK) - HALF;
             w[sd][q >> 2] |= ((uint32_t)(uint8_t)dg) << (8 * (q & 3));
-            t = (t - dg) >> 7;
+            t = (t - dg) >> DB;
           }
           w[S - 1][q >> 2] |= ((uint32_t)(uint8_t)t) << (8 * (q & 3));
         }
@@ -1505,6 +1529,175 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
   }
 }
 
+// K-major copies for the narrow form's corrections: codes [rows][K] (bp8) ->
+// [K][ldt] (ldt = rows rounded up to 16, padding columns zero), so that a tail
+// element's column of the other operand is one contiguous row.  64 x 64-byte
+// tiles: each thread transposes a 4 x 4 byte block in registers (byte
+// permutes), parks the four column words in shared memory, then stores 16
+// bytes of one output row.  Grid (ceil(K / 64), ceil(ldt / 64)).
+__global__ void __launch_bounds__(256) k_transpose_bp8(const uint8_t *__restrict__ src, int rows, int K,
+                                                       uint8_t *__restrict__ dst, int ldt) {
+  __shared__ uint32_t tw[64][17];   // [k][row / 4], one pad word
+  const int t = threadIdx.x;
+  const int k0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
+  const int br = t >> 4, bc = t & 15;   // 4 x 4 block: rows r0 + 4br.., columns k0 + 4bc..
+  const bool vec = (K & 3) == 0 && (((uintptr_t)src) & 3u) == 0;
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + 4 * br + i, k = k0 + 4 * bc;
+    uint32_t v = 0u;
+    if (r < rows) {
+      const uint8_t *row = src + (size_t)r * K;
+      if (vec && k + 4 <= K) {
+        v = *(const uint32_t *)(row + k);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (k + q < K) v |= (uint32_t)row[k + q] << (8 * q);
+      }
+    }
+    w[i] = v;
+  }
+  // column q of the block: byte q of each row word
+  const uint32_t a01 = __byte_perm(w[0], w[1], 0x5140), a23 = __byte_perm(w[2], w[3], 0x5140);
+  const uint32_t b01 = __byte_perm(w[0], w[1], 0x7362), b23 = __byte_perm(w[2], w[3], 0x7362);
+  tw[4 * bc + 0][br] = __byte_perm(a01, a23, 0x5410);
+  tw[4 * bc + 1][br] = __byte_perm(a01, a23, 0x7632);
+  tw[4 * bc + 2][br] = __byte_perm(b01, b23, 0x5410);
+  tw[4 * bc + 3][br] = __byte_perm(b01, b23, 0x7632);
+  __syncthreads();
+  const int kk = t >> 2, c = t & 3;   // output row k0 + kk, bytes r0 + 16c .. + 15
+  const int k = k0 + kk, r = r0 + 16 * c;
+  if (k < K && r < ldt)
+    *(uint4 *)(dst + (size_t)k * ldt + r) =
+        make_uint4(tw[kk][4 * c], tw[kk][4 * c + 1], tw[kk][4 * c + 2], tw[kk][4 * c + 3]);
+}
+
+// Tail corrections of the narrow form (bp8, unscaled), the same sums as
+// k_tc_corr read from the other operand's K-major copy:
+//   C[s][y] = sum over tail elements (x, k) of row x (slot s):  v(X[x,k]) * v(Y[y,k])
+// in units of 2^(la_x + la_y), skipping Y's own tail elements when YL is given.
+// A block takes a slot's tail list into shared memory (column k, mantissa,
+// lsb above la_x), then each thread owns kCorrCols consecutive y and reads
+// their codes of row k of Yt as one 8-byte word per tail element, kCorrTU
+// tail elements' words in flight at a time (the kernel runs beside the GEMM
+// and was bound by the latency of these loads).  The sums are int64 when the
+// largest term and the term count leave them exact (the row statistics bound
+// the shift), else 128-bit.
+constexpr int kCorrCols = 8, kCorrTU = 4, kCorrSpan = 256 * kCorrCols;   // columns per block pass
+
+struct CorrT {
+  const uint8_t *X, *Yt;
+  int Yrows, ldt;
+  const int4 *xst, *yst;
+  const int *YL;
+  const int4 *seg;
+  const int *tails;
+  const TcCounters *ctr;
+  int cap;
+  ulonglong2 *Cout;
+  int gx, gy;
+};
+
+template <bool WIDE>
+__device__ __forceinline__ void corr_cols(const CorrT &c, const uint32_t *s_dec, const int2 *s_t, int T, int y,
+                                          const int (&lay)[kCorrCols], const int (&ly)[kCorrCols],
+                                          ulonglong2 (&out)[kCorrCols]) {
+  using Acc = typename std::conditional<WIDE, unsigned __int128, unsigned long long>::type;
+  Acc acc[kCorrCols];
+#pragma unroll
+  for (int q = 0; q < kCorrCols; ++q) acc[q] = 0;
+  const uint8_t *col = c.Yt + y;
+  for (int t0 = 0; t0 < T; t0 += kCorrTU) {
+    uint2 w[kCorrTU];
+    int2 te[kCorrTU];
+#pragma unroll
+    for (int u = 0; u < kCorrTU; ++u) {
+      const bool v = t0 + u < T;
+      te[u] = s_t[v ? t0 + u : t0];
+      // a missing element reads as zero codes, which add nothing
+      w[u] = v ? __ldg((const uint2 *)(col + (size_t)te[u].x * c.ldt)) : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kCorrTU; ++u) {
+      const int ma = (int)(short)(te[u].y & 0xFFFF), ea = te[u].y >> 16;
+#pragma unroll
+      for (int q = 0; q < kCorrCols; ++q) {
+        const uint32_t d = s_dec[((q < 4 ? w[u].x : w[u].y) >> (8 * (q & 3))) & 0xFFu];
+        const int m = dec_m(d), lsb = dec_lsb(d);
+        if (m != 0 && lsb >= ly[q]) {
+          if (WIDE) {
+            const int sh = min(max(ea + lsb - lay[q], 0), 127);
+            acc[q] += (unsigned __int128)(__int128)(long long)(ma * m) << sh;
+          } else {
+            acc[q] += (unsigned long long)(long long)(ma * m) << (ea + lsb - lay[q]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < kCorrCols; ++q) {
+    if (WIDE) out[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((unsigned __int128)acc[q] >> 64));
+    else out[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((long long)acc[q] >> 63));
+  }
+}
+
+__global__ void __launch_bounds__(256) k_tc_corr_t(const CorrT s0, const CorrT s1, int K) {
+  __shared__ uint32_t s_dec[256];
+  __shared__ int2 s_t[TAILCAP];   // (k, mantissa | (lsb - la_x) << 16)
+  __shared__ int s_emax;
+  const CorrT c = blockIdx.z ? s1 : s0;
+  if ((int)blockIdx.x >= c.gx || (int)blockIdx.y >= c.gy) return;
+  for (int q = threadIdx.x; q < 256; q += blockDim.x) {
+    int m, e;
+    posit_to_me<8, 2>((uint32_t)q, m, e);
+    int hb = m ? e + 31 - __clz(m < 0 ? -m : m) : 0;
+    s_dec[q] = dec_pack(e, hb, m);
+  }
+  const int nslots = min(c.ctr->v[0], c.cap);
+  for (int sl = blockIdx.x; sl < nslots; sl += c.gx) {
+    const int4 sg = c.seg[sl];
+    const int x = sg.z, T = sg.y;
+    const int la_x = c.xst[x].x;
+    __syncthreads();   // the previous slot's list is no longer read
+    if (threadIdx.x == 0) s_emax = 0;
+    __syncthreads();
+    int em = 0;
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+      const int k = c.tails[sg.x + t];
+      const uint32_t d = s_dec[c.X[(size_t)x * K + k]];
+      const int er = dec_lsb(d) - la_x;   // >= 0: la_x is the row's min lsb
+      s_t[t] = make_int2(k, (dec_m(d) & 0xFFFF) | (er << 16));
+      em = max(em, er);
+    }
+    atomicMax(&s_emax, em);
+    __syncthreads();
+    const int emax = s_emax;
+    const int lgT = 32 - __clz(max(T, 1));   // >= ceil(log2(T + 1))
+    for (int y = blockIdx.y * kCorrSpan + kCorrCols * threadIdx.x; y < c.Yrows; y += c.gy * kCorrSpan) {
+      int lay[kCorrCols], ly[kCorrCols], hr = 0;
+#pragma unroll
+      for (int q = 0; q < kCorrCols; ++q) {
+        const bool v = y + q < c.Yrows;
+        const int4 st = v ? c.yst[y + q] : make_int4(0, 0, 0, 0);
+        lay[q] = st.x;
+        ly[q] = (v && c.YL) ? c.YL[y + q] : -0x3FFFFFFF;
+        hr = max(hr, st.y - st.x);
+      }
+      ulonglong2 out[kCorrCols];
+      // |term| < 2^(8 + emax + hr), at most T terms: int64 is exact (added as
+      // two's complement words)
+      if (emax + hr + 8 + lgT <= 62) corr_cols<false>(c, s_dec, s_t, T, y, lay, ly, out);
+      else corr_cols<true>(c, s_dec, s_t, T, y, lay, ly, out);
+#pragma unroll
+      for (int q = 0; q < kCorrCols; ++q)
+        if (y + q < c.Yrows) c.Cout[(size_t)sl * c.Yrows + y + q] = out[q];
+    }
+  }
+}
+
 // ----------------------------------------------------------------- fixup ---
 template <int FMT>
 __global__ void __launch_bounds__(256) k_tc_fixup(GemmArgs a, const int4 *__restrict__ sta,
@@ -1563,9 +1756,24 @@ int make_plane_map(CUtensorMap *m, void *base, int Kp, int rows, int S, int box_
 inline size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
 struct TcLayout {
-  int S, Kp, nkb, capA, capB, pool;
-  size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, part, total;
+  int S, Kp, nkb, capA, capB, pool, ldtA, ldtB;
+  size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, TA, TB, part, total;
 };
+
+// K at and above which unscaled bp8 takes the narrow form on its own (algo 0,
+// 2, 3): 4 digit-pair MMAs instead of 9 per K block, against tail lists of a
+// few tens of elements per row for rows whose values spread like N(0, 1)
+// (15-bit window) corrected beside the GEMM.
+constexpr int kNarrowMinK = 16384;
+
+// Digit planes of a call: 2 (narrow bp8 form), 3 (wide bp8) or 4 (bp16).
+// algo 4 forces the narrow form and algo 5 the wide one (bp8).
+int tc_planes(int fmt, int K, bool scaled, int algo) {
+  if (fmt != 8) return 4;
+  if (algo == 4) return 2;
+  if (algo == 5) return 3;
+  return (!scaled && K >= kNarrowMinK) ? 2 : 3;
+}
 
 // Correction buffers hold at most this many bytes per side; tail rows beyond
 // the cap are finished by the fixup kernel instead.
@@ -1587,11 +1795,11 @@ int tc_wave_capacity(bool pair);
 TcSchedule tc_schedule(int S, int M, int N, int nkb, bool pair) {
   TcSchedule sc{};
   sc.MM = pair ? 2 * BM : BM;
-  sc.BN = S == 3 ? Cfg<3>::BN : Cfg<4>::BN;
-  sc.QW = S == 3 ? Cfg<3>::QW : Cfg<4>::QW;
+  sc.BN = S == 2 ? Cfg<2>::BN : (S == 3 ? Cfg<3>::BN : Cfg<4>::BN);
+  sc.QW = S == 2 ? Cfg<2>::QW : (S == 3 ? Cfg<3>::QW : Cfg<4>::QW);
   sc.ntn = (N + sc.BN - 1) / sc.BN;
   sc.ntiles = sc.ntn * ((M + sc.MM - 1) / sc.MM);
-  const int exact = (S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK) / BK;
+  const int exact = (S == 2 ? Cfg<2>::KCHUNK : (S == 3 ? Cfg<3>::KCHUNK : Cfg<4>::KCHUNK)) / BK;
   const int min_split = (nkb + exact - 1) / exact;
   const int P = std::max(1, tc_wave_capacity(pair));
   if (min_split > 1) {
@@ -1616,14 +1824,18 @@ size_t tc_qbuf_bytes(const TcSchedule &sc) {
   return 8 * (size_t)sc.QW * ((size_t)sc.whole + (size_t)(sc.ntiles - sc.whole) * sc.split) * sc.MM * sc.BN;
 }
 
-TcLayout tc_layout(int fmt, int M, int N, int K) {
+// Workspace layout for a call with S digit planes.  The narrow form (S = 2)
+// adds the K-major copies of both operands' codes and a deeper tail pool.
+TcLayout tc_layout(int fmt, int M, int N, int K, int S) {
   TcLayout L{};
-  L.S = fmt == 8 ? 3 : 4;
+  L.S = S;
   L.Kp = (K + 127) / 128 * 128;
   L.nkb = L.Kp / BK;
   L.capA = (int)std::min<size_t>((size_t)M, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(N, 1))));
   L.capB = (int)std::min<size_t>((size_t)N, std::max<size_t>(1, kCorrBudget / (16 * (size_t)std::max(M, 1))));
-  L.pool = std::max(65536, 8 * std::max(M, N));
+  L.pool = std::max(65536, (S == 2 ? 128 : 8) * std::max(M, N));
+  L.ldtA = (M + 15) / 16 * 16;
+  L.ldtB = (N + 15) / 16 * 16;
   size_t o = 0;
   L.planesA = o; o += al((size_t)L.S * M * L.Kp);
   L.planesB = o; o += al((size_t)L.S * N * L.Kp);
@@ -1638,7 +1850,12 @@ TcLayout tc_layout(int fmt, int M, int N, int K) {
   L.ctr = o; o += 256;
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
-  // room for either form's main sums (the form is chosen at launch)
+  L.TA = L.TB = 0;
+  if (S == 2) {
+    L.TA = o; o += al((size_t)K * L.ldtA * (fmt / 8));
+    L.TB = o; o += al((size_t)K * L.ldtB * (fmt / 8));
+  }
+  // room for either pairing's main sums (chosen at launch)
   L.part = o;
   o += al(std::max(tc_qbuf_bytes(tc_schedule(L.S, M, N, L.nkb, false)),
                    tc_qbuf_bytes(tc_schedule(L.S, M, N, L.nkb, M > BM && BK == 64))));
@@ -1850,19 +2067,29 @@ bool gemm_tc_supported(int fmt, int M, int N, int K) {
   return M > 0 && N > 0 && K > 0 && (size_t)K <= (size_t)1 << 30 && M <= 65535 * BM;
 }
 
-size_t gemm_tc_workspace(int fmt, int M, int N, int K) { return tc_layout(fmt, M, N, K).total; }
+// Enough for every plane form the call may take (scaled operands never take
+// the narrow form on their own, but their size is not known here).
+size_t gemm_tc_workspace(int fmt, int M, int N, int K, int algo) {
+  const int s_unscaled = tc_planes(fmt, K, false, algo), s_scaled = tc_planes(fmt, K, true, algo);
+  return std::max(tc_layout(fmt, M, N, K, s_unscaled).total, tc_layout(fmt, M, N, K, s_scaled).total);
+}
 
 // sta / stb are outputs here: the prep kernels write the row statistics.
 // One operand's preparation (statistics, digit planes, bases, tail lists,
 // counters) can be done alone (a_mode 2 for A, 3 for B) and reused by later
 // calls with the same operand, M, N, K and workspace that prepare only the
 // other one (a_mode 1 reuses A, 4 reuses B).
-int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, bool single_sm,
-                   int a_mode, cudaStream_t s) {
+int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_bytes, int algo, int a_mode,
+                   cudaStream_t s) {
   // a_mode 0: prepare A and B and multiply; 1: A already prepared (reuse);
   // 2: prepare A only; 3: prepare B only; 4: B already prepared (reuse)
   const bool reuse_a = a_mode == 1, a_only = a_mode == 2, b_only = a_mode == 3, reuse_b = a_mode == 4;
-  TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K);
+  const bool single_sm = algo == 3;
+  const int S = tc_planes(a.fmt, a.K, a.sa != nullptr || a.sb != nullptr, algo);
+  // K-major corrections: the narrow form on unscaled operands (group-scaled
+  // ones, which take the narrow form only when algo 4 asks, keep k_tc_corr)
+  const bool kmajor = S == 2 && a.sa == nullptr && a.sb == nullptr;
+  TcLayout L = tc_layout(a.fmt, a.M, a.N, a.K, S);
   if (ws_bytes < L.total) return set_error(kEWorkspace, "quire_gemm: tensor-core workspace too small");
   char *w = (char *)ws;
   int8_t *planesA = (int8_t *)(w + L.planesA), *planesB = (int8_t *)(w + L.planesB);
@@ -1885,21 +2112,53 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   PrepOp pb{a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB};
   if (reuse_a || b_only) pa.rows = 0;
   if (reuse_b || a_only) pb.rows = 0;
+  // The narrow form's K-major code copies of the operands prepared here, on
+  // the side stream beside the prep (the corrections that read them follow
+  // there); without a side stream, on the caller's stream.
+  SideStream *side = L.nkb >= 256 ? side_stream() : nullptr;
   int rc = kOk;
+  if (kmajor && pa.rows + pb.rows > 0) {
+    cudaStream_t ts = s;
+    if (side) {
+      if (cudaEventRecord(side->ev[3], s) == cudaSuccess && cudaStreamWaitEvent(side->st, side->ev[3], 0) == cudaSuccess)
+        ts = side->st;
+      else
+        return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    if (pa.rows) {
+      k_transpose_bp8<<<dim3((unsigned)((a.K + 63) / 64), (unsigned)((L.ldtA + 63) / 64)), 256, 0, ts>>>(
+          (const uint8_t *)a.A, a.M, a.K, (uint8_t *)(w + L.TA), L.ldtA);
+      rc = check_launch("tc_transpose");
+    }
+    if (!rc && pb.rows) {
+      k_transpose_bp8<<<dim3((unsigned)((a.K + 63) / 64), (unsigned)((L.ldtB + 63) / 64)), 256, 0, ts>>>(
+          (const uint8_t *)a.B, a.N, a.K, (uint8_t *)(w + L.TB), L.ldtB);
+      rc = check_launch("tc_transpose");
+    }
+    if (side && (a_only || b_only || rc)) {
+      // nothing else of this call runs on the side stream: join it here
+      if (cudaEventRecord(side->ev[4], side->st) != cudaSuccess || cudaStreamWaitEvent(s, side->ev[4], 0) != cudaSuccess)
+        if (!rc) rc = set_error(kECuda, "quire_gemm: side stream join: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    if (rc) return rc;
+  }
   if (pa.rows + pb.rows > 0) {
     const int g = std::min(pa.rows + pb.rows, sms * 8);
-    if (a.fmt == 8)
-      k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
-    else
+    if (a.fmt == 16)
       k_tc_prep<16, 4><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+    else if (S == 2)
+      k_tc_prep<8, 2><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+    else
+      k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     rc = check_launch("tc_prep");
   }
   if (rc || a_only || b_only) return rc;
 
-  int S = L.S;
   // Paired SMs whenever the tile has a second 128-row half to work on.
   const bool pair = !single_sm && BK == 64 && a.M > BM;
-  const int bnb = S == 3 ? (pair ? Cfg<3, true>::BNB : Cfg<3>::BNB) : (pair ? Cfg<4, true>::BNB : Cfg<4>::BNB);
+  const int bnb = S == 2   ? (pair ? Cfg<2, true>::BNB : Cfg<2>::BNB)
+                  : S == 3 ? (pair ? Cfg<3, true>::BNB : Cfg<3>::BNB)
+                           : (pair ? Cfg<4, true>::BNB : Cfg<4>::BNB);
   CUtensorMap ma, mb;
   rc = make_plane_map(&ma, planesA, L.Kp, a.M, S, BM);
   if (rc) return rc;
@@ -1927,21 +2186,32 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   // Only the finish kernels read them: with long K (64-deep K blocks >= 256)
   // they run on the side stream, at most two blocks per SM beside the GEMM's
   // first segment, instead of ahead of it.
-  SideStream *side = L.nkb >= 256 ? side_stream() : nullptr;
   if (side && (cudaEventRecord(side->ev[3], s) != cudaSuccess ||
                cudaStreamWaitEvent(side->st, side->ev[3], 0) != cudaSuccess)) {
+    // the narrow form's copies were queued there: corrections stay behind them
+    if (kmajor) return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
     cudaGetLastError();
     side = nullptr;   // corrections on the caller's stream instead
   }
   const cudaStream_t cs = side ? side->st : s;
-  const int cy = side ? 2 : 64;
-  const CorrSide ca{a.A, a.B, a.N, a.sa, a.sb, sta, stb, nullptr, segA, tailA, cA, L.capA, CA,
-                    std::min(L.capA, side ? sms : sms * 2), std::min((a.N + 255) / 256, cy)};
-  const CorrSide cb{a.B, a.A, a.M, a.sb, a.sa, stb, sta, LA, segB, tailB, cB, L.capB, CB,
-                    std::min(L.capB, side ? sms : sms * 2), std::min((a.M + 255) / 256, cy)};
-  const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
-  if (a.fmt == 8) k_tc_corr<8><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
-  else k_tc_corr<16><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+  if (kmajor) {
+    // each side's blocks: slots x column blocks of kCorrSpan
+    const CorrT ca{(const uint8_t *)a.A, (const uint8_t *)(w + L.TB), a.N, L.ldtB, sta, stb, nullptr, segA, tailA,
+                   cA, L.capA, CA, std::min(L.capA, sms * 4), (a.N + kCorrSpan - 1) / kCorrSpan};
+    const CorrT cb{(const uint8_t *)a.B, (const uint8_t *)(w + L.TA), a.M, L.ldtA, stb, sta, LA, segB, tailB,
+                   cB, L.capB, CB, std::min(L.capB, sms * 4), (a.M + kCorrSpan - 1) / kCorrSpan};
+    const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
+    k_tc_corr_t<<<gc, 256, 0, cs>>>(ca, cb, a.K);
+  } else {
+    const int cy = side ? 2 : 64;
+    const CorrSide ca{a.A, a.B, a.N, a.sa, a.sb, sta, stb, nullptr, segA, tailA, cA, L.capA, CA,
+                      std::min(L.capA, side ? sms : sms * 2), std::min((a.N + 255) / 256, cy)};
+    const CorrSide cb{a.B, a.A, a.M, a.sb, a.sa, stb, sta, LA, segB, tailB, cB, L.capB, CB,
+                      std::min(L.capB, side ? sms : sms * 2), std::min((a.M + 255) / 256, cy)};
+    const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
+    if (a.fmt == 8) k_tc_corr<8><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+    else k_tc_corr<16><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+  }
   rc = check_launch("tc_corr");
   cudaEvent_t corr_done = nullptr;
   if (side) {
@@ -1955,7 +2225,10 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     }
   }
   if (rc) return rc;
-  if (S == 3)
+  if (S == 2)
+    rc = pair ? launch_tc_schedule<2, true>(ma, mb, p, sc, gf, s, corr_done)
+              : launch_tc_schedule<2, false>(ma, mb, p, sc, gf, s, corr_done);
+  else if (S == 3)
     rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s, corr_done)
               : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s, corr_done);
   else

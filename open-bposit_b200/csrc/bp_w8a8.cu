@@ -3,9 +3,9 @@
 // and the truncating bp8 encode of the row scaled by 2^-e
 // (encode_bposit8 on floats, reference/bposit_ref.py:258-270).
 //
-// One warp per row (rows staged in the warp's slice of shared memory, as many
-// warps per block as 36 KB of rows allow; only rows beyond 7372 elements are
-// re-read through L2), no block-wide barrier, float4 loads several at a time:
+// One warp per row (rows up to ~1800 elements staged in the warp's slice of
+// shared memory, at least 4 warps per block; longer rows read through L2 by
+// each pass), no block-wide barrier, float4 loads eight at a time per lane:
 //   rms  = sqrt(sum(x^2) / K)                       float64, warp reduction
 //   p95  = numpy's 'linear' percentile of |x| at 95: the order statistics at
 //          ranks lo = floor(0.95 (K - 1)) and lo + 1 by a 4-pass radix select
@@ -168,18 +168,40 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
     const double two_rms = 2.0 * rms;
     const uint32_t tkey = __float_as_uint(__double2float_rd(two_rms)) & 0x7FFFFFFFu;
     uint32_t cnt = 0u, mx_non = 0u, mn_cand = 0xFFFFFFFFu;
-    for (int k = lane; k < kpad; k += 32) {
-      const uint32_t key = k < K ? (__float_as_uint(xr[k]) & 0x7FFFFFFFu) : 0u;
-      const bool c = k < K && key > tkey;
+    auto take = [&](uint32_t key, bool valid) {   // whole warp
+      const bool c = valid && key > tkey;
       const uint32_t bal = __ballot_sync(0xFFFFFFFFu, c);
       if (c) {
         const uint32_t at = cnt + __popc(bal & lt_mask);
         if (at <= (uint32_t)(K / 4)) cand[at] = key;   // always: Chebyshev bounds the count by K / 4
         mn_cand = min(mn_cand, key);
-      } else if (k < K) {
+      } else if (valid) {
         mx_non = max(mx_non, key);
       }
       cnt += __popc(bal);
+    };
+    if (VEC) {
+      // eight float4 per lane in flight, then their 32 keys (the list's order is free)
+      const uint4 *r4 = reinterpret_cast<const uint4 *>(xr);
+      for (int u0 = 0; u0 < K4; u0 += 256) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int u = u0 + 32 * j + lane;
+          v[j] = u < K4 ? r4[u] : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (u0 + 32 * j >= K4) break;   // warp-uniform
+          const bool ok = u0 + 32 * j + lane < K4;
+          take(v[j].x & 0x7FFFFFFFu, ok);
+          take(v[j].y & 0x7FFFFFFFu, ok);
+          take(v[j].z & 0x7FFFFFFFu, ok);
+          take(v[j].w & 0x7FFFFFFFu, ok);
+        }
+      }
+    } else {
+      for (int k = lane; k < kpad; k += 32) take(k < K ? (__float_as_uint(xr[k]) & 0x7FFFFFFFu) : 0u, k < K);
     }
     __syncwarp();
     // The percentile only matters when it exceeds 2 rms: c <= K - lo - 2 means
@@ -266,10 +288,15 @@ __global__ void __launch_bounds__(kT) k_w8a8_rows(const float *__restrict__ x, i
     if (VEC) {
       const uint4 *r4 = reinterpret_cast<const uint4 *>(xr);
       uint32_t *cw = reinterpret_cast<uint32_t *>(cr);
-      for (int u = lane; u < K4; u += 32) {
-        const uint4 v = r4[u];
-        cw[u] = w8a8_code(tbl, v.x, e, zkey) | (w8a8_code(tbl, v.y, e, zkey) << 8) |
-                (w8a8_code(tbl, v.z, e, zkey) << 16) | (w8a8_code(tbl, v.w, e, zkey) << 24);
+      for (int u0 = lane; u0 < K4; u0 += 256) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = u0 + 32 * j < K4 ? r4[u0 + 32 * j] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (u0 + 32 * j < K4)
+            cw[u0 + 32 * j] = w8a8_code(tbl, v[j].x, e, zkey) | (w8a8_code(tbl, v[j].y, e, zkey) << 8) |
+                              (w8a8_code(tbl, v[j].z, e, zkey) << 16) | (w8a8_code(tbl, v[j].w, e, zkey) << 24);
       }
     } else {
       for (int k = lane; k < K; k += 32) cr[k] = (uint8_t)w8a8_code(tbl, __float_as_uint(xr[k]), e, zkey);
@@ -285,14 +312,15 @@ int launch_w8a8_rows(const float *x, int rows, int K, int32_t *exps, uint8_t *co
   const bool vec = (K % 4) == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)codes & 3u) == 0;
   const size_t list = (size_t)w8a8_list_words(K) * sizeof(uint32_t);   // candidate list per warp
   const size_t staged = (size_t)w8a8_row_floats(K) * sizeof(float) + list;
-  if (staged <= kStageBytes) {
+  if (staged <= kStageBytes / 4) {   // at least 4 warps per block with staged rows
     // rows staged in shared memory: as many warps per block as the budget allows
     const int w = std::max(1, std::min(kWarps, (int)(kStageBytes / staged)));
     const int blocks = std::min((rows + w - 1) / w, sm_count() * 16);
     if (vec) k_w8a8_rows<true, true><<<blocks, 32 * w, w * staged, s>>>(x, rows, K, exps, codes);
     else k_w8a8_rows<true, false><<<blocks, 32 * w, w * staged, s>>>(x, rows, K, exps, codes);
   } else {
-    // very long rows re-read through L2 (only the candidate lists in shared memory)
+    // longer rows are read through L2 by each pass (only the candidate lists in
+    // shared memory, so more warps per SM): ~7 warps per block for K = 4864
     const int w = std::max(1, std::min(kWarps, (int)(kStageBytes / list)));
     if (list > kStageBytes) return set_error(kERange, "w8a8_rows: rows of %d elements are too long", K);
     const int blocks = std::min((rows + w - 1) / w, sm_count() * 4);

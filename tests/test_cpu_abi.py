@@ -52,8 +52,8 @@ def test_host_argument_validation():
     assert rc == _lib.BP_EINVAL
     rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, vp(16), 5, 0, None, 0, None)
     assert rc == _lib.BP_EINVAL
-    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 4, None, 0, None)
-    assert rc == _lib.BP_EINVAL   # algo 0..3
+    rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 6, None, 0, None)
+    assert rc == _lib.BP_EINVAL   # algo 0..5
     rc = L.bp_quire_gemm(8, vp(16), vp(16), 2, 4, 8, None, None, 128, vp(16), 4, None, 0, 0, vp(17), 1 << 20, None)
     assert rc == _lib.BP_EALIGN
     assert L.bp_decode(9, vp(16), 4, vp(16), None) == _lib.BP_EFMT
@@ -63,6 +63,23 @@ def test_host_argument_validation():
     # zero-size calls are no-ops that succeed without touching a device
     assert L.bp_quire_gemm(8, None, None, 0, 5, 3, None, None, 128, None, 5, None, 0, 0, None, 0, None) == 0
     assert L.bp_quire_gemm_workspace_size(8, 16, 16, 16, 1) >= 16 * 2 * 16
+
+
+def test_plane_form_workspace():
+    """The narrow bp8 form (algo 4, or auto for K >= 16384) holds K-major copies
+    of both operands' codes beside its two digit planes; the wide form (algo 5)
+    does not.  Auto sizes for whichever form the call may take."""
+    from bposit_b200 import _lib
+    L = _lib.lib()
+    M, N, K = 256, 512, 4096
+    narrow = L.bp_quire_gemm_workspace_size(8, M, N, K, 4)
+    wide = L.bp_quire_gemm_workspace_size(8, M, N, K, 5)
+    assert narrow >= 3 * (M + N) * K and wide >= 3 * (M + N) * K   # 2 planes + copies / 3 planes
+    assert L.bp_quire_gemm_workspace_size(8, M, N, K, 0) == wide
+    K = 65536
+    assert L.bp_quire_gemm_workspace_size(8, M, N, K, 0) >= L.bp_quire_gemm_workspace_size(8, M, N, K, 4)
+    assert L.bp_quire_gemm_workspace_size(8, M, N, K, 0) >= L.bp_quire_gemm_workspace_size(8, M, N, K, 5)
+    assert L.bp_quire_gemm_workspace_size(16, M, N, K, 4) == L.bp_quire_gemm_workspace_size(16, M, N, K, 5)
 
 
 def test_python_errors_match_reference_types():

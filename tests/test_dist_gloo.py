@@ -95,3 +95,77 @@ def test_block_grid_covers_output_once(world):
                 assert 0 <= m0 <= m1 <= M and 0 <= n0 <= n1 <= N
                 cover[m0:m1, n0:n1] += 1
             assert (cover == 1).all()
+
+
+def _watchdog_worker(rank, world, port, q):
+    """Rank 1 never joins rank 0's collective (it leaves between steps); rank 0's
+    guarded all_reduce must end with BpositError once the watchdog trips."""
+    import datetime
+    import sys
+    import time
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [repo, os.path.join(repo, "open-bposit_b200")]
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=6))
+    from bposit_b200._lib import BpositError
+    from bposit_b200.dist import CallWatchdog
+    fired = []
+    wd = CallWatchdog(1.0, on_timeout=lambda what: fired.append((what, time.monotonic())))
+    t = torch.ones(1)
+    with wd.guard("step 0"):          # both ranks: completes well inside the deadline
+        dist.all_reduce(t)
+    if rank == 1:
+        time.sleep(8)                 # gone for rank 0's next step
+        q.put(("rank1", True))
+        wd.close()
+        return
+    t0 = time.monotonic()
+    try:
+        with wd.guard("step 1"):
+            dist.all_reduce(t)       # rank 1 never joins: gloo's own timeout ends it
+        q.put(("rank0", "no error"))
+    except BpositError as exc:
+        ok = bool(fired) and fired[0][0] == "step 1" and 0.8 < fired[0][1] - t0 < 5.0 and "deadline" in str(exc)
+        try:
+            with wd.guard("step 2"):  # tripped: later calls refuse at once
+                pass
+            ok = False
+        except BpositError:
+            pass
+        q.put(("rank0", ok))
+    except Exception as exc:          # noqa: BLE001
+        q.put(("rank0", f"other error {type(exc).__name__}: {exc}"))
+    wd.close()
+
+
+def test_call_watchdog_gloo():
+    """Host failure made on the host: a rank that never joins a step.  The
+    watchdog fires its callback about 1 s into the step, the step raises
+    BpositError naming the deadline, and the watchdog stays tripped."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_watchdog_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    res = dict(q.get(timeout=5) for _ in range(2))
+    assert res["rank0"] is True, res
+    assert res["rank1"] is True
+
+
+def test_call_watchdog_quiet_when_fast():
+    """Guarded blocks that end in time never fire the callback; errors inside
+    a guard pass through unchanged."""
+    from bposit_b200.dist import CallWatchdog
+    fired = []
+    wd = CallWatchdog(5.0, on_timeout=fired.append)
+    for _ in range(100):
+        with wd.guard("fast"):
+            pass
+    with pytest.raises(KeyError):
+        with wd.guard("raises"):
+            raise KeyError("x")
+    wd.close()
+    assert fired == [] and wd.tripped is None

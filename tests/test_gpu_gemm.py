@@ -11,7 +11,10 @@ from conftest import golden
 
 pytestmark = pytest.mark.gpu
 
-ALGOS = [1, 2, 3]   # 1 = CUDA cores, 2 = tensor cores (paired SMs when M > 128), 3 = tensor cores, one SM per tile
+# 1 = CUDA cores, 2 = tensor cores (paired SMs when M > 128), 3 = tensor cores, one SM per
+# tile, 4 / 5 = tensor cores with the narrow (2 base-256 planes) / wide (3 base-128) bp8 form
+ALGOS = [1, 2, 3, 4, 5]
+ALGOS16 = [1, 2, 3]
 
 
 @pytest.fixture(scope="module")
@@ -68,7 +71,7 @@ def test_fast_selftest_dots(ops):
 def test_w8a8_linear_golden(ops, algo):
     """16x576x576 group-scaled W8A8 linear: every quire and bp32 word."""
     g = golden("w8a8_linear")
-    if algo in (2, 3) and not tc_ok(ops, 8, 16, 576, 576):
+    if algo >= 2 and not tc_ok(ops, 8, 16, 576, 576):
         pytest.skip("tensor-core path not available for this shape")
     out, q = run(ops, g["xc"], g["wc"], 8, algo, sa=g["sx"], sb=g["sw"], quire_limbs=8)
     assert np.array_equal(q, g["quire"])
@@ -88,7 +91,7 @@ SHAPES = [(1, 1, 1), (1, 1, 0), (3, 5, 7), (17, 33, 65), (64, 48, 130), (129, 13
 @pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("M,N,K", SHAPES)
 def test_bp8_random_vs_oracle(ops, orc, algo, M, N, K):
-    if algo in (2, 3) and not tc_ok(ops, 8, M, N, K):
+    if algo >= 2 and not tc_ok(ops, 8, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(M * 1000 + N * 10 + K)
     A, B = rand_codes(rng, (M, K), 8), rand_codes(rng, (N, K), 8)
@@ -101,7 +104,7 @@ def test_bp8_random_vs_oracle(ops, orc, algo, M, N, K):
 @pytest.mark.parametrize("algo", ALGOS)
 @pytest.mark.parametrize("M,N,K,group", [(5, 7, 300, 128), (40, 70, 576, 128), (130, 66, 1000, 64)])
 def test_bp8_group_scaled_vs_oracle(ops, orc, algo, M, N, K, group):
-    if algo in (2, 3) and not tc_ok(ops, 8, M, N, K):
+    if algo >= 2 and not tc_ok(ops, 8, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(K + group)
     X = (rng.standard_normal((M, K)) * np.exp2(rng.integers(-6, 6, (M, 1)))).astype(np.float32)
@@ -129,12 +132,12 @@ def test_bp8_truncating_terms(ops, orc):
     assert np.array_equal(out, rb)
 
 
-@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("algo", ALGOS16)
 @pytest.mark.parametrize("M,N,K", [(2, 3, 5), (33, 17, 100), (128, 64, 256)])
 def test_bp16_random_vs_oracle(ops, orc, algo, M, N, K):
     """bp16 quire GEMM on uniformly random codes (exponents up to +-112, so
     products span 2^-224..2^224 and many terms truncate per term)."""
-    if algo in (2, 3) and not tc_ok(ops, 16, M, N, K):
+    if algo >= 2 and not tc_ok(ops, 16, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     rng = np.random.default_rng(M + N + K)
     A, B = rand_codes(rng, (M, K), 16), rand_codes(rng, (N, K), 16)
@@ -144,12 +147,12 @@ def test_bp16_random_vs_oracle(ops, orc, algo, M, N, K):
     assert np.array_equal(out, rb)
 
 
-@pytest.mark.parametrize("algo", ALGOS)
+@pytest.mark.parametrize("algo", ALGOS16)
 def test_bp16_normal_range_vs_oracle(ops, orc, algo):
     """bp16 operands ~ N(0,1) * 2^U{-8..8} per row (the large-GEMM distribution)."""
     from bposit_b200 import workloads
     M, N, K = 96, 160, 1024
-    if algo in (2, 3) and not tc_ok(ops, 16, M, N, K):
+    if algo >= 2 and not tc_ok(ops, 16, M, N, K):
         pytest.skip("tensor-core path not available for this shape")
     A = orc.encode_bp16(workloads.per_row_po2(M, K, 1), True)
     B = orc.encode_bp16(workloads.per_row_po2(N, K, 2), True)
@@ -218,10 +221,12 @@ def test_smollm_layer_shapes_row_subsample(ops, orc):
         assert np.array_equal(out.cpu().numpy()[rows], ref), name
 
 
-def test_large_bp8_k65536_row_subsample(ops, orc):
+@pytest.mark.parametrize("algo", [0, 5])
+def test_large_bp8_k65536_row_subsample(ops, orc, algo):
     """bp8 4096 x 4096 x 65536 (operands N(0,1) * 2^U{-8..8} per row): every
-    output on the device, 2 full rows and a 64-column block checked against
-    the oracle."""
+    output on the device, 3 full rows and a 64-column block checked against
+    the oracle; auto (the narrow form, tens of tail elements per row) and the
+    wide form."""
     from bposit_b200 import workloads
     M = N = 4096
     K = 65536
@@ -234,13 +239,14 @@ def test_large_bp8_k65536_row_subsample(ops, orc):
         return ops.quantize_bp8(x * torch.exp2(e), nearest=True)
 
     A, B = operand(M), operand(N)
-    out, _ = ops.quire_gemm(A, B, 8)
+    out, _ = ops.quire_gemm(A, B, 8, algo=algo)
     o = out.cpu().numpy()
     An, Bn = A.cpu().numpy(), B.cpu().numpy()
     rows = np.array([0, 3900, 4095])   # the last tiles (last M block, both halves) run K-split
     assert np.array_equal(o[rows], orc.quire_gemm(An[rows], Bn, 8))
     cols = np.arange(1000, 1064)
     assert np.array_equal(o[:64, cols], orc.quire_gemm(An[:64], Bn[cols], 8))
+    assert _device_error() == 0
     del A, B, out
     torch.cuda.empty_cache()
 
@@ -274,7 +280,7 @@ def test_large_bp16_8192_row_subsample(ops, orc):
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("algo", [2, 3])
+@pytest.mark.parametrize("algo", [2, 3, 4])
 def test_balanced_last_wave(ops, orc, algo):
     """96 paired (192 single) tiles: one full wave runs whole, the remaining tiles
     run split along K with 128-bit partials; rows in whole and split tiles."""
@@ -295,8 +301,8 @@ def _device_error():
     return v.value
 
 
-@pytest.mark.parametrize("fmt", [8, 16])
-def test_tc_listed_tails(ops, orc, fmt):
+@pytest.mark.parametrize("fmt,algo", [(8, 2), (8, 4), (16, 2)])
+def test_tc_listed_tails(ops, orc, fmt, algo):
     """Rows whose values span more than the tensor-core digit window: a few
     tiny elements per row become listed tails, corrected exactly on CUDA cores."""
     rng = np.random.default_rng(40 + fmt)
@@ -311,14 +317,15 @@ def test_tc_listed_tails(ops, orc, fmt):
         A, B = orc.quantize_bp8(X)[0], orc.quantize_bp8(Y)[0]
     else:
         A, B = orc.encode_bp16(X, True), orc.encode_bp16(Y, True)
-    out, q = run(ops, A, B, fmt, 2, quire_limbs=16)
+    out, q = run(ops, A, B, fmt, algo, quire_limbs=16)
     rb, rq = orc.quire_gemm(A, B, fmt, nlimbs=16)
     assert np.array_equal(q, rq)
     assert np.array_equal(out, rb)
     assert _device_error() == 0
 
 
-def test_tc_tail_overflow_goes_to_fixup(ops, orc):
+@pytest.mark.parametrize("algo", [2, 4])
+def test_tc_tail_overflow_goes_to_fixup(ops, orc, algo):
     """More tail elements in a row than the tail list holds: that row's
     outputs are recomputed by the exact fixup kernel."""
     rng = np.random.default_rng(9)
@@ -329,18 +336,20 @@ def test_tc_tail_overflow_goes_to_fixup(ops, orc):
     A[3, 2000] = 0x7F           # maxpos: the row's window cannot reach minpos
     B[7, ::2] = 0xFF            # -minpos
     B[7, 1] = 0x7E
-    out, _ = run(ops, A, B, 8, 2)
+    out, _ = run(ops, A, B, 8, algo)
     assert np.array_equal(out, orc.quire_gemm(A, B, 8))
     assert _device_error() == 0
 
 
-def test_tc_split_k(ops, orc):
-    """K beyond one exact int32 chunk: per-chunk 128-bit partial sums."""
+@pytest.mark.parametrize("algo", [2, 5])
+def test_tc_split_k(ops, orc, algo):
+    """K beyond one exact int32 chunk: per-chunk 128-bit partial sums (auto
+    takes the narrow form here, with its tail lists; 5 the wide one)."""
     rng = np.random.default_rng(10)
     M, N, K = 64, 96, 200000
     A = orc.quantize_bp8(rng.standard_normal((M, K)).astype(np.float32))[0]
     B = orc.quantize_bp8(rng.standard_normal((N, K)).astype(np.float32))[0]
-    out, _ = run(ops, A, B, 8, 2)
+    out, _ = run(ops, A, B, 8, algo)
     rows = np.array([0, 17, 63])
     assert np.array_equal(out[rows], orc.quire_gemm(A[rows], B, 8))
     assert _device_error() == 0
