@@ -54,7 +54,8 @@ const char *bp_last_error(void);
 unsigned long long bp_launch_count(void);
 
 /* Reads and clears the current device's kernel error word: nonzero when a
- * bounded wait inside a tensor-core GEMM kernel gave up.  That kernel then
+ * bounded wait inside a kernel of the tensor-core path (the GEMM, its staged
+ * finish, the narrow form's tail corrections) gave up.  That kernel then
  * drained its own copies in flight (bounded), released its tensor memory and
  * returned; from then until this call clears the word, every bposit32 output
  * of the tensor-core path (bp_quire_gemm, _multi, _host) is NaR (0x80000000),

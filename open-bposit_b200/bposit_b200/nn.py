@@ -100,6 +100,7 @@ class BpositLinear(torch.nn.Module):
         self._ws = None          # GEMM workspace, grown on demand
         self._ws_key = None
         self.sharded = False     # split the GEMM over the process group (shard_linears)
+        self.algo = 0            # bp_quire_gemm algo of this layer's GEMM (0: the library's choice)
 
     @classmethod
     def from_linear(cls, lin: torch.nn.Linear, group: int = 128, scales: str = "w8a8",
@@ -128,9 +129,9 @@ class BpositLinear(torch.nn.Module):
 
     def _workspace(self, M: int, device):
         fmt = 16 if self.act == "bp16" else 8
-        key = (M, self.out_features, self.in_features, fmt)
+        key = (M, self.out_features, self.in_features, fmt, self.algo)
         if self._ws_key != key:
-            need = ops.gemm_workspace_size(fmt, M, self.out_features, self.in_features)
+            need = ops.gemm_workspace_size(fmt, M, self.out_features, self.in_features, self.algo)
             if self._ws is None or self._ws.numel() < need:
                 self._ws = torch.empty(max(need, 256), dtype=torch.uint8, device=device)
             self._ws_key = key
@@ -170,7 +171,7 @@ class BpositLinear(torch.nn.Module):
                       sb=None if sb is None else sb[n0:n1])
             return ops.bp32_to_f32(codes, row_exp=row_exp, col_exp=col_exp, bias=bias)
         return ops.quire_gemm_f32(xc, wc, fmt, sa=sa, sb=sb, group=self.group, row_exp=row_exp, col_exp=col_exp,
-                                  bias=bias, workspace=self._workspace(M, xc.device))
+                                  bias=bias, algo=self.algo, workspace=self._workspace(M, xc.device))
 
     def extra_repr(self) -> str:
         arith = "bp8 W8A8" if self.act == "bp8" else "bp8 weights, bp16 activations"

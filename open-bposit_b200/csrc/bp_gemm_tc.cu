@@ -104,7 +104,9 @@ struct Cfg {
   static constexpr int A_BYTES = S * BM * BK;
   static constexpr int B_BYTES = S * BNB * BK;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = PAIR ? (S == 2 ? 8 : (S == 3 ? 6 : 5))
+  // (S = 2 paired: 7 stages, 177 KB, leave room on the SM for the narrow form's
+  // copy and correction blocks that run beside the GEMM)
+  static constexpr int STAGES = PAIR ? (S == 2 ? 7 : (S == 3 ? 6 : 5))
                                      : (BK == 128 ? 2 : (S == 2 ? 6 : (S == 3 ? 5 : 4)));
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + BN * 32;
   static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -120,7 +122,8 @@ struct Cfg {
 };
 
 // Per-operand device counters, zeroed before each call:
-//   v[0] correction slots used, v[1] tail-list entries used,
+//   v[0] correction slots used, v[1] tail-list entries used, v[8] (side A)
+//   the narrow form's correction work counter,
 //   v[2] BIG - min la over nonzero rows, v[3] max (hb - la), v[4] any row whose
 //   tail could not be listed, v[5] any nonzero row.
 struct TcCounters {
@@ -130,6 +133,7 @@ struct TcCounters {
 struct TcParams {
   int M, N, K, Kp, nkb, kb_per_chunk;
   int tile0, ntn;              // first linear tile of this launch; tiles along N
+  int ntl;                     // tiles of this launch
   int split;                   // K chunks per tile in this launch (1: whole tiles)
   const int4 *sta, *stb;
   const int *LA, *LB, *slotA, *slotB;
@@ -336,15 +340,16 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, i
 // `remote` (the paired form's second CTA, whose copies complete on the
 // leader's barriers): sleep a settle time instead.
 template <int STAGES>
-__device__ __noinline__ void drain_loads(uint64_t *full, int issued, bool remote) {
+__device__ __noinline__ void drain_loads(uint64_t *full, uint32_t first, uint32_t end, bool remote) {
   if (remote) {
     for (int i = 0; i < 400; ++i) __nanosleep(1000);   // ~0.4 ms
     return;
   }
-  for (int it = issued > STAGES ? issued - STAGES : 0; it < issued; ++it) {
+  // loads [first, end) of the ring's running count; the last round of each stage
+  for (uint32_t g = end - first > (uint32_t)STAGES ? end - STAGES : first; g < end; ++g) {
     const long long t0 = clock64();
-    const uint32_t par = (uint32_t)(it / STAGES) & 1u;
-    while (!mbar_try_wait(&full[it % STAGES], par) && clock64() - t0 < DRAIN_LIMIT) __nanosleep(256);
+    const uint32_t par = (g / STAGES) & 1u;
+    while (!mbar_try_wait(&full[g % STAGES], par) && clock64() - t0 < DRAIN_LIMIT) __nanosleep(256);
   }
 }
 
@@ -426,15 +431,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = PAIR ? cluster_rank() : 0u;      // 0: issues the pair's MMAs
-  // tiles in tile_coords order; y = K chunk
-  const int tile = p.tile0 + (PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x);
-  int tm, tn;
-  tile_coords(tile, (p.M + C::MM - 1) / C::MM, p.ntn, tm, tn);
-  const int n0 = tn * C::BN;
-  const int m0 = tm * C::MM + (int)rank * BM, chunk = blockIdx.y;
-  const int kb0 = chunk * p.kb_per_chunk;
-  const int kb1 = min(p.nkb, kb0 + p.kb_per_chunk);
-  const int nkb = kb1 - kb0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -451,152 +447,194 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  bool ok = true;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      int issued = 0;   // K blocks whose loads were issued
-      for (int it = 0; it < nkb && ok; ++it) {
-        int st = it % C::STAGES;
-        uint32_t round = (uint32_t)(it / C::STAGES);
-        ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1, abort);
-        if (!ok) break;
-        issued = it + 1;
-        uint8_t *sa = smem + st * C::STAGE_BYTES;
-        if (PAIR) {
-          // both CTAs' loads complete on the leader's barrier, which expects both
-          if (rank == 0) mbar_expect_tx(&full[st], 2 * C::STAGE_BYTES);
-          const uint32_t fb = cluster_smem(&full[st], 0);
-          tma_load_3d_pair(sa, &tmA, fb, (kb0 + it) * BK, m0, 0);
-          tma_load_3d_pair(sa + C::A_BYTES, &tmB, fb, (kb0 + it) * BK, n0 + (int)rank * C::BNB, 0);
-        } else {
-          mbar_expect_tx(&full[st], C::STAGE_BYTES);
-          tma_load_3d(sa, &tmA, &full[st], (kb0 + it) * BK, m0, 0);
-          tma_load_3d(sa + C::A_BYTES, &tmB, &full[st], (kb0 + it) * BK, n0, 0);
+  // Persistent: the CTA (pair) takes work units u = (tile, K chunk) of this
+  // launch, u = cta, cta + ncta, ...; the stage ring's phases run on across
+  // units (gk: K blocks of this CTA's earlier units), tfull completes once per
+  // unit.  A unit's epilogue stages its sums in the pipeline buffers, so the
+  // next unit's loads start after the whole CTA (pair) has finished it.
+  const int cta = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int ncta = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int nunits = p.ntl * p.split;
+  uint32_t gk = 0, ucount = 0;
+  for (int u = cta; u < nunits; u += ncta, ++ucount) {
+    const int tl = u / p.split, chunk = u - tl * p.split;
+    const int tile = p.tile0 + tl;
+    int tm, tn;
+    tile_coords(tile, (p.M + C::MM - 1) / C::MM, p.ntn, tm, tn);
+    const int n0 = tn * C::BN;
+    const int m0 = tm * C::MM + (int)rank * BM;
+    const int kb0 = chunk * p.kb_per_chunk;
+    const int kb1 = min(p.nkb, kb0 + p.kb_per_chunk);
+    const int nkb = kb1 - kb0;
+    bool ok = true;
+
+    if (warp == 0) {
+      if (lane == 0) {
+        int issued = 0;   // K blocks of this unit whose loads were issued
+        for (int it = 0; it < nkb && ok; ++it) {
+          const uint32_t g = gk + (uint32_t)it;
+          const int st = (int)(g % C::STAGES);
+          const uint32_t round = g / C::STAGES;
+          ok = mbar_wait(&empty[st], (round & 1u) ^ 1u, 1, abort);
+          if (!ok) break;
+          issued = it + 1;
+          uint8_t *sa = smem + st * C::STAGE_BYTES;
+          if (PAIR) {
+            // both CTAs' loads complete on the leader's barrier, which expects both
+            if (rank == 0) mbar_expect_tx(&full[st], 2 * C::STAGE_BYTES);
+            const uint32_t fb = cluster_smem(&full[st], 0);
+            tma_load_3d_pair(sa, &tmA, fb, (kb0 + it) * BK, m0, 0);
+            tma_load_3d_pair(sa + C::A_BYTES, &tmB, fb, (kb0 + it) * BK, n0 + (int)rank * C::BNB, 0);
+          } else {
+            mbar_expect_tx(&full[st], C::STAGE_BYTES);
+            tma_load_3d(sa, &tmA, &full[st], (kb0 + it) * BK, m0, 0);
+            tma_load_3d(sa + C::A_BYTES, &tmB, &full[st], (kb0 + it) * BK, n0, 0);
+          }
         }
+        // After a timeout, the loads still in flight land before this CTA
+        // releases its shared memory: wait (bounded, regardless of the abort
+        // word) for the last issued round of every stage.  In the paired form
+        // the leader's barriers count both CTAs' bytes; the other CTA, whose
+        // loads complete on the leader's barriers, waits a settle time instead.
+        if (!ok || *abort) drain_loads<C::STAGES>(full, gk, gk + (uint32_t)issued, PAIR && rank != 0);
       }
-      // After a timeout, the loads still in flight land before this CTA
-      // releases its shared memory: wait (bounded, regardless of the abort
-      // word) for the last issued round of every stage.  In the paired form
-      // the leader's barriers count both CTAs' bytes; the other CTA, whose
-      // loads complete on the leader's barriers, waits a settle time instead.
-      if (!ok || *abort) drain_loads<C::STAGES>(full, issued, PAIR && rank != 0);
-    }
-    __syncwarp();
-  } else if ((warp == 1 || warp == 2) && rank == 0) {
-    // Two issuing warps take alternate K blocks.  A warp waits for its block's
-    // data while the other warp issues, then takes the hand-off (named barrier
-    // 1 or 2 between the two warps, bracketed by tcgen05 fences so the MMAs of
-    // consecutive blocks stay ordered in the tensor pipe): the full-barrier
-    // poll, which stalls MMA issue for ~200 cycles when the issuing warp does
-    // it, is off the critical path.  Every iteration takes the same hand-off
-    // steps whether or not its wait succeeded, so a timeout cannot strand the
-    // partner at a named barrier.
-    const int me = warp - 1;
-    uint32_t init = me ? (1u << C::D) - 1u : 0u;   // block 0 (warp 1) initialises every diagonal
-    for (int it = me; it < nkb; it += 2) {
-      const int st = it % C::STAGES;
-      const uint32_t round = (uint32_t)(it / C::STAGES);
-      if (ok) ok = mbar_wait_warp(&full[st], round & 1u, 2, abort);
-      if (it > 0) {
-        asm volatile("bar.sync %0, 64;" ::"r"(1 + me) : "memory");
-        tc_fence_after();
-      }
-      if (ok) {
-        uint32_t a0 = smem_u32(smem + st * C::STAGE_BYTES);
-        uint32_t b0 = a0 + C::A_BYTES;
+      __syncwarp();
+    } else if ((warp == 1 || warp == 2) && rank == 0) {
+      // Two issuing warps take alternate K blocks of the unit.  A warp waits for
+      // its block's data while the other warp issues, then takes the hand-off
+      // (named barrier 1 or 2 between the two warps, bracketed by tcgen05
+      // fences so the MMAs of consecutive blocks stay ordered in the tensor
+      // pipe): the full-barrier poll, which stalls MMA issue for ~200 cycles
+      // when the issuing warp does it, is off the critical path.  Every
+      // iteration takes the same hand-off steps whether or not its wait
+      // succeeded, so a timeout cannot strand the partner at a named barrier;
+      // each unit's hand-offs pair up within the unit.
+      const int me = warp - 1;
+      uint32_t init = me ? (1u << C::D) - 1u : 0u;   // block 0 (warp 1) initialises every diagonal
+      for (int it = me; it < nkb; it += 2) {
+        const uint32_t g = gk + (uint32_t)it;
+        const int st = (int)(g % C::STAGES);
+        const uint32_t round = g / C::STAGES;
+        if (ok) ok = mbar_wait_warp(&full[st], round & 1u, 2, abort);
+        if (it > 0) {
+          asm volatile("bar.sync %0, 64;" ::"r"(1 + me) : "memory");
+          tc_fence_after();
+        }
+        if (ok) {
+          uint32_t a0 = smem_u32(smem + st * C::STAGE_BYTES);
+          uint32_t b0 = a0 + C::A_BYTES;
 #pragma unroll
-        for (int ks = 0; ks < BK / 32; ++ks) {
+          for (int ks = 0; ks < BK / 32; ++ks) {
 #pragma unroll
-          for (int s = 0; s < S; ++s) {
-            uint64_t ad = sw64_desc(a0 + s * BM * BK + ks * 32);
+            for (int s = 0; s < S; ++s) {
+              uint64_t ad = sw64_desc(a0 + s * BM * BK + ks * 32);
 #pragma unroll
-            for (int t = 0; t < S; ++t) {
-              const int d = s + t;
-              uint64_t bd = sw64_desc(b0 + t * C::BNB * BK + ks * 32);
-              const uint32_t acc = (init >> d) & 1u;
-              if (t == 0) umma_i8<0, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
-              else if (t == S - 1) umma_i8<2, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
-              else umma_i8<1, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
-              init |= 1u << d;
+              for (int t = 0; t < S; ++t) {
+                const int d = s + t;
+                uint64_t bd = sw64_desc(b0 + t * C::BNB * BK + ks * 32);
+                const uint32_t acc = (init >> d) & 1u;
+                if (t == 0) umma_i8<0, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+                else if (t == S - 1) umma_i8<2, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+                else umma_i8<1, PAIR>(tmem + d * C::BN, ad, bd, C::IDESC, acc);
+                init |= 1u << d;
+              }
             }
           }
-        }
-        if (PAIR) {   // the slot is free in both CTAs
-          umma_commit_pair(&empty[st]);
-        } else {
-          umma_commit(&empty[st]);
-        }
-      }
-      if (it + 1 < nkb) {
-        tc_fence_before();
-        asm volatile("bar.arrive %0, 64;" ::"r"(1 + (me ^ 1)) : "memory");
-      }
-    }
-    if (PAIR) {
-      umma_commit_pair(tfull);
-    } else {
-      umma_commit(tfull);
-    }
-    __syncwarp();
-  }
-
-  // ---------------------------------------------------------------- epilogue
-  // Eight warps: warp w reads TMEM lane quarter w & 3 (tile rows 32q..32q+31,
-  // the only lanes its tcgen05.ld may touch) and column half w >> 2.
-  // The issuing warps commit to tfull whether or not they aborted, so this wait
-  // (bounded, but not cut short by the abort word) also drains every MMA in
-  // flight before TMEM is read or released.
-  ok = mbar_wait(tfull, 0, 4, nullptr, true) && ok && !*abort;
-  tc_fence_after();
-  const int q4 = warp & 3, half = warp >> 2;
-  const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
-  // The epilogue only moves the exact main sums out (Q = sum_d acc_d 128^d, in
-  // Cfg::QW int64 words) -- staged per lane quarter in the idle pipeline
-  // buffers, [32 rows][BN + 1] int64 per word, conflict-free both ways -- and
-  // stores them row by row (coalesced) into this launch's tile-compact buffer.
-  // Rounding, tail corrections and the stores of the bposit32 outputs run in
-  // k_tc_finish at full occupancy: done here, with one CTA of 8 warps per SM,
-  // they took a third to three quarters of a short-K tile's time.
-  constexpr int CW = C::BN / 2, QW = C::QW, STG = 4 * 32 * (C::BN + 1);
-  static_assert(C::BN % 32 == 0 && CW % 16 == 0, "BN must be a multiple of 32");
-  static_assert(QW * STG * 8 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
-  long long *stg = (long long *)smem + q4 * 32 * (C::BN + 1);
-#pragma unroll 1
-  for (int c0 = half * CW; c0 < half * CW + CW; c0 += 16) {
-    uint32_t v[C::D][16];
-#pragma unroll
-    for (int d = 0; d < C::D; ++d) tmem_ld16(trow + d * C::BN + c0, v[d]);
-    tmem_ld_wait();
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-      long long lo = 0, hi = 0;
-#pragma unroll
-      for (int d = 0; d < C::D; ++d) {
-        if (QW == 1 || d < 4) lo += (long long)(int)v[d][jj] * (1ll << (C::DB * d));
-        else hi += (long long)(int)v[d][jj] * (1ll << (C::DB * (d - 4)));
-      }
-      stg[lane * (C::BN + 1) + c0 + jj] = lo;
-      if (QW == 2) stg[STG + lane * (C::BN + 1) + c0 + jj] = hi;
-    }
-  }
-  {
-    // the two warps of a lane quarter meet, then each stores half of its rows
-    asm volatile("bar.sync %0, 64;" ::"r"(3 + q4) : "memory");
-    long long *dst = p.qbuf + ((size_t)(tile - p.tile0) * p.split + chunk) * QW * C::MM * C::BN +
-                     (size_t)(rank * BM + q4 * 32) * C::BN;
-    if (ok) {
-#pragma unroll 1
-      for (int rr = half * 16; rr < half * 16 + 16; ++rr) {
-#pragma unroll
-        for (int w = 0; w < QW; ++w)
-#pragma unroll
-          for (int qq = 0; qq < C::BN / 32; ++qq) {
-            const int cc = qq * 32 + lane;
-            dst[(size_t)w * C::MM * C::BN + (size_t)rr * C::BN + cc] = stg[w * STG + rr * (C::BN + 1) + cc];
+          if (PAIR) {   // the slot is free in both CTAs
+            umma_commit_pair(&empty[st]);
+          } else {
+            umma_commit(&empty[st]);
           }
+        }
+        if (it + 1 < nkb) {
+          tc_fence_before();
+          asm volatile("bar.arrive %0, 64;" ::"r"(1 + (me ^ 1)) : "memory");
+        }
+      }
+      if (PAIR) {
+        umma_commit_pair(tfull);
+      } else {
+        umma_commit(tfull);
+      }
+      __syncwarp();
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    // Eight warps: warp w reads TMEM lane quarter w & 3 (tile rows 32q..32q+31,
+    // the only lanes its tcgen05.ld may touch) and column half w >> 2.
+    // The issuing warps commit to tfull whether or not they aborted, so this wait
+    // (bounded, but not cut short by the abort word) also drains every MMA in
+    // flight before TMEM is read or released.
+    ok = mbar_wait(tfull, ucount & 1u, 4, nullptr, true) && ok && !*abort;
+    tc_fence_after();
+    const int q4 = warp & 3, half = warp >> 2;
+    const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+    // The epilogue only moves the exact main sums out (Q = sum_d acc_d 2^(DB d),
+    // in Cfg::QW int64 words) -- staged per lane quarter in the idle pipeline
+    // buffers, [32 rows][BN + 1] int64 per word, conflict-free both ways -- and
+    // stores them row by row (coalesced) into this launch's tile-compact buffer.
+    // Rounding, tail corrections and the stores of the bposit32 outputs run in
+    // k_tc_finish at full occupancy: done here, with one CTA of 8 warps per SM,
+    // they took a third to three quarters of a short-K tile's time.
+    constexpr int CW = C::BN / 2, QW = C::QW, STG = 4 * 32 * (C::BN + 1);
+    static_assert(C::BN % 32 == 0 && CW % 16 == 0, "BN must be a multiple of 32");
+    static_assert(QW * STG * 8 <= C::STAGES * C::STAGE_BYTES, "staging fits the pipeline");
+    long long *stg = (long long *)smem + q4 * 32 * (C::BN + 1);
+#pragma unroll 1
+    for (int c0 = half * CW; c0 < half * CW + CW; c0 += 16) {
+      uint32_t v[C::D][16];
+#pragma unroll
+      for (int d = 0; d < C::D; ++d) tmem_ld16(trow + d * C::BN + c0, v[d]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        long long lo = 0, hi = 0;
+#pragma unroll
+        for (int d = 0; d < C::D; ++d) {
+          if (QW == 1 || d < 4) lo += (long long)(int)v[d][jj] * (1ll << (C::DB * d));
+          else hi += (long long)(int)v[d][jj] * (1ll << (C::DB * (d - 4)));
+        }
+        stg[lane * (C::BN + 1) + c0 + jj] = lo;
+        if (QW == 2) stg[STG + lane * (C::BN + 1) + c0 + jj] = hi;
       }
     }
+    {
+      // the two warps of a lane quarter meet, then each stores half of its rows
+      asm volatile("bar.sync %0, 64;" ::"r"(3 + q4) : "memory");
+      long long *dst = p.qbuf + ((size_t)tl * p.split + chunk) * QW * C::MM * C::BN +
+                       (size_t)(rank * BM + q4 * 32) * C::BN;
+      if (ok) {
+#pragma unroll 1
+        for (int rr = half * 16; rr < half * 16 + 16; ++rr) {
+#pragma unroll
+          for (int w = 0; w < QW; ++w)
+#pragma unroll
+            for (int qq = 0; qq < C::BN / 32; ++qq) {
+              const int cc = qq * 32 + lane;
+              dst[(size_t)w * C::MM * C::BN + (size_t)rr * C::BN + cc] = stg[w * STG + rr * (C::BN + 1) + cc];
+            }
+        }
+      }
+    }
+    gk += (uint32_t)nkb;
+    // the staging above (generic proxy) before the next unit's loads (async
+    // proxy) into the same buffers; TMEM reads before the next unit's MMAs
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    if (PAIR) cluster_sync_all();
+    else __syncthreads();
+    tc_fence_after();
+    // A CTA that gave up on a bounded wait takes no further units, nor does its
+    // partner: both read both abort words after the barrier (every wait of the
+    // unit has ended by then, so the words are final and both CTAs agree).
+    bool stop = *abort != 0;
+    if (PAIR) {
+      uint32_t peer;
+      asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(peer) : "r"(cluster_smem((const void *)abort, rank ^ 1u)));
+      stop = stop || peer != 0u;
+    }
+    if (stop) break;
   }
   if (p.n_extra) __threadfence_system();   // peer stores complete before the kernel does
   tc_fence_before();
@@ -769,10 +807,12 @@ __device__ __forceinline__ void finish_row_f32(const TcParams &p, const FinishCo
     uint32_t code = 0u;
     float f = 0.0f;
     if (QW == 1) {
-      // the fp32 hand-off straight from the exact sum (bp32_value_i64) when the
-      // code is not stored; otherwise from the code
+      // the fp32 hand-off straight from the exact sum when the code is not
+      // stored: in integers without a bias (bp32_f32_i64), else through
+      // float64 (bp32_value_i64); otherwise from the code
       double v;
-      if (frow && !orow && p.n_extra == 0 && bp32_value_i64(qv[q], L, rex + c.fe[q], v)) {
+      if (frow && !orow && p.n_extra == 0 && c.fb[q] == 0.0f && bp32_f32_i64(qv[q], L, rex + c.fe[q], f)) {
+      } else if (frow && !orow && p.n_extra == 0 && bp32_value_i64(qv[q], L, rex + c.fe[q], v)) {
         f = __double2float_rn(v + (double)c.fb[q]);
       } else {
         code = bp32_from_i64(qv[q], L);
@@ -997,15 +1037,28 @@ __global__ void __launch_bounds__(256, F32 ? 3 : 4) k_tc_finish_staged(TcParams 
     }
     return;
   }
-  auto issue = [&](long long g) {   // thread 0: bulk copies of chunk g into buffer g % kFinStages
-    const long long it = blockIdx.x + (g / cpi) * gridDim.x;
-    const int c = (int)(g % cpi);
-    const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
-    const long long *src = p.qbuf + (size_t)tl * QW * PT + (size_t)(part * rpp + 8 * c) * BN;
+  // Chunk g of this block is chunk g % cpi of its item g / cpi; both are
+  // walked with counters (a 64-bit division per chunk cost more than the
+  // chunk's rounding).  Thread 0's issue cursor: item ii, chunk ic, the
+  // item's source rows.
+  long long ii = 0;
+  int ic = 0;
+  const long long *isrc = nullptr;
+  auto issue = [&](long long g) {   // thread 0: bulk copies of the next chunk (g) into buffer g % kFinStages
+    if (ic == 0) {
+      const long long it = blockIdx.x + ii * gridDim.x;
+      const int tl = (int)(it / parts), part = (int)(it - (long long)tl * parts);
+      isrc = p.qbuf + (size_t)tl * QW * PT + (size_t)(part * rpp) * BN;
+    }
+    const long long *src = isrc + (size_t)(8 * ic) * BN;
     const int st = (int)(g % kFinStages);
     mbar_expect_tx(&bar[st], QW * CHUNK);
 #pragma unroll
     for (int w = 0; w < QW; ++w) bulk_g2s(buf + ((size_t)st * QW + w) * 8 * BN, src + w * PT, CHUNK, &bar[st]);
+    if (++ic == cpi) {
+      ic = 0;
+      ++ii;
+    }
   };
   if (threadIdx.x == 0) {
     for (int st = 0; st < kFinStages; ++st) mbar_init(&bar[st], 1);
@@ -1015,13 +1068,11 @@ __global__ void __launch_bounds__(256, F32 ? 3 : 4) k_tc_finish_staged(TcParams 
   }
   __syncthreads();
   FinishCols<PL> c;
-  long long cur = -1;
+  long long item = 0;
+  int ci = 0;
   int tm = 0, tn = 0, j0 = 0, part = 0, rend = 0;
   for (long long g = 0; g < total; ++g) {
-    const long long item = g / cpi;
-    const int ci = (int)(g % cpi);
-    if (item != cur) {   // columns of the new item, loaded once
-      cur = item;
+    if (ci == 0) {   // columns of the new item, loaded once
       const long long it = blockIdx.x + item * gridDim.x;
       const int tl = (int)(it / parts);
       part = (int)(it - (long long)tl * parts);
@@ -1073,6 +1124,10 @@ __global__ void __launch_bounds__(256, F32 ? 3 : 4) k_tc_finish_staged(TcParams 
     __syncthreads();   // every warp is done with buffer st
     if (s_abort) break;
     if (threadIdx.x == 0 && g + kFinStages < total) issue(g + kFinStages);
+    if (++ci == cpi) {
+      ci = 0;
+      ++item;
+    }
   }
   if (p.n_extra) __threadfence_system();
 }
@@ -1529,172 +1584,338 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
   }
 }
 
-// K-major copies for the narrow form's corrections: codes [rows][K] (bp8) ->
-// [K][ldt] (ldt = rows rounded up to 16, padding columns zero), so that a tail
-// element's column of the other operand is one contiguous row.  64 x 64-byte
-// tiles: each thread transposes a 4 x 4 byte block in registers (byte
-// permutes), parks the four column words in shared memory, then stores 16
-// bytes of one output row.  Grid (ceil(K / 64), ceil(ldt / 64)).
-__global__ void __launch_bounds__(256) k_transpose_bp8(const uint8_t *__restrict__ src, int rows, int K,
-                                                       uint8_t *__restrict__ dst, int ldt) {
-  __shared__ uint32_t tw[64][17];   // [k][row / 4], one pad word
-  const int t = threadIdx.x;
-  const int k0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
-  const int br = t >> 4, bc = t & 15;   // 4 x 4 block: rows r0 + 4br.., columns k0 + 4bc..
-  const bool vec = (K & 3) == 0 && (((uintptr_t)src) & 3u) == 0;
-  uint32_t w[4];
+// K-major copies for the narrow form's corrections, decoded: codes [rows][K]
+// (bp8) -> two byte planes [K][ldt] (ldt = rows rounded up to 16, padding
+// columns zero): M, the signed mantissa m (value = m 2^lsb, |m| <= 15), and E,
+// the lsb exponent above the row's minimum, lsb - la_r (0 .. hb_r - la_r, below
+// 64 for bp8).  A tail element's column of the other operand is then one
+// contiguous row of each plane, and the correction needs no table.  With `Lr`
+// (the rows' main bases) every element whose lsb lies below its row's base --
+// a listed tail element -- is written as m = 0: the copy holds the main part.
+// Zero and NaR are m = 0.
+// Blocks stride over tiles of 64 rows x 256 columns: thread t loads 16 bytes
+// of each of 4 rows, transposes the 4 x 16 block in registers (byte
+// permutes), decodes its 64 codes through a table replicated per lane (entry
+// (code, lane) at word 32 code + lane: every lane in its own bank; built once
+// per block), parks the M and E words in shared memory (row k's word slots
+// rotated by k / 16, so a warp's 32 stores hit 32 banks), then stores 64
+// bytes of one output row of each plane.  kKmajSmem bytes of dynamic shared
+// memory.
+constexpr int kKmajK = 256;
+constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 32 * 4;
+
+__global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
+                                                    int8_t *__restrict__ dm, uint8_t *__restrict__ de, int ldt,
+                                                    const int4 *__restrict__ st, const int *__restrict__ Lr) {
+  extern __shared__ __align__(16) uint32_t kms[];
+  uint32_t(*tm)[17] = (uint32_t(*)[17])kms;                // [k][row / 4], one pad word
+  uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
+  uint32_t *s_dec = kms + 2 * kKmajK * 17;                 // (lsb + 128) << 8 | (uint8) m, per lane
+  __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
+  const int t = threadIdx.x, lane = t & 31;
+  {
+    int m, e;
+    posit_to_me<8, 2>((uint32_t)t, m, e);
+    // bp8 lsb exponents lie in [-24, 24]: the entry of a nonzero code is nonzero
+    const uint32_t d = m ? ((uint32_t)(e + 128) << 8) | (uint32_t)(uint8_t)(int8_t)m : 0u;
+    for (int l = 0; l < 32; ++l) s_dec[t * 32 + l] = d;
+  }
+  const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 16bc .. + 15
+  const bool vec = (K & 15) == 0 && (((uintptr_t)src) & 15u) == 0;
+  const int tk = (K + kKmajK - 1) / kKmajK, tr = (ldt + 63) / 64;
+  for (long long tile = blockIdx.x; tile < (long long)tk * tr; tile += gridDim.x) {
+    const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
+    __syncthreads();   // the previous tile's rows and staging are no longer read
+    if (t < 64) {
+      const bool v = r0 + t < rows;
+      s_la[t] = v ? st[r0 + t].x : 0;
+      s_L[t] = (v && Lr) ? Lr[r0 + t] : -0x3FFFFFFF;
+    }
+    __syncthreads();
+    // per byte i (row 4br + i): la + 128 and the base L + 128 clamped to 0 .. 255
+    uint32_t la4 = 0u, L4 = 0u;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int r = r0 + 4 * br + i, k = k0 + 4 * bc;
-    uint32_t v = 0u;
-    if (r < rows) {
-      const uint8_t *row = src + (size_t)r * K;
-      if (vec && k + 4 <= K) {
-        v = *(const uint32_t *)(row + k);
-      } else {
+    for (int i = 0; i < 4; ++i) {
+      la4 |= (uint32_t)(s_la[4 * br + i] + 128) << (8 * i);
+      L4 |= (uint32_t)min(max(s_L[4 * br + i] + 128, 0), 255) << (8 * i);
+    }
+    uint4 w[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (k + q < K) v |= (uint32_t)row[k + q] << (8 * q);
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + 4 * br + i, k = k0 + 16 * bc;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < rows) {
+        const uint8_t *row = src + (size_t)r * K;
+        if (vec && k + 16 <= K) {
+          v = __ldcs((const uint4 *)(row + k));
+        } else {
+          uint32_t b[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (k + q < K) b[q >> 2] |= (uint32_t)row[k + q] << (8 * (q & 3));
+          v = make_uint4(b[0], b[1], b[2], b[3]);
+        }
+      }
+      w[i] = v;
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {   // columns 4g .. 4g + 3 of the thread's 16
+      const uint32_t r0w = g == 0 ? w[0].x : g == 1 ? w[0].y : g == 2 ? w[0].z : w[0].w;
+      const uint32_t r1w = g == 0 ? w[1].x : g == 1 ? w[1].y : g == 2 ? w[1].z : w[1].w;
+      const uint32_t r2w = g == 0 ? w[2].x : g == 1 ? w[2].y : g == 2 ? w[2].z : w[2].w;
+      const uint32_t r3w = g == 0 ? w[3].x : g == 1 ? w[3].y : g == 2 ? w[3].z : w[3].w;
+      // column q: byte q of each row word (bytes in row order)
+      const uint32_t a01 = __byte_perm(r0w, r1w, 0x5140), a23 = __byte_perm(r2w, r3w, 0x5140);
+      const uint32_t b01 = __byte_perm(r0w, r1w, 0x7362), b23 = __byte_perm(r2w, r3w, 0x7362);
+      const uint32_t cw[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
+                              __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        // the four rows' entries; byte i of lw is row i's lsb + 128 (0 for zero / NaR)
+        const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 32 + lane];
+        const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 32 + lane];
+        const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 32 + lane];
+        const uint32_t d3 = s_dec[(cw[q] >> 24) * 32 + lane];
+        const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
+        const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
+        const uint32_t keep = __vcmpgeu4(lw, L4) & __vcmpne4(lw, 0u);
+        // word br of row k sits at slot (br + k / 16) % 16: the 32 lanes of a
+        // warp (bc = 0..15, two br) then store to 32 different banks
+        tm[16 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
+        te[16 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
       }
     }
-    w[i] = v;
+    __syncthreads();
+    // output rows k0 .. k0 + 255, 64 bytes (rows r0 .. r0 + 63) each per plane:
+    // four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
+    const int c = t & 3, r = r0 + 16 * c;
+#pragma unroll
+    for (int pass = 0; pass < kKmajK / 64; ++pass) {
+      const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 4;
+      if (k < K && r < ldt) {
+        uint32_t vm[4], ve[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          vm[j] = tm[kk][(4 * c + j + rot) & 15];
+          ve[j] = te[kk][(4 * c + j + rot) & 15];
+        }
+        *(uint4 *)(dm + (size_t)k * ldt + r) = make_uint4(vm[0], vm[1], vm[2], vm[3]);
+        *(uint4 *)(de + (size_t)k * ldt + r) = make_uint4(ve[0], ve[1], ve[2], ve[3]);
+      }
+    }
   }
-  // column q of the block: byte q of each row word
-  const uint32_t a01 = __byte_perm(w[0], w[1], 0x5140), a23 = __byte_perm(w[2], w[3], 0x5140);
-  const uint32_t b01 = __byte_perm(w[0], w[1], 0x7362), b23 = __byte_perm(w[2], w[3], 0x7362);
-  tw[4 * bc + 0][br] = __byte_perm(a01, a23, 0x5410);
-  tw[4 * bc + 1][br] = __byte_perm(a01, a23, 0x7632);
-  tw[4 * bc + 2][br] = __byte_perm(b01, b23, 0x5410);
-  tw[4 * bc + 3][br] = __byte_perm(b01, b23, 0x7632);
-  __syncthreads();
-  const int kk = t >> 2, c = t & 3;   // output row k0 + kk, bytes r0 + 16c .. + 15
-  const int k = k0 + kk, r = r0 + 16 * c;
-  if (k < K && r < ldt)
-    *(uint4 *)(dst + (size_t)k * ldt + r) =
-        make_uint4(tw[kk][4 * c], tw[kk][4 * c + 1], tw[kk][4 * c + 2], tw[kk][4 * c + 3]);
 }
 
 // Tail corrections of the narrow form (bp8, unscaled), the same sums as
-// k_tc_corr read from the other operand's K-major copy:
+// k_tc_corr read from the other operand's decoded K-major copy:
 //   C[s][y] = sum over tail elements (x, k) of row x (slot s):  v(X[x,k]) * v(Y[y,k])
-// in units of 2^(la_x + la_y), skipping Y's own tail elements when YL is given.
-// A block takes a slot's tail list into shared memory (column k, mantissa,
-// lsb above la_x), then each thread owns kCorrCols consecutive y and reads
-// their codes of row k of Yt as one 8-byte word per tail element, kCorrTU
-// tail elements' words in flight at a time (the kernel runs beside the GEMM
-// and was bound by the latency of these loads).  The sums are int64 when the
-// largest term and the term count leave them exact (the row statistics bound
-// the shift), else 128-bit.
-constexpr int kCorrCols = 8, kCorrTU = 4, kCorrSpan = 256 * kCorrCols;   // columns per block pass
+// in units of 2^(la_x + la_y).  Side 0 (A's tail rows) reads all of B; side 1
+// (B's tail rows) reads A's main part -- its copy has A's own tail elements
+// zeroed -- so the two sides add up to A.B - A_main.B_main.
+// One warp per slot, no block barrier.  The warp lists up to kCorrChunk of the
+// slot's tail elements in its own shared memory (column k, m_a, lsb_a - la_x)
+// and takes the columns in passes of kCorrPass: for each tail element, lane 0
+// streams that pass's slice of row k of both planes into the warp's ring of
+// kCorrRing shared-memory stages by bulk copies (one mbarrier per stage,
+// kCorrRing elements in flight), and each lane adds the terms of its
+// kCorrCols columns from the stage (the register-load form was bound by the
+// latency of its loads).  A term is (m_a << ea) * (m << e) with ea = lsb_a -
+// la_x <= emax (the slot's largest) and e = lsb - la_y <= hr (the other
+// operand's widest row range, from the prep's counters); |term| <
+// 2^(8 + emax + hr).  While 8 + emax + hr + lgT <= 62 the sums are int64 (two's
+// complement words): one 32 x 32 -> 64-bit multiply-add per term when both
+// factors fit 32 bits (emax <= 26, hr <= 27), else a 64-bit shift of m_a m.
+// Otherwise 128-bit shifts.  Every wait is bounded: a timeout records code 32
+// in g_tc_error, waits (bounded) for the warp's copies in flight and ends the
+// warp.
+constexpr int kCorrCols = 16, kCorrChunk = 256, kCorrPass = 32 * kCorrCols, kCorrRing = 8, kCorrWarps = 8;
+constexpr size_t kCorrWarpSmem = 2 * (size_t)kCorrRing * kCorrPass + (size_t)kCorrChunk * 8 + kCorrRing * 8;
+constexpr size_t kCorrSmem = kCorrWarps * kCorrWarpSmem;
 
 struct CorrT {
-  const uint8_t *X, *Yt;
+  const uint8_t *X;
+  const int8_t *Ym;
+  const uint8_t *Ye;
   int Yrows, ldt;
-  const int4 *xst, *yst;
-  const int *YL;
+  const int4 *xst;
   const int4 *seg;
   const int *tails;
-  const TcCounters *ctr;
+  const TcCounters *ctr, *yctr;   // this side's slots; the other operand's counters (v[3]: max hb - la)
   int cap;
   ulonglong2 *Cout;
-  int gx, gy;
 };
 
-template <bool WIDE>
-__device__ __forceinline__ void corr_cols(const CorrT &c, const uint32_t *s_dec, const int2 *s_t, int T, int y,
-                                          const int (&lay)[kCorrCols], const int (&ly)[kCorrCols],
-                                          ulonglong2 (&out)[kCorrCols]) {
+enum { kCorrMul = 0, kCorrShift = 1, kCorrWide = 2 };
+
+// The warp's shared memory: the ring's M and E stages, the list, the barriers.
+struct CorrWarp {
+  uint8_t *rm, *re;
+  int2 *lst;
+  uint64_t *bar;
+  uint32_t g;   // bulk copies issued so far (stage g % kCorrRing, phase (g / kCorrRing) & 1)
+};
+
+// Lane 0: the copies of tail element `k`'s pass slice into stage g % kCorrRing.
+__device__ __forceinline__ void corr_issue(const CorrT &c, CorrWarp &w, uint32_t g, int k, int y0, int bytes) {
+  const int st = (int)(g % kCorrRing);
+  mbar_expect_tx(&w.bar[st], 2u * (uint32_t)bytes);
+  const size_t off = (size_t)k * c.ldt + y0;
+  bulk_g2s(w.rm + st * kCorrPass, c.Ym + off, (uint32_t)bytes, &w.bar[st]);
+  bulk_g2s(w.re + st * kCorrPass, c.Ye + off, (uint32_t)bytes, &w.bar[st]);
+}
+
+// One pass (columns y0 .. y0 + kCorrPass - 1) of one slot.  Returns false
+// after a timed-out wait (the warp's copies in flight have been waited for).
+template <int MODE>
+__device__ __forceinline__ bool corr_pass(const CorrT &c, CorrWarp &w, int4 sg, int la_x, int K, int y0, int lane,
+                                          ulonglong2 *__restrict__ o) {
+  constexpr bool WIDE = MODE == kCorrWide;
   using Acc = typename std::conditional<WIDE, unsigned __int128, unsigned long long>::type;
   Acc acc[kCorrCols];
 #pragma unroll
   for (int q = 0; q < kCorrCols; ++q) acc[q] = 0;
-  const uint8_t *col = c.Yt + y;
-  for (int t0 = 0; t0 < T; t0 += kCorrTU) {
-    uint2 w[kCorrTU];
-    int2 te[kCorrTU];
-#pragma unroll
-    for (int u = 0; u < kCorrTU; ++u) {
-      const bool v = t0 + u < T;
-      te[u] = s_t[v ? t0 + u : t0];
-      // a missing element reads as zero codes, which add nothing
-      w[u] = v ? __ldg((const uint2 *)(col + (size_t)te[u].x * c.ldt)) : make_uint2(0u, 0u);
+  const int T = sg.y;
+  const int bytes = min(kCorrPass, c.ldt - y0);   // a multiple of 16
+  const bool mine = 16 * lane < bytes;            // this lane's 16 columns lie in the slice
+  for (int c0 = 0; c0 < T; c0 += kCorrChunk) {
+    const int n = min(kCorrChunk, T - c0);
+    if (T > kCorrChunk) {   // longer lists are re-read per chunk (no copy in flight here)
+      __syncwarp();
+      for (int t = lane; t < n; t += 32) {
+        const int k = c.tails[sg.x + c0 + t];
+        int m, e;
+        posit_to_me<8, 2>((uint32_t)c.X[(size_t)sg.z * K + k], m, e);
+        w.lst[t] = make_int2(k, (m & 0xFFFF) | ((e - la_x) << 16));
+      }
+      __syncwarp();
     }
-#pragma unroll
-    for (int u = 0; u < kCorrTU; ++u) {
-      const int ma = (int)(short)(te[u].y & 0xFFFF), ea = te[u].y >> 16;
-#pragma unroll
-      for (int q = 0; q < kCorrCols; ++q) {
-        const uint32_t d = s_dec[((q < 4 ? w[u].x : w[u].y) >> (8 * (q & 3))) & 0xFFu];
-        const int m = dec_m(d), lsb = dec_lsb(d);
-        if (m != 0 && lsb >= ly[q]) {
-          if (WIDE) {
-            const int sh = min(max(ea + lsb - lay[q], 0), 127);
-            acc[q] += (unsigned __int128)(__int128)(long long)(ma * m) << sh;
-          } else {
-            acc[q] += (unsigned long long)(long long)(ma * m) << (ea + lsb - lay[q]);
+    const uint32_t g0 = w.g;
+    if (lane == 0)
+      for (int j = 0; j < min(kCorrRing, n); ++j) corr_issue(c, w, g0 + j, w.lst[j].x, y0, bytes);
+    for (int t = 0; t < n; ++t) {
+      const uint32_t gi = g0 + t;
+      const int st = (int)(gi % kCorrRing);
+      if (!mbar_wait_warp(&w.bar[st], (gi / kCorrRing) & 1u, 32)) {
+        // wait, bounded, for the copies still in flight, then give up
+        if (lane == 0)
+          for (int u = t; u < min(n, t + kCorrRing); ++u) {   // issued: 0 .. t + kCorrRing - 1
+            const uint32_t gu = g0 + u;
+            const long long t1 = clock64();
+            while (!mbar_try_wait(&w.bar[gu % kCorrRing], (gu / kCorrRing) & 1u) && clock64() - t1 < DRAIN_LIMIT)
+              __nanosleep(256);
           }
+        __syncwarp();
+        return false;
+      }
+      if (mine) {
+        const uint4 wm = *(const uint4 *)(w.rm + st * kCorrPass + 16 * lane);
+        const uint4 we = *(const uint4 *)(w.re + st * kCorrPass + 16 * lane);
+        const int me = w.lst[t].y;
+        const int ma = (int)(short)(me & 0xFFFF), ea = me >> 16;
+        const int a32 = (int)((unsigned)ma << (ea & 31));   // used when ea <= 26
+#pragma unroll
+        for (int q = 0; q < kCorrCols; ++q) {
+          const uint32_t wmq = q < 4 ? wm.x : q < 8 ? wm.y : q < 12 ? wm.z : wm.w;
+          const uint32_t weq = q < 4 ? we.x : q < 8 ? we.y : q < 12 ? we.z : we.w;
+          const int m = (int)(int8_t)(wmq >> (8 * (q & 3)));
+          const int e = (int)((weq >> (8 * (q & 3))) & 0xFFu);
+          if (MODE == kCorrWide) acc[q] += (unsigned __int128)(__int128)(ma * m) << min(ea + e, 127);
+          else if (MODE == kCorrShift) acc[q] += (unsigned long long)(long long)(ma * m) << (ea + e);
+          else acc[q] += (unsigned long long)((long long)a32 * (long long)(int)((unsigned)m << e));
         }
       }
+      __syncwarp();   // every lane is done with stage st
+      if (lane == 0 && t + kCorrRing < n) corr_issue(c, w, gi + kCorrRing, w.lst[t + kCorrRing].x, y0, bytes);
+    }
+    w.g = g0 + (uint32_t)n;
+  }
+  const int y = y0 + kCorrCols * lane;
+  if (y < c.Yrows) {
+#pragma unroll
+    for (int q = 0; q < kCorrCols; ++q) {
+      if (y + q >= c.Yrows) continue;
+      if (WIDE) o[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((unsigned __int128)acc[q] >> 64));
+      else o[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((long long)acc[q] >> 63));
     }
   }
-#pragma unroll
-  for (int q = 0; q < kCorrCols; ++q) {
-    if (WIDE) out[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((unsigned __int128)acc[q] >> 64));
-    else out[q] = make_ulonglong2((unsigned long long)acc[q], (unsigned long long)((long long)acc[q] >> 63));
-  }
+  return true;
 }
 
-__global__ void __launch_bounds__(256) k_tc_corr_t(const CorrT s0, const CorrT s1, int K) {
-  __shared__ uint32_t s_dec[256];
-  __shared__ int2 s_t[TAILCAP];   // (k, mantissa | (lsb - la_x) << 16)
-  __shared__ int s_emax;
-  const CorrT c = blockIdx.z ? s1 : s0;
-  if ((int)blockIdx.x >= c.gx || (int)blockIdx.y >= c.gy) return;
-  for (int q = threadIdx.x; q < 256; q += blockDim.x) {
-    int m, e;
-    posit_to_me<8, 2>((uint32_t)q, m, e);
-    int hb = m ? e + 31 - __clz(m < 0 ? -m : m) : 0;
-    s_dec[q] = dec_pack(e, hb, m);
+// The 128-bit form out of line (rare: rows spanning more than ~50 binades).
+__device__ __noinline__ bool corr_pass_wide(const CorrT &c, CorrWarp &w, int4 sg, int la_x, int K, int y0, int lane,
+                                            ulonglong2 *__restrict__ o) {
+  return corr_pass<kCorrWide>(c, w, sg, la_x, K, y0, lane, o);
+}
+
+__global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0, const CorrT s1, int K) {
+  extern __shared__ __align__(16) uint8_t kcs[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t *base = kcs + warp * kCorrWarpSmem;
+  CorrWarp w;
+  w.rm = base;
+  w.re = base + kCorrRing * kCorrPass;
+  w.lst = (int2 *)(base + 2 * kCorrRing * kCorrPass);
+  w.bar = (uint64_t *)(base + 2 * kCorrRing * kCorrPass + kCorrChunk * 8);
+  w.g = 0;
+  if (lane == 0) {
+    for (int r = 0; r < kCorrRing; ++r) mbar_init(&w.bar[r], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  const int nslots = min(c.ctr->v[0], c.cap);
-  for (int sl = blockIdx.x; sl < nslots; sl += c.gx) {
-    const int4 sg = c.seg[sl];
-    const int x = sg.z, T = sg.y;
-    const int la_x = c.xst[x].x;
-    __syncthreads();   // the previous slot's list is no longer read
-    if (threadIdx.x == 0) s_emax = 0;
-    __syncthreads();
-    int em = 0;
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-      const int k = c.tails[sg.x + t];
-      const uint32_t d = s_dec[c.X[(size_t)x * K + k]];
-      const int er = dec_lsb(d) - la_x;   // >= 0: la_x is the row's min lsb
-      s_t[t] = make_int2(k, (dec_m(d) & 0xFFFF) | (er << 16));
-      em = max(em, er);
-    }
-    atomicMax(&s_emax, em);
-    __syncthreads();
-    const int emax = s_emax;
-    const int lgT = 32 - __clz(max(T, 1));   // >= ceil(log2(T + 1))
-    for (int y = blockIdx.y * kCorrSpan + kCorrCols * threadIdx.x; y < c.Yrows; y += c.gy * kCorrSpan) {
-      int lay[kCorrCols], ly[kCorrCols], hr = 0;
-#pragma unroll
-      for (int q = 0; q < kCorrCols; ++q) {
-        const bool v = y + q < c.Yrows;
-        const int4 st = v ? c.yst[y + q] : make_int4(0, 0, 0, 0);
-        lay[q] = st.x;
-        ly[q] = (v && c.YL) ? c.YL[y + q] : -0x3FFFFFFF;
-        hr = max(hr, st.y - st.x);
+  __syncwarp();
+  // Work units: (slot, 512-column pass), slot-major, taken one at a time from
+  // a counter (TcCounters v[8] of side 0, zeroed with the counters): slots hold
+  // 2 to ~80 tail elements, and a fixed split left most warps idle behind a few.
+  const int n0 = min(s0.ctr->v[0], s0.cap), n1 = min(s1.ctr->v[0], s1.cap);
+  const int np0 = (s0.Yrows + kCorrPass - 1) / kCorrPass, np1 = (s1.Yrows + kCorrPass - 1) / kCorrPass;
+  const long long nu0 = (long long)n0 * np0, nu = nu0 + (long long)n1 * np1;
+  int *queue = const_cast<int *>(&s0.ctr->v[8]);
+  int cur = -1;   // the slot item whose list is loaded
+  int4 sg = make_int4(0, 0, 0, 0);
+  int la_x = 0, mode = kCorrShift;
+  for (;;) {
+    long long u = 0;
+    if (lane == 0) u = atomicAdd(queue, 1);
+    u = __shfl_sync(0xFFFFFFFFu, u, 0);
+    if (u >= nu) break;
+    const bool second = u >= nu0;
+    const CorrT &c = second ? s1 : s0;
+    const long long uu = second ? u - nu0 : u;
+    const int np = second ? np1 : np0;
+    const int sl = (int)(uu / np), y0 = (int)(uu % np) * kCorrPass;
+    const int item = second ? n0 + sl : sl;
+    if (item != cur) {
+      cur = item;
+      sg = c.seg[sl];
+      const int x = sg.z, T = sg.y;
+      la_x = c.xst[x].x;
+      // the first chunk of the list, and the slot's largest tail exponent
+      int em = 0;
+      __syncwarp();
+      for (int t = lane; t < min(T, kCorrChunk); t += 32) {
+        const int k = c.tails[sg.x + t];
+        int m, e;
+        posit_to_me<8, 2>((uint32_t)c.X[(size_t)x * K + k], m, e);
+        w.lst[t] = make_int2(k, (m & 0xFFFF) | ((e - la_x) << 16));   // e >= la_x: the row's min lsb
+        em = max(em, e - la_x);
       }
-      ulonglong2 out[kCorrCols];
-      // |term| < 2^(8 + emax + hr), at most T terms: int64 is exact (added as
-      // two's complement words)
-      if (emax + hr + 8 + lgT <= 62) corr_cols<false>(c, s_dec, s_t, T, y, lay, ly, out);
-      else corr_cols<true>(c, s_dec, s_t, T, y, lay, ly, out);
-#pragma unroll
-      for (int q = 0; q < kCorrCols; ++q)
-        if (y + q < c.Yrows) c.Cout[(size_t)sl * c.Yrows + y + q] = out[q];
+      for (int t = kCorrChunk + lane; t < T; t += 32) {
+        int m, e;
+        posit_to_me<8, 2>((uint32_t)c.X[(size_t)x * K + c.tails[sg.x + t]], m, e);
+        em = max(em, e - la_x);
+      }
+      em = __reduce_max_sync(0xFFFFFFFFu, em);
+      __syncwarp();
+      const int hr = c.yctr->v[3];
+      const int lgT = 32 - __clz(max(T, 1));   // >= ceil(log2(T + 1))
+      mode = em + hr + 8 + lgT > 62 ? kCorrWide : (em <= 26 && hr <= 27) ? kCorrMul : kCorrShift;
     }
+    ulonglong2 *o = c.Cout + (size_t)sl * c.Yrows + y0 + kCorrCols * lane;
+    bool ok;
+    if (mode == kCorrMul) ok = corr_pass<kCorrMul>(c, w, sg, la_x, K, y0, lane, o);
+    else if (mode == kCorrShift) ok = corr_pass<kCorrShift>(c, w, sg, la_x, K, y0, lane, o);
+    else ok = corr_pass_wide(c, w, sg, la_x, K, y0, lane, o);
+    if (!ok) return;
+    if (sg.y > kCorrChunk) cur = -1;   // the list buffer now holds a later chunk
   }
 }
 
@@ -1851,9 +2072,9 @@ TcLayout tc_layout(int fmt, int M, int N, int K, int S) {
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
   L.TA = L.TB = 0;
-  if (S == 2) {
-    L.TA = o; o += al((size_t)K * L.ldtA * (fmt / 8));
-    L.TB = o; o += al((size_t)K * L.ldtB * (fmt / 8));
+  if (S == 2) {   // two byte planes (mantissa, relative lsb) per copy
+    L.TA = o; o += al(2 * (size_t)K * L.ldtA);
+    L.TB = o; o += al(2 * (size_t)K * L.ldtB);
   }
   // room for either pairing's main sums (chosen at launch)
   L.part = o;
@@ -1921,8 +2142,12 @@ int launch_tc_gemm_kernel(const CUtensorMap &ma, const CUtensorMap &mb, const Tc
   cudaError_t attr_err = tc_kernel_attr<S, PAIR>();
   if (attr_err != cudaSuccess)
     return set_error(kECuda, "quire_gemm: cannot set shared memory size: %s", cudaGetErrorString(attr_err));
-  dim3 grid((unsigned)((PAIR ? 2 : 1) * ntiles), (unsigned)p.split, 1);
-  if (grid.y > 65535u) return set_error(kERange, "quire_gemm: too many K chunks");
+  // persistent: at most one resident CTA (pair) per SM (pair), each striding
+  // over the launch's (tile, K chunk) units
+  const long long units = (long long)ntiles * p.split;
+  if (units > 0x7FFFFFFFLL) return set_error(kERange, "quire_gemm: too many K chunks");
+  const int ncta = (int)std::min<long long>(units, std::max(1, tc_wave_capacity(PAIR)));
+  dim3 grid((unsigned)((PAIR ? 2 : 1) * ncta), 1, 1);
   if (!PAIR) {
     k_quire_gemm_tc<S, false><<<grid, THREADS, C::SMEM, s>>>(ma, mb, p);
     return check_launch("quire_gemm_tc");
@@ -2021,6 +2246,7 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
     p.kb_per_chunk = seg[k].kbc;
     // every tile before this segment ran whole
     p.qbuf = qbuf + (size_t)seg[k].tile0 * C::QW * C::MM * C::BN;
+    p.ntl = seg[k].n;
     rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, seg[k].n, s);
     if (rc) break;
     const bool on_s = k == nseg - 1 || !side || seg[k].n > 2 * seg[k + 1].kbc;
@@ -2112,36 +2338,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   PrepOp pb{a.B, a.N, a.sb, stb, planesB, LB, slotB, segB, tailB, L.capB, cB};
   if (reuse_a || b_only) pa.rows = 0;
   if (reuse_b || a_only) pb.rows = 0;
-  // The narrow form's K-major code copies of the operands prepared here, on
-  // the side stream beside the prep (the corrections that read them follow
-  // there); without a side stream, on the caller's stream.
-  SideStream *side = L.nkb >= 256 ? side_stream() : nullptr;
   int rc = kOk;
-  if (kmajor && pa.rows + pb.rows > 0) {
-    cudaStream_t ts = s;
-    if (side) {
-      if (cudaEventRecord(side->ev[3], s) == cudaSuccess && cudaStreamWaitEvent(side->st, side->ev[3], 0) == cudaSuccess)
-        ts = side->st;
-      else
-        return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
-    }
-    if (pa.rows) {
-      k_transpose_bp8<<<dim3((unsigned)((a.K + 63) / 64), (unsigned)((L.ldtA + 63) / 64)), 256, 0, ts>>>(
-          (const uint8_t *)a.A, a.M, a.K, (uint8_t *)(w + L.TA), L.ldtA);
-      rc = check_launch("tc_transpose");
-    }
-    if (!rc && pb.rows) {
-      k_transpose_bp8<<<dim3((unsigned)((a.K + 63) / 64), (unsigned)((L.ldtB + 63) / 64)), 256, 0, ts>>>(
-          (const uint8_t *)a.B, a.N, a.K, (uint8_t *)(w + L.TB), L.ldtB);
-      rc = check_launch("tc_transpose");
-    }
-    if (side && (a_only || b_only || rc)) {
-      // nothing else of this call runs on the side stream: join it here
-      if (cudaEventRecord(side->ev[4], side->st) != cudaSuccess || cudaStreamWaitEvent(s, side->ev[4], 0) != cudaSuccess)
-        if (!rc) rc = set_error(kECuda, "quire_gemm: side stream join: %s", cudaGetErrorString(cudaGetLastError()));
-    }
-    if (rc) return rc;
-  }
   if (pa.rows + pb.rows > 0) {
     const int g = std::min(pa.rows + pb.rows, sms * 8);
     if (a.fmt == 16)
@@ -2151,6 +2348,35 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     else
       k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     rc = check_launch("tc_prep");
+  }
+  // The narrow form's decoded K-major copies of the operands prepared here:
+  // B's whole, A's main part (its tail elements zeroed, by LA)
+  if (!rc && kmajor) {   // the copy kernel's shared-memory opt-in, once per device
+    static std::atomic<bool> attr_set[128];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128 ||
+        (!attr_set[dev].load() &&
+         cudaFuncSetAttribute(k_kmajor_bp8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKmajSmem) != cudaSuccess))
+      rc = set_error(kECuda, "quire_gemm: k-major copy attribute: %s", cudaGetErrorString(cudaGetLastError()));
+    else
+      attr_set[dev].store(true);
+  }
+  // the copy kernel's grid: three blocks per SM (67 KB each), striding over tiles
+  auto kmg = [&](int K, int ldt) {
+    const long long tiles = (long long)((K + kKmajK - 1) / kKmajK) * ((ldt + 63) / 64);
+    return (unsigned)std::max<long long>(1, std::min<long long>(tiles, 3LL * sms));
+  };
+  if (!rc && kmajor && pa.rows) {
+    int8_t *tm = (int8_t *)(w + L.TA);
+    k_kmajor_bp8<<<kmg(a.K, L.ldtA), 256, kKmajSmem, s>>>(
+        (const uint8_t *)a.A, a.M, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtA), L.ldtA, sta, LA);
+    rc = check_launch("tc_kmajor");
+  }
+  if (!rc && kmajor && pb.rows) {
+    int8_t *tm = (int8_t *)(w + L.TB);
+    k_kmajor_bp8<<<kmg(a.K, L.ldtB), 256, kKmajSmem, s>>>(
+        (const uint8_t *)a.B, a.N, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtB), L.ldtB, stb, nullptr);
+    rc = check_launch("tc_kmajor");
   }
   if (rc || a_only || b_only) return rc;
 
@@ -2186,22 +2412,37 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   // Only the finish kernels read them: with long K (64-deep K blocks >= 256)
   // they run on the side stream, at most two blocks per SM beside the GEMM's
   // first segment, instead of ahead of it.
+  // The narrow form's corrections run on the caller's stream, ahead of the
+  // GEMM: beside it, on the low-priority side stream, they were held back
+  // until the GEMM's last CTAs were dispatched and then kept its last wave
+  // from starting (their blocks' registers).
+  SideStream *side = (L.nkb >= 256 && !kmajor) ? side_stream() : nullptr;
   if (side && (cudaEventRecord(side->ev[3], s) != cudaSuccess ||
                cudaStreamWaitEvent(side->st, side->ev[3], 0) != cudaSuccess)) {
-    // the narrow form's copies were queued there: corrections stay behind them
-    if (kmajor) return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
     cudaGetLastError();
     side = nullptr;   // corrections on the caller's stream instead
   }
   const cudaStream_t cs = side ? side->st : s;
   if (kmajor) {
-    // each side's blocks: slots x column blocks of kCorrSpan
-    const CorrT ca{(const uint8_t *)a.A, (const uint8_t *)(w + L.TB), a.N, L.ldtB, sta, stb, nullptr, segA, tailA,
-                   cA, L.capA, CA, std::min(L.capA, sms * 4), (a.N + kCorrSpan - 1) / kCorrSpan};
-    const CorrT cb{(const uint8_t *)a.B, (const uint8_t *)(w + L.TA), a.M, L.ldtA, stb, sta, LA, segB, tailB,
-                   cB, L.capB, CB, std::min(L.capB, sms * 4), (a.M + kCorrSpan - 1) / kCorrSpan};
-    const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
-    k_tc_corr_t<<<gc, 256, 0, cs>>>(ca, cb, a.K);
+    // one warp per slot of either side, two 8-warp blocks per SM
+    const int8_t *tA = (const int8_t *)(w + L.TA), *tB = (const int8_t *)(w + L.TB);
+    const CorrT ca{(const uint8_t *)a.A, tB, (const uint8_t *)(tB + (size_t)a.K * L.ldtB), a.N, L.ldtB, sta,
+                   segA, tailA, cA, cB, L.capA, CA};
+    const CorrT cb{(const uint8_t *)a.B, tA, (const uint8_t *)(tA + (size_t)a.K * L.ldtA), a.M, L.ldtA, stb,
+                   segB, tailB, cB, cA, L.capB, CB};
+    static std::atomic<bool> corr_attr[128];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128 ||
+        (!corr_attr[dev].load() &&
+         cudaFuncSetAttribute(k_tc_corr_t, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCorrSmem) != cudaSuccess))
+      return set_error(kECuda, "quire_gemm: correction attribute: %s", cudaGetErrorString(cudaGetLastError()));
+    corr_attr[dev].store(true);
+    const int gc = sms * 2;
+    // the kernel's work counter (side A's v[8]; a call that reuses A's prepared
+    // state did not zero A's counters)
+    if (cudaMemsetAsync(&cA->v[8], 0, sizeof(int), cs) != cudaSuccess)
+      return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
+    k_tc_corr_t<<<gc, 32 * kCorrWarps, kCorrSmem, cs>>>(ca, cb, a.K);
   } else {
     const int cy = side ? 2 : 64;
     const CorrSide ca{a.A, a.B, a.N, a.sa, a.sb, sta, stb, nullptr, segA, tailA, cA, L.capA, CA,
