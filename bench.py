@@ -254,7 +254,7 @@ def kernel_breakdown(ctx, fn, steps=2):
             name = ev.name
             key = next((g for g, pats in (
                 ("prep", ("k_tc_prep",)), ("gemm", ("k_quire_gemm_tc", "k_quire_gemm_simt")),
-                ("tail_corr", ("k_tc_corr",)), ("kmajor_copy", ("k_transpose",)), ("finish", ("k_tc_finish",)),
+                ("tail_corr", ("k_tc_corr",)), ("kmajor_copy", ("k_kmajor",)), ("finish", ("k_tc_finish",)),
                 ("fixup", ("k_tc_fixup",)),
                 ("row_stats", ("k_row_stats",)), ("nccl", ("nccl",)), ("memcpy", ("Memcpy", "memcpy")),
                 ("memset", ("Memset", "memset"))) if any(p in name for p in pats)), "other")

@@ -33,19 +33,6 @@ BP_HD int clz64(uint64_t x) {
 #endif
 }
 
-// Index of the most significant set bit of x != 0, with one 32-bit
-// count-leading-zeros on the word that holds it (the finish kernels issue it
-// once per output; count-leading-zeros and type conversions share one pipe
-// of a quarter of the integer rate).
-BP_HD int msb64(uint64_t x) {
-  const uint32_t hi = (uint32_t)(x >> 32);
-#ifdef __CUDA_ARCH__
-  return hi ? 63 - __clz((int)hi) : 31 - __clz((int)(uint32_t)x);
-#else
-  return hi ? 63 - __builtin_clz(hi) : 31 - __builtin_clz((uint32_t)x);
-#endif
-}
-
 // Decoded posit: kind 0 = finite nonzero, 1 = zero, 2 = NaR.  For finite values
 // |value| = (2^fw + fbits) * 2^(scale - fw), scale = k*2^eS + e is the binade.
 struct Dec {
@@ -415,73 +402,45 @@ BP_HD uint32_t shr_clamp(uint32_t x, int s) {
 #endif
 }
 
+// Q as a double rounded toward zero (|Q| cut to 53 significant bits; exact
+// below 2^53): the device's conversion instruction, emulated on the host.
+BP_HD uint64_t i64_to_f64_rz_bits(long long Q) {
+#ifdef __CUDA_ARCH__
+  return (uint64_t)__double_as_longlong(__ll2double_rz(Q));
+#else
+  const bool neg = Q < 0;
+  uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
+  const int lz = clz64(m);
+  if (lz < 11) m &= ~((1ull << (11 - lz)) - 1ull);   // keep 53 significant bits
+  double d = (double)m;                              // now exact
+  if (neg) d = -d;
+  uint64_t b;
+  memcpy(&b, &d, 8);
+  return b;
+#endif
+}
+
 // bp32_from_mag for a sum that fits a signed 64-bit integer: value Q * 2^lsb_exp,
-// cut to the bposit32 bit string.  The leading one of |Q| gives the binade and
-// the 32 bits below it the top fraction bits (integer operations only: a
-// 64-bit conversion to double here kept the conversion pipe of the finish
-// kernels saturated).  The regime, the three exponent bits and those fraction
-// bits are laid out left-aligned in one 32-bit word W whose top 31 bits are the
+// cut to the bposit32 bit string.  Q goes through one round-toward-zero
+// conversion to double (a cut of |Q| to 53 bits, then the cut below to at most
+// 27 bits: the same as one cut), which hands over the binade and the top
+// fraction bits.  The regime, the three exponent bits and those fraction bits
+// are laid out left-aligned in one 32-bit word W whose top 31 bits are the
 // truncated field; te is clamped to regimes -30 .. 30, where W already reads
 // maxpos (31 ones) or minpos (a single one in bit 1).  Selects only.
 BP_HD uint32_t bp32_from_i64(long long Q, int lsb_exp) {
-  if (Q == 0) return 0u;
-  const bool neg = Q < 0;
-  const uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
-  const int msb = msb64(m);
-  const uint32_t f = (uint32_t)((m << (63 - msb)) >> 31);   // the 32 bits below the leading one
-  int te = msb + lsb_exp;
+  const uint64_t bits = i64_to_f64_rz_bits(Q);
+  const uint32_t hi = (uint32_t)(bits >> 32);
+  const uint32_t f = (uint32_t)(bits >> 20);   // top 32 bits of the 52-bit fraction field
+  int te = (int)((hi >> 20) & 0x7FFu) - 1023 + lsb_exp;
   te = te < -240 ? -240 : (te > 247 ? 247 : te);
   const int k = te >> 3, e = te & 7;
   const int rl = k >= 0 ? k + 2 : 1 - k;   // 2 .. 31
   const uint32_t R = k >= 0 ? (~0u << (31 - k)) : (1u << (31 + k));
   const uint32_t W = R | (((uint32_t)e << 29) >> rl) | shr_clamp(f, rl + 3);
   const uint32_t field = W >> 1;
-  return neg ? 0u - field : field;
-}
-
-// The fp32 hand-off of bp32_from_i64(Q, lsb_exp) with no bias: the bposit32
-// value times 2^extra rounded to nearest even -- |Q| cut to the 29 - rl
-// significant bits the bposit32 keeps, then rounded to 24 -- in integer
-// arithmetic.  For sums whose bposit32 keeps all three exponent bits (regime
-// of at most 28 bits) and whose result is a normal fp32 (else false: the
-// caller takes the float64 route).  Q = 0 gives +0.
-BP_HD bool bp32_f32_i64(long long Q, int lsb_exp, int extra, float &out) {
-  if (Q == 0) {
-    out = 0.0f;
-    return true;
-  }
-  const bool neg = Q < 0;
-  uint64_t m = neg ? 0ull - (uint64_t)Q : (uint64_t)Q;
-  const int msb = msb64(m);
-  const int te = msb + lsb_exp;
-  const int k = te >> 3;
-  const int rl = k >= 0 ? k + 2 : 1 - k;
-  if (rl > 28) return false;
-  const int drop = msb + 1 - (29 - rl);
-  if (drop > 0) m &= ~((1ull << drop) - 1ull);
-  int E = te + extra;   // binade of the result
-  uint64_t q;
-  if (msb <= 23) {
-    q = m << (23 - msb);
-  } else {
-    const int sh = msb - 23;
-    q = m >> sh;
-    const uint64_t rem = m & ((1ull << sh) - 1ull), half = 1ull << (sh - 1);
-    if (rem > half || (rem == half && (q & 1ull))) ++q;
-    if (q >> 24) {   // carried into the next binade
-      q >>= 1;
-      ++E;
-    }
-  }
-  if (E < -126 || E > 127) return false;
-  uint32_t bits = ((uint32_t)(E + 127) << 23) | ((uint32_t)q & 0x7FFFFFu);
-  if (neg) bits |= 0x80000000u;
-#ifdef __CUDA_ARCH__
-  out = __uint_as_float(bits);
-#else
-  memcpy(&out, &bits, 4);
-#endif
-  return true;
+  const uint32_t code = (hi >> 31) ? 0u - field : field;
+  return Q ? code : 0u;
 }
 
 // The exact value of bp32_from_i64(Q, lsb_exp) as a double times 2^extra, for

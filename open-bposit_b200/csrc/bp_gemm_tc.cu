@@ -42,6 +42,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <functional>
 #include <mutex>
 #include <type_traits>
 
@@ -807,12 +808,10 @@ __device__ __forceinline__ void finish_row_f32(const TcParams &p, const FinishCo
     uint32_t code = 0u;
     float f = 0.0f;
     if (QW == 1) {
-      // the fp32 hand-off straight from the exact sum when the code is not
-      // stored: in integers without a bias (bp32_f32_i64), else through
-      // float64 (bp32_value_i64); otherwise from the code
+      // the fp32 hand-off straight from the exact sum (bp32_value_i64) when the
+      // code is not stored; otherwise from the code
       double v;
-      if (frow && !orow && p.n_extra == 0 && c.fb[q] == 0.0f && bp32_f32_i64(qv[q], L, rex + c.fe[q], f)) {
-      } else if (frow && !orow && p.n_extra == 0 && bp32_value_i64(qv[q], L, rex + c.fe[q], v)) {
+      if (frow && !orow && p.n_extra == 0 && bp32_value_i64(qv[q], L, rex + c.fe[q], v)) {
         f = __double2float_rn(v + (double)c.fb[q]);
       } else {
         code = bp32_from_i64(qv[q], L);
@@ -1596,28 +1595,30 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
 // Blocks stride over tiles of 64 rows x 256 columns: thread t loads 16 bytes
 // of each of 4 rows, transposes the 4 x 16 block in registers (byte
 // permutes), decodes its 64 codes through a table replicated per lane (entry
-// (code, lane) at word 32 code + lane: every lane in its own bank; built once
-// per block), parks the M and E words in shared memory (row k's word slots
+// (code, lane) at half-word 32 code + lane: at most two lanes of a warp meet
+// in a bank; built once per block), parks the M and E words in shared memory (row k's word slots
 // rotated by k / 16, so a warp's 32 stores hit 32 banks), then stores 64
-// bytes of one output row of each plane.  kKmajSmem bytes of dynamic shared
-// memory.
+// bytes of one output row of each plane.  The blocks of the first column of
+// tiles also record, per 64 rows, the widest row range hb - la (hr64, zeroed
+// by the caller).  kKmajSmem bytes of dynamic shared memory.
 constexpr int kKmajK = 256;
-constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 32 * 4;
+constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 32 * 2;
 
 __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
                                                     int8_t *__restrict__ dm, uint8_t *__restrict__ de, int ldt,
-                                                    const int4 *__restrict__ st, const int *__restrict__ Lr) {
+                                                    const int4 *__restrict__ st, const int *__restrict__ Lr,
+                                                    int *__restrict__ hr64) {
   extern __shared__ __align__(16) uint32_t kms[];
   uint32_t(*tm)[17] = (uint32_t(*)[17])kms;                // [k][row / 4], one pad word
   uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
-  uint32_t *s_dec = kms + 2 * kKmajK * 17;                 // (lsb + 128) << 8 | (uint8) m, per lane
+  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 128) << 8 | (uint8) m, per lane
   __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
   const int t = threadIdx.x, lane = t & 31;
   {
     int m, e;
     posit_to_me<8, 2>((uint32_t)t, m, e);
     // bp8 lsb exponents lie in [-24, 24]: the entry of a nonzero code is nonzero
-    const uint32_t d = m ? ((uint32_t)(e + 128) << 8) | (uint32_t)(uint8_t)(int8_t)m : 0u;
+    const uint16_t d = m ? (uint16_t)(((e + 128) << 8) | (uint8_t)(int8_t)m) : (uint16_t)0;
     for (int l = 0; l < 32; ++l) s_dec[t * 32 + l] = d;
   }
   const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 16bc .. + 15
@@ -1628,8 +1629,17 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
     __syncthreads();   // the previous tile's rows and staging are no longer read
     if (t < 64) {
       const bool v = r0 + t < rows;
-      s_la[t] = v ? st[r0 + t].x : 0;
+      const int4 rs = v ? st[r0 + t] : make_int4(0, 0, 0, 0);
+      s_la[t] = rs.x;
       s_L[t] = (v && Lr) ? Lr[r0 + t] : -0x3FFFFFFF;
+      // the widest row range (hb - la) of these 64 rows, once per row block:
+      // it bounds the E plane here, for the corrections' choice of arithmetic
+      if (k0 == 0) {
+        int h = rs.y - rs.x;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) h = max(h, __shfl_xor_sync(0xFFFFFFFFu, h, o));
+        if ((t & 31) == 0) atomicMax(&hr64[r0 / 64], h);
+      }
     }
     __syncthreads();
     // per byte i (row 4br + i): la + 128 and the base L + 128 clamped to 0 .. 255
@@ -1720,15 +1730,15 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 // kCorrRing elements in flight), and each lane adds the terms of its
 // kCorrCols columns from the stage (the register-load form was bound by the
 // latency of its loads).  A term is (m_a << ea) * (m << e) with ea = lsb_a -
-// la_x <= emax (the slot's largest) and e = lsb - la_y <= hr (the other
-// operand's widest row range, from the prep's counters); |term| <
+// la_x <= emax (the slot's largest) and e = lsb - la_y <= hr (the widest row
+// range hb - la among the pass's columns, per 64 rows from the copy); |term| <
 // 2^(8 + emax + hr).  While 8 + emax + hr + lgT <= 62 the sums are int64 (two's
 // complement words): one 32 x 32 -> 64-bit multiply-add per term when both
 // factors fit 32 bits (emax <= 26, hr <= 27), else a 64-bit shift of m_a m.
 // Otherwise 128-bit shifts.  Every wait is bounded: a timeout records code 32
 // in g_tc_error, waits (bounded) for the warp's copies in flight and ends the
 // warp.
-constexpr int kCorrCols = 16, kCorrChunk = 256, kCorrPass = 32 * kCorrCols, kCorrRing = 8, kCorrWarps = 8;
+constexpr int kCorrCols = 16, kCorrChunk = 256, kCorrPass = 32 * kCorrCols, kCorrRing = 4, kCorrWarps = 8;
 constexpr size_t kCorrWarpSmem = 2 * (size_t)kCorrRing * kCorrPass + (size_t)kCorrChunk * 8 + kCorrRing * 8;
 constexpr size_t kCorrSmem = kCorrWarps * kCorrWarpSmem;
 
@@ -1740,7 +1750,8 @@ struct CorrT {
   const int4 *xst;
   const int4 *seg;
   const int *tails;
-  const TcCounters *ctr, *yctr;   // this side's slots; the other operand's counters (v[3]: max hb - la)
+  const TcCounters *ctr;
+  const int *yhr;   // the other operand's widest row range hb - la per 64 rows
   int cap;
   ulonglong2 *Cout;
 };
@@ -1871,7 +1882,7 @@ __global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0
   int *queue = const_cast<int *>(&s0.ctr->v[8]);
   int cur = -1;   // the slot item whose list is loaded
   int4 sg = make_int4(0, 0, 0, 0);
-  int la_x = 0, mode = kCorrShift;
+  int la_x = 0, em = 0, lgT = 0;
   for (;;) {
     long long u = 0;
     if (lane == 0) u = atomicAdd(queue, 1);
@@ -1889,7 +1900,7 @@ __global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0
       const int x = sg.z, T = sg.y;
       la_x = c.xst[x].x;
       // the first chunk of the list, and the slot's largest tail exponent
-      int em = 0;
+      em = 0;
       __syncwarp();
       for (int t = lane; t < min(T, kCorrChunk); t += 32) {
         const int k = c.tails[sg.x + t];
@@ -1905,10 +1916,12 @@ __global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0
       }
       em = __reduce_max_sync(0xFFFFFFFFu, em);
       __syncwarp();
-      const int hr = c.yctr->v[3];
-      const int lgT = 32 - __clz(max(T, 1));   // >= ceil(log2(T + 1))
-      mode = em + hr + 8 + lgT > 62 ? kCorrWide : (em <= 26 && hr <= 27) ? kCorrMul : kCorrShift;
+      lgT = 32 - __clz(max(T, 1));   // >= ceil(log2(T + 1))
     }
+    // the widest row range among this pass's 512 columns (8 blocks of 64)
+    int hr = lane < kCorrPass / 64 && y0 + 64 * lane < c.Yrows ? c.yhr[y0 / 64 + lane] : 0;
+    hr = __reduce_max_sync(0xFFFFFFFFu, hr);
+    const int mode = em + hr + 8 + lgT > 62 ? kCorrWide : (em <= 26 && hr <= 27) ? kCorrMul : kCorrShift;
     ulonglong2 *o = c.Cout + (size_t)sl * c.Yrows + y0 + kCorrCols * lane;
     bool ok;
     if (mode == kCorrMul) ok = corr_pass<kCorrMul>(c, w, sg, la_x, K, y0, lane, o);
@@ -1978,7 +1991,7 @@ inline size_t al(size_t v) { return (v + 255) / 256 * 256; }
 
 struct TcLayout {
   int S, Kp, nkb, capA, capB, pool, ldtA, ldtB;
-  size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, TA, TB, part, total;
+  size_t planesA, planesB, LA, LB, slotA, slotB, segA, segB, tailA, tailB, ctr, CA, CB, TA, TB, HA, HB, part, total;
 };
 
 // K at and above which unscaled bp8 takes the narrow form on its own (algo 0,
@@ -2071,10 +2084,12 @@ TcLayout tc_layout(int fmt, int M, int N, int K, int S) {
   L.ctr = o; o += 256;
   L.CA = o; o += al(16 * (size_t)L.capA * N);
   L.CB = o; o += al(16 * (size_t)L.capB * M);
-  L.TA = L.TB = 0;
-  if (S == 2) {   // two byte planes (mantissa, relative lsb) per copy
+  L.TA = L.TB = L.HA = L.HB = 0;
+  if (S == 2) {   // two byte planes (mantissa, relative lsb) per copy; row ranges per 64 rows
     L.TA = o; o += al(2 * (size_t)K * L.ldtA);
     L.TB = o; o += al(2 * (size_t)K * L.ldtB);
+    L.HA = o; o += al(4 * (size_t)(L.ldtA / 16 + 4));
+    L.HB = o; o += al(4 * (size_t)(L.ldtB / 16 + 4));
   }
   // room for either pairing's main sums (chosen at launch)
   L.part = o;
@@ -2091,6 +2106,12 @@ cudaError_t tc_kernel_attr() {
   std::call_once(once, [] {
     err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                Cfg<S, PAIR>::SMEM);
+    // the whole unified L1 as shared memory: with the smallest carveout that
+    // holds the CTA, the narrow form's copy and correction blocks found no
+    // room beside it
+    if (err == cudaSuccess)
+      err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
   });
   return err;
 }
@@ -2217,7 +2238,8 @@ SideStream *side_stream() {
 // waits for the side stream.
 template <int S, bool PAIR>
 int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
-                       int grid_finish, cudaStream_t s, cudaEvent_t corr_done) {
+                       int grid_finish, cudaStream_t s, cudaEvent_t corr_done,
+                       const std::function<int()> *after_first = nullptr) {
   using C = Cfg<S, PAIR>;
   struct Seg {
     int tile0, n, split, kbc;
@@ -2249,6 +2271,9 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
     p.ntl = seg[k].n;
     rc = launch_tc_gemm_kernel<S, PAIR>(ma, mb, p, seg[k].n, s);
     if (rc) break;
+    // work that runs beside the GEMM (it records corr_done): after the first
+    // segment's CTAs, so that they are placed first
+    if (k == 0 && after_first && (rc = (*after_first)()) != kOk) break;
     const bool on_s = k == nseg - 1 || !side || seg[k].n > 2 * seg[k + 1].kbc;
     cudaStream_t fs = on_s ? s : side->st;
     if (!on_s) {
@@ -2349,35 +2374,72 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
       k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     rc = check_launch("tc_prep");
   }
-  // The narrow form's decoded K-major copies of the operands prepared here:
-  // B's whole, A's main part (its tail elements zeroed, by LA)
-  if (!rc && kmajor) {   // the copy kernel's shared-memory opt-in, once per device
+  // The narrow form's decoded K-major copies of the operands prepared here --
+  // B's whole, A's main part (its tail elements zeroed, by LA) -- and its tail
+  // corrections from them.  With long K they run on the side stream beside the
+  // GEMM, launched right after its first (persistent) segment, whose CTAs then
+  // hold every SM and leave room for one copy or correction block each (52 and
+  // 50 KB of shared memory beside the GEMM's 178 KB; every kernel asks for the
+  // whole L1 as shared memory); otherwise they run on the caller's stream
+  // ahead of the GEMM.
+  if (!rc && kmajor) {   // the shared-memory opt-ins, once per device
     static std::atomic<bool> attr_set[128];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128 ||
         (!attr_set[dev].load() &&
-         cudaFuncSetAttribute(k_kmajor_bp8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKmajSmem) != cudaSuccess))
-      rc = set_error(kECuda, "quire_gemm: k-major copy attribute: %s", cudaGetErrorString(cudaGetLastError()));
+         (cudaFuncSetAttribute(k_kmajor_bp8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKmajSmem) != cudaSuccess ||
+          cudaFuncSetAttribute(k_tc_corr_t, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCorrSmem) != cudaSuccess ||
+          cudaFuncSetAttribute(k_kmajor_bp8, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared) != cudaSuccess ||
+          cudaFuncSetAttribute(k_tc_corr_t, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared) != cudaSuccess)))
+      rc = set_error(kECuda, "quire_gemm: k-major kernels' attributes: %s", cudaGetErrorString(cudaGetLastError()));
     else
       attr_set[dev].store(true);
   }
-  // the copy kernel's grid: three blocks per SM (67 KB each), striding over tiles
-  auto kmg = [&](int K, int ldt) {
-    const long long tiles = (long long)((K + kKmajK - 1) / kKmajK) * ((ldt + 63) / 64);
-    return (unsigned)std::max<long long>(1, std::min<long long>(tiles, 3LL * sms));
+  // the copies of the operands prepared here, on `st`, at most `cap` blocks each
+  auto launch_copies = [&](cudaStream_t st, long long cap) -> int {
+    auto kmg = [&](int K, int ldt) {
+      const long long tiles = (long long)((K + kKmajK - 1) / kKmajK) * ((ldt + 63) / 64);
+      return (unsigned)std::max<long long>(1, std::min<long long>(tiles, cap));
+    };
+    if (pa.rows) {
+      int8_t *tm = (int8_t *)(w + L.TA);
+      if (cudaMemsetAsync(w + L.HA, 0, 4 * (size_t)(L.ldtA / 16 + 4), st) != cudaSuccess)
+        return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
+      k_kmajor_bp8<<<kmg(a.K, L.ldtA), 256, kKmajSmem, st>>>(
+          (const uint8_t *)a.A, a.M, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtA), L.ldtA, sta, LA,
+          (int *)(w + L.HA));
+      const int r = check_launch("tc_kmajor");
+      if (r) return r;
+    }
+    if (pb.rows) {
+      int8_t *tm = (int8_t *)(w + L.TB);
+      if (cudaMemsetAsync(w + L.HB, 0, 4 * (size_t)(L.ldtB / 16 + 4), st) != cudaSuccess)
+        return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
+      k_kmajor_bp8<<<kmg(a.K, L.ldtB), 256, kKmajSmem, st>>>(
+          (const uint8_t *)a.B, a.N, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtB), L.ldtB, stb, nullptr,
+          (int *)(w + L.HB));
+      return check_launch("tc_kmajor");
+    }
+    return kOk;
   };
-  if (!rc && kmajor && pa.rows) {
-    int8_t *tm = (int8_t *)(w + L.TA);
-    k_kmajor_bp8<<<kmg(a.K, L.ldtA), 256, kKmajSmem, s>>>(
-        (const uint8_t *)a.A, a.M, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtA), L.ldtA, sta, LA);
-    rc = check_launch("tc_kmajor");
-  }
-  if (!rc && kmajor && pb.rows) {
-    int8_t *tm = (int8_t *)(w + L.TB);
-    k_kmajor_bp8<<<kmg(a.K, L.ldtB), 256, kKmajSmem, s>>>(
-        (const uint8_t *)a.B, a.N, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtB), L.ldtB, stb, nullptr);
-    rc = check_launch("tc_kmajor");
-  }
+  // the corrections (one warp per slot and column pass), on `st`, `grid` blocks
+  auto launch_corr_t = [&](cudaStream_t st, int grid) -> int {
+    const int8_t *tA = (const int8_t *)(w + L.TA), *tB = (const int8_t *)(w + L.TB);
+    const CorrT ca{(const uint8_t *)a.A, tB, (const uint8_t *)(tB + (size_t)a.K * L.ldtB), a.N, L.ldtB, sta,
+                   segA, tailA, cA, (const int *)(w + L.HB), L.capA, CA};
+    const CorrT cb{(const uint8_t *)a.B, tA, (const uint8_t *)(tA + (size_t)a.K * L.ldtA), a.M, L.ldtA, stb,
+                   segB, tailB, cB, (const int *)(w + L.HA), L.capB, CB};
+    // the kernel's work counter (side A's v[8]; a call that reuses A's prepared
+    // state did not zero A's counters)
+    if (cudaMemsetAsync(&cA->v[8], 0, sizeof(int), st) != cudaSuccess)
+      return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
+    k_tc_corr_t<<<grid, 32 * kCorrWarps, kCorrSmem, st>>>(ca, cb, a.K);
+    return check_launch("tc_corr");
+  };
+  SideStream *oside = (!rc && kmajor && L.nkb >= 256 && !a_only && !b_only) ? side_stream() : nullptr;
+  if (!rc && kmajor && !oside) rc = launch_copies(s, 3LL * sms);
   if (rc || a_only || b_only) return rc;
 
   // Paired SMs whenever the tile has a second 128-row half to work on.
@@ -2424,25 +2486,8 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   }
   const cudaStream_t cs = side ? side->st : s;
   if (kmajor) {
-    // one warp per slot of either side, two 8-warp blocks per SM
-    const int8_t *tA = (const int8_t *)(w + L.TA), *tB = (const int8_t *)(w + L.TB);
-    const CorrT ca{(const uint8_t *)a.A, tB, (const uint8_t *)(tB + (size_t)a.K * L.ldtB), a.N, L.ldtB, sta,
-                   segA, tailA, cA, cB, L.capA, CA};
-    const CorrT cb{(const uint8_t *)a.B, tA, (const uint8_t *)(tA + (size_t)a.K * L.ldtA), a.M, L.ldtA, stb,
-                   segB, tailB, cB, cA, L.capB, CB};
-    static std::atomic<bool> corr_attr[128];
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128 ||
-        (!corr_attr[dev].load() &&
-         cudaFuncSetAttribute(k_tc_corr_t, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCorrSmem) != cudaSuccess))
-      return set_error(kECuda, "quire_gemm: correction attribute: %s", cudaGetErrorString(cudaGetLastError()));
-    corr_attr[dev].store(true);
-    const int gc = sms * 2;
-    // the kernel's work counter (side A's v[8]; a call that reuses A's prepared
-    // state did not zero A's counters)
-    if (cudaMemsetAsync(&cA->v[8], 0, sizeof(int), cs) != cudaSuccess)
-      return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
-    k_tc_corr_t<<<gc, 32 * kCorrWarps, kCorrSmem, cs>>>(ca, cb, a.K);
+    // ahead of the GEMM, two 8-warp blocks per SM; beside it, from the hook below
+    if (!oside) rc = launch_corr_t(s, sms * 2);
   } else {
     const int cy = side ? 2 : 64;
     const CorrSide ca{a.A, a.B, a.N, a.sa, a.sb, sta, stb, nullptr, segA, tailA, cA, L.capA, CA,
@@ -2452,9 +2497,23 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     const dim3 gc((unsigned)std::max(ca.gx, cb.gx), (unsigned)std::max(ca.gy, cb.gy), 2u);
     if (a.fmt == 8) k_tc_corr<8><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
     else k_tc_corr<16><<<gc, 256, 0, cs>>>(ca, cb, a.K, a.G, a.group);
+    rc = check_launch("tc_corr");
   }
-  rc = check_launch("tc_corr");
   cudaEvent_t corr_done = nullptr;
+  std::function<int()> beside;   // the narrow form's side work, launched after the first GEMM segment
+  if (!rc && oside) {
+    // the side stream starts after the prep (this record precedes the GEMM's launch)
+    if (cudaEventRecord(oside->ev[3], s) != cudaSuccess || cudaStreamWaitEvent(oside->st, oside->ev[3], 0) != cudaSuccess)
+      return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
+    beside = [&]() -> int {
+      int r = launch_copies(oside->st, sms);
+      if (!r) r = launch_corr_t(oside->st, sms);
+      if (cudaEventRecord(oside->ev[4], oside->st) != cudaSuccess && !r)
+        r = set_error(kECuda, "quire_gemm: side stream event: %s", cudaGetErrorString(cudaGetLastError()));
+      return r;
+    };
+    corr_done = oside->ev[4];
+  }
   if (side) {
     // the caller's stream always joins the side stream, on the error path too
     if (cudaEventRecord(side->ev[4], side->st) == cudaSuccess) corr_done = side->ev[4];
@@ -2467,14 +2526,14 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   }
   if (rc) return rc;
   if (S == 2)
-    rc = pair ? launch_tc_schedule<2, true>(ma, mb, p, sc, gf, s, corr_done)
-              : launch_tc_schedule<2, false>(ma, mb, p, sc, gf, s, corr_done);
+    rc = pair ? launch_tc_schedule<2, true>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr)
+              : launch_tc_schedule<2, false>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr);
   else if (S == 3)
-    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s, corr_done)
-              : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s, corr_done);
+    rc = pair ? launch_tc_schedule<3, true>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr)
+              : launch_tc_schedule<3, false>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr);
   else
-    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, gf, s, corr_done)
-              : launch_tc_schedule<4, false>(ma, mb, p, sc, gf, s, corr_done);
+    rc = pair ? launch_tc_schedule<4, true>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr)
+              : launch_tc_schedule<4, false>(ma, mb, p, sc, gf, s, corr_done, beside ? &beside : nullptr);
   if (rc) return rc;
   if (a.fmt == 8) k_tc_fixup<8><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);
   else k_tc_fixup<16><<<g, 256, 0, s>>>(a, sta, stb, slotA, slotB, cA, cB);

@@ -263,31 +263,6 @@ int main(int argc, char **argv) {
         ++bad;
       }
     }
-    // the integer fp32 hand-off without bias against the float64 route
-    // (value of the bposit32, times 2^extra, rounded to fp32), over sums of
-    // every width, exponents across the fp32 range and past it
-    for (int it = 0; it < 4000000; ++it) {
-      const int bits = (int)(rnd() % 63) + 1;
-      const uint64_t mm = rnd() & ((1ull << bits) - 1);
-      const int L = (int)(rnd() % 401) - 200, extra = (int)(rnd() % 161) - 80;
-      const long long Q = (rnd() & 1) ? -(long long)mm : (long long)mm;
-      float f;
-      if (!bp::bp32_f32_i64(Q, L, extra, f)) continue;
-      double v = 0.0;
-      if (Q != 0 && !bp::bp32_value_i64(Q, L, extra, v)) {
-        if (bad < 5) fprintf(stderr, "bp32 f32 taken where the value route is not Q=%lld L=%d\n", Q, L);
-        ++bad;
-        continue;
-      }
-      const float ref = (float)v;
-      uint32_t a, b;
-      memcpy(&a, &f, 4);
-      memcpy(&b, &ref, 4);
-      if (a != b) {
-        if (bad < 5) fprintf(stderr, "bp32 f32 mismatch Q=%lld L=%d extra=%d: %08x vs %08x\n", Q, L, extra, a, b);
-        ++bad;
-      }
-    }
     // the 64-bit form against the 128-bit one over exponents past both ends
     // of the bposit32 range (minpos / maxpos saturation)
     for (int it = 0; it < 400000; ++it) {
