@@ -447,8 +447,11 @@ def run_headline(ctx, fmt=8, M=M_, N=N_, K=K_):
     ctx.check_device()
     tops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
     k_tops = 2.0 * (m1 - m0) * (n1 - n0) * K / (kms * 1e-3) / 1e12
-    slice_pairs = (9 if fmt == 8 else 16) if ops.gemm_workspace_size(fmt, m1 - m0, n1 - n0, K, 2) and args.algo != 1 \
-        else None
+    # int8 MMAs per useful MAC: 4 in the narrow bp8 form (unscaled, K >= 16384 or
+    # algo 4), 9 in the wide bp8 form, 16 for bp16
+    narrow = fmt == 8 and args.algo in (0, 2, 3, 4) and (K >= 16384 or args.algo == 4)
+    slice_pairs = (16 if fmt == 16 else (4 if narrow else 9)) \
+        if ops.gemm_workspace_size(fmt, m1 - m0, n1 - n0, K, 2) and args.algo != 1 else None
     breakdown = kernel_breakdown(ctx, lambda: shard_step(A, Bs))
     per_rank = gather_obj(ctx, breakdown)
     nccl_variant = None
@@ -507,7 +510,11 @@ def run_headline(ctx, fmt=8, M=M_, N=N_, K=K_):
     if os.path.exists(tp):
         with open(tp) as f:
             tj = json.load(f)
-        ent = tj.get(f"quire_gemm_{'tc' if args.algo != 1 else 'simt'}" + ("" if fmt == 8 else "_bp16"))
+        # the bp8 tensor-core call takes the narrow two-plane form for K >= 16384
+        # (algo 0, 2, 3, 4), else the wide one; each has its own capture
+        narrow = fmt == 8 and args.algo in (0, 2, 3, 4) and (K >= 16384 or args.algo == 4)
+        ent = tj.get(f"quire_gemm_{'tc' if args.algo != 1 else 'simt'}" + ("" if fmt == 8 else "_bp16") +
+                     ("_narrow" if narrow and args.algo != 1 else ""))
         if ent and ent.get("shape") == [m1 - m0, n1 - n0, K]:
             traffic = ent["dram_bytes_per_call"]
             traffic_note = ent.get("note", "DRAM bytes read+written by one call (ncu)")

@@ -1592,17 +1592,19 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
 // (the rows' main bases) every element whose lsb lies below its row's base --
 // a listed tail element -- is written as m = 0: the copy holds the main part.
 // Zero and NaR are m = 0.
-// Blocks stride over tiles of 64 rows x 256 columns: thread t loads 16 bytes
-// of each of 4 rows, transposes the 4 x 16 block in registers (byte
-// permutes), decodes its 64 codes through a table replicated per lane (entry
-// (code, lane) at half-word 32 code + lane: at most two lanes of a warp meet
-// in a bank; built once per block), parks the M and E words in shared memory (row k's word slots
-// rotated by k / 16, so a warp's 32 stores hit 32 banks), then stores 64
-// bytes of one output row of each plane.  The blocks of the first column of
-// tiles also record, per 64 rows, the widest row range hb - la (hr64, zeroed
-// by the caller).  kKmajSmem bytes of dynamic shared memory.
-constexpr int kKmajK = 256;
-constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 32 * 2;
+// Blocks stride over tiles of 64 rows x 128 columns: thread t loads 8 bytes
+// of each of 4 rows, transposes the two 4 x 4 blocks in registers (byte
+// permutes), decodes its 32 codes through a 16-bit table replicated 16 times
+// (entry (code, lane % 16) at half-word 16 code + lane % 16; built once per
+// block), parks the M and E words in shared memory (local row kk's word slots
+// rotated by kk / 8, so a warp's stores spread over the banks), then four
+// threads store the 64 bytes of one output row of each plane.  26 KB of
+// shared memory lets two blocks sit beside a narrow-form GEMM CTA.  The
+// blocks of the first column of tiles also record, per 64 rows, the widest
+// row range hb - la (hr64, zeroed by the caller).  kKmajSmem bytes of
+// dynamic shared memory.
+constexpr int kKmajK = 128;
+constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 16 * 2;
 
 __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
                                                     int8_t *__restrict__ dm, uint8_t *__restrict__ de, int ldt,
@@ -1611,18 +1613,18 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   extern __shared__ __align__(16) uint32_t kms[];
   uint32_t(*tm)[17] = (uint32_t(*)[17])kms;                // [k][row / 4], one pad word
   uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
-  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 128) << 8 | (uint8) m, per lane
+  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 128) << 8 | (uint8) m, per lane % 16
   __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
-  const int t = threadIdx.x, lane = t & 31;
+  const int t = threadIdx.x, tl16 = t & 15;
   {
     int m, e;
     posit_to_me<8, 2>((uint32_t)t, m, e);
     // bp8 lsb exponents lie in [-24, 24]: the entry of a nonzero code is nonzero
     const uint16_t d = m ? (uint16_t)(((e + 128) << 8) | (uint8_t)(int8_t)m) : (uint16_t)0;
-    for (int l = 0; l < 32; ++l) s_dec[t * 32 + l] = d;
+    for (int l = 0; l < 16; ++l) s_dec[t * 16 + l] = d;
   }
-  const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 16bc .. + 15
-  const bool vec = (K & 15) == 0 && (((uintptr_t)src) & 15u) == 0;
+  const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 8bc .. + 7
+  const bool vec = (K & 7) == 0 && (((uintptr_t)src) & 7u) == 0;
   const int tk = (K + kKmajK - 1) / kKmajK, tr = (ldt + 63) / 64;
   for (long long tile = blockIdx.x; tile < (long long)tk * tr; tile += gridDim.x) {
     const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
@@ -1649,31 +1651,29 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
       la4 |= (uint32_t)(s_la[4 * br + i] + 128) << (8 * i);
       L4 |= (uint32_t)min(max(s_L[4 * br + i] + 128, 0), 255) << (8 * i);
     }
-    uint4 w[4];
+    uint2 w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int r = r0 + 4 * br + i, k = k0 + 16 * bc;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      const int r = r0 + 4 * br + i, k = k0 + 8 * bc;
+      uint2 v = make_uint2(0u, 0u);
       if (r < rows) {
         const uint8_t *row = src + (size_t)r * K;
-        if (vec && k + 16 <= K) {
-          v = __ldcs((const uint4 *)(row + k));
+        if (vec && k + 8 <= K) {
+          v = __ldcs((const uint2 *)(row + k));
         } else {
-          uint32_t b[4] = {0u, 0u, 0u, 0u};
+          uint32_t b[2] = {0u, 0u};
 #pragma unroll
-          for (int q = 0; q < 16; ++q)
+          for (int q = 0; q < 8; ++q)
             if (k + q < K) b[q >> 2] |= (uint32_t)row[k + q] << (8 * (q & 3));
-          v = make_uint4(b[0], b[1], b[2], b[3]);
+          v = make_uint2(b[0], b[1]);
         }
       }
       w[i] = v;
     }
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {   // columns 4g .. 4g + 3 of the thread's 16
-      const uint32_t r0w = g == 0 ? w[0].x : g == 1 ? w[0].y : g == 2 ? w[0].z : w[0].w;
-      const uint32_t r1w = g == 0 ? w[1].x : g == 1 ? w[1].y : g == 2 ? w[1].z : w[1].w;
-      const uint32_t r2w = g == 0 ? w[2].x : g == 1 ? w[2].y : g == 2 ? w[2].z : w[2].w;
-      const uint32_t r3w = g == 0 ? w[3].x : g == 1 ? w[3].y : g == 2 ? w[3].z : w[3].w;
+    for (int g = 0; g < 2; ++g) {   // columns 4g .. 4g + 3 of the thread's 8
+      const uint32_t r0w = g ? w[0].y : w[0].x, r1w = g ? w[1].y : w[1].x;
+      const uint32_t r2w = g ? w[2].y : w[2].x, r3w = g ? w[3].y : w[3].x;
       // column q: byte q of each row word (bytes in row order)
       const uint32_t a01 = __byte_perm(r0w, r1w, 0x5140), a23 = __byte_perm(r2w, r3w, 0x5140);
       const uint32_t b01 = __byte_perm(r0w, r1w, 0x7362), b23 = __byte_perm(r2w, r3w, 0x7362);
@@ -1682,26 +1682,26 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         // the four rows' entries; byte i of lw is row i's lsb + 128 (0 for zero / NaR)
-        const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 32 + lane];
-        const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 32 + lane];
-        const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 32 + lane];
-        const uint32_t d3 = s_dec[(cw[q] >> 24) * 32 + lane];
+        const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 16 + tl16];
+        const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 16 + tl16];
+        const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 16 + tl16];
+        const uint32_t d3 = s_dec[(cw[q] >> 24) * 16 + tl16];
         const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
         const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
         const uint32_t keep = __vcmpgeu4(lw, L4) & __vcmpne4(lw, 0u);
-        // word br of row k sits at slot (br + k / 16) % 16: the 32 lanes of a
-        // warp (bc = 0..15, two br) then store to 32 different banks
-        tm[16 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
-        te[16 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
+        // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
+        // a warp (bc = 0..15, two br) spread over the banks
+        tm[8 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
+        te[8 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
       }
     }
     __syncthreads();
-    // output rows k0 .. k0 + 255, 64 bytes (rows r0 .. r0 + 63) each per plane:
-    // four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
+    // output rows k0 .. k0 + kKmajK - 1, 64 bytes (rows r0 .. r0 + 63) each per
+    // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
     const int c = t & 3, r = r0 + 16 * c;
 #pragma unroll
     for (int pass = 0; pass < kKmajK / 64; ++pass) {
-      const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 4;
+      const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 3;
       if (k < K && r < ldt) {
         uint32_t vm[4], ve[4];
 #pragma unroll
@@ -2100,19 +2100,21 @@ TcLayout tc_layout(int fmt, int M, int N, int K, int S) {
 }
 
 template <int S, bool PAIR>
-cudaError_t tc_kernel_attr() {
-  static std::once_flag once;
-  static cudaError_t err = cudaSuccess;
-  std::call_once(once, [] {
-    err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               Cfg<S, PAIR>::SMEM);
-    // the whole unified L1 as shared memory: with the smallest carveout that
-    // holds the CTA, the narrow form's copy and correction blocks found no
-    // room beside it
-    if (err == cudaSuccess)
-      err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared);
-  });
+cudaError_t tc_kernel_attr() {   // once per device
+  static std::atomic<bool> done[128];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev >= 0 && dev < 128 && done[dev].load()) return cudaSuccess;
+  err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg<S, PAIR>::SMEM);
+  // the whole unified L1 as shared memory: with the smallest carveout that
+  // holds the CTA, the narrow form's copy and correction blocks found no
+  // room beside it
+  if (err == cudaSuccess)
+    err = cudaFuncSetAttribute(k_quire_gemm_tc<S, PAIR>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+  if (err == cudaSuccess && dev >= 0 && dev < 128) done[dev].store(true);
   return err;
 }
 
@@ -2378,10 +2380,10 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   // B's whole, A's main part (its tail elements zeroed, by LA) -- and its tail
   // corrections from them.  With long K they run on the side stream beside the
   // GEMM, launched right after its first (persistent) segment, whose CTAs then
-  // hold every SM and leave room for one copy or correction block each (52 and
-  // 50 KB of shared memory beside the GEMM's 178 KB; every kernel asks for the
-  // whole L1 as shared memory); otherwise they run on the caller's stream
-  // ahead of the GEMM.
+  // hold every SM and leave room for two copy blocks or one correction block
+  // (2 x 26 or 50 KB of shared memory beside the GEMM's 178 KB; every kernel
+  // asks for the whole L1 as shared memory); otherwise they run on the
+  // caller's stream ahead of the GEMM.
   if (!rc && kmajor) {   // the shared-memory opt-ins, once per device
     static std::atomic<bool> attr_set[128];
     int dev = 0;
@@ -2439,7 +2441,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     return check_launch("tc_corr");
   };
   SideStream *oside = (!rc && kmajor && L.nkb >= 256 && !a_only && !b_only) ? side_stream() : nullptr;
-  if (!rc && kmajor && !oside) rc = launch_copies(s, 3LL * sms);
+  if (!rc && kmajor && !oside) rc = launch_copies(s, 4LL * sms);
   if (rc || a_only || b_only) return rc;
 
   // Paired SMs whenever the tile has a second 128-row half to work on.
@@ -2506,7 +2508,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     if (cudaEventRecord(oside->ev[3], s) != cudaSuccess || cudaStreamWaitEvent(oside->st, oside->ev[3], 0) != cudaSuccess)
       return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
     beside = [&]() -> int {
-      int r = launch_copies(oside->st, sms);
+      int r = launch_copies(oside->st, 2LL * sms);
       if (!r) r = launch_corr_t(oside->st, sms);
       if (cudaEventRecord(oside->ev[4], oside->st) != cudaSuccess && !r)
         r = set_error(kECuda, "quire_gemm: side stream event: %s", cudaGetErrorString(cudaGetLastError()));
