@@ -1598,13 +1598,129 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
 // (entry (code, lane % 16) at half-word 16 code + lane % 16; built once per
 // block), parks the M and E words in shared memory (local row kk's word slots
 // rotated by kk / 8, so a warp's stores spread over the banks), then four
-// threads store the 64 bytes of one output row of each plane.  26 KB of
+// threads store the 64 bytes of one output row of each plane.  Each thread
+// issues a tile's loads two tiles before it works on it (a copy with one
+// tile's loads in flight per thread was bound by their latency).  26 KB of
 // shared memory lets two blocks sit beside a narrow-form GEMM CTA.  The
 // blocks of the first column of tiles also record, per 64 rows, the widest
 // row range hb - la (hr64, zeroed by the caller).  kKmajSmem bytes of
 // dynamic shared memory.
 constexpr int kKmajK = 128;
 constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 16 * 2;
+
+// One tile's global loads, issued two tiles ahead of their use: the thread's
+// 8 bytes of each of its 4 rows, and (threads < 64) the tile row's minimum lsb
+// and main base.  A tile past the end loads nothing.
+struct KmajFetch {
+  uint2 w[4];
+  int la, L;
+};
+
+__device__ __forceinline__ void kmaj_fetch(long long tile, long long ntiles, int tk, const uint8_t *__restrict__ src,
+                                           int rows, int K, bool vec, const int4 *__restrict__ st,
+                                           const int *__restrict__ Lr, int t, int br, int bc, KmajFetch &f) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f.w[i] = make_uint2(0u, 0u);
+  f.la = 0;
+  f.L = -0x3FFFFFFF;
+  if (tile >= ntiles) return;
+  const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
+  if (t < 64 && r0 + t < rows) {
+    f.la = __ldg(&st[r0 + t].x);
+    if (Lr) f.L = __ldg(&Lr[r0 + t]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + 4 * br + i, k = k0 + 8 * bc;
+    if (r < rows) {
+      const uint8_t *row = src + (size_t)r * K;
+      if (vec && k + 8 <= K) {
+        f.w[i] = __ldcs((const uint2 *)(row + k));
+      } else {
+        uint32_t b[2] = {0u, 0u};
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (k + q < K) b[q >> 2] |= (uint32_t)row[k + q] << (8 * (q & 3));
+        f.w[i] = make_uint2(b[0], b[1]);
+      }
+    }
+  }
+}
+
+// One tile from its fetched loads: decode, transpose through shared memory,
+// store the two planes' 128 output rows of 64 bytes.
+__device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int K, int8_t *__restrict__ dm,
+                                          uint8_t *__restrict__ de, int ldt, const int4 *__restrict__ st,
+                                          int *__restrict__ hr64, int t, int br, int bc, const KmajFetch &f,
+                                          uint32_t (*tm)[17], uint32_t (*te)[17], const uint16_t *s_dec,
+                                          int *s_la, int *s_L) {
+  const int tl16 = t & 15;
+  const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
+  __syncthreads();   // the previous tile's rows and staging are no longer read
+  if (t < 64) {
+    s_la[t] = f.la;
+    s_L[t] = f.L;
+    // the widest row range (hb - la) of these 64 rows, once per row block: it
+    // bounds the E plane here, for the corrections' choice of arithmetic
+    if (k0 == 0) {
+      int h = r0 + t < rows ? __ldg(&st[r0 + t].y) - f.la : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) h = max(h, __shfl_xor_sync(0xFFFFFFFFu, h, o));
+      if ((t & 31) == 0) atomicMax(&hr64[r0 / 64], h);
+    }
+  }
+  __syncthreads();
+  // per byte i (row 4br + i): la + 128 and the base L + 128 clamped to 0 .. 255
+  uint32_t la4 = 0u, L4 = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    la4 |= (uint32_t)(s_la[4 * br + i] + 128) << (8 * i);
+    L4 |= (uint32_t)min(max(s_L[4 * br + i] + 128, 0), 255) << (8 * i);
+  }
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {   // columns 4g .. 4g + 3 of the thread's 8
+    const uint32_t r0w = g ? f.w[0].y : f.w[0].x, r1w = g ? f.w[1].y : f.w[1].x;
+    const uint32_t r2w = g ? f.w[2].y : f.w[2].x, r3w = g ? f.w[3].y : f.w[3].x;
+    // column q: byte q of each row word (bytes in row order)
+    const uint32_t a01 = __byte_perm(r0w, r1w, 0x5140), a23 = __byte_perm(r2w, r3w, 0x5140);
+    const uint32_t b01 = __byte_perm(r0w, r1w, 0x7362), b23 = __byte_perm(r2w, r3w, 0x7362);
+    const uint32_t cw[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
+                            __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      // the four rows' entries; byte i of lw is row i's lsb + 128 (0 for zero / NaR)
+      const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 16 + tl16];
+      const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 16 + tl16];
+      const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 16 + tl16];
+      const uint32_t d3 = s_dec[(cw[q] >> 24) * 16 + tl16];
+      const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
+      const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
+      const uint32_t keep = __vcmpgeu4(lw, L4) & __vcmpne4(lw, 0u);
+      // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
+      // a warp (bc = 0..15, two br) spread over the banks
+      tm[8 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
+      te[8 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
+    }
+  }
+  __syncthreads();
+  // output rows k0 .. k0 + kKmajK - 1, 64 bytes (rows r0 .. r0 + 63) each per
+  // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
+  const int c = t & 3, r = r0 + 16 * c;
+#pragma unroll
+  for (int pass = 0; pass < kKmajK / 64; ++pass) {
+    const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 3;
+    if (k < K && r < ldt) {
+      uint32_t vm[4], ve[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        vm[j] = tm[kk][(4 * c + j + rot) & 15];
+        ve[j] = te[kk][(4 * c + j + rot) & 15];
+      }
+      *(uint4 *)(dm + (size_t)k * ldt + r) = make_uint4(vm[0], vm[1], vm[2], vm[3]);
+      *(uint4 *)(de + (size_t)k * ldt + r) = make_uint4(ve[0], ve[1], ve[2], ve[3]);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
                                                     int8_t *__restrict__ dm, uint8_t *__restrict__ de, int ldt,
@@ -1615,7 +1731,7 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
   uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 128) << 8 | (uint8) m, per lane % 16
   __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
-  const int t = threadIdx.x, tl16 = t & 15;
+  const int t = threadIdx.x;
   {
     int m, e;
     posit_to_me<8, 2>((uint32_t)t, m, e);
@@ -1626,93 +1742,25 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 8bc .. + 7
   const bool vec = (K & 7) == 0 && (((uintptr_t)src) & 7u) == 0;
   const int tk = (K + kKmajK - 1) / kKmajK, tr = (ldt + 63) / 64;
-  for (long long tile = blockIdx.x; tile < (long long)tk * tr; tile += gridDim.x) {
-    const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
-    __syncthreads();   // the previous tile's rows and staging are no longer read
-    if (t < 64) {
-      const bool v = r0 + t < rows;
-      const int4 rs = v ? st[r0 + t] : make_int4(0, 0, 0, 0);
-      s_la[t] = rs.x;
-      s_L[t] = (v && Lr) ? Lr[r0 + t] : -0x3FFFFFFF;
-      // the widest row range (hb - la) of these 64 rows, once per row block:
-      // it bounds the E plane here, for the corrections' choice of arithmetic
-      if (k0 == 0) {
-        int h = rs.y - rs.x;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) h = max(h, __shfl_xor_sync(0xFFFFFFFFu, h, o));
-        if ((t & 31) == 0) atomicMax(&hr64[r0 / 64], h);
-      }
-    }
-    __syncthreads();
-    // per byte i (row 4br + i): la + 128 and the base L + 128 clamped to 0 .. 255
-    uint32_t la4 = 0u, L4 = 0u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      la4 |= (uint32_t)(s_la[4 * br + i] + 128) << (8 * i);
-      L4 |= (uint32_t)min(max(s_L[4 * br + i] + 128, 0), 255) << (8 * i);
-    }
-    uint2 w[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int r = r0 + 4 * br + i, k = k0 + 8 * bc;
-      uint2 v = make_uint2(0u, 0u);
-      if (r < rows) {
-        const uint8_t *row = src + (size_t)r * K;
-        if (vec && k + 8 <= K) {
-          v = __ldcs((const uint2 *)(row + k));
-        } else {
-          uint32_t b[2] = {0u, 0u};
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            if (k + q < K) b[q >> 2] |= (uint32_t)row[k + q] << (8 * (q & 3));
-          v = make_uint2(b[0], b[1]);
-        }
-      }
-      w[i] = v;
-    }
-#pragma unroll
-    for (int g = 0; g < 2; ++g) {   // columns 4g .. 4g + 3 of the thread's 8
-      const uint32_t r0w = g ? w[0].y : w[0].x, r1w = g ? w[1].y : w[1].x;
-      const uint32_t r2w = g ? w[2].y : w[2].x, r3w = g ? w[3].y : w[3].x;
-      // column q: byte q of each row word (bytes in row order)
-      const uint32_t a01 = __byte_perm(r0w, r1w, 0x5140), a23 = __byte_perm(r2w, r3w, 0x5140);
-      const uint32_t b01 = __byte_perm(r0w, r1w, 0x7362), b23 = __byte_perm(r2w, r3w, 0x7362);
-      const uint32_t cw[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
-                              __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        // the four rows' entries; byte i of lw is row i's lsb + 128 (0 for zero / NaR)
-        const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 16 + tl16];
-        const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 16 + tl16];
-        const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 16 + tl16];
-        const uint32_t d3 = s_dec[(cw[q] >> 24) * 16 + tl16];
-        const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
-        const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
-        const uint32_t keep = __vcmpgeu4(lw, L4) & __vcmpne4(lw, 0u);
-        // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
-        // a warp (bc = 0..15, two br) spread over the banks
-        tm[8 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
-        te[8 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
-      }
-    }
-    __syncthreads();
-    // output rows k0 .. k0 + kKmajK - 1, 64 bytes (rows r0 .. r0 + 63) each per
-    // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
-    const int c = t & 3, r = r0 + 16 * c;
-#pragma unroll
-    for (int pass = 0; pass < kKmajK / 64; ++pass) {
-      const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 3;
-      if (k < K && r < ldt) {
-        uint32_t vm[4], ve[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          vm[j] = tm[kk][(4 * c + j + rot) & 15];
-          ve[j] = te[kk][(4 * c + j + rot) & 15];
-        }
-        *(uint4 *)(dm + (size_t)k * ldt + r) = make_uint4(vm[0], vm[1], vm[2], vm[3]);
-        *(uint4 *)(de + (size_t)k * ldt + r) = make_uint4(ve[0], ve[1], ve[2], ve[3]);
-      }
-    }
+  const long long ntiles = (long long)tk * tr, g = gridDim.x;
+  // three fetch buffers in rotation, the loop unrolled by three: each buffer is
+  // refilled (tile + 3g) right after its tile is written, so two tiles' loads
+  // are in flight while one is worked on, and no register waits on a load
+  // before its tile comes up
+  KmajFetch fa, fb, fc;
+  long long tile = blockIdx.x;
+  kmaj_fetch(tile, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fa);
+  kmaj_fetch(tile + g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
+  kmaj_fetch(tile + 2 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
+  for (; tile < ntiles; tile += 3 * g) {
+    kmaj_tile(tile, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fa, tm, te, s_dec, s_la, s_L);
+    kmaj_fetch(tile + 3 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fa);
+    if (tile + g >= ntiles) break;
+    kmaj_tile(tile + g, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fb, tm, te, s_dec, s_la, s_L);
+    kmaj_fetch(tile + 4 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
+    if (tile + 2 * g >= ntiles) break;
+    kmaj_tile(tile + 2 * g, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fc, tm, te, s_dec, s_la, s_L);
+    kmaj_fetch(tile + 5 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
   }
 }
 
@@ -1730,11 +1778,14 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 // kCorrRing elements in flight), and each lane adds the terms of its
 // kCorrCols columns from the stage (the register-load form was bound by the
 // latency of its loads).  A term is (m_a << ea) * (m << e) with ea = lsb_a -
-// la_x <= emax (the slot's largest) and e = lsb - la_y <= hr (the widest row
-// range hb - la among the pass's columns, per 64 rows from the copy); |term| <
-// 2^(8 + emax + hr).  While 8 + emax + hr + lgT <= 62 the sums are int64 (two's
-// complement words): one 32 x 32 -> 64-bit multiply-add per term when both
-// factors fit 32 bits (emax <= 26, hr <= 27), else a 64-bit shift of m_a m.
+// la_x <= emax (the slot's largest) and e = lsb - la_y (hr: the widest row
+// range hb - la among the pass's columns, hb the largest binade, per 64 rows
+// from the copy).  A factor m << e is v / 2^la_y with |v| < 2^(hb + 1), so
+// |m << e| < 2^(hr + 1); and |m_a| < 2^4 (at most 3 fraction bits), so
+// |m_a << ea| < 2^(emax + 4): |term| < 2^(emax + hr + 5), and a sum of T <
+// 2^lgT terms stays inside int64 while emax + hr + lgT <= 58 (two's
+// complement words).  Then one 32 x 32 -> 64-bit multiply-add per term when
+// both factors fit int32 (emax <= 27, hr <= 30), else a 64-bit shift of m_a m.
 // Otherwise 128-bit shifts.  Every wait is bounded: a timeout records code 32
 // in g_tc_error, waits (bounded) for the warp's copies in flight and ends the
 // warp.
@@ -1823,7 +1874,7 @@ __device__ __forceinline__ bool corr_pass(const CorrT &c, CorrWarp &w, int4 sg, 
         const uint4 we = *(const uint4 *)(w.re + st * kCorrPass + 16 * lane);
         const int me = w.lst[t].y;
         const int ma = (int)(short)(me & 0xFFFF), ea = me >> 16;
-        const int a32 = (int)((unsigned)ma << (ea & 31));   // used when ea <= 26
+        const int a32 = (int)((unsigned)ma << (ea & 31));   // used when ea <= 27
 #pragma unroll
         for (int q = 0; q < kCorrCols; ++q) {
           const uint32_t wmq = q < 4 ? wm.x : q < 8 ? wm.y : q < 12 ? wm.z : wm.w;
@@ -1921,7 +1972,7 @@ __global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0
     // the widest row range among this pass's 512 columns (8 blocks of 64)
     int hr = lane < kCorrPass / 64 && y0 + 64 * lane < c.Yrows ? c.yhr[y0 / 64 + lane] : 0;
     hr = __reduce_max_sync(0xFFFFFFFFu, hr);
-    const int mode = em + hr + 8 + lgT > 62 ? kCorrWide : (em <= 26 && hr <= 27) ? kCorrMul : kCorrShift;
+    const int mode = em + hr + lgT > 58 ? kCorrWide : (em <= 27 && hr <= 30) ? kCorrMul : kCorrShift;
     ulonglong2 *o = c.Cout + (size_t)sl * c.Yrows + y0 + kCorrCols * lane;
     bool ok;
     if (mode == kCorrMul) ok = corr_pass<kCorrMul>(c, w, sg, la_x, K, y0, lane, o);

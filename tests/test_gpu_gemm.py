@@ -324,6 +324,35 @@ def test_tc_listed_tails(ops, orc, fmt, algo):
     assert _device_error() == 0
 
 
+def test_tc_narrow_correction_term_bounds(ops, orc):
+    """Narrow-form tail corrections at the edges of their integer forms.  The
+    other operand's rows span 29, 30 and 31 binades (largest binade minus
+    smallest lsb) in its three 512-column passes; 31 leaves the int32
+    multiply form.  The tail rows' largest tail exponent above the row minimum
+    runs from about 21 to 30, so passes take the int32 multiply, the 64-bit
+    shift and the 128-bit forms.  Raw quires and bposit32 words bit-exact."""
+    rng = np.random.default_rng(77)
+    M, N, K = 64, 1536, 512
+    X = np.zeros((M, K), np.float32)
+    for i in range(M):
+        bx = 12 + i % 9                                   # largest binade 12 .. 20
+        cols = rng.choice(K, 40, replace=False)
+        X[i, cols[0]] = 2.0 ** bx
+        X[i, cols[1]] = 2.0 ** -24                        # minpos: lsb -24
+        X[i, cols[2:]] = (rng.standard_normal(38) * 2.0 ** rng.integers(-20, bx, 38)).astype(np.float32)
+    Y = rng.standard_normal((N, K)).astype(np.float32)
+    Y[:, 0] = 2.0 ** (5 + np.arange(N) // 512)            # largest binade 5, 6, 7 per pass
+    Y[:, 1] = 2.0 ** -24
+    A, B = orc.quantize_bp8(X)[0], orc.quantize_bp8(Y)[0]
+    out, q = run(ops, A, B, 8, 4, quire_limbs=16)
+    rb, rq = orc.quire_gemm(A, B, 8, nlimbs=16)
+    assert np.array_equal(q, rq)
+    assert np.array_equal(out, rb)
+    out2, _ = run(ops, A, B, 8, 4)
+    assert np.array_equal(out2, rb)
+    assert _device_error() == 0
+
+
 @pytest.mark.parametrize("algo", [2, 4])
 def test_tc_tail_overflow_goes_to_fixup(ops, orc, algo):
     """More tail elements in a row than the tail list holds: that row's
