@@ -1584,11 +1584,14 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
 }
 
 // K-major copies for the narrow form's corrections, decoded: codes [rows][K]
-// (bp8) -> two byte planes [K][ldt] (ldt = rows rounded up to 16, padding
-// columns zero): M, the signed mantissa m (value = m 2^lsb, |m| <= 15), and E,
-// the lsb exponent above the row's minimum, lsb - la_r (0 .. hb_r - la_r, below
-// 64 for bp8).  A tail element's column of the other operand is then one
-// contiguous row of each plane, and the correction needs no table.  With `Lr`
+// (bp8) -> [K][2 ldt] bytes (ldt = rows rounded up to 16, padding columns
+// zero) holding two byte planes: M, the signed mantissa m (value = m 2^lsb,
+// |m| <= 15), and E, the lsb exponent above the row's minimum, lsb - la_r
+// (0 .. hb_r - la_r, below 64 for bp8).  Row k is cut into blocks of
+// kCorrPass (512) columns, the last one narrower (w = min(512, ldt - 512 b)
+// for block b); block b sits at byte 1024 b of the row, its w M bytes first
+// and its w E bytes after them.  A correction pass over one block of a tail
+// element's column is then one contiguous copy, and needs no table.  With `Lr`
 // (the rows' main bases) every element whose lsb lies below its row's base --
 // a listed tail element -- is written as m = 0: the copy holds the main part.
 // Zero and NaR are m = 0.
@@ -1649,8 +1652,8 @@ __device__ __forceinline__ void kmaj_fetch(long long tile, long long ntiles, int
 
 // One tile from its fetched loads: decode, transpose through shared memory,
 // store the two planes' 128 output rows of 64 bytes.
-__device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int K, int8_t *__restrict__ dm,
-                                          uint8_t *__restrict__ de, int ldt, const int4 *__restrict__ st,
+__device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int K, uint8_t *__restrict__ dme,
+                                          int ldt, const int4 *__restrict__ st,
                                           int *__restrict__ hr64, int t, int br, int bc, const KmajFetch &f,
                                           uint32_t (*tm)[17], uint32_t (*te)[17], const uint16_t *s_dec,
                                           int *s_la, int *s_L) {
@@ -1704,8 +1707,10 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
   }
   __syncthreads();
   // output rows k0 .. k0 + kKmajK - 1, 64 bytes (rows r0 .. r0 + 63) each per
-  // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64 bytes
+  // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64
+  // bytes per plane.  The tile's 64 rows lie in one 512-column block (b, width w).
   const int c = t & 3, r = r0 + 16 * c;
+  const int blk = r0 & ~511, wb = min(512, ldt - blk);
 #pragma unroll
   for (int pass = 0; pass < kKmajK / 64; ++pass) {
     const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 3;
@@ -1716,14 +1721,15 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
         vm[j] = tm[kk][(4 * c + j + rot) & 15];
         ve[j] = te[kk][(4 * c + j + rot) & 15];
       }
-      *(uint4 *)(dm + (size_t)k * ldt + r) = make_uint4(vm[0], vm[1], vm[2], vm[3]);
-      *(uint4 *)(de + (size_t)k * ldt + r) = make_uint4(ve[0], ve[1], ve[2], ve[3]);
+      uint8_t *o = dme + (size_t)k * 2 * ldt + 2 * blk + (r - blk);
+      *(uint4 *)o = make_uint4(vm[0], vm[1], vm[2], vm[3]);
+      *(uint4 *)(o + wb) = make_uint4(ve[0], ve[1], ve[2], ve[3]);
     }
   }
 }
 
 __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
-                                                    int8_t *__restrict__ dm, uint8_t *__restrict__ de, int ldt,
+                                                    uint8_t *__restrict__ dme, int ldt,
                                                     const int4 *__restrict__ st, const int *__restrict__ Lr,
                                                     int *__restrict__ hr64) {
   extern __shared__ __align__(16) uint32_t kms[];
@@ -1753,13 +1759,13 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   kmaj_fetch(tile + g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
   kmaj_fetch(tile + 2 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
   for (; tile < ntiles; tile += 3 * g) {
-    kmaj_tile(tile, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fa, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fa, tm, te, s_dec, s_la, s_L);
     kmaj_fetch(tile + 3 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fa);
     if (tile + g >= ntiles) break;
-    kmaj_tile(tile + g, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fb, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile + g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fb, tm, te, s_dec, s_la, s_L);
     kmaj_fetch(tile + 4 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
     if (tile + 2 * g >= ntiles) break;
-    kmaj_tile(tile + 2 * g, tk, rows, K, dm, de, ldt, st, hr64, t, br, bc, fc, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile + 2 * g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fc, tm, te, s_dec, s_la, s_L);
     kmaj_fetch(tile + 5 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
   }
 }
@@ -1773,10 +1779,11 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 // One warp per slot, no block barrier.  The warp lists up to kCorrChunk of the
 // slot's tail elements in its own shared memory (column k, m_a, lsb_a - la_x)
 // and takes the columns in passes of kCorrPass: for each tail element, lane 0
-// streams that pass's slice of row k of both planes into the warp's ring of
-// kCorrRing shared-memory stages by bulk copies (one mbarrier per stage,
-// kCorrRing elements in flight), and each lane adds the terms of its
-// kCorrCols columns from the stage (the register-load form was bound by the
+// streams that pass's block of row k (its M bytes, then its E bytes: one
+// bulk copy; two copies per element, one per plane, ran at half the rate
+// beside the GEMM) into the warp's ring of kCorrRing shared-memory stages (one
+// mbarrier per stage, kCorrRing elements in flight), and each lane adds the
+// terms of its kCorrCols columns from the stage (the register-load form was bound by the
 // latency of its loads).  A term is (m_a << ea) * (m << e) with ea = lsb_a -
 // la_x <= emax (the slot's largest) and e = lsb - la_y (hr: the widest row
 // range hb - la among the pass's columns, hb the largest binade, per 64 rows
@@ -1790,13 +1797,13 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 // in g_tc_error, waits (bounded) for the warp's copies in flight and ends the
 // warp.
 constexpr int kCorrCols = 16, kCorrChunk = 256, kCorrPass = 32 * kCorrCols, kCorrRing = 4, kCorrWarps = 8;
+static_assert(kCorrPass == 512, "k_kmajor_bp8 lays its copies out in blocks of 512 columns");
 constexpr size_t kCorrWarpSmem = 2 * (size_t)kCorrRing * kCorrPass + (size_t)kCorrChunk * 8 + kCorrRing * 8;
 constexpr size_t kCorrSmem = kCorrWarps * kCorrWarpSmem;
 
 struct CorrT {
   const uint8_t *X;
-  const int8_t *Ym;
-  const uint8_t *Ye;
+  const uint8_t *Yme;   // the other operand's K-major copy, [K][2 ldt] (M and E per 512-column block)
   int Yrows, ldt;
   const int4 *xst;
   const int4 *seg;
@@ -1811,19 +1818,19 @@ enum { kCorrMul = 0, kCorrShift = 1, kCorrWide = 2 };
 
 // The warp's shared memory: the ring's M and E stages, the list, the barriers.
 struct CorrWarp {
-  uint8_t *rm, *re;
+  uint8_t *rme;   // stage s: [2 kCorrPass] bytes at s * 2 kCorrPass (the pass's M bytes, then its E bytes)
   int2 *lst;
   uint64_t *bar;
   uint32_t g;   // bulk copies issued so far (stage g % kCorrRing, phase (g / kCorrRing) & 1)
 };
 
-// Lane 0: the copies of tail element `k`'s pass slice into stage g % kCorrRing.
+// Lane 0: the copy of tail element `k`'s pass block (its `bytes` M bytes and
+// `bytes` E bytes, contiguous) into stage g % kCorrRing.
 __device__ __forceinline__ void corr_issue(const CorrT &c, CorrWarp &w, uint32_t g, int k, int y0, int bytes) {
   const int st = (int)(g % kCorrRing);
   mbar_expect_tx(&w.bar[st], 2u * (uint32_t)bytes);
-  const size_t off = (size_t)k * c.ldt + y0;
-  bulk_g2s(w.rm + st * kCorrPass, c.Ym + off, (uint32_t)bytes, &w.bar[st]);
-  bulk_g2s(w.re + st * kCorrPass, c.Ye + off, (uint32_t)bytes, &w.bar[st]);
+  bulk_g2s(w.rme + st * 2 * kCorrPass, c.Yme + (size_t)k * 2 * c.ldt + 2 * (size_t)y0, 2u * (uint32_t)bytes,
+           &w.bar[st]);
 }
 
 // One pass (columns y0 .. y0 + kCorrPass - 1) of one slot.  Returns false
@@ -1870,8 +1877,8 @@ __device__ __forceinline__ bool corr_pass(const CorrT &c, CorrWarp &w, int4 sg, 
         return false;
       }
       if (mine) {
-        const uint4 wm = *(const uint4 *)(w.rm + st * kCorrPass + 16 * lane);
-        const uint4 we = *(const uint4 *)(w.re + st * kCorrPass + 16 * lane);
+        const uint4 wm = *(const uint4 *)(w.rme + st * 2 * kCorrPass + 16 * lane);
+        const uint4 we = *(const uint4 *)(w.rme + st * 2 * kCorrPass + bytes + 16 * lane);
         const int me = w.lst[t].y;
         const int ma = (int)(short)(me & 0xFFFF), ea = me >> 16;
         const int a32 = (int)((unsigned)ma << (ea & 31));   // used when ea <= 27
@@ -1914,8 +1921,7 @@ __global__ void __launch_bounds__(32 * kCorrWarps, 2) k_tc_corr_t(const CorrT s0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t *base = kcs + warp * kCorrWarpSmem;
   CorrWarp w;
-  w.rm = base;
-  w.re = base + kCorrRing * kCorrPass;
+  w.rme = base;
   w.lst = (int2 *)(base + 2 * kCorrRing * kCorrPass);
   w.bar = (uint64_t *)(base + 2 * kCorrRing * kCorrPass + kCorrChunk * 8);
   w.g = 0;
@@ -2457,33 +2463,28 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
       return (unsigned)std::max<long long>(1, std::min<long long>(tiles, cap));
     };
     if (pa.rows) {
-      int8_t *tm = (int8_t *)(w + L.TA);
       if (cudaMemsetAsync(w + L.HA, 0, 4 * (size_t)(L.ldtA / 16 + 4), st) != cudaSuccess)
         return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
-      k_kmajor_bp8<<<kmg(a.K, L.ldtA), 256, kKmajSmem, st>>>(
-          (const uint8_t *)a.A, a.M, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtA), L.ldtA, sta, LA,
-          (int *)(w + L.HA));
+      k_kmajor_bp8<<<kmg(a.K, L.ldtA), 256, kKmajSmem, st>>>((const uint8_t *)a.A, a.M, a.K, (uint8_t *)(w + L.TA),
+                                                             L.ldtA, sta, LA, (int *)(w + L.HA));
       const int r = check_launch("tc_kmajor");
       if (r) return r;
     }
     if (pb.rows) {
-      int8_t *tm = (int8_t *)(w + L.TB);
       if (cudaMemsetAsync(w + L.HB, 0, 4 * (size_t)(L.ldtB / 16 + 4), st) != cudaSuccess)
         return set_error(kECuda, "quire_gemm: memset: %s", cudaGetErrorString(cudaGetLastError()));
-      k_kmajor_bp8<<<kmg(a.K, L.ldtB), 256, kKmajSmem, st>>>(
-          (const uint8_t *)a.B, a.N, a.K, tm, (uint8_t *)(tm + (size_t)a.K * L.ldtB), L.ldtB, stb, nullptr,
-          (int *)(w + L.HB));
+      k_kmajor_bp8<<<kmg(a.K, L.ldtB), 256, kKmajSmem, st>>>((const uint8_t *)a.B, a.N, a.K, (uint8_t *)(w + L.TB),
+                                                             L.ldtB, stb, nullptr, (int *)(w + L.HB));
       return check_launch("tc_kmajor");
     }
     return kOk;
   };
   // the corrections (one warp per slot and column pass), on `st`, `grid` blocks
   auto launch_corr_t = [&](cudaStream_t st, int grid) -> int {
-    const int8_t *tA = (const int8_t *)(w + L.TA), *tB = (const int8_t *)(w + L.TB);
-    const CorrT ca{(const uint8_t *)a.A, tB, (const uint8_t *)(tB + (size_t)a.K * L.ldtB), a.N, L.ldtB, sta,
-                   segA, tailA, cA, (const int *)(w + L.HB), L.capA, CA};
-    const CorrT cb{(const uint8_t *)a.B, tA, (const uint8_t *)(tA + (size_t)a.K * L.ldtA), a.M, L.ldtA, stb,
-                   segB, tailB, cB, (const int *)(w + L.HA), L.capB, CB};
+    const CorrT ca{(const uint8_t *)a.A, (const uint8_t *)(w + L.TB), a.N, L.ldtB, sta, segA, tailA, cA,
+                   (const int *)(w + L.HB), L.capA, CA};
+    const CorrT cb{(const uint8_t *)a.B, (const uint8_t *)(w + L.TA), a.M, L.ldtA, stb, segB, tailB, cB,
+                   (const int *)(w + L.HA), L.capB, CB};
     // the kernel's work counter (side A's v[8]; a call that reuses A's prepared
     // state did not zero A's counters)
     if (cudaMemsetAsync(&cA->v[8], 0, sizeof(int), st) != cudaSuccess)
