@@ -1798,7 +1798,12 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
 // warp.
 constexpr int kCorrCols = 16, kCorrChunk = 256, kCorrPass = 32 * kCorrCols, kCorrRing = 4, kCorrWarps = 8;
 static_assert(kCorrPass == 512, "k_kmajor_bp8 lays its copies out in blocks of 512 columns");
-constexpr size_t kCorrWarpSmem = 2 * (size_t)kCorrRing * kCorrPass + (size_t)kCorrChunk * 8 + kCorrRing * 8;
+// Each warp's region: the ring's stages, the list, the barriers; rounded up to
+// 16 bytes, so that every warp's stages stay 16-byte aligned for the bulk
+// copies and the lanes' 16-byte loads (an odd ring otherwise shifts them by 8).
+constexpr size_t kCorrWarpSmem =
+    (2 * (size_t)kCorrRing * kCorrPass + (size_t)kCorrChunk * 8 + kCorrRing * 8 + 15) / 16 * 16;
+static_assert(kCorrWarpSmem % 16 == 0 && (2 * (size_t)kCorrRing * kCorrPass) % 16 == 0, "16-byte stages");
 constexpr size_t kCorrSmem = kCorrWarps * kCorrWarpSmem;
 
 struct CorrT {
