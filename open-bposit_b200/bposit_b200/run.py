@@ -3,9 +3,12 @@
     python -m bposit_b200.run gemm M N K [--fmt bp8|bp16] [--group 128] [--calls 3] [--algo 0]
     python -m bposit_b200.run codec N [--fmt bp8|bp16] [--calls 3]
     python -m bposit_b200.run qwen05 [--batch 8] [--seq 1024] [--layers 24] [--fp32]
+    python -m bposit_b200.run linear M N K [--calls 3]
 
 ``gemm`` times bp_quire_gemm on operands N(0,1) * 2^U{-8..8} per row (the
-large-GEMM workload's distribution), quantized on the device; ``codec`` times
+large-GEMM workload's distribution), quantized on the device; ``linear`` times
+one BpositLinear (the W8A8 nn.Linear drop-in, fp32 out) of N x K random
+weights on M rows of N(0,1) activations; ``codec`` times
 the encode and decode kernels on the codec-sweep value mix; ``qwen05`` times
 the Qwen2.5-0.5B-shaped decoder forward with every linear a BpositLinear.  Each runs
 `--calls` untimed calls and then `--calls` calls timed with CUDA events, so a
@@ -78,6 +81,18 @@ def run_codec(a) -> str:
             f"decode {dec:.3f} ms ({a.n * b / dec / 1e6:.0f} GB/s)")
 
 
+def run_linear(a) -> str:
+    from .nn import BpositLinear
+    gen = torch.Generator(device="cuda").manual_seed(a.seed)
+    lin = BpositLinear(a.K, a.N, bias=True, device="cuda")
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn((a.N, a.K), device="cuda", generator=gen) * a.K ** -0.5)
+    x = torch.randn((a.M, a.K), device="cuda", generator=gen)
+    ms = _time(lambda: lin(x), a.calls)
+    return (f"linear (W8A8 BpositLinear, fp32 out) M={a.M} N={a.N} K={a.K}: {ms:.3f} ms/call, "
+            f"{2.0 * a.M * a.N * a.K / ms / 1e9:.1f} TOPS")
+
+
 def run_qwen05(a) -> str:
     from .forward import qwen05, synthetic_ids
     model = qwen05(layers=a.layers, bposit=not a.fp32)
@@ -107,13 +122,17 @@ def main(argv=None) -> int:
     w.add_argument("--seq", type=int, default=1024)
     w.add_argument("--layers", type=int, default=24)
     w.add_argument("--fp32", action="store_true", help="plain torch fp32 linears, for comparison")
-    for p in (g, c, w):
+    li = sub.add_parser("linear")
+    li.add_argument("M", type=int)
+    li.add_argument("N", type=int)
+    li.add_argument("K", type=int)
+    for p in (g, c, w, li):
         p.add_argument("--calls", type=int, default=3)
         p.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("no CUDA device")
-    fn = {"gemm": run_gemm, "codec": run_codec, "qwen05": run_qwen05}[a.what]
+    fn = {"gemm": run_gemm, "codec": run_codec, "qwen05": run_qwen05, "linear": run_linear}[a.what]
     print(fn(a), flush=True)
     return 0
 

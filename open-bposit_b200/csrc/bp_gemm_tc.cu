@@ -864,8 +864,28 @@ __device__ __forceinline__ void finish_row(const TcParams &p, const FinishCols<P
   else finish_row_codes<PL, QW>(p, c, i, j0, lane, qv, qh, ra, Li, si);
 }
 
+// Blocks per SM the finish kernels are compiled for.  Two (up to 128
+// registers) keeps the one-word (bp8) and fp32 variants free of spills: at four
+// (64 registers) the bp8 codes-only finish spilled about 600 bytes a thread
+// and took 0.53 ms instead of 0.31 beside the headline GEMM's last segment.
+// The two-word (bp16) codes-only finish spills little at 64 registers and
+// keeps four, so that two of its blocks fit beside a bp16 GEMM segment (at
+// two, bp16 8192^3 ran 162.6 TOPS against 168.9).
+#ifndef BP_FIN_MINB
+#define BP_FIN_MINB 2
+#endif
+#ifndef BP_FIN_MINB_QW2
+#define BP_FIN_MINB_QW2 4
+#endif
+#ifndef BP_FIN_MINB_F32
+#define BP_FIN_MINB_F32 2
+#endif
+#ifndef BP_FIN_STAGED_MINB_F32
+#define BP_FIN_STAGED_MINB_F32 2
+#endif
 template <int MM, int BN, int QW, bool F32>
-__global__ void __launch_bounds__(256, 4) k_tc_finish(TcParams p, int ntiles, int parts) {
+__global__ void __launch_bounds__(256, F32 ? BP_FIN_MINB_F32 : (QW == 2 ? BP_FIN_MINB_QW2 : BP_FIN_MINB))
+    k_tc_finish(TcParams p, int ntiles, int parts) {
   static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
   constexpr int PL = BN / 32;
   constexpr size_t PT = (size_t)MM * BN;   // words of one plane of a tile
@@ -1003,7 +1023,8 @@ size_t finish_staged_smem() {
 }
 
 template <int MM, int BN, int QW, bool F32>
-__global__ void __launch_bounds__(256, F32 ? 3 : 4) k_tc_finish_staged(TcParams p, int ntiles, int parts) {
+__global__ void __launch_bounds__(256, F32 ? BP_FIN_STAGED_MINB_F32 : (QW == 2 ? BP_FIN_MINB_QW2 : BP_FIN_MINB))
+    k_tc_finish_staged(TcParams p, int ntiles, int parts) {
   static_assert(BN % 32 == 0 && MM % 8 == 0 && (QW == 1 || QW == 2), "tile shape");
   constexpr int PL = BN / 32;
   constexpr size_t PT = (size_t)MM * BN;              // words of one plane of a tile
