@@ -1181,18 +1181,45 @@ __device__ __forceinline__ void load_codes16(const void *codes, size_t idx, uint
   }
 }
 
-__device__ __forceinline__ int block_min(int v, int *red) {
+// Block-wide min of lo and max of hi and nz in one exchange (one barrier).  The
+// caller keeps a barrier between two uses of `red` (the next row's exchange
+// starts only after this row's later barriers).
+__device__ __forceinline__ void block_minmax(int &lo, int &hi, int &nz, int4 *red) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
+    nz |= __shfl_xor_sync(0xFFFFFFFFu, nz, o);
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = make_int4(lo, hi, nz, 0);
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  int r = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) r = min(r, red[w]);
-  return r;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+    const int4 v = red[w];
+    lo = min(lo, v.x);
+    hi = max(hi, v.y);
+    nz |= v.z;
+  }
 }
 
-__device__ __forceinline__ int block_max(int v, int *red) { return -block_min(-v, red); }
+// Each byte of the result: 0xFF where bit 7 of that byte of a is set, else 0
+// (prmt's sign-replicating selector nibbles 8..B).
+__device__ __forceinline__ uint32_t byte_signs(uint32_t a) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(0u), "r"(0xBA98u));
+  return d;
+}
+
+// Two 16-bit lanes per register: native unsigned min / max (sm_90 and later).
+__device__ __forceinline__ uint32_t min_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 
 // bp8 decode table entry: lsb exponent, binade and signed mantissa packed in
 // 10 + 10 + 12 bits (bp8: |lsb|, |binade| <= 24, |mantissa| <= 15).
@@ -1236,7 +1263,7 @@ struct PrepOp {
 };
 
 template <int FMT, int S>
-__global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp opB, int K, int Kp, int G,
+__global__ void __launch_bounds__(256, 5) k_tc_prep(const PrepOp opA, const PrepOp opB, int K, int Kp, int G,
                                                  int group, int pool_cap) {
   constexpr int SPAN = Cfg<S>::SPAN;
   constexpr int DB = Cfg<S>::DB, HALF = Cfg<S>::HALF, DMASK = (1 << DB) - 1;   // digit base 2^DB
@@ -1245,7 +1272,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
   __shared__ int s_tail[TAILCAP];
   __shared__ uint32_t s_dec[FMT == 8 ? 256 : 1];  // packed lsb | binade | mantissa (dec_* below)
   __shared__ uint32_t s_dig[FMT == 8 ? 256 : 1];
-  __shared__ int red[8];
+  __shared__ int4 red[8];
   __shared__ int s_nt, s_off, s_slot;
   if (FMT == 8) {
     for (int c = threadIdx.x; c < 256; c += blockDim.x) {
@@ -1281,25 +1308,39 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
     int lo = 0x3FFFFFFF, hi = -0x3FFFFFFF, nz = 0;
     const bool chunk_groups = sc != nullptr && (group % EPT) == 0;
     if (FMT == 8 && sc == nullptr && vec) {
-      // unscaled bp8: running byte-wise min / max of the code magnitudes, four
-      // codes per SIMD op; zero and NaR (low 7 bits 0) count as 0xFF for the
-      // minimum and 0 for the maximum.  Decoded once at the end.
-      uint32_t mnw = 0xFFFFFFFFu, mxw = 0u;
+      // unscaled bp8: the code magnitudes |c| = min(c, 256 - c) in two 16-bit
+      // lanes per register (0 for zero, 128 only for NaR), a running max of
+      // |c| and a running min of |c| - 1 (zero -> 0x7FFF), seven instructions
+      // per two codes.  A NaR makes the max 128: the rare thread that saw one
+      // redoes its span code by code, leaving out zero and NaR.  Decoded once
+      // at the end.
+      uint32_t mnw = 0x7FFF7FFFu, mxw = 0u;
       for (int k0 = threadIdx.x * 16; k0 < K; k0 += blockDim.x * 16) {
         const uint4 cw = *(const uint4 *)((const uint8_t *)codes + rb + k0);
         const uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t w = ws[q];
-          const uint32_t neg = __vcmpgeu4(w, 0x80808080u);
-          const uint32_t mag = __vsub4(w ^ neg, neg);
-          const uint32_t inv = __vcmpeq4(w & 0x7F7F7F7Fu, 0u);
-          mnw = __vminu4(mnw, mag | inv);
-          mxw = __vmaxu4(mxw, mag & ~inv);
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t x = __byte_perm(ws[q >> 1], 0u, (q & 1) ? 0x4341u : 0x4240u);   // two codes, 16-bit lanes
+          const uint32_t mag = min_u16x2(x, 0x01000100u - x);
+          mxw = max_u16x2(mxw, mag);
+          mnw = min_u16x2(mnw, (mag + 0x7FFF7FFFu) & 0x7FFF7FFFu);   // no carry between the lanes: |c| <= 128
         }
       }
-      const uint32_t mn = min(min(mnw & 0xFFu, (mnw >> 8) & 0xFFu), min((mnw >> 16) & 0xFFu, mnw >> 24));
-      const uint32_t mx = max(max(mxw & 0xFFu, (mxw >> 8) & 0xFFu), max((mxw >> 16) & 0xFFu, mxw >> 24));
+      uint32_t mn = min(mnw & 0xFFFFu, mnw >> 16) + 1u;
+      uint32_t mx = max(mxw & 0xFFFFu, mxw >> 16);
+      if (mx == 128u) {
+        mn = 0xFFu;
+        mx = 0u;
+        for (int k0 = threadIdx.x * 16; k0 < K; k0 += blockDim.x * 16)
+          for (int q = 0; q < 16; ++q) {
+            const uint32_t c = ((const uint8_t *)codes)[rb + k0 + q];
+            if (c & 0x7Fu) {
+              const uint32_t mag = (c & 0x80u) ? 256u - c : c;
+              mn = min(mn, mag);
+              mx = max(mx, mag);
+            }
+          }
+      }
       if (mx) {
         lo = dec_lsb(s_dec[mn]);
         hi = dec_hb(s_dec[mx]);
@@ -1361,9 +1402,7 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
         }
       }
     }
-    lo = block_min(lo, red);
-    hi = block_max(hi, red);
-    nz = block_max(nz, red);
+    block_minmax(lo, hi, nz, red);
     const int L = nz ? max(lo, hi - (SPAN - 1)) : 0;
     if (threadIdx.x == 0) {
       stats[r] = make_int4(nz ? lo : 0, nz ? hi : 0, nz, 0);
@@ -1443,6 +1482,19 @@ __global__ void __launch_bounds__(256) k_tc_prep(const PrepOp opA, const PrepOp 
           }
 #pragma unroll
           for (int sd = 0; sd < 3; ++sd)
+            __stcs((uint4 *)(row + sd * plane + k0), make_uint4(wd[sd][0], wd[sd][1], wd[sd][2], wd[sd][3]));
+        } else if (S == 2) {
+          // 4 x 2 byte transpose per 4 codes: 4 permutes for the two plane words
+          uint32_t wd[2][4];
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint32_t a01 = __byte_perm(v[4 * g], v[4 * g + 1], 0x5140);      // d0 d0' d1 d1'
+            const uint32_t a23 = __byte_perm(v[4 * g + 2], v[4 * g + 3], 0x5140);
+            wd[0][g] = __byte_perm(a01, a23, 0x5410);
+            wd[1][g] = __byte_perm(a01, a23, 0x7632);
+          }
+#pragma unroll
+          for (int sd = 0; sd < 2; ++sd)
             __stcs((uint4 *)(row + sd * plane + k0), make_uint4(wd[sd][0], wd[sd][1], wd[sd][2], wd[sd][3]));
         } else {
 #pragma unroll
@@ -1694,12 +1746,13 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
     }
   }
   __syncthreads();
-  // per byte i (row 4br + i): la + 128 and the base L + 128 clamped to 0 .. 255
+  // per byte i (row 4br + i): la + 64 and the base L + 64 clamped to 1 .. 127
+  // (1 keeps every nonzero element: a row without a base, B's whole copy)
   uint32_t la4 = 0u, L4 = 0u;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    la4 |= (uint32_t)(s_la[4 * br + i] + 128) << (8 * i);
-    L4 |= (uint32_t)min(max(s_L[4 * br + i] + 128, 0), 255) << (8 * i);
+    la4 |= (uint32_t)(s_la[4 * br + i] + 64) << (8 * i);
+    L4 |= (uint32_t)min(max(s_L[4 * br + i] + 64, 1), 127) << (8 * i);
   }
 #pragma unroll
   for (int g = 0; g < 2; ++g) {   // columns 4g .. 4g + 3 of the thread's 8
@@ -1712,18 +1765,23 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
                             __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      // the four rows' entries; byte i of lw is row i's lsb + 128 (0 for zero / NaR)
+      // the four rows' entries; byte i of lw is row i's lsb + 64 (0 for zero / NaR)
       const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 16 + tl16];
       const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 16 + tl16];
       const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 16 + tl16];
       const uint32_t d3 = s_dec[(cw[q] >> 24) * 16 + tl16];
       const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
       const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
-      const uint32_t keep = __vcmpgeu4(lw, L4) & __vcmpne4(lw, 0u);
+      // per byte, lw | 0x80 minus L4 (or la4) cannot borrow from the next byte
+      // (lw | 0x80 >= 128 > L4, la4); its bit 7 is lw >= L4, which also leaves
+      // out zero and NaR (lw = 0 < 1 <= L4), spread to the byte by the
+      // permute's sign replication
+      const uint32_t x = lw | 0x80808080u;
+      const uint32_t keep = byte_signs(x - L4);
       // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
       // a warp (bc = 0..15, two br) spread over the banks
       tm[8 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
-      te[8 * bc + 4 * g + q][(br + bc) & 15] = __vsub4(lw, la4) & keep;
+      te[8 * bc + 4 * g + q][(br + bc) & 15] = (x - la4) & 0x7F7F7F7Fu & keep;   // lsb - la
     }
   }
   __syncthreads();
@@ -1756,14 +1814,14 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   extern __shared__ __align__(16) uint32_t kms[];
   uint32_t(*tm)[17] = (uint32_t(*)[17])kms;                // [k][row / 4], one pad word
   uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
-  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 128) << 8 | (uint8) m, per lane % 16
+  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 64) << 8 | (uint8) m, per lane % 16
   __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
   const int t = threadIdx.x;
   {
     int m, e;
     posit_to_me<8, 2>((uint32_t)t, m, e);
     // bp8 lsb exponents lie in [-24, 24]: the entry of a nonzero code is nonzero
-    const uint16_t d = m ? (uint16_t)(((e + 128) << 8) | (uint8_t)(int8_t)m) : (uint16_t)0;
+    const uint16_t d = m ? (uint16_t)(((e + 64) << 8) | (uint8_t)(int8_t)m) : (uint16_t)0;
     for (int l = 0; l < 16; ++l) s_dec[t * 16 + l] = d;
   }
   const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 8bc .. + 7
@@ -2450,7 +2508,7 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   if (reuse_b || a_only) pb.rows = 0;
   int rc = kOk;
   if (pa.rows + pb.rows > 0) {
-    const int g = std::min(pa.rows + pb.rows, sms * 8);
+    const int g = std::min(pa.rows + pb.rows, sms * 5);   // all resident (5 blocks per SM)
     if (a.fmt == 16)
       k_tc_prep<16, 4><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     else if (S == 2)
