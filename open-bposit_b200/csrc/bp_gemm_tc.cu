@@ -1314,9 +1314,14 @@ __global__ void __launch_bounds__(256, 5) k_tc_prep(const PrepOp opA, const Prep
       // per two codes.  A NaR makes the max 128: the rare thread that saw one
       // redoes its span code by code, leaving out zero and NaR.  Decoded once
       // at the end.
+      // Each thread's next 16 codes are loaded one step ahead.
       uint32_t mnw = 0x7FFF7FFFu, mxw = 0u;
-      for (int k0 = threadIdx.x * 16; k0 < K; k0 += blockDim.x * 16) {
-        const uint4 cw = *(const uint4 *)((const uint8_t *)codes + rb + k0);
+      const int step = blockDim.x * 16;
+      uint4 nxt = make_uint4(0u, 0u, 0u, 0u);
+      if (threadIdx.x * 16 < K) nxt = *(const uint4 *)((const uint8_t *)codes + rb + threadIdx.x * 16);
+      for (int k0 = threadIdx.x * 16; k0 < K; k0 += step) {
+        const uint4 cw = nxt;
+        if (k0 + step < K) nxt = *(const uint4 *)((const uint8_t *)codes + rb + k0 + step);
         const uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -1442,13 +1447,18 @@ __global__ void __launch_bounds__(256, 5) k_tc_prep(const PrepOp opA, const Prep
     if (lut && vec) {
       // unscaled bp8: every code's S digits come packed in one table word
       // (bit 31 = tail); plane words are assembled with byte permutes
-      for (int k0 = threadIdx.x * 16; k0 < Kp; k0 += blockDim.x * 16) {
+      // last read of these codes (each thread's next 16 loaded one step
+      // ahead); the plane stores below stream past L2 (evict-first) so that
+      // this second pass finds its row still there
+      const int step = blockDim.x * 16;
+      uint4 nxt = make_uint4(0u, 0u, 0u, 0u);
+      if (threadIdx.x * 16 < K) nxt = __ldcs((const uint4 *)((const uint8_t *)codes + rb + threadIdx.x * 16));
+      for (int k0 = threadIdx.x * 16; k0 < Kp; k0 += step) {
         uint32_t v[16];
         uint32_t any = 0u;
+        const uint4 cw = nxt;
+        if (k0 + step < K) nxt = __ldcs((const uint4 *)((const uint8_t *)codes + rb + k0 + step));
         if (k0 < K) {
-          // last read of these codes; the plane stores below stream past L2
-          // (evict-first) so that this second pass finds its row still there
-          uint4 cw = __ldcs((const uint4 *)((const uint8_t *)codes + rb + k0));
           uint32_t ws[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
@@ -1587,7 +1597,8 @@ __global__ void __launch_bounds__(256, 5) k_tc_prep(const PrepOp opA, const Prep
     __syncthreads();
     if (s_slot >= 0)
       for (int t = threadIdx.x; t < s_nt; t += blockDim.x) tails[s_off + t] = s_tail[t];
-    __syncthreads();
+    // no barrier here: the next row touches s_nt, s_tail and the tables only
+    // after the barrier of its statistics exchange
   }
 }
 
@@ -2508,13 +2519,18 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
   if (reuse_b || a_only) pb.rows = 0;
   int rc = kOk;
   if (pa.rows + pb.rows > 0) {
-    const int g = std::min(pa.rows + pb.rows, sms * 5);   // all resident (5 blocks per SM)
+    // one block per row at a time, sized to the row: a short row (the model
+    // linears' K = 896) leaves most of a 256-thread block idle in both passes,
+    // so short rows take 64 or 128 threads and more rows run at once; every
+    // block is resident (1280 threads per SM at 48 registers)
+    const int thr = a.K <= 2048 ? 64 : (a.K <= 8192 ? 128 : 256);
+    const int g = std::min(pa.rows + pb.rows, sms * (1280 / thr));
     if (a.fmt == 16)
-      k_tc_prep<16, 4><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+      k_tc_prep<16, 4><<<g, thr, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     else if (S == 2)
-      k_tc_prep<8, 2><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+      k_tc_prep<8, 2><<<g, thr, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     else
-      k_tc_prep<8, 3><<<g, 256, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
+      k_tc_prep<8, 3><<<g, thr, 0, s>>>(pa, pb, a.K, L.Kp, a.G, a.group, L.pool);
     rc = check_launch("tc_prep");
   }
   // The narrow form's decoded K-major copies of the operands prepared here --
