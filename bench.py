@@ -102,25 +102,41 @@ class Clocks:
                 pass
             self._stop.wait(0.02)
 
-    def start(self):
-        import threading
+    def prepare(self):
+        """The slow part of start() (NVML initialisation, several ms): done
+        before the ranks' barrier, so that start() at the timed region's
+        opening costs only a thread start and no rank begins late (a rank's
+        late start shows up on every other rank as time spent waiting in the
+        step's collectives)."""
         try:
             nv, h = self._nvml_handle()
             self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
-            self._thread = threading.Thread(target=self._run, args=(nv, h), daemon=True)
-            self._thread.start()
+            self._nv = (nv, h)
         except Exception:
-            try:
-                self._path = os.path.join("/tmp", f"bposit_clocks_{os.getpid()}.csv")
-                self._fh = open(self._path, "w")
-                self._proc = subprocess.Popen(
-                    ["nvidia-smi", f"--id={self.idx}", "--query-gpu=clocks.sm,clocks.max.sm,"
-                     "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                     "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                     "--format=csv,noheader,nounits", "-lms", "200"], stdout=self._fh, stderr=subprocess.DEVNULL)
-            except (OSError, ValueError):
-                self._proc = None
+            self._nv = None
+            self._start_smi()   # the fallback samples from here on (every 200 ms)
         return self
+
+    def start(self):
+        import threading
+        if not hasattr(self, "_nv"):
+            self.prepare()
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, args=self._nv, daemon=True)
+            self._thread.start()
+        return self
+
+    def _start_smi(self):
+        try:
+            self._path = os.path.join("/tmp", f"bposit_clocks_{os.getpid()}.csv")
+            self._fh = open(self._path, "w")
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", "--query-gpu=clocks.sm,clocks.max.sm,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self._fh, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self._proc = None
 
     def stop(self):
         if self._thread is not None:
@@ -201,8 +217,10 @@ class Ctx:
             if flush:
                 self.flush_l2()
             fn()
+        clocks = Clocks(self.local).prepare() if self.local == 0 else None
         self.sync_all()
-        clocks = Clocks(self.local).start() if self.local == 0 else None
+        if clocks is not None:
+            clocks.start()
         n0 = _lib.lib().bp_launch_count()
         st = self.stream()
         if flush:
