@@ -2393,7 +2393,7 @@ SideStream *side_stream() {
 template <int S, bool PAIR>
 int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p, const TcSchedule &sc,
                        int grid_finish, cudaStream_t s, cudaEvent_t corr_done,
-                       const std::function<int()> *after_first = nullptr) {
+                       const std::function<int(bool)> *after_first = nullptr) {
   using C = Cfg<S, PAIR>;
   struct Seg {
     int tile0, n, split, kbc;
@@ -2427,7 +2427,9 @@ int launch_tc_schedule(const CUtensorMap &ma, const CUtensorMap &mb, TcParams p,
     if (rc) break;
     // work that runs beside the GEMM (it records corr_done): after the first
     // segment's CTAs, so that they are placed first
-    if (k == 0 && after_first && (rc = (*after_first)()) != kOk) break;
+    // (told whether this is the only segment: then no later GEMM launch can be
+    // held back by its blocks that wait for the GEMM's SMs)
+    if (k == 0 && after_first && (rc = (*after_first)(nseg == 1)) != kOk) break;
     const bool on_s = k == nseg - 1 || !side || seg[k].n > 2 * seg[k + 1].kbc;
     cudaStream_t fs = on_s ? s : side->st;
     if (!on_s) {
@@ -2654,14 +2656,17 @@ int launch_gemm_tc(const GemmArgs &a, int4 *sta, int4 *stb, void *ws, size_t ws_
     rc = check_launch("tc_corr");
   }
   cudaEvent_t corr_done = nullptr;
-  std::function<int()> beside;   // the narrow form's side work, launched after the first GEMM segment
+  std::function<int(bool)> beside;   // the narrow form's side work, launched after the first GEMM segment
   if (!rc && oside) {
     // the side stream starts after the prep (this record precedes the GEMM's launch)
     if (cudaEventRecord(oside->ev[3], s) != cudaSuccess || cudaStreamWaitEvent(oside->st, oside->ev[3], 0) != cudaSuccess)
       return set_error(kECuda, "quire_gemm: side stream: %s", cudaGetErrorString(cudaGetLastError()));
-    beside = [&]() -> int {
+    beside = [&](bool only_segment) -> int {
       int r = launch_copies(oside->st, 2LL * sms);
-      if (!r) r = launch_corr_t(oside->st, sms);
+      // one block per SM fits beside the GEMM's CTA; when the GEMM is a single
+      // segment, a second block per SM (the work queue is dynamic) takes up
+      // the SMs its CTAs leave, as no later GEMM segment waits behind them
+      if (!r) r = launch_corr_t(oside->st, only_segment ? 2 * sms : sms);
       if (cudaEventRecord(oside->ev[4], oside->st) != cudaSuccess && !r)
         r = set_error(kECuda, "quire_gemm: side stream event: %s", cudaGetErrorString(cudaGetLastError()));
       return r;
