@@ -203,6 +203,32 @@ def test_zero_and_nar_only(ops):
     assert not out.any() and not q.any()
 
 
+@pytest.mark.parametrize("algo", [0, 4, 5])
+def test_tc_nar_codes_count_as_zero(ops, orc, algo):
+    """NaR codes inside tensor-core rows decode to 0, as code_value does
+    (reference/bposit_ref.py:1022-1025): rows with scattered NaRs, a row of NaR
+    and zero only, a row whose one nonzero code sits among NaRs.  K = 16384
+    takes the narrow form under auto, whose row statistics treat a span that
+    holds a NaR apart."""
+    rng = np.random.default_rng(11)
+    M, N, K = 384, 352, 16384     # M x N large enough for the tensor cores under auto
+
+    def codes(rows):   # magnitudes 0x28 .. 0x57 (values near 1), random signs
+        mag = rng.integers(0x28, 0x58, (rows, K))
+        return np.where(rng.random((rows, K)) < 0.5, mag, 256 - mag).astype(np.uint8)
+
+    A, B = codes(M), codes(N)
+    A[rng.random((M, K)) < 0.01] = 0x80
+    B[rng.random((N, K)) < 0.01] = 0x80
+    A[3] = np.where(rng.random(K) < 0.5, 0x80, 0).astype(np.uint8)
+    A[5] = 0x80
+    A[5, 777] = 0x41
+    B[7, :4096] = 0x80
+    out, _ = run(ops, A, B, 8, algo)
+    assert np.array_equal(out, orc.quire_gemm(A, B, 8))
+    assert not out[3].any()
+
+
 def test_smollm_layer_shapes_row_subsample(ops, orc):
     """The SmolLM2-135M-shaped projections at M=2048 (group-scaled RTN codes):
     all outputs computed on the device, 16 rows checked against the oracle."""
