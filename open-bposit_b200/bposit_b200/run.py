@@ -1,12 +1,13 @@
 """Run one workload of the library on the current GPU and print its timing.
 
-    python -m bposit_b200.run gemm M N K [--fmt bp8|bp16] [--group 128] [--calls 3] [--algo 0]
+    python -m bposit_b200.run gemm M N K [--fmt bp8|bp16] [--group 128] [--calls 3] [--algo 0] [--timeline]
     python -m bposit_b200.run codec N [--fmt bp8|bp16] [--calls 3]
     python -m bposit_b200.run qwen05 [--batch 8] [--seq 1024] [--layers 24] [--fp32]
     python -m bposit_b200.run linear M N K [--calls 3]
 
 ``gemm`` times bp_quire_gemm on operands N(0,1) * 2^U{-8..8} per row (the
-large-GEMM workload's distribution), quantized on the device; ``linear`` times
+large-GEMM workload's distribution), quantized on the device (``--timeline``
+adds the start and end of every kernel of one more call); ``linear`` times
 one BpositLinear (the W8A8 nn.Linear drop-in, fp32 out) of N x K random
 weights on M rows of N(0,1) activations; ``codec`` times
 the encode and decode kernels on the codec-sweep value mix; ``qwen05`` times
@@ -60,10 +61,35 @@ def run_gemm(a) -> str:
     ws = torch.empty(max(256, ops.gemm_workspace_size(fmt, a.M, a.N, a.K, a.algo)), dtype=torch.uint8,
                      device="cuda")
     out = torch.empty((a.M, a.N), dtype=torch.uint32, device="cuda")
-    ms = _time(lambda: ops.quire_gemm(A, B, fmt, sa=sa, sb=sb, group=a.group or 128, out=out, algo=a.algo,
-                                      workspace=ws), a.calls)
-    return (f"gemm {a.fmt} M={a.M} N={a.N} K={a.K} group={a.group}: {ms:.3f} ms/call, "
+
+    def call():
+        ops.quire_gemm(A, B, fmt, sa=sa, sb=sb, group=a.group or 128, out=out, algo=a.algo, workspace=ws)
+
+    ms = _time(call, a.calls)
+    line = (f"gemm {a.fmt} M={a.M} N={a.N} K={a.K} group={a.group}: {ms:.3f} ms/call, "
             f"{2.0 * a.M * a.N * a.K / ms / 1e9:.1f} TOPS")
+    return line + ("\n" + _timeline(call) if a.timeline else "")
+
+
+def _timeline(fn) -> str:
+    """Start and end (ms from the first launch) of every kernel and memset of
+    one more call, from torch.profiler's CUDA activity trace: which kernels
+    overlap and which one ends the call."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    evs = [e for e in prof.events() if str(getattr(e, "device_type", "")).split(".")[-1] == "CUDA"]
+    if not evs:
+        return "  (no CUDA activity recorded)"
+    t0 = min(e.time_range.start for e in evs)
+    rows = []
+    for e in sorted(evs, key=lambda e: e.time_range.start):
+        name = e.name.replace("(anonymous namespace)::", "").replace("void ", "").replace("bp::", "").split("(")[0]
+        rows.append(f"  {name[:48]:48s} {(e.time_range.start - t0) / 1e3:8.3f} -> {(e.time_range.end - t0) / 1e3:8.3f}"
+                    f" ms  ({(e.time_range.end - e.time_range.start) / 1e3:.3f})")
+    return "\n".join(rows)
 
 
 def run_codec(a) -> str:
@@ -114,6 +140,7 @@ def main(argv=None) -> int:
     g.add_argument("--fmt", default="bp8", choices=["bp8", "bp16"])
     g.add_argument("--group", type=int, default=0, help="per-group power-of-two scales (bp8)")
     g.add_argument("--algo", type=int, default=0)
+    g.add_argument("--timeline", action="store_true", help="print the kernel timeline of one more call")
     c = sub.add_parser("codec")
     c.add_argument("n", type=int)
     c.add_argument("--fmt", default="bp8", choices=["bp8", "bp16"])
