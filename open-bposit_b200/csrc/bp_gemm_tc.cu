@@ -1681,19 +1681,23 @@ __global__ void __launch_bounds__(256) k_tc_corr(const CorrSide s0, const CorrSi
 // Zero and NaR are m = 0.
 // Blocks stride over tiles of 64 rows x 128 columns: thread t loads 8 bytes
 // of each of 4 rows, transposes the two 4 x 4 blocks in registers (byte
-// permutes), decodes its 32 codes through a 16-bit table replicated 16 times
-// (entry (code, lane % 16) at half-word 16 code + lane % 16; built once per
-// block), parks the M and E words in shared memory (local row kk's word slots
-// rotated by kk / 8, so a warp's stores spread over the banks), then four
-// threads store the 64 bytes of one output row of each plane.  Each thread
+// permutes) and parks the raw code words in shared memory (local row kk's
+// word slots rotated by kk / 8, so a warp's stores spread over the banks);
+// then four threads take the 64 codes of one output row, each decoding its 16
+// through a table with one copy per lane (entry (code, lane) in the 32-bit
+// word 32 (code >> 1) + lane, half-word code & 1: every lane reads its own
+// bank), and store 16 bytes of each plane.  Decoding after the transpose
+// moves one byte per code through the staging instead of two; the decode
+// before it used a 16-copy table with up to 4-way bank conflicts.  Each thread
 // issues a tile's loads two tiles before it works on it (a copy with one
-// tile's loads in flight per thread was bound by their latency).  26 KB of
+// tile's loads in flight per thread was bound by their latency).  25 KB of
 // shared memory lets two blocks sit beside a narrow-form GEMM CTA.  The
 // blocks of the first column of tiles also record, per 64 rows, the widest
 // row range hb - la (hr64, zeroed by the caller).  kKmajSmem bytes of
 // dynamic shared memory.
 constexpr int kKmajK = 128;
-constexpr size_t kKmajSmem = 2 * (size_t)kKmajK * 17 * 4 + 256 * 16 * 2;
+constexpr size_t kKmajTable = 128 * 32 * 4;   // 256 codes x 32 lanes, 16-bit entries
+constexpr size_t kKmajSmem = (size_t)kKmajK * 17 * 4 + kKmajTable;
 
 // One tile's global loads, issued two tiles ahead of their use: the thread's
 // 8 bytes of each of its 4 rows, and (threads < 64) the tile row's minimum lsb
@@ -1734,19 +1738,37 @@ __device__ __forceinline__ void kmaj_fetch(long long tile, long long ntiles, int
   }
 }
 
-// One tile from its fetched loads: decode, transpose through shared memory,
-// store the two planes' 128 output rows of 64 bytes.
+// The (lsb + 64) << 8 | (uint8) m entries of the four codes in word v (bytes
+// in row order), read from this lane's copy of the table; byte address of
+// entry (code, lane): 128 (code >> 1) + 4 lane + 2 (code & 1).
+__device__ __forceinline__ void kmaj_decode4(uint32_t v, const uint8_t *s_tab, uint32_t lane4, uint32_t &mw,
+                                             uint32_t &lw) {
+  uint32_t d[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b = (v >> (8 * i)) & 0xFFu;
+    d[i] = *(const uint16_t *)(s_tab + (((b >> 1) << 7) | lane4 | ((b & 1u) << 1)));
+  }
+  const uint32_t lo = d[0] | (d[1] << 16), hi = d[2] | (d[3] << 16);
+  mw = __byte_perm(lo, hi, 0x6420);
+  lw = __byte_perm(lo, hi, 0x7531);
+}
+
+// One tile from its fetched loads: transpose the codes through shared memory,
+// decode, store the two planes' 128 output rows of 64 bytes.
 __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int K, uint8_t *__restrict__ dme,
                                           int ldt, const int4 *__restrict__ st,
                                           int *__restrict__ hr64, int t, int br, int bc, const KmajFetch &f,
-                                          uint32_t (*tm)[17], uint32_t (*te)[17], const uint16_t *s_dec,
-                                          int *s_la, int *s_L) {
-  const int tl16 = t & 15;
+                                          uint32_t (*tc)[17], const uint8_t *s_tab, uint8_t *s_la4,
+                                          uint8_t *s_L4) {
   const int k0 = (int)(tile % tk) * kKmajK, r0 = (int)(tile / tk) * 64;
   __syncthreads();   // the previous tile's rows and staging are no longer read
   if (t < 64) {
-    s_la[t] = f.la;
-    s_L[t] = f.L;
+    // per tile row: la + 64 and the base L + 64 clamped to 1 .. 127 (1 keeps
+    // every nonzero element: a row without a base, B's whole copy), one byte
+    // each, so that word w holds rows 4w .. 4w + 3
+    s_la4[t] = (uint8_t)(f.la + 64);
+    s_L4[t] = (uint8_t)min(max(f.L + 64, 1), 127);
     // the widest row range (hb - la) of these 64 rows, once per row block: it
     // bounds the E plane here, for the corrections' choice of arithmetic
     if (k0 == 0) {
@@ -1755,15 +1777,6 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
       for (int o = 16; o > 0; o >>= 1) h = max(h, __shfl_xor_sync(0xFFFFFFFFu, h, o));
       if ((t & 31) == 0) atomicMax(&hr64[r0 / 64], h);
     }
-  }
-  __syncthreads();
-  // per byte i (row 4br + i): la + 64 and the base L + 64 clamped to 1 .. 127
-  // (1 keeps every nonzero element: a row without a base, B's whole copy)
-  uint32_t la4 = 0u, L4 = 0u;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    la4 |= (uint32_t)(s_la[4 * br + i] + 64) << (8 * i);
-    L4 |= (uint32_t)min(max(s_L[4 * br + i] + 64, 1), 127) << (8 * i);
   }
 #pragma unroll
   for (int g = 0; g < 2; ++g) {   // columns 4g .. 4g + 3 of the thread's 8
@@ -1774,33 +1787,25 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
     const uint32_t b01 = __byte_perm(r0w, r1w, 0x7362), b23 = __byte_perm(r2w, r3w, 0x7362);
     const uint32_t cw[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
                             __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
+    // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
+    // a warp (bc = 0..15, two br) spread over the banks
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      // the four rows' entries; byte i of lw is row i's lsb + 64 (0 for zero / NaR)
-      const uint32_t d0 = s_dec[(cw[q] & 0xFFu) * 16 + tl16];
-      const uint32_t d1 = s_dec[((cw[q] >> 8) & 0xFFu) * 16 + tl16];
-      const uint32_t d2 = s_dec[((cw[q] >> 16) & 0xFFu) * 16 + tl16];
-      const uint32_t d3 = s_dec[(cw[q] >> 24) * 16 + tl16];
-      const uint32_t lo = d0 | (d1 << 16), hi = d2 | (d3 << 16);
-      const uint32_t mw = __byte_perm(lo, hi, 0x6420), lw = __byte_perm(lo, hi, 0x7531);
-      // per byte, lw | 0x80 minus L4 (or la4) cannot borrow from the next byte
-      // (lw | 0x80 >= 128 > L4, la4); its bit 7 is lw >= L4, which also leaves
-      // out zero and NaR (lw = 0 < 1 <= L4), spread to the byte by the
-      // permute's sign replication
-      const uint32_t x = lw | 0x80808080u;
-      const uint32_t keep = byte_signs(x - L4);
-      // word br of local row kk sits at slot (br + kk / 8) % 16, so the lanes of
-      // a warp (bc = 0..15, two br) spread over the banks
-      tm[8 * bc + 4 * g + q][(br + bc) & 15] = mw & keep;
-      te[8 * bc + 4 * g + q][(br + bc) & 15] = (x - la4) & 0x7F7F7F7Fu & keep;   // lsb - la
-    }
+    for (int q = 0; q < 4; ++q) tc[8 * bc + 4 * g + q][(br + bc) & 15] = cw[q];
   }
   __syncthreads();
   // output rows k0 .. k0 + kKmajK - 1, 64 bytes (rows r0 .. r0 + 63) each per
-  // plane: four threads per row (16 bytes each), so a warp stores 8 rows x 64
-  // bytes per plane.  The tile's 64 rows lie in one 512-column block (b, width w).
+  // plane: four threads per row, each decoding and storing 16 rows' bytes, so a
+  // warp stores 8 rows x 64 bytes per plane.  The tile's 64 rows lie in one
+  // 512-column block (b, width w).
   const int c = t & 3, r = r0 + 16 * c;
   const int blk = r0 & ~511, wb = min(512, ldt - blk);
+  const uint32_t lane4 = (uint32_t)(t & 31) << 2;
+  uint32_t la4[4], L4[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    la4[j] = ((const uint32_t *)s_la4)[4 * c + j];
+    L4[j] = ((const uint32_t *)s_L4)[4 * c + j];
+  }
 #pragma unroll
   for (int pass = 0; pass < kKmajK / 64; ++pass) {
     const int kk = pass * 64 + (t >> 2), k = k0 + kk, rot = kk >> 3;
@@ -1808,8 +1813,17 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
       uint32_t vm[4], ve[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        vm[j] = tm[kk][(4 * c + j + rot) & 15];
-        ve[j] = te[kk][(4 * c + j + rot) & 15];
+        // rows 16c + 4j .. + 3: byte i of lw is row i's lsb + 64 (0 for zero / NaR)
+        uint32_t mw, lw;
+        kmaj_decode4(tc[kk][(4 * c + j + rot) & 15], s_tab, lane4, mw, lw);
+        // per byte, lw | 0x80 minus L4 (or la4) cannot borrow from the next byte
+        // (lw | 0x80 >= 128 > L4, la4); its bit 7 is lw >= L4, which also leaves
+        // out zero and NaR (lw = 0 < 1 <= L4), spread to the byte by the
+        // permute's sign replication
+        const uint32_t x = lw | 0x80808080u;
+        const uint32_t keep = byte_signs(x - L4[j]);
+        vm[j] = mw & keep;
+        ve[j] = (x - la4[j]) & 0x7F7F7F7Fu & keep;   // lsb - la
       }
       uint8_t *o = dme + (size_t)k * 2 * ldt + 2 * blk + (r - blk);
       *(uint4 *)o = make_uint4(vm[0], vm[1], vm[2], vm[3]);
@@ -1818,22 +1832,21 @@ __device__ __forceinline__ void kmaj_tile(long long tile, int tk, int rows, int 
   }
 }
 
-__global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
+__global__ void __launch_bounds__(256, 4) k_kmajor_bp8(const uint8_t *__restrict__ src, int rows, int K,
                                                     uint8_t *__restrict__ dme, int ldt,
                                                     const int4 *__restrict__ st, const int *__restrict__ Lr,
                                                     int *__restrict__ hr64) {
   extern __shared__ __align__(16) uint32_t kms[];
-  uint32_t(*tm)[17] = (uint32_t(*)[17])kms;                // [k][row / 4], one pad word
-  uint32_t(*te)[17] = (uint32_t(*)[17])(kms + kKmajK * 17);
-  uint16_t *s_dec = (uint16_t *)(kms + 2 * kKmajK * 17);   // (lsb + 64) << 8 | (uint8) m, per lane % 16
-  __shared__ int s_la[64], s_L[64];                        // per tile row: min lsb; main base
+  uint32_t(*tc)[17] = (uint32_t(*)[17])kms;                       // [k][row / 4] code words, one pad word
+  uint8_t *s_tab = (uint8_t *)(kms + kKmajK * 17);                 // kKmajTable bytes (kmaj_decode4)
+  __shared__ __align__(16) uint8_t s_la4[64], s_L4[64];           // per tile row: la + 64, L + 64
   const int t = threadIdx.x;
   {
     int m, e;
     posit_to_me<8, 2>((uint32_t)t, m, e);
     // bp8 lsb exponents lie in [-24, 24]: the entry of a nonzero code is nonzero
     const uint16_t d = m ? (uint16_t)(((e + 64) << 8) | (uint8_t)(int8_t)m) : (uint16_t)0;
-    for (int l = 0; l < 16; ++l) s_dec[t * 16 + l] = d;
+    for (int l = 0; l < 32; ++l) *(uint16_t *)(s_tab + (t >> 1) * 128 + 4 * l + 2 * (t & 1)) = d;
   }
   const int br = t >> 4, bc = t & 15;   // rows r0 + 4br .. + 3, columns k0 + 8bc .. + 7
   const bool vec = (K & 7) == 0 && (((uintptr_t)src) & 7u) == 0;
@@ -1849,13 +1862,13 @@ __global__ void __launch_bounds__(256) k_kmajor_bp8(const uint8_t *__restrict__ 
   kmaj_fetch(tile + g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
   kmaj_fetch(tile + 2 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
   for (; tile < ntiles; tile += 3 * g) {
-    kmaj_tile(tile, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fa, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fa, tc, s_tab, s_la4, s_L4);
     kmaj_fetch(tile + 3 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fa);
     if (tile + g >= ntiles) break;
-    kmaj_tile(tile + g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fb, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile + g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fb, tc, s_tab, s_la4, s_L4);
     kmaj_fetch(tile + 4 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fb);
     if (tile + 2 * g >= ntiles) break;
-    kmaj_tile(tile + 2 * g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fc, tm, te, s_dec, s_la, s_L);
+    kmaj_tile(tile + 2 * g, tk, rows, K, dme, ldt, st, hr64, t, br, bc, fc, tc, s_tab, s_la4, s_L4);
     kmaj_fetch(tile + 5 * g, ntiles, tk, src, rows, K, vec, st, Lr, t, br, bc, fc);
   }
 }
